@@ -1,0 +1,444 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 attention path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
+
+Workloads (synthetic seeded inputs of the named shapes; no dataset is involved):
+  decode_batched  config 2 (the headline): Llama-3.2-1B attention (32 Q / 8 KV heads, head_dim 64, interleaved
+                  RoPE theta 5e5); per GPU 64 sequences x 16 layers = 1024 independent rows, each a 4096-token
+                  fp16 paged cache plus one new token. A step = fused bias/RoPE/append of the 1024 new tokens +
+                  split-K flash-decode of all rows. Metric: decode attention HBM GB/s = algorithmic bytes / time,
+                  algorithmic bytes = fp16 K/V read (rows x 4097 x 8 x 64 x 2 x 2) + q, out, new-token traffic.
+  prefill         config 3: TinyLlama-1.1B attention (32 Q / 4 KV heads, theta 1e4), 8 sequences x 2048 bf16
+                  tokens x 22 layers = 176 items; a step = fused RoPE/append of all tokens + tcgen05 causal prefill.
+                  Metric: TFLOP/s with causal FLOPs 4 * H * D * sum(keys attended).
+With N > 1 (torchrun, one rank per GPU, NCCL) every rank runs its own shard of the same per-GPU work ("weak"
+scaling: the sequences shard with no collective); value = all ranks' work / max-over-ranks device time.
+
+--impl reference times nibble's own CPU attention (CpuBackend::attention with its AVX2/AVX-VNNI tier on a
+ThreadPool of all host threads, compiled from the reference sources into oracle/_ref) on a bounded sample of the
+same workload, in the same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+H2, KV2, D, CTX2, SEQ2, LAYERS2 = 32, 8, 64, 4096, 64, 16         # config 2
+H3, KV3, T3, SEQ3, LAYERS3 = 32, 4, 2048, 8, 22                     # config 3
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), float(p.get("bf16_tflops_sustained", p["bf16_tflops"])), "measured"
+    except Exception:
+        return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def profile_traffic(name):
+    """Per-launch DRAM bytes (read + write) recorded from an ncu capture in profiles/<name>.md, or None."""
+    path = os.path.join(ROOT, "profiles", name + ".md")
+    try:
+        with open(path) as f:
+            for line in f:
+                if line.startswith("traffic_bytes_per_launch:"):
+                    return float(line.split(":", 1)[1].strip())
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle sampling (200 ms) in the background; keeps timestamped samples."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.samples = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.device)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                self.samples.append((time.time(), parts))
+
+    def stop(self):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self, t0, t1):
+        win = [s for t, s in self.samples if t0 - 0.25 <= t <= t1 + 0.25] or [s for _, s in self.samples[-3:]]
+        if not win:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no nvidia-smi samples"], "samples": 0}
+        sm = [float(s[1]) for s in win if s[1].replace(".", "", 1).isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in win for i in range(4) if s[5 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": float(win[0][2]) if win else None,
+                "reasons": reasons, "samples": len(win)}
+
+
+# ---------------------------------------------------------------- distributed plumbing
+def dist_setup(gpus):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != gpus:
+        raise SystemExit(f"--gpus {gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x, world):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def fill_normal_(t, seed):
+    """Fills a 16-bit tensor with N(0,1) values rounded to its dtype, in chunks (bounded temporaries)."""
+    import torch
+    g = torch.Generator(device=t.device).manual_seed(seed)
+    flat = t.view(-1)
+    step = 1 << 27
+    for i in range(0, flat.numel(), step):
+        n = min(step, flat.numel() - i)
+        flat[i:i + n].copy_(torch.randn(n, generator=g, device=t.device, dtype=torch.float32).to(flat.dtype))
+
+
+# ---------------------------------------------------------------- config 2: batched decode
+def decode_batched(args, world, rank, local):
+    import torch
+    import nibble_b200 as nb
+    from nibble_b200.workloads import make_page_tables
+    rows = SEQ2 * LAYERS2
+    length = CTX2 + 1
+    ctx = nb.Context(local)
+    table, n_pages = make_page_tables([length] * rows, 16, shuffle_seed=100 + rank)
+    kv = ctx.kv_pool(n_pages, KV2)
+    fill_normal_(kv.tensor().view(torch.float16), seed=1000 + rank)
+    rng = np.random.default_rng(rank)
+    q_in_h = torch.from_numpy(rng.standard_normal((rows, H2, D)).astype(np.float32)).pin_memory()
+    k_in_h = torch.from_numpy(rng.standard_normal((rows, KV2, D)).astype(np.float32)).pin_memory()
+    v_in_h = torch.from_numpy(rng.standard_normal((rows, KV2, D)).astype(np.float32)).pin_memory()
+    out_h = torch.empty((rows, H2, D), dtype=torch.float32).pin_memory()
+    q_in, k_in, v_in = (t.cuda() for t in (q_in_h, k_in_h, v_in_h))
+    q = torch.empty((rows, H2, D), device="cuda")
+    out = torch.empty((rows, H2, D), device="cuda")
+    d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()  # noqa: E731
+    t_table = d(table)
+    lens = d(np.full(rows, length, np.int32))
+    tok_row = d(np.arange(rows, dtype=np.int32))
+    tok_pos = d(np.full(rows, CTX2, np.int32))
+    spec = nb.RopeSpec(5e5, False)
+    st = torch.cuda.current_stream()
+
+    def step(ev=None):
+        ctx.rope_kv_append(kv, q_in, k_in, v_in, q, tok_row, tok_pos, t_table, H2, spec)
+        if ev:
+            ev[0].record(st)
+        ctx.attn_decode(kv, q, t_table, lens, length, out)
+        if ev:
+            ev[1].record(st)
+
+    kv_bytes = rows * length * KV2 * D * 2 * 2
+    qo_bytes = 2 * rows * H2 * D * 4
+    append_bytes = rows * (H2 + 2 * KV2) * D * 4 + rows * H2 * D * 4 + rows * 2 * KV2 * D * 2
+    step_bytes = kv_bytes + qo_bytes + append_bytes
+    for _ in range(args.warmup):
+        step()
+    ctx.check()
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    barrier(world)
+    torch.cuda.synchronize()
+    t_wall0 = time.time()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for i in range(args.steps):
+        step(kev[i])
+    e1.record(st)
+    torch.cuda.synchronize()
+    barrier(world)
+    t_wall1 = time.time()
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+    kern_ms = statistics.mean(a.elapsed_time(b) for a, b in kev)
+    ctx.check()
+    # e2e through the C ABI: pinned host inputs -> nbl_write, kernels, nbl_read of the outputs, every step
+    for _ in range(max(1, args.warmup // 2)):
+        e2e_step(ctx, q_in_h, k_in_h, v_in_h, out_h, q_in, k_in, v_in, out, step)
+    barrier(world)
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(st)
+    for _ in range(args.steps):
+        e2e_step(ctx, q_in_h, k_in_h, v_in_h, out_h, q_in, k_in, v_in, out, step)
+    f1.record(st)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(f0.elapsed_time(f1) / args.steps, world)
+    sampler.stop()
+    hbm, _, _, src = peaks()
+    decode_bytes = kv_bytes + qo_bytes
+    achieved = decode_bytes / (kern_ms * 1e-3) / 1e9
+    traffic = profile_traffic("decode_kernel_cfg2")
+    res = {
+        "metric": "decode attn HBM GB/s", "value": world * step_bytes / (ms * 1e-3) / 1e9, "unit": "GB/s",
+        "ms_per_step": ms, "dtype": "fp16 KV, fp32 accumulate",
+        "config": {"workload": "config 2: Llama-3.2-1B batched decode", "heads": f"{H2}q/{KV2}kv", "head_dim": D,
+                   "sequences_per_gpu": SEQ2, "layers": LAYERS2, "kv_tokens": length, "page_size": 16,
+                   "kv_bytes_per_step_per_gpu": kv_bytes, "algorithmic_bytes_per_step_per_gpu": step_bytes,
+                   "l2": "inputs (8.6 GB/GPU) larger than L2; no flush needed", "parallelism": f"sequence-sharded x{world}"},
+        "e2e": {"value": world * step_bytes / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": int(q_in_h.numel() * 4 + k_in_h.numel() * 4 + v_in_h.numel() * 4),
+                "d2h_bytes_per_step": int(out_h.numel() * 4)},
+        "roofline": {"kernel": "decode_kernel", "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                     "frac": achieved / hbm, "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured" else "fallback 6650 GB/s",
+                     "frac_of_nominal_8000": achieved / 8000.0, "kernel_ms": kern_ms,
+                     "algorithmic_bytes_per_launch": decode_bytes, "traffic": traffic},
+        "gpu_launches_per_step": 2,
+        "clocks": sampler.summary(t_wall0, t_wall1),
+    }
+    kv.close()
+    ctx.close()
+    return res
+
+
+def e2e_step(ctx, q_in_h, k_in_h, v_in_h, out_h, q_in, k_in, v_in, out, step):
+    ctx.write(q_in.data_ptr(), q_in_h.numpy(), q_in_h.numel())
+    ctx.write(k_in.data_ptr(), k_in_h.numpy(), k_in_h.numel())
+    ctx.write(v_in.data_ptr(), v_in_h.numpy(), v_in_h.numel())
+    step()
+    ctx.read(out_h.numpy(), out.data_ptr(), out_h.numel())
+
+
+# ---------------------------------------------------------------- config 3: prefill
+def prefill(args, world, rank, local, steps=None, warmup=None):
+    import torch
+    import nibble_b200 as nb
+    from nibble_b200.workloads import make_page_tables
+    steps = steps or args.steps
+    warmup = warmup or args.warmup
+    items = SEQ3 * LAYERS3
+    ctx = nb.Context(local)
+    table, n_pages = make_page_tables([T3] * items, 16, shuffle_seed=200 + rank)
+    kv = ctx.kv_pool(n_pages, KV3, dtype=nb.BF16)
+    n_tok = items * T3
+    q_in = torch.empty((n_tok, H3, D), device="cuda", dtype=torch.bfloat16)
+    k_in = torch.empty((n_tok, KV3, D), device="cuda", dtype=torch.bfloat16)
+    v_in = torch.empty((n_tok, KV3, D), device="cuda", dtype=torch.bfloat16)
+    for i, t in enumerate((q_in, k_in, v_in)):
+        fill_normal_(t, seed=3000 + 10 * rank + i)
+    q = torch.empty_like(q_in)
+    out = torch.empty((n_tok, H3, D), device="cuda", dtype=torch.bfloat16)
+    d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()  # noqa: E731
+    t_table = d(table)
+    tok_row = d(np.repeat(np.arange(items, dtype=np.int32), T3))
+    tok_pos = d(np.tile(np.arange(T3, dtype=np.int32), items))
+    q_start = d(np.arange(items, dtype=np.int32) * T3)
+    q_len = d(np.full(items, T3, np.int32))
+    pos0 = d(np.zeros(items, np.int32))
+    spec = nb.RopeSpec(1e4, False)
+    st = torch.cuda.current_stream()
+
+    def step(ev=None):
+        ctx.rope_kv_append(kv, q_in, k_in, v_in, q, tok_row, tok_pos, t_table, H3, spec)
+        if ev:
+            ev[0].record(st)
+        ctx.attn_prefill(kv, q, q_start, q_len, pos0, t_table, T3, out)
+        if ev:
+            ev[1].record(st)
+
+    for _ in range(warmup):
+        step()
+    ctx.check()
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for i in range(steps):
+        step(kev[i])
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
+    kern_ms = statistics.mean(a.elapsed_time(b) for a, b in kev)
+    ctx.check()
+    flops = 4.0 * H3 * D * items * (T3 * (T3 + 1) / 2)
+    _, bf16, bf16_sus, src = peaks()
+    ach = flops / (kern_ms * 1e-3) / 1e12
+    res = {
+        "metric": "prefill attn TFLOP/s", "value": world * flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+        "ms_per_step": ms, "kernel_ms": kern_ms, "dtype": "bf16 operands, fp32 accumulate",
+        "config": {"workload": "config 3: TinyLlama-1.1B causal prefill", "heads": f"{H3}q/{KV3}kv", "head_dim": D,
+                   "sequences_per_gpu": SEQ3, "tokens": T3, "layers": LAYERS3, "flops_per_step_per_gpu": flops},
+        "roofline": {"kernel": "prefill_kernel", "bound": "tensor", "achieved": ach, "peak": bf16, "unit": "TFLOP/s",
+                     "frac": ach / bf16, "peak_source": f"{src} bf16_tflops (burst)", "frac_of_sustained": ach / bf16_sus,
+                     "frac_of_nominal_2250": ach / 2250.0, "traffic": profile_traffic("prefill_kernel_cfg3")},
+    }
+    kv.close()
+    ctx.close()
+    return res
+
+
+# ---------------------------------------------------------------- CPU baseline: nibble's own CpuBackend
+def cpu_baseline(seconds=10.0, n_bufs=48):
+    """CpuBackend::attention (AVX2/AVX-VNNI tier, ThreadPool of all host threads) on config-2 rows: one call per
+    (sequence, layer) with q [1, 32, 64] and the row's 4097-token cache widened to fp32 [4097, 8, 64]. Enough
+    distinct caches to exceed the CPU caches; runs for about `seconds`."""
+    import oracle
+    threads = os.cpu_count() or 1
+    be = oracle.RefBackend(threads)
+    length = CTX2 + 1
+    be.reserve(length, H2, 1, H2 * D)
+    rng = np.random.default_rng(0)
+    bufs = []
+    for _ in range(n_bufs):
+        k = rng.standard_normal((length, KV2, D)).astype(np.float16).astype(np.float32)
+        v = rng.standard_normal((length, KV2, D)).astype(np.float16).astype(np.float32)
+        bufs.append((k, v))
+    q = rng.standard_normal((1, H2, D)).astype(np.float32)
+    out = np.empty((1, H2, D), np.float32)
+    for k, v in bufs[:4]:
+        be.attention_into(q, k, v, out, 1, CTX2, H2, KV2, D)
+    calls = 0
+    t0 = time.perf_counter()
+    while True:
+        k, v = bufs[calls % n_bufs]
+        be.attention_into(q, k, v, out, 1, CTX2, H2, KV2, D)
+        calls += 1
+        el = time.perf_counter() - t0
+        if el >= seconds and calls >= 8:
+            break
+    row_bytes = length * KV2 * D * 2 * 2 + 2 * H2 * D * 4  # the GPU metric's algorithmic bytes for one row
+    return {"value": calls * row_bytes / el / 1e9, "unit": "GB/s", "cores": be.threads, "kind": "reference",
+            "sample": f"{calls} CpuBackend::attention calls (config-2 rows, ctx 4097, fp32 K/V widened from fp16) "
+                      f"in {el:.1f} s on {be.threads} threads; kernels tier {oracle.ref_kernels_name()}",
+            "ms_per_row": 1e3 * el / calls}
+
+
+def reference_arm(args):
+    """--impl reference: nibble's own CPU attention on config 2, each step a bounded sample of 32 rows."""
+    import oracle
+    threads = os.cpu_count() or 1
+    be = oracle.RefBackend(threads)
+    length = CTX2 + 1
+    rows_per_step = 32
+    rng = np.random.default_rng(0)
+    bufs = [(rng.standard_normal((length, KV2, D)).astype(np.float16).astype(np.float32),
+             rng.standard_normal((length, KV2, D)).astype(np.float16).astype(np.float32)) for _ in range(rows_per_step)]
+    q = rng.standard_normal((1, H2, D)).astype(np.float32)
+    out = np.empty((1, H2, D), np.float32)
+
+    def step():
+        for k, v in bufs:
+            be.attention_into(q, k, v, out, 1, CTX2, H2, KV2, D)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    el = time.perf_counter() - t0
+    row_bytes = length * KV2 * D * 2 * 2 + 2 * H2 * D * 4
+    val = rows_per_step * args.steps * row_bytes / el / 1e9
+    sample = (f"{rows_per_step} config-2 rows per step (1/32 of the per-GPU 1024-row step), CpuBackend::attention "
+              f"on {be.threads} threads, tier {oracle.ref_kernels_name()}")
+    return {"impl": "reference", "metric": "decode attn HBM GB/s", "value": val, "unit": "GB/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * el / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic (seeded N(0,1), fp16-rounded)",
+            "config": {"workload": "config 2: Llama-3.2-1B batched decode", "rows_per_step": rows_per_step,
+                       "kv_tokens": length},
+            "cpu_baseline": {"value": val, "unit": "GB/s", "cores": be.threads, "kind": "reference", "sample": sample},
+            "e2e": {"value": val, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["decode_batched", "prefill"], default="decode_batched")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the config-3 prefill leg of the default run")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    if args.impl == "reference":
+        if int(os.environ.get("RANK", "0")) != 0:
+            return
+        print(json.dumps(reference_arm(args)), flush=True)
+        return
+
+    world, rank, local = dist_setup(args.gpus)
+    if args.workload == "prefill":
+        res = prefill(args, world, rank, local)
+    else:
+        res = decode_batched(args, world, rank, local)
+        if not args.no_prefill:
+            res["prefill"] = prefill(args, world, rank, local, steps=max(3, args.steps // 10), warmup=3)
+    res.update({"n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "data": "synthetic (seeded N(0,1))"})
+    res["gpu_launches"] = res.pop("gpu_launches_per_step", 2) * args.steps
+    if rank == 0 and world == 1:
+        res["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

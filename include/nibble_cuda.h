@@ -1,0 +1,175 @@
+/* nibble_cuda.h -- C ABI of the B200 (sm_100a) attention backend for nibble.
+ *
+ * This is the boundary a nibble build binds to replace its CPU attention path. Every entry point is
+ * extern "C" with plain pointers and sizes; no C++ or torch type crosses it. Device pointers are CUDA
+ * device addresses on the context's device. All kernels run on the context's stream, in call order.
+ *
+ * Each declaration names the reference interface it replaces (paths inside the nibble source tree):
+ *   src/backend/backend.h          the abstract Backend the Transformer calls (alloc/free/read/reserve/
+ *                                  add_bias/rope/attention)
+ *   src/backend/cpu/cpu_backend.*  its CPU implementation
+ *   src/model/transformer.cpp      the caller: K/V projected into cache rows, bias, rope, attention
+ *
+ * Error convention. Every function returns an nbl_status (0 = NBL_OK). On failure, nbl_last_error() gives a
+ * self-contained message for the calling thread, the way nibble::Error::what() does (include/nibble/error.h);
+ * the C++ host layer (nibble_b200/csrc/host/cuda_backend.h) rethrows non-zero statuses as nibble::Error.
+ * Bad sizes and null pointers are rejected on the host before any launch. Device-resident indices (page
+ * tables, sequence lengths) are range-checked inside the kernels: an out-of-range entry is skipped and sets
+ * a sticky flag that nbl_ctx_check() reports as NBL_E_DEVICE.
+ */
+#ifndef NIBBLE_CUDA_H
+#define NIBBLE_CUDA_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NBL_ABI_VERSION 1
+
+/* The library is built with hidden visibility; only the entry points below are exported. */
+#if defined(__GNUC__)
+#define NBL_API __attribute__((visibility("default")))
+#else
+#define NBL_API
+#endif
+
+typedef enum {
+  NBL_OK = 0,
+  NBL_E_INVALID = 1,     /* bad argument (size, null pointer, unsupported shape) */
+  NBL_E_CUDA = 2,        /* a CUDA runtime call failed */
+  NBL_E_NOMEM = 3,       /* device allocation failed */
+  NBL_E_UNSUPPORTED = 4, /* valid request this build does not run (e.g. head_dim != 64 on a paged kernel) */
+  NBL_E_DEVICE = 5       /* a kernel found an out-of-range device-side index (see nbl_ctx_check) */
+} nbl_status;
+
+typedef enum { NBL_F32 = 0, NBL_F16 = 1, NBL_BF16 = 2 } nbl_dtype;
+
+typedef struct nbl_ctx nbl_ctx; /* device, stream, scratch, RoPE tables, allocation registry */
+typedef struct nbl_kv nbl_kv;   /* one paged K/V pool */
+
+/* Rotary-embedding options; same fields and meaning as nibble::RopeParams (src/backend/backend.h:16-20).
+ * freq_factors is HOST memory (head_dim/2 floats) or NULL. */
+typedef struct {
+  float freq_base;
+  int32_t neox; /* nonzero: rotate (i, i + head_dim/2); zero: rotate (2i, 2i + 1) */
+  const float* freq_factors;
+} nbl_rope_params;
+
+/* Paged K/V pool. A page holds page_size consecutive token positions of one sequence for every KV head:
+ *   pool[page][2 (K then V)][n_kv_heads][page_size][head_dim]  (dtype F16 or BF16)
+ * so the K rows of one (page, KV head) are one contiguous page_size*head_dim block. Sequences own pages
+ * through page tables (int32 page ids, row-major [rows, pt_stride]); pages need not be contiguous or
+ * ordered. Replaces the flat fp32 per-layer cache of src/model/transformer.cpp:74-90. */
+typedef struct {
+  int64_t n_pages;
+  int32_t n_kv_heads;
+  int32_t head_dim;  /* 64 on the TMA/tensor-core kernels */
+  int32_t page_size; /* 16 */
+  int32_t dtype;     /* NBL_F16 or NBL_BF16 */
+} nbl_kv_config;
+
+/* ABI version the library was built with (NBL_ABI_VERSION). */
+NBL_API int nbl_abi_version(void);
+/* Copies the calling thread's last error message (NUL-terminated, truncated to cap) and returns its full
+ * length. Mirrors nibble::Error::what(). */
+NBL_API size_t nbl_last_error(char* buf, size_t cap);
+
+/* ---- context (the Backend object itself; CpuBackend ctor/dtor src/backend/cpu/cpu_backend.cpp:20,70) ---- */
+NBL_API int nbl_ctx_create(int device, nbl_ctx** out);
+/* Frees every allocation, pool and table the context still owns (CpuBackend::~CpuBackend frees unfreed
+ * blocks, cpu_backend.cpp:70-72). */
+NBL_API int nbl_ctx_destroy(nbl_ctx* ctx);
+/* Runs later launches on `stream` (a cudaStream_t; NULL restores the context's own stream). */
+NBL_API int nbl_ctx_set_stream(nbl_ctx* ctx, void* stream);
+NBL_API void* nbl_ctx_stream(nbl_ctx* ctx);
+NBL_API int nbl_ctx_sync(nbl_ctx* ctx);
+/* Synchronises, then returns NBL_E_DEVICE (and clears the flag) if any kernel since the last check skipped
+ * an out-of-range page id, position or length. */
+NBL_API int nbl_ctx_check(nbl_ctx* ctx);
+
+/* ---- Backend memory ops ---- */
+/* Backend::reserve (backend.h:42-45; CpuBackend::reserve cpu_backend.cpp:24-67): sizes the split-K scratch and
+ * the RoPE tables for up to n_ctx positions and n_heads heads, so later attention calls within those limits
+ * allocate nothing. max_rows/max_width are accepted for interface parity. */
+NBL_API int nbl_reserve(nbl_ctx* ctx, int64_t n_ctx, int64_t n_heads, int64_t max_rows, int64_t max_width);
+/* Backend::alloc (backend.h:46-47): zeroed device block of n_floats floats (256-byte aligned). n_floats < 0 or
+ * an allocation failure is an error. */
+NBL_API int nbl_alloc(nbl_ctx* ctx, int64_t n_floats, float** out);
+/* Backend::free (backend.h:48-51): NULL is a no-op; a pointer this context did not allocate is ignored. */
+NBL_API int nbl_free(nbl_ctx* ctx, float* p);
+/* Backend::read (backend.h:52-53): copies n floats device -> host; returns after the copy completes. */
+NBL_API int nbl_read(nbl_ctx* ctx, float* host_dst, const float* src, int64_t n);
+/* Host -> device copy of n floats (no Backend counterpart: the CPU backend's memory is host memory, so the
+ * model writes activations directly; a device backend needs this for inputs). */
+NBL_API int nbl_write(nbl_ctx* ctx, float* dst, const float* host_src, int64_t n);
+
+/* ---- Backend ops on fp32 device activations (the drop-in path) ---- */
+/* Backend::add_bias (backend.h:63; ref_ops.cpp:156-161): x[t, i] += bias[i] for t < n, i < width. bias is a
+ * device pointer. */
+NBL_API int nbl_add_bias(nbl_ctx* ctx, float* x, const float* bias, int64_t width, int64_t n);
+/* Backend::rope (backend.h:64; ref_ops.cpp:166-185): in place on x[n, n_heads, head_dim] at positions pos0..
+ * Angles and cos/sin are evaluated in double on the host, as the reference does, and cached per
+ * (freq_base, head_dim, freq_factors); the rotation is two uncontracted float products. Bit-identical to
+ * nibble's cpu::rope. */
+NBL_API int nbl_rope(nbl_ctx* ctx, float* x, int64_t n, int64_t n_heads, int64_t head_dim, int64_t pos0,
+             const nbl_rope_params* rope);
+/* Backend::attention (backend.h:66-69; CpuBackend::attention cpu_backend.cpp:272-290): q,out [n, n_heads,
+ * head_dim]; k,v [>= pos0+n, n_kv_heads, head_dim], all fp32 device memory; row t has position pos0+t and
+ * attends to 0..pos0+t. n_heads % n_kv_heads == 0, head_dim even and <= 256. */
+NBL_API int nbl_attention(nbl_ctx* ctx, const float* q, const float* k, const float* v, float* out, int64_t n, int64_t pos0,
+                  int64_t n_heads, int64_t n_kv_heads, int64_t head_dim);
+
+/* ---- paged K/V path (B200-native layout; the reference keeps fp32 flat caches) ---- */
+/* Allocates and zeroes a pool (see nbl_kv_config) and the TMA descriptors over it. */
+NBL_API int nbl_kv_create(nbl_ctx* ctx, const nbl_kv_config* cfg, nbl_kv** out);
+NBL_API int nbl_kv_destroy(nbl_kv* kv);
+/* Base device address and size of the pool (for bulk fills and read-back in tests). */
+NBL_API int nbl_kv_pool(const nbl_kv* kv, void** base, int64_t* bytes);
+
+/* Fused bias -> RoPE -> narrowing -> page write for new tokens: the sequence transformer.cpp:171-198 runs as
+ * matmul_multi into cache rows, add_bias(q/k/v), rope(q), rope(k). For token r (r < n_tok):
+ *   q_out[r] = rope(q_in[r] + bq) at position tok_pos[r]            (n_heads heads, dtype q_out_dtype)
+ *   page(tok_row[r], tok_pos[r]) <- narrow(rope(k_in[r] + bk)), narrow(v_in[r] + bv)   (n_kv_heads heads)
+ * where page(row, pos) is slot pos % page_size of page page_table[row * pt_stride + pos / page_size].
+ * q_in/k_in/v_in are [n_tok, heads, head_dim] of in_dtype (F32, F16 or BF16); biases are fp32 device vectors or
+ * NULL; q_out may alias q_in when the dtypes match. All index arrays are device memory. */
+NBL_API int nbl_rope_kv_append(nbl_ctx* ctx, nbl_kv* kv, const void* q_in, const void* k_in, const void* v_in,
+                       int32_t in_dtype, const float* bq, const float* bk, const float* bv, void* q_out,
+                       int32_t q_out_dtype, const int32_t* tok_row, const int32_t* tok_pos, const int32_t* page_table,
+                       int32_t pt_stride, int64_t n_tok, int32_t n_heads, const nbl_rope_params* rope);
+
+/* Single-token decode (Backend::attention with n = 1, backend.h:66-69) over the paged pool, for n_rows
+ * independent (sequence, layer) rows at once. Row r: query q[r] ([n_heads, head_dim] fp32, already roped),
+ * keys/values 0..seq_lens[r]-1 through page-table row r. Writes out[r] ([n_heads, head_dim] fp32) and, if lse
+ * is non-NULL, lse[r, h] = ln(sum_j exp(score_j)) (natural log; the partial form the LSE merge consumes).
+ * seq_lens[r] == 0 gives out = 0 and lse = -inf. max_seq_len bounds every seq_lens[r] (it sizes the splits;
+ * the kernel also checks each length against pt_stride * page_size). n_splits: KV splits per row (0 = chosen
+ * from the sizes); more than one uses context scratch sized by nbl_reserve (grown on demand otherwise).
+ * head_dim 64, n_heads / n_kv_heads <= 8. */
+NBL_API int nbl_attn_decode(nbl_ctx* ctx, const nbl_kv* kv, const float* q, const int32_t* page_table, int32_t pt_stride,
+                    const int32_t* seq_lens, int32_t max_seq_len, int32_t n_rows, int32_t n_heads, float* out,
+                    float* lse, int32_t n_splits);
+
+/* Causal prefill (Backend::attention with n >= 1) over the paged pool for n_items independent items. q and out
+ * hold n_q_rows rows of [n_heads, head_dim]. Item i: query rows q[q_start[i] .. q_start[i] + q_len[i])
+ * (q_dtype = the pool dtype, already roped) at positions kv_pos0[i] + t, attending keys 0..kv_pos0[i]+t of
+ * page-table row i (those keys must already be in the pool). max_q_len bounds every q_len[i]. Writes the
+ * items' out rows in out_dtype (F32 or the pool dtype). Tensor-core kernel (tcgen05): bf16/fp16 operands, fp32
+ * accumulation in TMEM. */
+NBL_API int nbl_attn_prefill(nbl_ctx* ctx, const nbl_kv* kv, const void* q, int32_t q_dtype, int64_t n_q_rows,
+                     const int32_t* q_start, const int32_t* q_len, const int32_t* kv_pos0, const int32_t* page_table,
+                     int32_t pt_stride, int32_t n_items, int32_t n_heads, int32_t max_q_len, void* out,
+                     int32_t out_dtype);
+
+/* Log-sum-exp merge of n_parts partial results of the same rows (e.g. per-GPU KV chunks after an
+ * all-gather): part_o [n_parts, rows, head_dim] normalised outputs, part_lse [n_parts, rows] natural-log
+ * sums. Writes out [rows, head_dim] and, if non-NULL, lse [rows]. Parts with lse = -inf are ignored. */
+NBL_API int nbl_lse_merge(nbl_ctx* ctx, const float* part_o, const float* part_lse, int32_t n_parts, int64_t rows,
+                  int32_t head_dim, float* out, float* lse);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,95 @@
+"""ctypes binding of the C ABI in include/nibble_cuda.h (libnibble_cuda.so, built in-tree).
+
+This module is plumbing for Python callers (tests, bench, smoke): every call goes through the C ABI into the
+sm_100a kernels. There is no CPU fallback: if the library is missing or does not load, importing the package
+raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libnibble_cuda.so")
+
+NBL_OK, NBL_E_INVALID, NBL_E_CUDA, NBL_E_NOMEM, NBL_E_UNSUPPORTED, NBL_E_DEVICE = range(6)
+F32, F16, BF16 = 0, 1, 2
+STATUS_NAMES = {0: "NBL_OK", 1: "NBL_E_INVALID", 2: "NBL_E_CUDA", 3: "NBL_E_NOMEM", 4: "NBL_E_UNSUPPORTED",
+                5: "NBL_E_DEVICE"}
+
+
+class NibbleError(RuntimeError):
+    """A non-zero nbl_status, carrying nbl_last_error()'s message (the C-side nibble::Error)."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(f"{STATUS_NAMES.get(status, status)}: {message}")
+        self.status = status
+
+
+class RopeParams(C.Structure):
+    _fields_ = [("freq_base", C.c_float), ("neox", C.c_int32), ("freq_factors", C.c_void_p)]
+
+
+class KvConfig(C.Structure):
+    _fields_ = [("n_pages", C.c_int64), ("n_kv_heads", C.c_int32), ("head_dim", C.c_int32),
+                ("page_size", C.c_int32), ("dtype", C.c_int32)]
+
+
+_P = C.c_void_p
+_I32 = C.c_int32
+_I64 = C.c_int64
+
+# name -> argtypes (all return int status unless listed in _RESTYPES)
+SIGNATURES = {
+    "nbl_abi_version": [],
+    "nbl_last_error": [C.c_char_p, C.c_size_t],
+    "nbl_ctx_create": [C.c_int, C.POINTER(_P)],
+    "nbl_ctx_destroy": [_P],
+    "nbl_ctx_set_stream": [_P, _P],
+    "nbl_ctx_stream": [_P],
+    "nbl_ctx_sync": [_P],
+    "nbl_ctx_check": [_P],
+    "nbl_reserve": [_P, _I64, _I64, _I64, _I64],
+    "nbl_alloc": [_P, _I64, C.POINTER(_P)],
+    "nbl_free": [_P, _P],
+    "nbl_read": [_P, _P, _P, _I64],
+    "nbl_write": [_P, _P, _P, _I64],
+    "nbl_add_bias": [_P, _P, _P, _I64, _I64],
+    "nbl_rope": [_P, _P, _I64, _I64, _I64, _I64, C.POINTER(RopeParams)],
+    "nbl_attention": [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64],
+    "nbl_kv_create": [_P, C.POINTER(KvConfig), C.POINTER(_P)],
+    "nbl_kv_destroy": [_P],
+    "nbl_kv_pool": [_P, C.POINTER(_P), C.POINTER(_I64)],
+    "nbl_rope_kv_append": [_P, _P, _P, _P, _P, _I32, _P, _P, _P, _P, _I32, _P, _P, _P, _I32, _I64, _I32,
+                           C.POINTER(RopeParams)],
+    "nbl_attn_decode": [_P, _P, _P, _P, _I32, _P, _I32, _I32, _I32, _P, _P, _I32],
+    "nbl_attn_prefill": [_P, _P, _P, _I32, _I64, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _P, _I32],
+    "nbl_lse_merge": [_P, _P, _P, _I32, _I64, _I32, _P, _P],
+}
+_RESTYPES = {"nbl_last_error": C.c_size_t, "nbl_ctx_stream": _P}
+
+
+def _load() -> C.CDLL:
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(f"{LIB_PATH} is missing: build it with `python -m nibble_b200.build` (nvcc, sm_100a)")
+    lib = C.CDLL(LIB_PATH)
+    for name, args in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = _RESTYPES.get(name, C.c_int)
+    return lib
+
+
+lib = _load()
+
+
+def last_error() -> str:
+    n = lib.nbl_last_error(None, 0)
+    buf = C.create_string_buffer(n + 1)
+    lib.nbl_last_error(buf, n + 1)
+    return buf.value.decode(errors="replace")
+
+
+def check(status: int) -> None:
+    if status != NBL_OK:
+        raise NibbleError(status, last_error())

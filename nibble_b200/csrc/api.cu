@@ -1,0 +1,488 @@
+// The C ABI (include/nibble_cuda.h): argument validation, context state and kernel dispatch.
+//
+// Every entry point catches everything at the boundary and turns it into an nbl_status plus a thread-local
+// message, the C-side form of nibble's "throw nibble::Error with a self-contained message" convention
+// (include/nibble/error.h). No exception crosses the ABI.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <mutex>
+#include <new>
+#include <string>
+
+#include "nbl_internal.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int set_error(int status, const std::string& msg) {
+  g_last_error = msg;
+  return status;
+}
+
+template <class F>
+int guarded(F&& f) {
+  try {
+    f();
+    return NBL_OK;
+  } catch (const nbl::Failure& e) {
+    return set_error(e.status, e.what());
+  } catch (const std::bad_alloc&) {
+    return set_error(NBL_E_NOMEM, "host allocation failed");
+  } catch (const std::exception& e) {
+    return set_error(NBL_E_INVALID, e.what());
+  }
+}
+
+void require(bool ok, const std::string& msg) {
+  if (!ok) nbl::fail(NBL_E_INVALID, msg);
+}
+
+// Makes the context's device current for the calling thread.
+void use_device(nbl_ctx* ctx) { nbl::check_cuda(cudaSetDevice(ctx->device), "cudaSetDevice"); }
+
+void* device_alloc(size_t bytes, const char* what) {
+  void* p = nullptr;
+  const cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) {
+    cudaGetLastError();  // clear the sticky-free error so later calls are not poisoned
+    nbl::fail(NBL_E_NOMEM, std::string(what) + ": cannot allocate " + std::to_string(bytes) + " bytes of device memory (" +
+                               cudaGetErrorString(e) + ")");
+  }
+  return p;
+}
+
+// Grows the context's split-K scratch to at least `bytes` (device allocation; not during stream capture).
+void ensure_scratch(nbl_ctx* ctx, size_t bytes) {
+  if (ctx->scratch_bytes >= bytes) return;
+  void* p = device_alloc(bytes, "attention scratch");
+  if (ctx->scratch) {
+    nbl::check_cuda(cudaStreamSynchronize(ctx->stream), "scratch sync");
+    cudaFree(ctx->scratch);
+  }
+  ctx->scratch = p;
+  ctx->scratch_bytes = bytes;
+}
+
+// Returns the device cos/sin table for (base, head_dim, factors) covering positions [0, n_pos), building it
+// on the host in double with the reference's expression (src/backend/cpu/ref_ops.cpp:173-176) if needed.
+const nbl::RopeTable& rope_table(nbl_ctx* ctx, const nbl_rope_params& rp, int64_t head_dim, int64_t n_pos) {
+  const int64_t half = head_dim / 2;
+  std::vector<float> ff;
+  if (rp.freq_factors) ff.assign(rp.freq_factors, rp.freq_factors + half);
+  for (auto& t : ctx->rope_tables)
+    if (t.base == rp.freq_base && t.head_dim == head_dim && t.factors == ff && t.n_pos >= n_pos) return t;
+  // Build (grow to the larger of the request and the reserved context length).
+  const int64_t want = std::max<int64_t>(n_pos, ctx->reserved_ctx);
+  std::vector<float2> host(static_cast<size_t>(want * half));
+  for (int64_t pos = 0; pos < want; ++pos)
+    for (int64_t i = 0; i < half; ++i) {
+      double theta = static_cast<double>(pos) *
+                     std::pow(static_cast<double>(rp.freq_base), -2.0 * static_cast<double>(i) / static_cast<double>(head_dim));
+      if (!ff.empty()) theta /= ff[static_cast<size_t>(i)];
+      host[static_cast<size_t>(pos * half + i)] = make_float2(static_cast<float>(std::cos(theta)), static_cast<float>(std::sin(theta)));
+    }
+  auto* dev = static_cast<float2*>(device_alloc(host.size() * sizeof(float2), "RoPE table"));
+  nbl::check_cuda(cudaMemcpyAsync(dev, host.data(), host.size() * sizeof(float2), cudaMemcpyHostToDevice, ctx->stream),
+                  "RoPE table upload");
+  nbl::check_cuda(cudaStreamSynchronize(ctx->stream), "RoPE table upload");
+  for (auto it = ctx->rope_tables.begin(); it != ctx->rope_tables.end(); ++it)
+    if (it->base == rp.freq_base && it->head_dim == head_dim && it->factors == ff) {  // replace a smaller table
+      cudaFree(it->dev);
+      ctx->rope_tables.erase(it);
+      break;
+    }
+  nbl::RopeTable t;
+  t.base = rp.freq_base;
+  t.head_dim = head_dim;
+  t.factors = std::move(ff);
+  t.n_pos = want;
+  t.dev = dev;
+  ctx->rope_tables.push_back(std::move(t));
+  return ctx->rope_tables.back();
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  if (!fn) nbl::fail(NBL_E_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  return fn;
+}
+
+}  // namespace
+
+void nbl::encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, void* base, const cuuint64_t* dims,
+                      const cuuint64_t* strides_bytes, const cuuint32_t* box) {
+  const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  const CUresult r = tensor_map_encoder()(map, dtype, static_cast<cuuint32_t>(rank), base, dims, strides_bytes, box,
+                                          estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) nbl::fail(NBL_E_CUDA, "cuTensorMapEncodeTiled failed (CUresult " + std::to_string(r) + ")");
+}
+
+namespace {
+
+bool is_dtype(int32_t d) { return d == NBL_F32 || d == NBL_F16 || d == NBL_BF16; }
+
+}  // namespace
+
+extern "C" {
+
+int nbl_abi_version(void) { return NBL_ABI_VERSION; }
+
+size_t nbl_last_error(char* buf, size_t cap) {
+  if (buf && cap) {
+    const size_t n = std::min(cap - 1, g_last_error.size());
+    std::memcpy(buf, g_last_error.data(), n);
+    buf[n] = 0;
+  }
+  return g_last_error.size();
+}
+
+int nbl_ctx_create(int device, nbl_ctx** out) {
+  return guarded([&] {
+    require(out != nullptr, "nbl_ctx_create: out is NULL");
+    *out = nullptr;
+    int count = 0;
+    nbl::check_cuda(cudaGetDeviceCount(&count), "cudaGetDeviceCount");
+    require(device >= 0 && device < count, "nbl_ctx_create: device " + std::to_string(device) + " out of range (" +
+                                               std::to_string(count) + " devices)");
+    nbl::check_cuda(cudaSetDevice(device), "cudaSetDevice");
+    int major = 0, minor = 0;
+    nbl::check_cuda(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device), "cc");
+    nbl::check_cuda(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device), "cc");
+    if (major != 10 || minor != 0)
+      nbl::fail(NBL_E_UNSUPPORTED, "nbl_ctx_create: this library is built for sm_100a (B200); device " +
+                                       std::to_string(device) + " is sm_" + std::to_string(major) + std::to_string(minor));
+    auto* ctx = new nbl_ctx();
+    ctx->device = device;
+    try {
+      nbl::check_cuda(cudaDeviceGetAttribute(&ctx->num_sms, cudaDevAttrMultiProcessorCount, device), "SM count");
+      nbl::check_cuda(cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking), "cudaStreamCreate");
+      ctx->stream = ctx->own_stream;
+      ctx->d_err = static_cast<int*>(device_alloc(sizeof(int), "error word"));
+      nbl::check_cuda(cudaMemset(ctx->d_err, 0, sizeof(int)), "error word init");
+    } catch (...) {
+      if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
+      delete ctx;
+      throw;
+    }
+    *out = ctx;
+  });
+}
+
+int nbl_ctx_destroy(nbl_ctx* ctx) {
+  if (!ctx) return NBL_OK;
+  return guarded([&] {
+    use_device(ctx);
+    cudaStreamSynchronize(ctx->stream);
+    for (nbl_kv* kv : ctx->kvs) {
+      cudaFree(kv->pool);
+      delete kv;
+    }
+    for (auto& a : ctx->allocs) cudaFree(a.first);
+    for (auto& t : ctx->rope_tables) cudaFree(t.dev);
+    if (ctx->scratch) cudaFree(ctx->scratch);
+    cudaFree(ctx->d_err);
+    cudaStreamDestroy(ctx->own_stream);
+    delete ctx;
+  });
+}
+
+int nbl_ctx_set_stream(nbl_ctx* ctx, void* stream) {
+  return guarded([&] {
+    require(ctx != nullptr, "nbl_ctx_set_stream: ctx is NULL");
+    ctx->stream = stream ? static_cast<cudaStream_t>(stream) : ctx->own_stream;
+  });
+}
+
+void* nbl_ctx_stream(nbl_ctx* ctx) { return ctx ? static_cast<void*>(ctx->stream) : nullptr; }
+
+int nbl_ctx_sync(nbl_ctx* ctx) {
+  return guarded([&] {
+    require(ctx != nullptr, "nbl_ctx_sync: ctx is NULL");
+    use_device(ctx);
+    nbl::check_cuda(cudaStreamSynchronize(ctx->stream), "stream synchronize");
+  });
+}
+
+int nbl_ctx_check(nbl_ctx* ctx) {
+  return guarded([&] {
+    require(ctx != nullptr, "nbl_ctx_check: ctx is NULL");
+    use_device(ctx);
+    int host = 0;
+    nbl::check_cuda(cudaMemcpyAsync(&host, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream), "error word");
+    nbl::check_cuda(cudaStreamSynchronize(ctx->stream), "error word");
+    if (host) {
+      nbl::check_cuda(cudaMemsetAsync(ctx->d_err, 0, sizeof(int), ctx->stream), "error word reset");
+      std::string what;
+      if (host & nbl::kErrPageId) what += " page id outside the pool;";
+      if (host & nbl::kErrLength) what += " sequence length or position outside the page table / RoPE table;";
+      if (host & nbl::kErrTimeout) what += " a bounded wait on a copy or MMA completion gave up;";
+      if (host & nbl::kErrTmemAlloc) what += " tensor-memory allocation failed;";
+      nbl::fail(NBL_E_DEVICE, "device-side check failed (flags " + std::to_string(host) + "):" + what);
+    }
+  });
+}
+
+int nbl_reserve(nbl_ctx* ctx, int64_t n_ctx, int64_t n_heads, int64_t max_rows, int64_t max_width) {
+  return guarded([&] {
+    require(ctx != nullptr, "nbl_reserve: ctx is NULL");
+    require(n_ctx >= 0 && n_heads >= 0 && max_rows >= 0 && max_width >= 0,
+            "reserve: negative size (n_ctx=" + std::to_string(n_ctx) + " n_heads=" + std::to_string(n_heads) +
+                " max_rows=" + std::to_string(max_rows) + " max_width=" + std::to_string(max_width) + ")");
+    use_device(ctx);
+    ctx->reserved_ctx = std::max(ctx->reserved_ctx, n_ctx);
+    ctx->reserved_heads = std::max(ctx->reserved_heads, n_heads);
+    // Split-K scratch for one decode row per head set at this context length: the planner's worst case for
+    // a single row is one split per 8 pages.
+    const auto plan = nbl::plan_decode(1, 1, 1, static_cast<int>(n_heads), static_cast<int>(std::min<int64_t>(n_ctx, INT32_MAX)),
+                                       16, ctx->num_sms, 0);
+    if (plan.scratch_bytes) ensure_scratch(ctx, plan.scratch_bytes);
+  });
+}
+
+int nbl_alloc(nbl_ctx* ctx, int64_t n_floats, float** out) {
+  return guarded([&] {
+    require(ctx != nullptr && out != nullptr, "nbl_alloc: ctx or out is NULL");
+    *out = nullptr;
+    if (n_floats < 0) nbl::fail(NBL_E_INVALID, "alloc: negative size " + std::to_string(n_floats) + " floats");
+    if (static_cast<uint64_t>(n_floats) > (UINT64_MAX - 255) / sizeof(float))
+      nbl::fail(NBL_E_INVALID, "alloc: size of " + std::to_string(n_floats) + " floats overflows");
+    use_device(ctx);
+    size_t bytes = static_cast<size_t>(n_floats) * sizeof(float);
+    bytes = std::max<size_t>((bytes + 255) & ~size_t(255), 256);
+    void* p = device_alloc(bytes, "alloc");
+    const cudaError_t e = cudaMemsetAsync(p, 0, bytes, ctx->stream);
+    if (e != cudaSuccess) {
+      cudaFree(p);
+      nbl::check_cuda(e, "alloc zero-fill");
+    }
+    try {
+      ctx->allocs.emplace(p, bytes);
+    } catch (...) {
+      cudaFree(p);
+      throw;
+    }
+    *out = static_cast<float*>(p);
+  });
+}
+
+int nbl_free(nbl_ctx* ctx, float* p) {
+  return guarded([&] {
+    require(ctx != nullptr, "nbl_free: ctx is NULL");
+    if (!p) return;
+    auto it = ctx->allocs.find(p);
+    if (it == ctx->allocs.end()) return;  // not ours: ignored, like CpuBackend::free (cpu_backend.cpp:96-102)
+    use_device(ctx);
+    nbl::check_cuda(cudaStreamSynchronize(ctx->stream), "free sync");
+    cudaFree(p);
+    ctx->allocs.erase(it);
+  });
+}
+
+int nbl_read(nbl_ctx* ctx, float* host_dst, const float* src, int64_t n) {
+  return guarded([&] {
+    require(ctx && host_dst && src && n >= 0, "read: dst/src NULL or n < 0");
+    use_device(ctx);
+    nbl::check_cuda(cudaMemcpyAsync(host_dst, src, static_cast<size_t>(n) * sizeof(float), cudaMemcpyDeviceToHost,
+                                    ctx->stream),
+                    "read");
+    nbl::check_cuda(cudaStreamSynchronize(ctx->stream), "read");
+  });
+}
+
+int nbl_write(nbl_ctx* ctx, float* dst, const float* host_src, int64_t n) {
+  return guarded([&] {
+    require(ctx && dst && host_src && n >= 0, "write: dst/src NULL or n < 0");
+    use_device(ctx);
+    nbl::check_cuda(cudaMemcpyAsync(dst, host_src, static_cast<size_t>(n) * sizeof(float), cudaMemcpyHostToDevice,
+                                    ctx->stream),
+                    "write");
+    nbl::check_cuda(cudaStreamSynchronize(ctx->stream), "write");
+  });
+}
+
+int nbl_add_bias(nbl_ctx* ctx, float* x, const float* bias, int64_t width, int64_t n) {
+  return guarded([&] {
+    require(ctx && x && bias && width > 0 && n > 0, "add_bias: x/bias NULL or width/n not positive");
+    use_device(ctx);
+    nbl::launch_add_bias(ctx->stream, x, bias, width, n);
+  });
+}
+
+int nbl_rope(nbl_ctx* ctx, float* x, int64_t n, int64_t n_heads, int64_t head_dim, int64_t pos0,
+             const nbl_rope_params* rope) {
+  return guarded([&] {
+    require(ctx && x && rope, "rope: ctx/x/params NULL");
+    require(n > 0 && n_heads > 0 && head_dim > 0 && head_dim % 2 == 0 && pos0 >= 0,
+            "rope: n=" + std::to_string(n) + " n_heads=" + std::to_string(n_heads) + " head_dim=" +
+                std::to_string(head_dim) + " (must be even) pos0=" + std::to_string(pos0));
+    use_device(ctx);
+    const auto& tab = rope_table(ctx, *rope, head_dim, pos0 + n);
+    nbl::launch_rope_f32(ctx->stream, x, n, n_heads, head_dim, pos0, rope->neox != 0, tab.dev, ctx->d_err);
+  });
+}
+
+int nbl_attention(nbl_ctx* ctx, const float* q, const float* k, const float* v, float* out, int64_t n, int64_t pos0,
+                  int64_t n_heads, int64_t n_kv_heads, int64_t head_dim) {
+  return guarded([&] {
+    require(ctx && q && k && v && out, "attention: NULL pointer");
+    require(n > 0 && pos0 >= 0 && n_heads > 0 && n_kv_heads > 0 && n_heads % n_kv_heads == 0 && head_dim > 0 &&
+                head_dim % 2 == 0 && head_dim <= 256,
+            "attention: n=" + std::to_string(n) + " pos0=" + std::to_string(pos0) + " n_heads=" +
+                std::to_string(n_heads) + " n_kv_heads=" + std::to_string(n_kv_heads) + " head_dim=" +
+                std::to_string(head_dim) + " (n_heads must be a multiple of n_kv_heads; head_dim even, <= 256)");
+    use_device(ctx);
+    const float scale = 1.0f / std::sqrt(static_cast<float>(head_dim));
+    nbl::launch_attention_f32(ctx->stream, q, k, v, out, n, pos0, n_heads, n_kv_heads, head_dim, scale);
+  });
+}
+
+int nbl_kv_create(nbl_ctx* ctx, const nbl_kv_config* cfg, nbl_kv** out) {
+  return guarded([&] {
+    require(ctx && cfg && out, "kv_create: NULL argument");
+    *out = nullptr;
+    const nbl_kv_config c = *cfg;
+    require(c.n_pages > 0 && c.n_kv_heads > 0 && c.head_dim > 0 && c.page_size > 0,
+            "kv_create: n_pages, n_kv_heads, head_dim and page_size must be positive");
+    require(c.dtype == NBL_F16 || c.dtype == NBL_BF16, "kv_create: dtype must be NBL_F16 or NBL_BF16");
+    if (c.head_dim != 64 || c.page_size != 16)
+      nbl::fail(NBL_E_UNSUPPORTED, "kv_create: the paged kernels take head_dim 64 and page_size 16 (got " +
+                                       std::to_string(c.head_dim) + ", " + std::to_string(c.page_size) + ")");
+    const uint64_t rows = static_cast<uint64_t>(c.n_pages) * 2u * static_cast<uint64_t>(c.n_kv_heads) *
+                          static_cast<uint64_t>(c.page_size);
+    if (rows >= (1ull << 31))
+      nbl::fail(NBL_E_INVALID, "kv_create: pool of " + std::to_string(c.n_pages) +
+                                   " pages exceeds 2^31 rows (tensor-map coordinate range)");
+    use_device(ctx);
+    auto* kv = new nbl_kv();
+    kv->ctx = ctx;
+    kv->cfg = c;
+    kv->bytes = rows * static_cast<uint64_t>(c.head_dim) * 2u;
+    try {
+      kv->pool = device_alloc(kv->bytes, "kv pool");
+      nbl::check_cuda(cudaMemsetAsync(kv->pool, 0, kv->bytes, ctx->stream), "kv pool zero-fill");
+      const cuuint64_t dims[2] = {static_cast<cuuint64_t>(c.head_dim), rows};
+      const cuuint64_t strides[1] = {static_cast<cuuint64_t>(c.head_dim) * 2u};
+      const cuuint32_t box[2] = {static_cast<cuuint32_t>(c.head_dim), static_cast<cuuint32_t>(c.page_size)};
+      nbl::encode_tmap(&kv->tmap,
+                       c.dtype == NBL_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                       kv->pool, dims, strides, box);
+      kv->has_tmap = true;
+      nbl::check_cuda(cudaStreamSynchronize(ctx->stream), "kv pool zero-fill");
+      ctx->kvs.push_back(kv);
+    } catch (...) {
+      if (kv->pool) cudaFree(kv->pool);
+      delete kv;
+      throw;
+    }
+    *out = kv;
+  });
+}
+
+int nbl_kv_destroy(nbl_kv* kv) {
+  if (!kv) return NBL_OK;
+  return guarded([&] {
+    nbl_ctx* ctx = kv->ctx;
+    use_device(ctx);
+    nbl::check_cuda(cudaStreamSynchronize(ctx->stream), "kv_destroy sync");
+    ctx->kvs.erase(std::remove(ctx->kvs.begin(), ctx->kvs.end(), kv), ctx->kvs.end());
+    cudaFree(kv->pool);
+    delete kv;
+  });
+}
+
+int nbl_kv_pool(const nbl_kv* kv, void** base, int64_t* bytes) {
+  return guarded([&] {
+    require(kv && base && bytes, "kv_pool: NULL argument");
+    *base = kv->pool;
+    *bytes = static_cast<int64_t>(kv->bytes);
+  });
+}
+
+int nbl_rope_kv_append(nbl_ctx* ctx, nbl_kv* kv, const void* q_in, const void* k_in, const void* v_in,
+                       int32_t in_dtype, const float* bq, const float* bk, const float* bv, void* q_out,
+                       int32_t q_out_dtype, const int32_t* tok_row, const int32_t* tok_pos, const int32_t* page_table,
+                       int32_t pt_stride, int64_t n_tok, int32_t n_heads, const nbl_rope_params* rope) {
+  return guarded([&] {
+    require(ctx && kv && q_in && k_in && v_in && q_out && tok_row && tok_pos && page_table && rope,
+            "rope_kv_append: NULL argument");
+    require(kv->ctx == ctx, "rope_kv_append: pool belongs to another context");
+    require(is_dtype(in_dtype) && is_dtype(q_out_dtype), "rope_kv_append: bad dtype");
+    require(n_tok >= 0 && n_tok <= INT32_MAX && pt_stride > 0, "rope_kv_append: n_tok or pt_stride out of range");
+    require(n_heads > 0 && n_heads % kv->cfg.n_kv_heads == 0, "rope_kv_append: n_heads must be a multiple of n_kv_heads");
+    if (n_tok == 0) return;
+    use_device(ctx);
+    const int64_t max_pos = int64_t(pt_stride) * kv->cfg.page_size;
+    const auto& tab = rope_table(ctx, *rope, kv->cfg.head_dim, max_pos);
+    nbl::launch_rope_kv_append(ctx->stream, kv, q_in, k_in, v_in, in_dtype, bq, bk, bv, q_out, q_out_dtype, tok_row,
+                               tok_pos, page_table, pt_stride, n_tok, n_heads, rope->neox != 0, tab.dev, tab.n_pos,
+                               ctx->d_err);
+  });
+}
+
+int nbl_attn_decode(nbl_ctx* ctx, const nbl_kv* kv, const float* q, const int32_t* page_table, int32_t pt_stride,
+                    const int32_t* seq_lens, int32_t max_seq_len, int32_t n_rows, int32_t n_heads, float* out,
+                    float* lse, int32_t n_splits) {
+  return guarded([&] {
+    require(ctx && kv && q && page_table && seq_lens && out, "attn_decode: NULL argument");
+    require(kv->ctx == ctx, "attn_decode: pool belongs to another context");
+    require(kv->cfg.dtype == NBL_F16, "attn_decode: the decode kernel reads an NBL_F16 pool");
+    require(n_rows >= 0 && pt_stride > 0 && max_seq_len >= 0 && n_splits >= 0, "attn_decode: negative size");
+    require(n_heads > 0 && n_heads % kv->cfg.n_kv_heads == 0 && n_heads / kv->cfg.n_kv_heads <= 8,
+            "attn_decode: n_heads must be a multiple of n_kv_heads with at most 8 query heads per KV head");
+    require(int64_t(max_seq_len) <= int64_t(pt_stride) * kv->cfg.page_size,
+            "attn_decode: max_seq_len exceeds pt_stride * page_size");
+    if (n_rows == 0) return;
+    use_device(ctx);
+    const auto plan = nbl::plan_decode(n_rows, kv->cfg.n_kv_heads, n_heads / kv->cfg.n_kv_heads, n_heads,
+                                       max_seq_len, kv->cfg.page_size, ctx->num_sms, n_splits);
+    if (plan.scratch_bytes) ensure_scratch(ctx, plan.scratch_bytes);
+    nbl::launch_decode(ctx->stream, kv, q, page_table, pt_stride, seq_lens, n_rows, n_heads, out, lse, plan,
+                       ctx->scratch, ctx->d_err);
+  });
+}
+
+int nbl_attn_prefill(nbl_ctx* ctx, const nbl_kv* kv, const void* q, int32_t q_dtype, int64_t n_q_rows,
+                     const int32_t* q_start, const int32_t* q_len, const int32_t* kv_pos0, const int32_t* page_table,
+                     int32_t pt_stride, int32_t n_items, int32_t n_heads, int32_t max_q_len, void* out,
+                     int32_t out_dtype) {
+  return guarded([&] {
+    require(ctx && kv && q && q_start && q_len && kv_pos0 && page_table && out, "attn_prefill: NULL argument");
+    require(kv->ctx == ctx, "attn_prefill: pool belongs to another context");
+    require(q_dtype == kv->cfg.dtype, "attn_prefill: q must have the pool's dtype");
+    require(out_dtype == NBL_F32 || out_dtype == kv->cfg.dtype, "attn_prefill: out must be F32 or the pool dtype");
+    require(n_items >= 0 && pt_stride > 0 && max_q_len >= 0 && n_q_rows >= 0, "attn_prefill: negative size");
+    require(kv->cfg.head_dim == 64, "attn_prefill: head_dim 64 only");
+    require(n_heads > 0 && n_heads % kv->cfg.n_kv_heads == 0, "attn_prefill: n_heads must be a multiple of n_kv_heads");
+    if (n_items == 0 || max_q_len == 0) return;
+    use_device(ctx);
+    if (n_q_rows == 0) return;
+    nbl::launch_prefill(ctx->stream, kv, q, n_q_rows, q_start, q_len, kv_pos0, page_table, pt_stride, n_items,
+                        n_heads, max_q_len, out, out_dtype, ctx->d_err);
+  });
+}
+
+int nbl_lse_merge(nbl_ctx* ctx, const float* part_o, const float* part_lse, int32_t n_parts, int64_t rows,
+                  int32_t head_dim, float* out, float* lse) {
+  return guarded([&] {
+    require(ctx && part_o && part_lse && out, "lse_merge: NULL argument");
+    require(n_parts > 0 && rows >= 0 && head_dim > 0 && head_dim <= 256, "lse_merge: bad size");
+    if (rows == 0) return;
+    use_device(ctx);
+    nbl::launch_lse_merge(ctx->stream, part_o, part_lse, n_parts, rows, head_dim, out, lse);
+  });
+}
+
+}  // extern "C"

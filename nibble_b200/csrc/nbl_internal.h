@@ -1,0 +1,101 @@
+// Internal host-side declarations shared by the C-ABI layer (api.cu) and the kernel files.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/nibble_cuda.h"
+#include "nbl_errors.h"
+
+namespace nbl {
+
+// A failure carrying the status the C ABI returns; thrown inside the library, caught at the ABI boundary.
+struct Failure : std::runtime_error {
+  int status;
+  Failure(int s, const std::string& m) : std::runtime_error(m), status(s) {}
+};
+
+[[noreturn]] inline void fail(int status, const std::string& msg) { throw Failure(status, msg); }
+inline void check_cuda(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) fail(NBL_E_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+// Cached cos/sin table for one RoPE configuration: tab[pos * half + i] = (cos, sin) of
+// pos * base^(-2i/head_dim) / freq_factors[i], evaluated in double on the host.
+struct RopeTable {
+  float base = 0.f;
+  int64_t head_dim = 0;
+  std::vector<float> factors;  // empty when none
+  int64_t n_pos = 0;
+  float2* dev = nullptr;
+};
+
+}  // namespace nbl
+
+struct nbl_ctx {
+  int device = 0;
+  int num_sms = 148;
+  cudaStream_t own_stream = nullptr;
+  cudaStream_t stream = nullptr;
+  int* d_err = nullptr;                        // device error word (nbl_ctx_check)
+  std::unordered_map<void*, size_t> allocs;    // Backend::alloc registry
+  void* scratch = nullptr;                     // split-K partials
+  size_t scratch_bytes = 0;
+  int64_t reserved_ctx = 0, reserved_heads = 0;
+  std::vector<nbl::RopeTable> rope_tables;
+  std::vector<nbl_kv*> kvs;
+};
+
+struct nbl_kv {
+  nbl_ctx* ctx = nullptr;
+  nbl_kv_config cfg{};
+  void* pool = nullptr;
+  size_t bytes = 0;
+  CUtensorMap tmap;  // 2-D view [n_pages*2*n_kv_heads*page_size rows, head_dim], box page_size x head_dim, 128B swizzle
+  bool has_tmap = false;
+};
+
+namespace nbl {
+
+// Encodes a tiled TMA descriptor (driver entry point resolved once through the runtime; no libcuda link).
+// dims/strides in elements/bytes as cuTensorMapEncodeTiled takes them; 128-byte swizzle, zero OOB fill.
+void encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, void* base, const cuuint64_t* dims,
+                 const cuuint64_t* strides_bytes, const cuuint32_t* box);
+
+// ---- launches (defined in the kernel .cu files; all asynchronous on `st`) ----
+// rope.cu
+void launch_add_bias(cudaStream_t st, float* x, const float* bias, int64_t width, int64_t n);
+void launch_rope_f32(cudaStream_t st, float* x, int64_t n, int64_t n_heads, int64_t head_dim, int64_t pos0,
+                     bool neox, const float2* tab, int* err);
+void launch_rope_kv_append(cudaStream_t st, const nbl_kv* kv, const void* q_in, const void* k_in, const void* v_in,
+                           int in_dtype, const float* bq, const float* bk, const float* bv, void* q_out,
+                           int q_out_dtype, const int32_t* tok_row, const int32_t* tok_pos,
+                           const int32_t* page_table, int32_t pt_stride, int64_t n_tok, int n_heads, bool neox,
+                           const float2* tab, int64_t tab_pos, int* err);
+// attn_f32.cu
+void launch_attention_f32(cudaStream_t st, const float* q, const float* k, const float* v, float* out, int64_t n,
+                          int64_t pos0, int64_t n_heads, int64_t n_kv_heads, int64_t head_dim, float scale);
+// decode.cu
+struct DecodePlan {
+  int n_splits = 1;
+  int pages_per_split = 0;
+  size_t scratch_bytes = 0;
+};
+DecodePlan plan_decode(int n_rows, int n_kv_heads, int group, int n_heads, int max_seq_len, int page_size,
+                       int num_sms, int requested_splits);
+void launch_decode(cudaStream_t st, const nbl_kv* kv, const float* q, const int32_t* page_table, int32_t pt_stride,
+                   const int32_t* seq_lens, int n_rows, int n_heads, float* out, float* lse, const DecodePlan& plan,
+                   void* scratch, int* err);
+void launch_lse_merge(cudaStream_t st, const float* part_o, const float* part_lse, int n_parts, int64_t rows,
+                      int head_dim, float* out, float* lse);
+// prefill.cu
+void launch_prefill(cudaStream_t st, const nbl_kv* kv, const void* q, int64_t n_q_rows, const int32_t* q_start,
+                    const int32_t* q_len, const int32_t* kv_pos0, const int32_t* page_table, int32_t pt_stride,
+                    int n_items, int n_heads, int max_q_len, void* out, int out_dtype, int* err);
+
+}  // namespace nbl

@@ -1,0 +1,296 @@
+"""ctypes bindings for the CPU checkers (TEST INFRASTRUCTURE ONLY).
+
+Only tests/, ``__graft_entry__.smoke()`` and bench.py's CPU-baseline / reference leg import this package, and
+only as the checker or the timed CPU baseline. The product (``nibble_b200`` and ``libnibble_cuda.so``) never
+imports it and has no CPU fallback.
+
+Two libraries are wrapped:
+
+* ``liboracle.so`` -- the plain-C restatement of nibble's scalar attention path (``nbl_oracle.c``; each
+  function cites the reference function it restates).
+* ``_ref/libnibble_ref.so`` -- nibble's own sources (``src/backend/cpu/ref_ops.cpp``, the AVX2 tiers,
+  ``CpuBackend``, ``ThreadPool``) compiled by ``oracle/Makefile`` behind ``ref_shim.cpp``. It exists only where
+  the reference tree was available at build time; ``have_ref()`` says whether it loaded.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_SO = os.path.join(HERE, "liboracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libnibble_ref.so")
+REF_TREE = os.environ.get("NIBBLE_REFERENCE_TREE", "/root/reference")
+
+_f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+_u16p = np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS")
+_i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
+_i64 = C.c_int64
+
+_lib = None
+_ref = None
+
+
+def build(with_ref: bool | None = None) -> None:
+    """Compiles liboracle.so, and oracle/_ref when the reference tree is present (or with_ref is True)."""
+    targets = ["oracle"]
+    if with_ref or (with_ref is None and os.path.isdir(os.path.join(REF_TREE, "src"))):
+        targets.append("ref")
+    subprocess.run(["make", "-s", "-C", HERE, f"REF={REF_TREE}", "-j8", *targets], check=True)
+
+
+def _load_oracle():
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(ORACLE_SO):
+        build(with_ref=False)
+    lib = C.CDLL(ORACLE_SO)
+    lib.orc_fp16_to_fp32.argtypes = [C.c_uint16]
+    lib.orc_fp16_to_fp32.restype = C.c_float
+    lib.orc_fp32_to_fp16.argtypes = [C.c_float]
+    lib.orc_fp32_to_fp16.restype = C.c_uint16
+    for name, a, b in (("orc_fp16_to_fp32_n", _u16p, _f32p), ("orc_fp32_to_fp16_n", _f32p, _u16p),
+                       ("orc_bf16_to_fp32_n", _u16p, _f32p), ("orc_fp32_to_bf16_n", _f32p, _u16p)):
+        getattr(lib, name).argtypes = [a, b, _i64]
+        getattr(lib, name).restype = None
+    lib.orc_softmax_inplace.argtypes = [_f32p, _i64]
+    lib.orc_rope.argtypes = [_f32p, _i64, _i64, _i64, _i64, C.c_float, C.c_int, C.c_void_p]
+    lib.orc_attention.argtypes = [_f32p, _f32p, _f32p, _f32p, _i64, _i64, _i64, _i64, _i64]
+    lib.orc_attention.restype = C.c_int
+    lib.orc_add_bias.argtypes = [_f32p, _f32p, _i64, _i64]
+    lib.orc_gather_pages.argtypes = [_u16p, _i32p, _i64, _i64, _i64, _i64, C.c_int, _f32p, _f32p]
+    lib.orc_lse_merge.argtypes = [_f32p, _f32p, _i64, _i64, _i64, _f32p, C.c_void_p]
+    _lib = lib
+    return lib
+
+
+def have_ref() -> bool:
+    """True when oracle/_ref/libnibble_ref.so (nibble's own code) is built and loads."""
+    try:
+        _load_ref()
+        return True
+    except OSError:
+        return False
+
+
+def _load_ref():
+    global _ref
+    if _ref is not None:
+        return _ref
+    if not os.path.exists(REF_SO) and os.path.isdir(os.path.join(REF_TREE, "src")):
+        build(with_ref=True)
+    lib = C.CDLL(REF_SO)
+    lib.nref_last_error.restype = C.c_char_p
+    lib.nref_attention_scalar.argtypes = [_f32p, _f32p, _f32p, _f32p, _i64, _i64, _i64, _i64, _i64, _f32p]
+    lib.nref_rope.argtypes = [_f32p, _i64, _i64, _i64, _i64, C.c_float, C.c_int, C.c_void_p]
+    lib.nref_softmax.argtypes = [_f32p, _i64]
+    lib.nref_fp16_to_fp32.argtypes = [C.c_uint16]
+    lib.nref_fp16_to_fp32.restype = C.c_float
+    lib.nref_fp32_to_fp16.argtypes = [C.c_float]
+    lib.nref_fp32_to_fp16.restype = C.c_uint16
+    lib.nref_fp16_to_fp32_n.argtypes = [_u16p, _f32p, _i64]
+    lib.nref_fp32_to_fp16_n.argtypes = [_f32p, _u16p, _i64]
+    lib.nref_kernels_name.restype = C.c_char_p
+    lib.nref_backend_create.argtypes = [C.c_int]
+    lib.nref_backend_create.restype = C.c_void_p
+    lib.nref_backend_destroy.argtypes = [C.c_void_p]
+    lib.nref_backend_threads.argtypes = [C.c_void_p]
+    lib.nref_backend_reserve.argtypes = [C.c_void_p, _i64, _i64, _i64, _i64]
+    lib.nref_backend_attention.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                           _i64, _i64, _i64, _i64, _i64]
+    lib.nref_backend_rope.argtypes = [C.c_void_p, _f32p, _i64, _i64, _i64, _i64, C.c_float, C.c_int, C.c_void_p]
+    _ref = lib
+    return lib
+
+
+def _c(a, dtype=np.float32):
+    return np.ascontiguousarray(a, dtype=dtype)
+
+
+# ---------------------------------------------------------------- the C restatement
+def fp16_bits_to_f32(bits: np.ndarray) -> np.ndarray:
+    b = _c(bits, np.uint16).ravel()
+    out = np.empty(b.size, np.float32)
+    _load_oracle().orc_fp16_to_fp32_n(b, out, b.size)
+    return out.reshape(np.shape(bits))
+
+
+def f32_to_fp16_bits(x: np.ndarray) -> np.ndarray:
+    a = _c(x).ravel()
+    out = np.empty(a.size, np.uint16)
+    _load_oracle().orc_fp32_to_fp16_n(a, out, a.size)
+    return out.reshape(np.shape(x))
+
+
+def bf16_bits_to_f32(bits: np.ndarray) -> np.ndarray:
+    b = _c(bits, np.uint16).ravel()
+    out = np.empty(b.size, np.float32)
+    _load_oracle().orc_bf16_to_fp32_n(b, out, b.size)
+    return out.reshape(np.shape(bits))
+
+
+def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    a = _c(x).ravel()
+    out = np.empty(a.size, np.uint16)
+    _load_oracle().orc_fp32_to_bf16_n(a, out, a.size)
+    return out.reshape(np.shape(x))
+
+
+def softmax(x: np.ndarray) -> np.ndarray:
+    y = _c(x).copy()
+    _load_oracle().orc_softmax_inplace(y, y.size)
+    return y
+
+
+def _ff(freq_factors):
+    if freq_factors is None:
+        return None, None
+    ff = _c(freq_factors)
+    return ff, ff.ctypes.data_as(C.c_void_p)
+
+
+def rope(x: np.ndarray, n_heads: int, head_dim: int, pos0: int, freq_base: float, neox: bool,
+         freq_factors=None) -> np.ndarray:
+    """Returns a roped copy of x viewed as [n, n_heads, head_dim] (nbl_oracle.c orc_rope)."""
+    y = _c(x).copy()
+    n = y.size // (n_heads * head_dim)
+    ff, ffp = _ff(freq_factors)
+    _load_oracle().orc_rope(y, n, n_heads, head_dim, pos0, freq_base, int(neox), ffp)
+    return y
+
+
+def attention(q, k, v, n, pos0, n_heads, n_kv_heads, head_dim) -> np.ndarray:
+    """Scalar causal GQA attention (nbl_oracle.c orc_attention); returns out [n, n_heads, head_dim]."""
+    q, k, v = _c(q), _c(k), _c(v)
+    out = np.empty((n, n_heads, head_dim), np.float32)
+    if _load_oracle().orc_attention(q, k, v, out, n, pos0, n_heads, n_kv_heads, head_dim) != 0:
+        raise MemoryError("oracle attention scratch")
+    return out
+
+
+def add_bias(x, bias, n) -> np.ndarray:
+    y = _c(x).copy()
+    b = _c(bias)
+    _load_oracle().orc_add_bias(y, b, b.size, n)
+    return y
+
+
+def gather_pages(pool_bits, page_table, length, n_kv_heads, head_dim, page_size, bf16=False):
+    """Widens one sequence's paged K/V (uint16 bits) into contiguous fp32 [length, n_kv_heads, head_dim]."""
+    k = np.empty((length, n_kv_heads, head_dim), np.float32)
+    v = np.empty_like(k)
+    _load_oracle().orc_gather_pages(_c(pool_bits, np.uint16).ravel(), _c(page_table, np.int32), length, n_kv_heads,
+                                    head_dim, page_size, int(bf16), k, v)
+    return k, v
+
+
+def lse_merge(part_o, part_lse):
+    """part_o [P, rows, D], part_lse [P, rows] -> (out [rows, D], lse [rows])."""
+    part_o, part_lse = _c(part_o), _c(part_lse)
+    p, rows, d = part_o.shape
+    out = np.empty((rows, d), np.float32)
+    lse = np.empty(rows, np.float32)
+    _load_oracle().orc_lse_merge(part_o, part_lse, p, rows, d, out, lse.ctypes.data_as(C.c_void_p))
+    return out, lse
+
+
+# ---------------------------------------------------------------- nibble's own code (oracle/_ref)
+def ref_attention_scalar(q, k, v, n, pos0, n_heads, n_kv_heads, head_dim) -> np.ndarray:
+    """nibble::cpu::attention_heads over all heads (src/backend/cpu/ref_ops.cpp:188)."""
+    q, k, v = _c(q), _c(k), _c(v)
+    out = np.empty((n, n_heads, head_dim), np.float32)
+    scratch = np.empty(pos0 + n, np.float32)
+    _load_ref().nref_attention_scalar(q, k, v, out, n, pos0, n_heads, n_kv_heads, head_dim, scratch)
+    return out
+
+
+def ref_rope(x, n_heads, head_dim, pos0, freq_base, neox, freq_factors=None) -> np.ndarray:
+    """nibble::cpu::rope (src/backend/cpu/ref_ops.cpp:166)."""
+    y = _c(x).copy()
+    n = y.size // (n_heads * head_dim)
+    ff, ffp = _ff(freq_factors)
+    _load_ref().nref_rope(y, n, n_heads, head_dim, pos0, freq_base, int(neox), ffp)
+    return y
+
+
+def ref_softmax(x) -> np.ndarray:
+    y = _c(x).copy()
+    _load_ref().nref_softmax(y, y.size)
+    return y
+
+
+def ref_fp16_bits_to_f32(bits) -> np.ndarray:
+    """nibble::fp16_to_fp32 over an array (src/fp16.h:18)."""
+    b = _c(bits, np.uint16).ravel()
+    out = np.empty(b.size, np.float32)
+    _load_ref().nref_fp16_to_fp32_n(b, out, b.size)
+    return out
+
+
+def ref_f32_to_fp16_bits(x) -> np.ndarray:
+    """nibble::fp32_to_fp16 over an array (src/fp16.h:46)."""
+    a = _c(x).ravel()
+    out = np.empty(a.size, np.uint16)
+    _load_ref().nref_fp32_to_fp16_n(a, out, a.size)
+    return out
+
+
+def ref_kernels_name() -> str:
+    name = _load_ref().nref_kernels_name()
+    if name is None:
+        raise RuntimeError(_load_ref().nref_last_error().decode())
+    return name.decode()
+
+
+class RefBackend:
+    """nibble's CpuBackend on a ThreadPool of `threads` (the reference's timed AVX2 attention path)."""
+
+    def __init__(self, threads: int):
+        self._lib = _load_ref()
+        self._h = self._lib.nref_backend_create(threads)
+        if not self._h:
+            raise RuntimeError(self._lib.nref_last_error().decode())
+
+    @property
+    def threads(self) -> int:
+        return self._lib.nref_backend_threads(self._h)
+
+    def reserve(self, n_ctx, n_heads, max_rows, max_width):
+        if self._lib.nref_backend_reserve(self._h, n_ctx, n_heads, max_rows, max_width):
+            raise RuntimeError(self._lib.nref_last_error().decode())
+
+    def attention_into(self, q, k, v, out, n, pos0, n_heads, n_kv_heads, head_dim):
+        """CpuBackend::attention on preallocated float32 C-contiguous arrays (no copies: for timing)."""
+        rc = self._lib.nref_backend_attention(self._h, q.ctypes.data, k.ctypes.data, v.ctypes.data, out.ctypes.data,
+                                              n, pos0, n_heads, n_kv_heads, head_dim)
+        if rc:
+            raise RuntimeError(self._lib.nref_last_error().decode())
+
+    def attention(self, q, k, v, n, pos0, n_heads, n_kv_heads, head_dim):
+        q, k, v = _c(q), _c(k), _c(v)
+        out = np.empty((n, n_heads, head_dim), np.float32)
+        self.attention_into(q, k, v, out, n, pos0, n_heads, n_kv_heads, head_dim)
+        return out
+
+    def rope(self, x, n_heads, head_dim, pos0, freq_base, neox, freq_factors=None):
+        y = _c(x).copy()
+        n = y.size // (n_heads * head_dim)
+        ff, ffp = _ff(freq_factors)
+        if self._lib.nref_backend_rope(self._h, y, n, n_heads, head_dim, pos0, freq_base, int(neox), ffp):
+            raise RuntimeError(self._lib.nref_last_error().decode())
+        return y
+
+    def close(self):
+        if self._h:
+            self._lib.nref_backend_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

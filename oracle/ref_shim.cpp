@@ -1,0 +1,129 @@
+// extern "C" shim over nibble's own attention-path code, compiled together with the reference sources
+// (oracle/Makefile) into oracle/_ref/libnibble_ref.so.
+//
+// TEST INFRASTRUCTURE ONLY: tests use it to pin the C oracle (nbl_oracle.c) against the reference itself, the
+// golden-fixture generator uses it, and bench.py's CPU-baseline / reference arm times CpuBackend::attention
+// through it. The product library never loads it.
+//
+// Wrapped entry points:
+//   nibble::cpu::attention_heads   src/backend/cpu/ref_ops.cpp:188   (scalar oracle)
+//   nibble::cpu::rope              src/backend/cpu/ref_ops.cpp:166
+//   nibble::cpu::softmax_inplace   src/backend/cpu/ref_ops.cpp:66
+//   nibble::cpu::CpuBackend        src/backend/cpu/cpu_backend.cpp:20 (ctor), :272 (attention) on a ThreadPool
+//   nibble::simd::select           src/backend/cpu/simd/dispatch.cpp:123 (the kernel tier the backend runs)
+//   nibble::fp16_to_fp32 / fp32_to_fp16   src/fp16.h:18, :46
+#include <cstdint>
+#include <cstring>
+#include <exception>
+#include <new>
+#include <vector>
+
+#include "backend/cpu/cpu_backend.h"
+#include "backend/cpu/ref_ops.h"
+#include "backend/cpu/simd/dispatch.h"
+#include "fp16.h"
+#include "thread_pool.h"
+
+namespace {
+thread_local char g_err[512];
+void set_err(const char* m) {
+  std::strncpy(g_err, m, sizeof g_err - 1);
+  g_err[sizeof g_err - 1] = 0;
+}
+// A thread pool plus the CPU backend that runs on it (the pair Model::Impl builds, src/nibble.cpp:79-81).
+struct RefBackend {
+  nibble::ThreadPool pool;
+  nibble::cpu::CpuBackend be;
+  explicit RefBackend(int threads) : pool(threads), be(pool) {}
+};
+}  // namespace
+
+extern "C" {
+
+const char* nref_last_error() { return g_err; }
+
+void nref_attention_scalar(const float* q, const float* k, const float* v, float* out, int64_t n, int64_t pos0,
+                           int64_t n_heads, int64_t n_kv_heads, int64_t head_dim, float* scratch) {
+  nibble::cpu::attention_heads(q, k, v, out, n, pos0, n_heads, n_kv_heads, head_dim, 0, n_heads, scratch);
+}
+
+void nref_rope(float* x, int64_t n, int64_t n_heads, int64_t head_dim, int64_t pos0, float freq_base, int neox,
+               const float* freq_factors) {
+  const nibble::RopeParams p{freq_base, neox != 0, freq_factors};
+  nibble::cpu::rope(x, n, n_heads, head_dim, pos0, p);
+}
+
+void nref_softmax(float* x, int64_t n) { nibble::cpu::softmax_inplace(x, n); }
+
+float nref_fp16_to_fp32(uint16_t h) { return nibble::fp16_to_fp32(h); }
+uint16_t nref_fp32_to_fp16(float f) { return nibble::fp32_to_fp16(f); }
+// Bulk forms: results never pass through a host-language float, so NaN payloads arrive unchanged.
+void nref_fp16_to_fp32_n(const uint16_t* src, float* dst, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) dst[i] = nibble::fp16_to_fp32(src[i]);
+}
+void nref_fp32_to_fp16_n(const float* src, uint16_t* dst, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) dst[i] = nibble::fp32_to_fp16(src[i]);
+}
+
+// Name of the SIMD tier CpuBackend selects on this CPU ("scalar" when none).
+const char* nref_kernels_name() {
+  try {
+    const nibble::simd::Kernels* k = nibble::simd::select();
+    return k ? k->name : "scalar";
+  } catch (const std::exception& e) {
+    set_err(e.what());
+    return nullptr;
+  }
+}
+
+// Creates a ThreadPool of `threads` (caller included) and a CpuBackend on it; nullptr on failure.
+void* nref_backend_create(int threads) {
+  try {
+    return new RefBackend(threads);
+  } catch (const std::exception& e) {
+    set_err(e.what());
+    return nullptr;
+  }
+}
+
+void nref_backend_destroy(void* h) { delete static_cast<RefBackend*>(h); }
+
+int nref_backend_threads(void* h) { return static_cast<RefBackend*>(h)->pool.size(); }
+
+// Backend::reserve(ReserveParams{n_ctx, n_heads, max_rows, max_width}); 0 on success.
+int nref_backend_reserve(void* h, int64_t n_ctx, int64_t n_heads, int64_t max_rows, int64_t max_width) {
+  try {
+    static_cast<RefBackend*>(h)->be.reserve({n_ctx, n_heads, max_rows, max_width});
+    return 0;
+  } catch (const std::exception& e) {
+    set_err(e.what());
+    return 1;
+  }
+}
+
+// CpuBackend::attention on host buffers (the CPU backend's memory is host memory).
+int nref_backend_attention(void* h, const float* q, const float* k, const float* v, float* out, int64_t n,
+                           int64_t pos0, int64_t n_heads, int64_t n_kv_heads, int64_t head_dim) {
+  try {
+    static_cast<RefBackend*>(h)->be.attention(q, k, v, out, n, pos0, n_heads, n_kv_heads, head_dim);
+    return 0;
+  } catch (const std::exception& e) {
+    set_err(e.what());
+    return 1;
+  }
+}
+
+// CpuBackend::rope (scalar cpu::rope behind the backend's dispatch).
+int nref_backend_rope(void* h, float* x, int64_t n, int64_t n_heads, int64_t head_dim, int64_t pos0, float freq_base,
+                      int neox, const float* freq_factors) {
+  try {
+    const nibble::RopeParams p{freq_base, neox != 0, freq_factors};
+    static_cast<RefBackend*>(h)->be.rope(x, n, n_heads, head_dim, pos0, p);
+    return 0;
+  } catch (const std::exception& e) {
+    set_err(e.what());
+    return 1;
+  }
+}
+
+}  // extern "C"

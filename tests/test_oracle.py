@@ -1,0 +1,168 @@
+"""Pins the CPU oracle (oracle/nbl_oracle.c) before anything is checked against it.
+
+* The reference's own known-answer cases, restated (tests/test_ref_ops.cpp:41-96, :130-135 in nibble).
+* The committed golden fixtures made by nibble's own compiled code (tests/golden/make_golden.py): the scalar
+  restatement must be bit-identical to cpu::attention_heads / cpu::rope / softmax_inplace / fp16.h, and within
+  the reference's own SIMD tolerance of CpuBackend::attention (tests/test_ops.cpp:195-216: 2e-6 per unit of q
+  scale).
+* Live comparison with oracle/_ref when it is built (this container; skipped where the reference tree is absent).
+"""
+import glob
+import math
+import os
+
+import numpy as np
+import pytest
+
+import oracle
+
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def rel(a, b, eps=1e-6, margin=1e-7):
+    return abs(a - b) <= margin + eps * abs(b)
+
+
+# ---------------------------------------------------------------- known answers (test_ref_ops.cpp)
+def test_rope_known_answers():
+    c1, s1, c2, s2 = math.cos(1.0), math.sin(1.0), math.cos(0.01), math.sin(0.01)
+    x = np.array([1, 0, 1, 0], np.float32)
+    y = oracle.rope(x, 1, 4, 1, 10000.0, False)
+    assert rel(y[0], c1) and rel(y[1], s1) and rel(y[2], c2) and rel(y[3], s2)
+    y = oracle.rope(x, 1, 4, 1, 10000.0, True)
+    assert rel(y[0], c1 - s1) and rel(y[1], 0) and rel(y[2], s1 + c1) and rel(y[3], 0)
+    y = oracle.rope(x, 1, 4, 0, 10000.0, False)
+    assert np.array_equal(y, x)  # position 0 is the identity
+    y = oracle.rope(x, 1, 4, 1, 10000.0, False, np.array([1.0, 2.0], np.float32))
+    assert rel(y[2], math.cos(0.005)) and rel(y[3], math.sin(0.005))
+
+
+def test_attention_known_answer():
+    qkv = np.array([1, 0, 0, 1], np.float32)
+    out = oracle.attention(qkv, qkv, qkv, 2, 0, 1, 1, 2).ravel()
+    assert rel(out[0], 1) and rel(out[1], 0)
+    e = math.exp(1.0 / math.sqrt(2.0))
+    assert rel(out[2], 1.0 / (1.0 + e)) and rel(out[3], e / (1.0 + e))
+
+
+def test_attention_gqa_mapping():
+    H, KV, D, N = 4, 2, 2, 3
+    q = np.ones((1, H, D), np.float32)
+    k = np.zeros((N, KV, D), np.float32)
+    v = np.zeros((N, KV, D), np.float32)
+    for j in range(N):
+        for g in range(KV):
+            for d in range(D):
+                v[j, g, d] = 10 * g + j + d
+    out = oracle.attention(q, k, v, 1, N - 1, H, KV, D)
+    for h in range(H):
+        for d in range(D):
+            assert rel(out[0, h, d], 10 * (h // 2) + 1 + d)
+
+
+def test_softmax_overflow_safe():
+    y = oracle.softmax(np.array([1000.0, 1000.0], np.float32))
+    assert rel(y[0], 0.5) and rel(y[1], 0.5)
+
+
+def test_lse_merge_reproduces_full_softmax():
+    rng = np.random.default_rng(0)
+    H, KV, D, ctx = 4, 2, 16, 97
+    q = rng.standard_normal((1, H, D)).astype(np.float32)
+    k = rng.standard_normal((ctx, KV, D)).astype(np.float32)
+    v = rng.standard_normal((ctx, KV, D)).astype(np.float32)
+    full = oracle.attention(q, k, v, 1, ctx - 1, H, KV, D)[0]
+    cuts = [0, 10, 40, 41, 97]
+    parts_o, parts_lse = [], []
+    scale = 1.0 / math.sqrt(D)
+    for a, b in zip(cuts[:-1], cuts[1:]):
+        kk, vv = k[a:b].astype(np.float64), v[a:b].astype(np.float64)
+        s = np.einsum("hd,jhd->hj", np.repeat(q[0].astype(np.float64), 1, 0), np.repeat(kk, H // KV, 1)) * scale
+        m = s.max(1, keepdims=True)
+        p = np.exp(s - m)
+        parts_o.append((np.einsum("hj,jhd->hd", p, np.repeat(vv, H // KV, 1)) / p.sum(1, keepdims=True)))
+        parts_lse.append((m[:, 0] + np.log(p.sum(1))))
+    parts_o.append(np.zeros((H, D)))  # an empty part (lse = -inf) must not contribute
+    parts_lse.append(np.full(H, -np.inf))
+    out, lse = oracle.lse_merge(np.array(parts_o, np.float32), np.array(parts_lse, np.float32))
+    np.testing.assert_allclose(out, full, atol=2e-6, rtol=0)
+
+
+# ---------------------------------------------------------------- golden fixtures (nibble's own outputs)
+@pytest.mark.parametrize("path", sorted(glob.glob(os.path.join(GOLD, "attention_*.npz"))),
+                         ids=lambda p: os.path.basename(p)[10:-4])
+def test_attention_matches_golden(path):
+    f = np.load(path)
+    n, pos0, H, KV, D = (int(x) for x in f["meta"])
+    out = oracle.attention(f["q"], f["k"], f["v"], n, pos0, H, KV, D)
+    assert np.array_equal(out, f["out_scalar"]), "scalar restatement must be bit-identical to cpu::attention_heads"
+    qscale = max(1.0, float(np.abs(f["q"]).max()) / 4.0)
+    assert np.abs(out - f["out_backend"]).max() <= 2e-6 * max(1.0, qscale)
+
+
+@pytest.mark.parametrize("path", sorted(glob.glob(os.path.join(GOLD, "rope_*.npz"))),
+                         ids=lambda p: os.path.basename(p)[5:-4])
+def test_rope_matches_golden(path):
+    f = np.load(path)
+    n, H, D, pos0, neox = (int(x) for x in f["meta"])
+    ff = f["ff"] if f["ff"].size else None
+    out = oracle.rope(f["x"], H, D, pos0, float(f["base"]), bool(neox), ff)
+    assert np.array_equal(out, f["out"])
+
+
+def test_softmax_matches_golden():
+    f = np.load(os.path.join(GOLD, "softmax.npz"))
+    assert np.array_equal(oracle.softmax(f["x"]), f["out"])
+
+
+def test_fp16_matches_golden():
+    f = np.load(os.path.join(GOLD, "fp16.npz"))
+    widened = oracle.fp16_bits_to_f32(np.arange(65536, dtype=np.uint16))
+    same = (widened.view(np.uint32) == f["widened"].view(np.uint32))
+    assert same.all(), "every fp16 bit pattern (NaN payloads included) widens like src/fp16.h"
+    assert np.array_equal(oracle.f32_to_fp16_bits(f["sample"]), f["narrowed"])
+    # numpy's IEEE conversion agrees with the reference on finite values (round to nearest even)
+    fin = np.isfinite(f["sample"]) & (np.abs(f["sample"]) < 65520)
+    assert np.array_equal(f["sample"][fin].astype(np.float16).view(np.uint16), f["narrowed"][fin])
+
+
+def test_bf16_rounding_is_rne():
+    x = np.array([1.0, 1.00390625, 1.005859375, -3.1415927, 1e-40, np.inf], np.float32)
+    bits = oracle.f32_to_bf16_bits(x)
+    back = oracle.bf16_bits_to_f32(bits)
+    assert back[0] == 1.0 and back[1] == 1.0 and back[2] == np.float32(1.0078125)
+    assert back[5] == np.inf
+    assert np.all(np.abs(back[:4] - x[:4]) <= np.abs(x[:4]) * 2.0 ** -8)
+
+
+def test_gather_pages_layout():
+    KV, D, P = 2, 4, 16
+    n_pages, length = 5, 37
+    rng = np.random.default_rng(1)
+    pool = rng.integers(0, 2 ** 14, size=(n_pages, 2, KV, P, D), dtype=np.uint16)  # finite fp16 patterns
+    table = np.array([3, 0, 4], np.int32)
+    k, v = oracle.gather_pages(pool, table, length, KV, D, P)
+    for j in (0, 15, 16, 36):
+        page, slot = table[j // P], j % P
+        np.testing.assert_array_equal(k[j], oracle.fp16_bits_to_f32(pool[page, 0, :, slot, :]))
+        np.testing.assert_array_equal(v[j], oracle.fp16_bits_to_f32(pool[page, 1, :, slot, :]))
+
+
+# ---------------------------------------------------------------- live reference (where it was built)
+needs_ref = pytest.mark.skipif(not oracle.have_ref(), reason="oracle/_ref not built (no reference tree)")
+
+
+@needs_ref
+@pytest.mark.parametrize("shape", [(1, 0, 14, 2, 64), (9, 31, 32, 8, 64), (3, 100, 32, 4, 64), (2, 5, 6, 3, 10)])
+def test_oracle_bit_identical_to_reference(shape):
+    n, pos0, H, KV, D = shape
+    rng = np.random.default_rng(sum(shape))
+    q = rng.standard_normal((n, H, D)).astype(np.float32)
+    k = rng.standard_normal((pos0 + n, KV, D)).astype(np.float32)
+    v = rng.standard_normal((pos0 + n, KV, D)).astype(np.float32)
+    assert np.array_equal(oracle.attention(q, k, v, n, pos0, H, KV, D),
+                          oracle.ref_attention_scalar(q, k, v, n, pos0, H, KV, D))
+    x = rng.standard_normal((n, H, D)).astype(np.float32)
+    for neox in (False, True):
+        assert np.array_equal(oracle.rope(x, H, D, pos0 + 70000, 5e5, neox),
+                              oracle.ref_rope(x, H, D, pos0 + 70000, 5e5, neox))
