@@ -159,7 +159,8 @@ def decode_batched(args, world, rank, local):
     import torch
     import nibble_b200 as nb
     from nibble_b200.workloads import make_page_tables
-    rows = SEQ2 * LAYERS2
+    seqs = args.seqs or SEQ2
+    rows = seqs * LAYERS2
     length = CTX2 + 1
     ctx = nb.Context(local)
     table, n_pages = make_page_tables([length] * rows, 16, shuffle_seed=100 + rank)
@@ -214,18 +215,20 @@ def decode_batched(args, world, rank, local):
     ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
     kern_ms = statistics.mean(a.elapsed_time(b) for a, b in kev)
     ctx.check()
-    # e2e through the C ABI: pinned host inputs -> nbl_write, kernels, nbl_read of the outputs, every step
-    for _ in range(max(1, args.warmup // 2)):
-        e2e_step(ctx, q_in_h, k_in_h, v_in_h, out_h, q_in, k_in, v_in, out, step)
-    barrier(world)
-    torch.cuda.synchronize()
-    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    f0.record(st)
-    for _ in range(args.steps):
-        e2e_step(ctx, q_in_h, k_in_h, v_in_h, out_h, q_in, k_in, v_in, out, step)
-    f1.record(st)
-    torch.cuda.synchronize()
-    e2e_ms = max_over_ranks(f0.elapsed_time(f1) / args.steps, world)
+    e2e_ms = None
+    if not args.no_e2e:
+        # e2e through the C ABI: pinned host inputs -> nbl_write, kernels, nbl_read of the outputs, every step
+        for _ in range(max(1, args.warmup // 2)):
+            e2e_step(ctx, q_in_h, k_in_h, v_in_h, out_h, q_in, k_in, v_in, out, step)
+        barrier(world)
+        torch.cuda.synchronize()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(st)
+        for _ in range(args.steps):
+            e2e_step(ctx, q_in_h, k_in_h, v_in_h, out_h, q_in, k_in, v_in, out, step)
+        f1.record(st)
+        torch.cuda.synchronize()
+        e2e_ms = max_over_ranks(f0.elapsed_time(f1) / args.steps, world)
     sampler.stop()
     hbm, _, _, src = peaks()
     decode_bytes = kv_bytes + qo_bytes
@@ -235,12 +238,14 @@ def decode_batched(args, world, rank, local):
         "metric": "decode attn HBM GB/s", "value": world * step_bytes / (ms * 1e-3) / 1e9, "unit": "GB/s",
         "ms_per_step": ms, "dtype": "fp16 KV, fp32 accumulate",
         "config": {"workload": "config 2: Llama-3.2-1B batched decode", "heads": f"{H2}q/{KV2}kv", "head_dim": D,
-                   "sequences_per_gpu": SEQ2, "layers": LAYERS2, "kv_tokens": length, "page_size": 16,
+                   "sequences_per_gpu": seqs, "layers": LAYERS2, "kv_tokens": length, "page_size": 16,
                    "kv_bytes_per_step_per_gpu": kv_bytes, "algorithmic_bytes_per_step_per_gpu": step_bytes,
                    "l2": "inputs (8.6 GB/GPU) larger than L2; no flush needed", "parallelism": f"sequence-sharded x{world}"},
-        "e2e": {"value": world * step_bytes / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": e2e_ms,
-                "h2d_bytes_per_step": int(q_in_h.numel() * 4 + k_in_h.numel() * 4 + v_in_h.numel() * 4),
-                "d2h_bytes_per_step": int(out_h.numel() * 4)},
+        "e2e": None if e2e_ms is None else {
+            "value": world * step_bytes / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": e2e_ms,
+            "h2d_bytes_per_step": int(q_in_h.numel() * 4 + k_in_h.numel() * 4 + v_in_h.numel() * 4),
+            "d2h_bytes_per_step": int(out_h.numel() * 4),
+            "path": "nbl_write (pinned host q/k/v) -> nbl_rope_kv_append -> nbl_attn_decode -> nbl_read (out)"},
         "roofline": {"kernel": "decode_kernel", "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                      "frac": achieved / hbm, "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured" else "fallback 6650 GB/s",
                      "frac_of_nominal_8000": achieved / 8000.0, "kernel_ms": kern_ms,
@@ -268,7 +273,8 @@ def prefill(args, world, rank, local, steps=None, warmup=None):
     from nibble_b200.workloads import make_page_tables
     steps = steps or args.steps
     warmup = warmup or args.warmup
-    items = SEQ3 * LAYERS3
+    seqs = args.prefill_seqs or SEQ3
+    items = seqs * LAYERS3
     ctx = nb.Context(local)
     table, n_pages = make_page_tables([T3] * items, 16, shuffle_seed=200 + rank)
     kv = ctx.kv_pool(n_pages, KV3, dtype=nb.BF16)
@@ -320,11 +326,156 @@ def prefill(args, world, rank, local, steps=None, warmup=None):
         "metric": "prefill attn TFLOP/s", "value": world * flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s",
         "ms_per_step": ms, "kernel_ms": kern_ms, "dtype": "bf16 operands, fp32 accumulate",
         "config": {"workload": "config 3: TinyLlama-1.1B causal prefill", "heads": f"{H3}q/{KV3}kv", "head_dim": D,
-                   "sequences_per_gpu": SEQ3, "tokens": T3, "layers": LAYERS3, "flops_per_step_per_gpu": flops},
+                   "sequences_per_gpu": seqs, "tokens": T3, "layers": LAYERS3, "flops_per_step_per_gpu": flops},
         "roofline": {"kernel": "prefill_kernel", "bound": "tensor", "achieved": ach, "peak": bf16, "unit": "TFLOP/s",
                      "frac": ach / bf16, "peak_source": f"{src} bf16_tflops (burst)", "frac_of_sustained": ach / bf16_sus,
                      "frac_of_nominal_2250": ach / 2250.0, "traffic": profile_traffic("prefill_kernel_cfg3")},
     }
+    kv.close()
+    ctx.close()
+    return res
+
+
+# ---------------------------------------------------------------- config 4: one long context, KV split over ranks
+H4, KV4, LEN4, LAYERS4 = 32, 8, 131072, 16
+
+
+def decode_long(args, world, rank, local, steps, warmup):
+    """Config 4: one sequence with a 131072-token fp16 cache + 1 new token, 16 layers (16 independent rows). The
+    KV sequence is split into contiguous page-aligned chunks over the ranks; each rank attends its chunk with the
+    split-K decode (lse out), then one NCCL all-gather of the packed (O, lse) partials of all 16 layers and the
+    LSE merge give every rank the full result. Strong scaling: the total work is fixed."""
+    import torch
+    import nibble_b200 as nb
+    from nibble_b200 import dist as ndist
+    from nibble_b200.workloads import kv_split, make_page_tables
+    length = LEN4 + 1
+    a, b = kv_split(length, world)[rank]
+    my_len = b - a
+    rows = LAYERS4
+    ctx = nb.Context(local)
+    table, n_pages = make_page_tables([my_len] * rows, 16, shuffle_seed=400 + rank)
+    kv = ctx.kv_pool(max(1, n_pages), KV4)
+    fill_normal_(kv.tensor().view(torch.float16), seed=4000 + rank)
+    rng = np.random.default_rng(7)  # the query is the same on every rank
+    q = torch.from_numpy(rng.standard_normal((rows, H4, D)).astype(np.float32)).cuda()
+    out = torch.empty((rows, H4, D), device="cuda")
+    lse = torch.empty((rows, H4), device="cuda")
+    merged = torch.empty((rows * H4, D), device="cuda")
+    d = lambda x: torch.from_numpy(np.ascontiguousarray(x)).cuda()  # noqa: E731
+    t_table, lens = d(table), d(np.full(rows, my_len, np.int32))
+    st = torch.cuda.current_stream()
+
+    def step(ev=None):
+        if ev:
+            ev[0].record(st)
+        ctx.attn_decode(kv, q, t_table, lens, max(1, my_len), out, lse)
+        if ev:
+            ev[1].record(st)
+        if world > 1:
+            g = ndist.all_gather_partials(ndist.pack_partials(out, lse))
+            po, pl = ndist.unpack_partials(g, rows, H4, D)
+            ctx.lse_merge(po, pl, merged)
+
+    for _ in range(warmup):
+        step()
+    ctx.check()
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for i in range(steps):
+        step(kev[i])
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
+    kern_ms = statistics.mean(x.elapsed_time(y) for x, y in kev)
+    ctx.check()
+    total_kv = rows * length * KV4 * D * 2 * 2
+    my_kv = rows * my_len * KV4 * D * 2 * 2
+    hbm, _, _, src = peaks()
+    ach = (my_kv + 2 * rows * H4 * D * 4) / (kern_ms * 1e-3) / 1e9
+    res = {"metric": "decode attn HBM GB/s", "value": total_kv / (ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ms,
+           "scaling": "strong",
+           "config": {"workload": "config 4: long-context decode, KV split over ranks", "kv_tokens": length,
+                      "layers": LAYERS4, "heads": f"{H4}q/{KV4}kv", "kv_tokens_this_rank": my_len,
+                      "exchange": "one NCCL all-gather of packed (O, lse) for all layers + LSE merge" if world > 1
+                      else "none (one GPU)"},
+           "roofline": {"kernel": "decode_kernel (+ lse_merge)", "bound": "hbm", "achieved": ach, "peak": hbm,
+                        "unit": "GB/s", "frac": ach / hbm, "peak_source": src, "kernel_ms": kern_ms}}
+    kv.close()
+    ctx.close()
+    return res
+
+
+# ---------------------------------------------------------------- config 5: ragged paged decode, LPT-balanced
+H5, KV5, SEQ5, LAYERS5, MAXLEN5 = 14, 2, 256, 24, 8192
+
+
+def decode_ragged(args, world, rank, local, steps, warmup):
+    """Config 5: Qwen2.5-0.5B heads, 256 sequences with seeded lengths U[1, 8192], 24 layers, 16-token fp16 pages
+    shuffled in one shared pool; one new token per sequence (appended, then attended). Sequences are bin-packed
+    over ranks by KV length (LPT). Strong scaling: the total work is fixed."""
+    import torch
+    import nibble_b200 as nb
+    from nibble_b200.workloads import lpt_partition, make_page_tables, ragged_lengths
+    ctx_lens = ragged_lengths(SEQ5, 1, MAXLEN5, seed=5)
+    mine = lpt_partition(ctx_lens + 1, world)[rank]
+    my_ctx = np.repeat(ctx_lens[mine], LAYERS5)  # rows = (sequence, layer), sequence-major
+    lens_after = (my_ctx + 1).astype(np.int32)
+    rows = len(lens_after)
+    ctx = nb.Context(local)
+    table, n_pages = make_page_tables(lens_after, 16, shuffle_seed=500 + rank)
+    kv = ctx.kv_pool(n_pages, KV5)
+    fill_normal_(kv.tensor().view(torch.float16), seed=5000 + rank)
+    rng = np.random.default_rng(rank)
+    q_in = torch.from_numpy(rng.standard_normal((rows, H5, D)).astype(np.float32)).cuda()
+    k_in = torch.from_numpy(rng.standard_normal((rows, KV5, D)).astype(np.float32)).cuda()
+    v_in = torch.from_numpy(rng.standard_normal((rows, KV5, D)).astype(np.float32)).cuda()
+    q = torch.empty_like(q_in)
+    out = torch.empty_like(q_in)
+    d = lambda x: torch.from_numpy(np.ascontiguousarray(x)).cuda()  # noqa: E731
+    t_table, t_lens = d(table), d(lens_after)
+    tok_row, tok_pos = d(np.arange(rows, dtype=np.int32)), d(my_ctx.astype(np.int32))
+    spec = nb.RopeSpec(1e6, True)
+    st = torch.cuda.current_stream()
+    max_len = int(lens_after.max())
+
+    def step(ev=None):
+        ctx.rope_kv_append(kv, q_in, k_in, v_in, q, tok_row, tok_pos, t_table, H5, spec)
+        if ev:
+            ev[0].record(st)
+        ctx.attn_decode(kv, q, t_table, t_lens, max_len, out)
+        if ev:
+            ev[1].record(st)
+
+    for _ in range(warmup):
+        step()
+    ctx.check()
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for i in range(steps):
+        step(kev[i])
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
+    kern_ms = statistics.mean(x.elapsed_time(y) for x, y in kev)
+    ctx.check()
+    total_kv = int((ctx_lens + 1).sum()) * LAYERS5 * KV5 * D * 2 * 2
+    my_kv = int(lens_after.sum()) * KV5 * D * 2 * 2
+    hbm, _, _, src = peaks()
+    ach = (my_kv + 2 * rows * H5 * D * 4) / (kern_ms * 1e-3) / 1e9
+    res = {"metric": "decode attn HBM GB/s", "value": total_kv / (ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ms,
+           "scaling": "strong",
+           "config": {"workload": "config 5: ragged paged decode (Qwen2.5-0.5B heads)", "sequences": SEQ5,
+                      "layers": LAYERS5, "ctx_lengths": "U[1, 8192] seed 5", "kv_bytes_total": total_kv,
+                      "sequences_this_rank": len(mine), "balance": "LPT by KV length"},
+           "roofline": {"kernel": "decode_kernel", "bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s",
+                        "frac": ach / hbm, "peak_source": src, "kernel_ms": kern_ms}}
     kv.close()
     ctx.close()
     return res
@@ -408,9 +559,14 @@ def main():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["decode_batched", "prefill"], default="decode_batched")
+    ap.add_argument("--workload", choices=["decode_batched", "prefill", "decode_long", "decode_ragged"],
+                    default="decode_batched")
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-3 prefill leg of the default run")
-    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-extra", action="store_true", help="skip the config-4/5 legs of the default run")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffers) leg")
+    ap.add_argument("--seqs", type=int, default=0, help="config-2 sequences per GPU (default 64; smaller for profiling)")
+    ap.add_argument("--prefill-seqs", type=int, default=0, help="config-3 sequences per GPU (default 8)")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample length (0 skips it)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -421,16 +577,25 @@ def main():
         return
 
     world, rank, local = dist_setup(args.gpus)
+    legs = max(3, args.steps // 5)
     if args.workload == "prefill":
         res = prefill(args, world, rank, local)
+    elif args.workload == "decode_long":
+        res = decode_long(args, world, rank, local, args.steps, args.warmup)
+    elif args.workload == "decode_ragged":
+        res = decode_ragged(args, world, rank, local, args.steps, args.warmup)
     else:
         res = decode_batched(args, world, rank, local)
         if not args.no_prefill:
-            res["prefill"] = prefill(args, world, rank, local, steps=max(3, args.steps // 10), warmup=3)
+            res["prefill"] = prefill(args, world, rank, local, steps=legs, warmup=3)
+        if not args.no_extra:
+            res["decode_long"] = decode_long(args, world, rank, local, legs, 3)
+            res["decode_ragged"] = decode_ragged(args, world, rank, local, legs, 3)
+    res.setdefault("scaling", "weak")
     res.update({"n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "data": "synthetic (seeded N(0,1))"})
+                "vs_baseline": None, "data": "synthetic (seeded N(0,1))"})
     res["gpu_launches"] = res.pop("gpu_launches_per_step", 2) * args.steps
-    if rank == 0 and world == 1:
+    if rank == 0 and world == 1 and args.cpu_seconds > 0:
         res["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
     if world > 1:
         import torch.distributed as dist

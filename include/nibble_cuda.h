@@ -81,8 +81,11 @@ NBL_API int nbl_ctx_create(int device, nbl_ctx** out);
 /* Frees every allocation, pool and table the context still owns (CpuBackend::~CpuBackend frees unfreed
  * blocks, cpu_backend.cpp:70-72). */
 NBL_API int nbl_ctx_destroy(nbl_ctx* ctx);
-/* Runs later launches on `stream` (a cudaStream_t; NULL restores the context's own stream). */
+/* Runs later launches on `stream` (a cudaStream_t; NULL is CUDA's default stream). A new context runs on a
+ * stream of its own until this is called. */
 NBL_API int nbl_ctx_set_stream(nbl_ctx* ctx, void* stream);
+/* Returns the context to its own stream. */
+NBL_API int nbl_ctx_use_own_stream(nbl_ctx* ctx);
 NBL_API void* nbl_ctx_stream(nbl_ctx* ctx);
 NBL_API int nbl_ctx_sync(nbl_ctx* ctx);
 /* Synchronises, then returns NBL_E_DEVICE (and clears the flag) if any kernel since the last check skipped
@@ -117,7 +120,7 @@ NBL_API int nbl_rope(nbl_ctx* ctx, float* x, int64_t n, int64_t n_heads, int64_t
              const nbl_rope_params* rope);
 /* Backend::attention (backend.h:66-69; CpuBackend::attention cpu_backend.cpp:272-290): q,out [n, n_heads,
  * head_dim]; k,v [>= pos0+n, n_kv_heads, head_dim], all fp32 device memory; row t has position pos0+t and
- * attends to 0..pos0+t. n_heads % n_kv_heads == 0, head_dim even and <= 256. */
+ * attends to 0..pos0+t. n_heads % n_kv_heads == 0, head_dim <= 256 (any parity, as in the reference). */
 NBL_API int nbl_attention(nbl_ctx* ctx, const float* q, const float* k, const float* v, float* out, int64_t n, int64_t pos0,
                   int64_t n_heads, int64_t n_kv_heads, int64_t head_dim);
 

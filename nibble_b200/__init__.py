@@ -120,6 +120,7 @@ class Context:
 
     # ---- context
     def set_stream(self, stream: int | None):
+        """Runs later kernels on this cudaStream_t (0 / None = CUDA's default stream)."""
         check(_abi.lib.nbl_ctx_set_stream(self.handle, stream))
 
     def sync(self):

@@ -1,8 +1,8 @@
 """ctypes binding of the C ABI in include/nibble_cuda.h (libnibble_cuda.so, built in-tree).
 
 This module is plumbing for Python callers (tests, bench, smoke): every call goes through the C ABI into the
-sm_100a kernels. There is no CPU fallback: if the library is missing or does not load, importing the package
-raises.
+sm_100a kernels. There is no CPU fallback: the library is loaded on first use, and a missing or unloadable
+library raises ImportError there.
 """
 from __future__ import annotations
 
@@ -46,6 +46,7 @@ SIGNATURES = {
     "nbl_ctx_create": [C.c_int, C.POINTER(_P)],
     "nbl_ctx_destroy": [_P],
     "nbl_ctx_set_stream": [_P, _P],
+    "nbl_ctx_use_own_stream": [_P],
     "nbl_ctx_stream": [_P],
     "nbl_ctx_sync": [_P],
     "nbl_ctx_check": [_P],
@@ -80,10 +81,25 @@ def _load() -> C.CDLL:
     return lib
 
 
-lib = _load()
+_lib = None
+
+
+def get_lib() -> C.CDLL:
+    """The loaded library (loaded on first use, so the build step can import this package without it)."""
+    global _lib
+    if _lib is None:
+        _lib = _load()
+    return _lib
+
+
+def __getattr__(name):
+    if name == "lib":
+        return get_lib()
+    raise AttributeError(name)
 
 
 def last_error() -> str:
+    lib = get_lib()
     n = lib.nbl_last_error(None, 0)
     buf = C.create_string_buffer(n + 1)
     lib.nbl_last_error(buf, n + 1)

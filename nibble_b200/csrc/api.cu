@@ -202,7 +202,14 @@ int nbl_ctx_destroy(nbl_ctx* ctx) {
 int nbl_ctx_set_stream(nbl_ctx* ctx, void* stream) {
   return guarded([&] {
     require(ctx != nullptr, "nbl_ctx_set_stream: ctx is NULL");
-    ctx->stream = stream ? static_cast<cudaStream_t>(stream) : ctx->own_stream;
+    ctx->stream = static_cast<cudaStream_t>(stream);  // NULL is CUDA's default stream, as everywhere in CUDA
+  });
+}
+
+int nbl_ctx_use_own_stream(nbl_ctx* ctx) {
+  return guarded([&] {
+    require(ctx != nullptr, "nbl_ctx_use_own_stream: ctx is NULL");
+    ctx->stream = ctx->own_stream;
   });
 }
 
@@ -339,10 +346,10 @@ int nbl_attention(nbl_ctx* ctx, const float* q, const float* k, const float* v, 
   return guarded([&] {
     require(ctx && q && k && v && out, "attention: NULL pointer");
     require(n > 0 && pos0 >= 0 && n_heads > 0 && n_kv_heads > 0 && n_heads % n_kv_heads == 0 && head_dim > 0 &&
-                head_dim % 2 == 0 && head_dim <= 256,
+                head_dim <= 256,
             "attention: n=" + std::to_string(n) + " pos0=" + std::to_string(pos0) + " n_heads=" +
                 std::to_string(n_heads) + " n_kv_heads=" + std::to_string(n_kv_heads) + " head_dim=" +
-                std::to_string(head_dim) + " (n_heads must be a multiple of n_kv_heads; head_dim even, <= 256)");
+                std::to_string(head_dim) + " (n_heads must be a multiple of n_kv_heads; head_dim <= 256)");
     use_device(ctx);
     const float scale = 1.0f / std::sqrt(static_cast<float>(head_dim));
     nbl::launch_attention_f32(ctx->stream, q, k, v, out, n, pos0, n_heads, n_kv_heads, head_dim, scale);

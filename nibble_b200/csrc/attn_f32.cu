@@ -57,13 +57,18 @@ __global__ void __launch_bounds__(kWarps * 32) attention_f32_kernel(const float*
     const int64_t j = j0 + lane;
     float s = -INFINITY;
     if (j < len) {
-      const float2* kj = reinterpret_cast<const float2*>(kbase + j * kv_stride);
-      const float2* q2 = reinterpret_cast<const float2*>(qw);
+      const float* kj = kbase + j * kv_stride;
       float dot = 0.f;
-      for (int d = 0; d < head_dim / 2; ++d) {
-        const float2 kk = kj[d], qq = q2[d];
-        dot = fmaf(qq.x, kk.x, dot);
-        dot = fmaf(qq.y, kk.y, dot);
+      if ((head_dim & 1) == 0) {  // rows start on 8-byte boundaries: paired loads
+        const float2* k2 = reinterpret_cast<const float2*>(kj);
+        const float2* q2 = reinterpret_cast<const float2*>(qw);
+        for (int d = 0; d < head_dim / 2; ++d) {
+          const float2 kk = k2[d], qq = q2[d];
+          dot = fmaf(qq.x, kk.x, dot);
+          dot = fmaf(qq.y, kk.y, dot);
+        }
+      } else {
+        for (int d = 0; d < head_dim; ++d) dot = fmaf(qw[d], kj[d], dot);
       }
       s = dot * scale;
     }
