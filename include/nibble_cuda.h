@@ -155,6 +155,20 @@ NBL_API int nbl_attn_decode(nbl_ctx* ctx, const nbl_kv* kv, const float* q, cons
                     const int32_t* seq_lens, int32_t max_seq_len, int32_t n_rows, int32_t n_heads, float* out,
                     float* lse, int32_t n_splits);
 
+/* Same arguments and results as nbl_attn_decode, but the call allocates no device memory: the split partials
+ * live in a fixed 8 MiB array inside the library (held on every GPU that loads it, until the process exits)
+ * instead of context scratch. For callers that may not allocate once running -- e.g. an engine that owns all
+ * device memory through its own pool, or a decode loop that cannot take cudaMalloc's device-wide sync.
+ * An explicit n_splits whose partials (n_splits * n_rows * n_heads * 65 floats) exceed the array is rejected
+ * with NBL_E_INVALID; with n_splits = 0 the split count is reduced until they fit. All calls on a device share
+ * the array (each call writes every partial it reads, so nothing needs clearing); calls whose kernels overlap
+ * on the GPU race on it and must be serialised. The first call on a device resolves the array's address and
+ * should come before any stream capture. No counterpart in the reference (nibble's CPU backend sizes its
+ * scratch once in reserve()). */
+NBL_API int nbl_attn_decode_static(nbl_ctx* ctx, const nbl_kv* kv, const float* q, const int32_t* page_table,
+                                   int32_t pt_stride, const int32_t* seq_lens, int32_t max_seq_len, int32_t n_rows,
+                                   int32_t n_heads, float* out, float* lse, int32_t n_splits);
+
 /* Causal prefill (Backend::attention with n >= 1) over the paged pool for n_items independent items. q and out
  * hold n_q_rows rows of [n_heads, head_dim]. Item i: query rows q[q_start[i] .. q_start[i] + q_len[i])
  * (q_dtype = the pool dtype, already roped) at positions kv_pos0[i] + t, attending keys 0..kv_pos0[i]+t of

@@ -64,6 +64,7 @@ SIGNATURES = {
     "nbl_rope_kv_append": [_P, _P, _P, _P, _P, _I32, _P, _P, _P, _P, _I32, _P, _P, _P, _I32, _I64, _I32,
                            C.POINTER(RopeParams)],
     "nbl_attn_decode": [_P, _P, _P, _P, _I32, _P, _I32, _I32, _I32, _P, _P, _I32],
+    "nbl_attn_decode_static": [_P, _P, _P, _P, _I32, _P, _I32, _I32, _I32, _P, _P, _I32],
     "nbl_attn_prefill": [_P, _P, _P, _I32, _I64, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _P, _I32],
     "nbl_lse_merge": [_P, _P, _P, _I32, _I64, _I32, _P, _P],
 }

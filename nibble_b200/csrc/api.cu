@@ -130,6 +130,8 @@ void nbl::encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, voi
   if (r != CUDA_SUCCESS) nbl::fail(NBL_E_CUDA, "cuTensorMapEncodeTiled failed (CUresult " + std::to_string(r) + ")");
 }
 
+int nbl::record_error(int status, const std::string& msg) { return set_error(status, msg); }
+
 namespace {
 
 bool is_dtype(int32_t d) { return d == NBL_F32 || d == NBL_F16 || d == NBL_BF16; }

@@ -62,6 +62,10 @@ struct nbl_kv {
 
 namespace nbl {
 
+// Stores msg as the calling thread's nbl_last_error() message and returns status (for entry points defined
+// outside api.cu).
+int record_error(int status, const std::string& msg);
+
 // Encodes a tiled TMA descriptor (driver entry point resolved once through the runtime; no libcuda link).
 // dims/strides in elements/bytes as cuTensorMapEncodeTiled takes them; 128-byte swizzle, zero OOB fill.
 void encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, void* base, const cuuint64_t* dims,

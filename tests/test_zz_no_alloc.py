@@ -1,0 +1,86 @@
+"""nbl_attn_decode_static -- the decode entry point that allocates no device memory -- against the ordinary
+nbl_attn_decode, through the C ABI.
+
+Some callers cannot allocate device memory once they are running: an engine that hands all of a GPU's memory to
+its own pool at start-up, or a decode loop that cannot absorb cudaMalloc's device-wide synchronisation. For them
+the library keeps the split-K partials in a fixed 8 MiB device array instead of growing context scratch. These
+tests check that its results equal the ordinary entry point's on two calls in a row (the array is shared and
+keeps old contents, so the second call must not be affected by the first), and that a request that does not fit
+is refused with an error instead of running. This file is collected last on purpose, and it builds its own
+context so it also passes when run alone.
+"""
+
+import numpy as np
+import pytest
+
+from helpers import max_rel_err_per_head
+from nibble_b200.workloads import make_page_tables
+
+pytestmark = pytest.mark.gpu
+D = 64
+
+
+def _static_decode(ctx, kv, q, table, lens, max_len, out, lse, n_splits):
+    from nibble_b200 import _abi
+    _abi.check(_abi.lib.nbl_attn_decode_static(ctx.handle, kv.handle, q.data_ptr(), table.data_ptr(),
+                                               table.shape[-1], lens.data_ptr(), max_len, q.shape[0], q.shape[1],
+                                               out.data_ptr(), lse.data_ptr(), n_splits))
+
+
+@pytest.fixture(scope="module")
+def setup():
+    import torch
+    import nibble_b200 as nb
+    ctx = nb.Context(0)
+    H, KV = 32, 8
+    lens = [4097, 1, 700, 131, 2048, 16]  # few rows: the library splits each row, so the partials are used
+    table, n_pages = make_page_tables(lens, 16, shuffle_seed=3)
+    kv = ctx.kv_pool(n_pages, KV)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    pool = kv.tensor().view(torch.float16)
+    pool.copy_(torch.randn(pool.shape, generator=g, device="cuda").half())
+    d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()  # noqa: E731
+    yield ctx, kv, d(table), d(np.array(lens, np.int32)), max(lens), H
+    kv.close()
+    ctx.close()
+
+
+@pytest.mark.parametrize("n_splits", [0, 5])
+def test_static_decode_matches_regular_on_two_calls_in_a_row(setup, n_splits):
+    import torch
+    ctx, kv, table, lens, max_len, H = setup
+    rows = lens.shape[0]
+    qs = [torch.randn((rows, H, D), device="cuda", generator=torch.Generator(device="cuda").manual_seed(s))
+          for s in (11, 12)]
+    got = []
+    for q in qs:  # two calls of the static entry point back to back, different queries
+        out = torch.full((rows, H, D), float("nan"), device="cuda")
+        lse = torch.full((rows, H), float("nan"), device="cuda")
+        _static_decode(ctx, kv, q, table, lens, max_len, out, lse, n_splits)
+        got.append((out, lse))
+    ctx.check()
+    for q, (out, lse) in zip(qs, got):
+        ref = torch.empty_like(out)
+        ref_lse = torch.empty_like(lse)
+        ctx.attn_decode(kv, q, table, lens, max_len, ref, ref_lse, n_splits=n_splits)
+        ctx.check()
+        torch.cuda.synchronize()
+        assert max_rel_err_per_head(out.cpu().numpy(), ref.cpu().numpy()) <= 1e-4
+        np.testing.assert_allclose(lse.cpu().numpy(), ref_lse.cpu().numpy(), rtol=0, atol=2e-5)
+
+
+def test_static_decode_refuses_partials_larger_than_its_array(setup):
+    import torch
+    import nibble_b200 as nb
+    ctx, kv, table, lens, max_len, H = setup
+    rows = 128  # 16 splits requested -> 10 splits of 2 pages: 10 x 128 rows x 32 heads x 65 floats = 10.6 MB > 8 MiB
+    big_table = torch.zeros((rows, table.shape[-1]), dtype=torch.int32, device="cuda")
+    big_lens = torch.full((rows,), 300, dtype=torch.int32, device="cuda")
+    q = torch.zeros((rows, H, D), device="cuda")
+    out = torch.zeros_like(q)
+    lse = torch.zeros((rows, H), device="cuda")
+    with pytest.raises(nb.NibbleError) as e:
+        _static_decode(ctx, kv, q, big_table, big_lens, 300, out, lse, 16)
+    assert e.value.status == nb._abi.NBL_E_INVALID and "static" in str(e.value)
+    _static_decode(ctx, kv, q, big_table, big_lens, 300, out, lse, 0)  # the library-chosen count fits
+    ctx.check()
