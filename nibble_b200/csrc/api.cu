@@ -239,6 +239,7 @@ int nbl_ctx_check(nbl_ctx* ctx) {
       if (host & nbl::kErrLength) what += " sequence length or position outside the page table / RoPE table;";
       if (host & nbl::kErrTimeout) what += " a bounded wait on a copy or MMA completion gave up;";
       if (host & nbl::kErrTmemAlloc) what += " tensor-memory allocation failed;";
+      if (host & nbl::kErrSmemAlign) what += " shared memory was not 1024-byte aligned;";
       nbl::fail(NBL_E_DEVICE, "device-side check failed (flags " + std::to_string(host) + "):" + what);
     }
   });

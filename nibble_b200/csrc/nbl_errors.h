@@ -8,5 +8,6 @@ enum : int {
   kErrLength = 2,     // a sequence length / position outside the page table or the RoPE table
   kErrTimeout = 4,    // a bounded wait gave up (lost TMA / MMA completion)
   kErrTmemAlloc = 8,  // tensor-memory allocation failed
+  kErrSmemAlign = 16, // dynamic shared memory not 1024-byte aligned (swizzled TMA tiles need it)
 };
 }  // namespace nbl

@@ -4,20 +4,28 @@
 // src/backend/cpu/ref_ops.cpp:188-214): query row t of an item has position kv_pos0 + t and attends keys
 // 0..kv_pos0+t; query head h reads KV head h / G.
 //
-// One CTA = one 128-row query tile of one head. Six warps, specialised:
-//   warp 0      TMA producer: the Q tile once (3-D map over q), then K/V tiles of 128 keys (8 pages, one
-//               16x64 box each for K and V) through a 3-stage shared-memory ring; 128-byte swizzle.
-//   warp 1      MMA issuer (one thread): S = Q K^T into TMEM (M=128, N=128, K=64), then O += P V into TMEM
-//               (M=128, N=64, K=128) with V used as an MN-major operand straight from the TMA tile. Completion
-//               is signalled with tcgen05.commit on mbarriers.
-//   warps 2-5   softmax: thread i owns query row i = TMEM lane i. It loads its S row from TMEM, applies the
-//               causal mask, keeps the online max/sum in fp32 (log2 domain), writes P as bf16/fp16 into a
-//               swizzled shared tile (the A operand of the PV MMA), rescales its O row in TMEM when the max
-//               moves, and finally normalises O and stores the output row.
-// S_{j+1} = Q K_{j+1}^T is issued as soon as the softmax has read S_j, so it overlaps the exponentials of
-// tile j; PV_j overlaps the exponentials of tile j+1.
-// CTAs of one (item, KV head) are numbered consecutively, so the G heads x query tiles that read the same K/V
-// run together and the K/V tiles come from L2 after the first read.
+// One CTA = one 128-row query tile for two query heads of the same KV group (NH = 2; the heads share every K/V
+// tile staged in shared memory, and an odd group leaves the last CTA with one head). Warps, specialised:
+//   warps 0..7   softmax, one warpgroup per head: thread i of a warpgroup owns query row i = TMEM lane i (a warp
+//                reaches the lane quarter warp % 4). Per K/V tile it loads its S row (64 fp32) from TMEM in one
+//                instruction, masks causally, takes the row max with a tree, and keeps a reference max m_ref (log2
+//                domain) that only moves when the tile max exceeds it by more than 2^8, so the O accumulator in
+//                TMEM is rescaled rarely; p = 2^(s*scale - m_ref) via ex2.approx with packed fp32x2 arguments, the
+//                row sum with packed adds; P is packed to bf16/fp16 pairs and stored into the first 32 columns of
+//                its S region as the A operand of the PV MMA.
+//   warp 8       TMA producer: the Q tiles once (3-D map over q), then K/V tiles of 64 keys (4 pages, one 16x64
+//                box each for K and V) through a 3-stage shared-memory ring; 128-byte swizzle.
+//   warp 9       MMA issuer (one thread): S_g = Q_g K_j^T (M=128, N=64, K=64, both operands K-major from shared
+//                memory) and O_g += P_g V_j (M=128, N=64, K=64) with P read from TMEM and V used as an MN-major
+//                operand straight from the TMA tile, issued per head as PV_g(j), S_g(j+1) so a head's next S never
+//                waits for the other head's softmax. MMAs execute in issue order, so S_g(j+1) may overwrite the
+//                TMEM columns PV_g(j) read P_g from.
+// Sizing: 320 threads at <= 102 registers, 256 TMEM columns (per head 64 for S/P and 64 for O) and 81 KB of shared
+// memory, so two CTAs share an SM: four independent softmax -> MMA -> softmax chains per SM hide each other's
+// hand-offs, and per-SM exp throughput (16 ex2 per clock, twice the tensor time of a 128x64 tile at head_dim 64)
+// sets the pace.
+// CTAs of one (item, KV head) are numbered consecutively (head pairs x query tiles, latest query tile first) so
+// the tiles that read the same K/V run together and hit L2.
 //
 // Every mbarrier wait is bounded (nbl_device.cuh): a lost completion ends the CTA with kErrTimeout set.
 #include <algorithm>
@@ -30,26 +38,35 @@ namespace nbl {
 namespace {
 
 constexpr int kD = 64;
-constexpr int kBM = 128;                 // query rows per CTA
-constexpr int kBN = 128;                 // keys per tile
+constexpr int kBM = 128;                  // query rows per tile
 constexpr int kPage = 16;
-constexpr int kPagesPerTile = kBN / kPage;
-constexpr int kStages = 3;
-constexpr int kTileBytes = kBN * kD * 2;  // one K (or V) tile: 16 KB
-constexpr int kQBytes = kBM * kD * 2;     // 16 KB
-constexpr int kPBytes = kBM * kBN * 2;    // 32 KB (two 64-key swizzle atoms of [128 rows][128 B])
+constexpr int kQBytes = kBM * kD * 2;     // one Q tile: 16 KB
 constexpr int kBoxBytes = kPage * kD * 2; // 2 KB
-constexpr int kOffQ = 0;
-constexpr int kOffKV = kOffQ + kQBytes;
-constexpr int kOffP = kOffKV + kStages * 2 * kTileBytes;
-constexpr int kOffBar = kOffP + kPBytes;
-constexpr int kSmemBytes = 1024 + kOffBar + 256;
-constexpr int kThreads = 192;
-constexpr uint32_t kTmemCols = 256;  // S: columns [0,128), O: [128,192)
-constexpr uint32_t kColS = 0, kColO = 128;
-// barrier slots
-constexpr int kBarQ = 0, kBarFull = 1, kBarEmpty = 1 + kStages, kBarSFull = 1 + 2 * kStages,
-              kBarSFree = kBarSFull + 1, kBarPFull = kBarSFull + 2, kBarODone = kBarSFull + 3;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units: p may reach 2^8 before the reference max moves
+
+template <int NH, int BN>
+struct Cfg {
+  static constexpr int kBN = BN;                       // keys per K/V tile
+  static constexpr int kPagesPerTile = BN / kPage;
+  static constexpr int kTileBytes = BN * kD * 2;       // one K (or V) tile
+  static constexpr int kStages = 3;
+  static constexpr int kThreads = (4 * NH + 2) * 32;
+  static constexpr int kWarpTma = 4 * NH, kWarpMma = 4 * NH + 1;
+  static constexpr int kCtasPerSm = 2;
+  static constexpr uint32_t kTmemCols = NH * (BN + kD) <= 128 ? 128 : (NH * (BN + kD) <= 256 ? 256 : 512);
+  static constexpr int kOffQ = 0;
+  static constexpr int kOffKV = NH * kQBytes;
+  static constexpr int kOffBar = kOffKV + kStages * 2 * kTileBytes;
+  static constexpr int kOffTmemSlot = kOffBar + 112;
+  static constexpr int kSmemBytes = kOffBar + 128;
+  // barrier slots
+  static constexpr int kBarQ = 0, kBarFull = 1, kBarEmpty = 1 + kStages, kBarSFull = 1 + 2 * kStages,
+                       kBarPFull = kBarSFull + NH, kBarODone = kBarSFull + 2 * NH;
+  static_assert((kBarODone + 1) * 8 <= 112, "barriers overlap the TMEM address slot");
+  // TMEM columns of head g's S region (P aliases its first BN/2 columns) and O accumulator
+  __host__ __device__ static constexpr uint32_t col_s(int g) { return g * BN; }
+  __host__ __device__ static constexpr uint32_t col_o(int g) { return NH * BN + g * kD; }
+};
 
 struct PrefillArgs {
   const int32_t* q_start;
@@ -62,7 +79,7 @@ struct PrefillArgs {
   int64_t n_q_rows;
   int32_t pt_stride;
   int out_f32;
-  int n_heads, n_kv_heads, group, m_tiles;
+  int n_heads, n_kv_heads, group, n_hgroups, m_tiles;
   float scale_log2;
 };
 
@@ -90,6 +107,16 @@ __device__ __forceinline__ void tmem_ld32_wait(uint32_t taddr, uint32_t (&r)[32]
       : "memory");
 }
 
+// 64 consecutive TMEM columns, waiting inside the same asm statement.
+__device__ __forceinline__ void tmem_ld64_wait(uint32_t taddr, uint32_t (&r)[64]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%64];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+      : "r"(taddr)
+      : "memory");
+}
+
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -112,22 +139,29 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* e
   return __all_sync(0xffffffffu, mbar_wait(bar, parity, err));
 }
 
-template <bool BF16>
-__global__ void __launch_bounds__(kThreads, 1)
+template <bool BF16, int NH, int BN>
+__global__ void __launch_bounds__(Cfg<NH, BN>::kThreads, Cfg<NH, BN>::kCtasPerSm)
     prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kvmap,
                    const PrefillArgs a) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  using C = Cfg<NH, BN>;
+  constexpr int kBN = C::kBN, kPagesPerTile = C::kPagesPerTile, kTileBytes = C::kTileBytes;
+  extern __shared__ __align__(1024) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (smem_u32(smem) & 1023u) {  // 128-byte-swizzled tiles need 1024-byte alignment; never expected to trip
+    if (threadIdx.x == 0) flag_error(a.err, kErrSmemAlign);
+    return;
+  }
 
   // ---- which tile: CTAs of one (item, KV head) are consecutive; heavier (later) query tiles first
-  const int per_group = a.m_tiles * a.group;
+  const int per_group = a.m_tiles * a.n_hgroups;
   const int grp = blockIdx.x / per_group;
   const int within = blockIdx.x % per_group;
-  const int mt = a.m_tiles - 1 - within / a.group;
-  const int g = within % a.group;
+  const int mt = a.m_tiles - 1 - within / a.n_hgroups;
+  const int hg = within % a.n_hgroups;
   const int item = grp / a.n_kv_heads, kvh = grp % a.n_kv_heads;
-  const int h = kvh * a.group + g;
+  const int g0 = NH * hg;
+  const int n_g = min(NH, a.group - g0);  // an odd group leaves the last pair with one head
+  const int head0 = kvh * a.group + g0;   // head of softmax warpgroup g is head0 + g
   const int qlen = a.q_len[item], pos0 = a.kv_pos0[item], qs = a.q_start[item];
   const int m0 = mt * kBM;
   if (qlen <= 0 || m0 >= qlen) return;
@@ -141,27 +175,27 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int n_item_pages = static_cast<int>((kv_len + kPage - 1) / kPage);
   const int32_t* pt_row = a.page_table + int64_t(item) * a.pt_stride;
 
-  uint8_t* sQ = smem + kOffQ;
-  uint8_t* sP = smem + kOffP;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffBar + 128);
-  auto sK = [&](int s) { return smem + kOffKV + s * 2 * kTileBytes; };
-  auto sV = [&](int s) { return smem + kOffKV + s * 2 * kTileBytes + kTileBytes; };
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kOffTmemSlot);
+  auto sQ = [&](int g) { return smem + C::kOffQ + g * kQBytes; };
+  auto sK = [&](int s) { return smem + C::kOffKV + s * 2 * kTileBytes; };
+  auto sV = [&](int s) { return smem + C::kOffKV + s * 2 * kTileBytes + kTileBytes; };
 
   if (threadIdx.x == 0) {
-    mbar_init(&bars[kBarQ], 1);
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&bars[kBarFull + s], 1);
-      mbar_init(&bars[kBarEmpty + s], 1);
+    mbar_init(&bars[C::kBarQ], 1);
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&bars[C::kBarFull + s], 1);
+      mbar_init(&bars[C::kBarEmpty + s], 1);
     }
-    mbar_init(&bars[kBarSFull], 1);
-    mbar_init(&bars[kBarSFree], 128);
-    mbar_init(&bars[kBarPFull], 128);
-    mbar_init(&bars[kBarODone], 1);
+    for (int g = 0; g < NH; ++g) {
+      mbar_init(&bars[C::kBarSFull + g], 1);
+      mbar_init(&bars[C::kBarPFull + g], 128);
+    }
+    mbar_init(&bars[C::kBarODone], 1);
     fence_barrier_init();
   }
-  if (warp == 0) {
-    tmem_alloc(tmem_slot, kTmemCols);
+  if (warp == C::kWarpMma) {
+    tmem_alloc(tmem_slot, C::kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -169,17 +203,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
+  if (warp == C::kWarpTma) {
     // ================= TMA producer
     if (lane == 0) {
       prefetch_tensormap(&qmap);
       prefetch_tensormap(&kvmap);
-      mbar_arrive_expect_tx(&bars[kBarQ], kQBytes);
-      tma_load_3d(sQ, &qmap, 0, h, qs + m0, &bars[kBarQ]);
+      mbar_arrive_expect_tx(&bars[C::kBarQ], n_g * kQBytes);
+      for (int g = 0; g < n_g; ++g) tma_load_3d(sQ(g), &qmap, 0, head0 + g, qs + m0, &bars[C::kBarQ]);
     }
     for (int j = 0; j < n_kv; ++j) {
-      const int s = j % kStages;
-      if (j >= kStages && !warp_wait(&bars[kBarEmpty + s], ((j / kStages) & 1) ^ 1, a.err)) break;
+      const int s = j % C::kStages;
+      if (j >= C::kStages && !warp_wait(&bars[C::kBarEmpty + s], ((j / C::kStages) & 1) ^ 1, a.err)) break;
       const int pg = j * kPagesPerTile + lane;
       int32_t pid = -1;
       if (lane < kPagesPerTile && pg < n_item_pages) {
@@ -189,8 +223,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           pid = -1;
         }
       }
-      const uint32_t present = __ballot_sync(0xffffffffu, pid >= 0) & 0xffu;
-      if (present != 0xffu) {
+      constexpr uint32_t kAllPages = (1u << kPagesPerTile) - 1u;
+      const uint32_t present = __ballot_sync(0xffffffffu, pid >= 0) & kAllPages;
+      if (present != kAllPages) {
         // Pages past the item's end (or rejected ids) are zero-filled so P*V sees finite data there.
         for (int p = 0; p < kPagesPerTile; ++p) {
           if ((present >> p) & 1u) continue;
@@ -201,182 +236,181 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_proxy_async_smem();
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive_expect_tx(&bars[kBarFull + s], __popc(present) * 2u * kBoxBytes);
+      if (lane == 0) mbar_arrive_expect_tx(&bars[C::kBarFull + s], __popc(present) * 2u * kBoxBytes);
       __syncwarp();
       if (pid >= 0) {
         const int32_t yk = ((pid * 2 + 0) * a.n_kv_heads + kvh) * kPage;
         const int32_t yv = ((pid * 2 + 1) * a.n_kv_heads + kvh) * kPage;
-        tma_load_2d(sK(s) + lane * kBoxBytes, &kvmap, 0, yk, &bars[kBarFull + s]);
-        tma_load_2d(sV(s) + lane * kBoxBytes, &kvmap, 0, yv, &bars[kBarFull + s]);
+        tma_load_2d(sK(s) + lane * kBoxBytes, &kvmap, 0, yk, &bars[C::kBarFull + s]);
+        tma_load_2d(sV(s) + lane * kBoxBytes, &kvmap, 0, yv, &bars[C::kBarFull + s]);
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == C::kWarpMma) {
     // ================= MMA issuer (one thread)
     if (lane == 0) {
       constexpr uint32_t idesc_qk = make_idesc_f16(kBM, kBN, BF16, false, false);
       constexpr uint32_t idesc_pv = make_idesc_f16(kBM, kD, BF16, false, true);
-      const uint32_t tS = tmem + kColS, tO = tmem + kColO;
-      const uint32_t q_addr = smem_u32(sQ), p_addr = smem_u32(sP);
-      bool ok = mbar_wait(&bars[kBarQ], 0, a.err);
-      auto qk = [&](int j) {
-        const int s = j % kStages;
-        ok = ok && mbar_wait(&bars[kBarFull + s], (j / kStages) & 1, a.err);
-        if (j > 0) ok = ok && mbar_wait(&bars[kBarSFree], (j - 1) & 1, a.err);
-        if (!ok) return;
-        tc_fence_after();
-        const uint32_t k_addr = smem_u32(sK(s));
+      // S_g = Q_g K_j^T for head g (signals S_g full).
+      auto qk = [&](int g, int j) {
+        const uint32_t q_addr = smem_u32(sQ(g)), k_addr = smem_u32(sK(j % C::kStages));
 #pragma unroll
         for (int kk = 0; kk < kD / 16; ++kk)
-          tc_mma_ss(tS, make_sdesc(q_addr + kk * 32, 16, 1024, 2), make_sdesc(k_addr + kk * 32, 16, 1024, 2), idesc_qk,
-                    kk > 0 ? 1u : 0u);
-        tc_commit(&bars[kBarSFull]);
+          tc_mma_ss(tmem + C::col_s(g), make_sdesc(q_addr + kk * 32, 16, 1024, 2),
+                    make_sdesc(k_addr + kk * 32, 16, 1024, 2), idesc_qk, kk > 0 ? 1u : 0u);
+        tc_commit(&bars[C::kBarSFull + g]);
       };
-      auto pv = [&](int j) {
-        const int s = j % kStages;
-        ok = ok && mbar_wait(&bars[kBarPFull], j & 1, a.err);
-        if (!ok) return;
+      // O_g += P_g V_j once head g's softmax has written P_g.
+      auto pv = [&](int g, int j) -> bool {
+        if (!mbar_wait(&bars[C::kBarPFull + g], j & 1, a.err)) return false;
         tc_fence_after();
-        const uint32_t v_addr = smem_u32(sV(s));
+        const uint32_t v_addr = smem_u32(sV(j % C::kStages));
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk)
-          tc_mma_ss(tO, make_sdesc(p_addr + (kk >> 2) * (kBM * 128) + (kk & 3) * 32, 16, 1024, 2),
-                    make_sdesc(v_addr + kk * 16 * 128, 0, 1024, 2), idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
-        tc_commit(&bars[kBarODone]);
-        tc_commit(&bars[kBarEmpty + s]);
+          tc_mma_ts(tmem + C::col_o(g), tmem + C::col_s(g) + kk * 8, make_sdesc(v_addr + kk * 16 * 128, 0, 1024, 2),
+                    idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+        return true;
       };
-      qk(0);
-      for (int j = 1; j < n_kv; ++j) {
-        qk(j);
-        pv(j - 1);
+      auto kv_ready = [&](int j) -> bool {
+        if (!mbar_wait(&bars[C::kBarFull + j % C::kStages], (j / C::kStages) & 1, a.err)) return false;
+        tc_fence_after();
+        return true;
+      };
+      bool ok = mbar_wait(&bars[C::kBarQ], 0, a.err) && kv_ready(0);
+      if (ok)
+        for (int g = 0; g < n_g; ++g) qk(g, 0);
+      for (int j = 0; j < n_kv && ok; ++j) {
+        const bool more = j + 1 < n_kv;
+        if (more) ok = kv_ready(j + 1);
+        for (int g = 0; g < n_g && ok; ++g) {
+          ok = pv(g, j);
+          if (ok && more) qk(g, j + 1);
+        }
+        tc_commit(&bars[C::kBarEmpty + j % C::kStages]);  // K_j and V_j fully consumed
       }
-      pv(n_kv - 1);
+      tc_commit(&bars[C::kBarODone]);
     }
     __syncwarp();
-  } else {
+  } else if ((warp >> 2) < n_g) {
     // ================= softmax / correction / epilogue: thread = query row = TMEM lane
+    const int g = warp >> 2;
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
-    const uint32_t t_lane = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t tS = tmem + C::col_s(g) + lane_off, tO = tmem + C::col_o(g) + lane_off;
     const int qpos = pos0 + m0 + r;
-    float m_run = -INFINITY, l_run = 0.f;
+    const float scale = a.scale_log2;
+    const float2 scale2 = make_float2(scale, scale);
+    float m_ref = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
-      ok = warp_wait(&bars[kBarSFull], j & 1, a.err);
+      ok = warp_wait(&bars[C::kBarSFull + g], j & 1, a.err);
       if (!ok) break;
       tc_fence_after();
-      float s[kBN];
-#pragma unroll
-      for (int c = 0; c < kBN / 32; ++c) {
-        uint32_t t[32];
-        tmem_ld32_wait(t_lane + kColS + c * 32, t);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(t[i]);
-      }
-      tc_fence_before();
-      mbar_arrive(&bars[kBarSFree]);
+      uint32_t t[kBN];
+      static_assert(kBN == 64, "one 64-column TMEM load per S row");
+      tmem_ld64_wait(tS, t);
       const int kbase = j * kBN;
-      if (kbase + kBN - 1 > qpos) {
+      if (kbase + kBN - 1 > qpos) {  // the tile holds keys past this row's position
 #pragma unroll
         for (int c = 0; c < kBN; ++c)
-          if (kbase + c > qpos) s[c] = -INFINITY;
+          if (kbase + c > qpos) t[c] = __float_as_uint(-INFINITY);
       }
-      float mx = s[0];
+      float mx[8];
 #pragma unroll
-      for (int c = 1; c < kBN; ++c) mx = fmaxf(mx, s[c]);
-      const float m_new = fmaxf(m_run, mx * a.scale_log2);
+      for (int i = 0; i < 8; ++i) mx[i] = __uint_as_float(t[i]);
+#pragma unroll
+      for (int c = 8; c < kBN; c += 8)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mx[i] = fmaxf(mx[i], __uint_as_float(t[c + i]));
+      const float m_tile = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                                 fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * scale;
+      const bool need = m_tile > m_ref + kRescaleThreshold;  // false for m_tile = -inf
+      const float m_new = need ? m_tile : m_ref;
       const float m_use = m_new == -INFINITY ? 0.f : m_new;
-      const float alpha = fast_exp2(m_run - m_use);
-      float sum = 0.f;
+      const float alpha = need ? fast_exp2(m_ref - m_use) : 1.f;  // m_ref = -inf gives 0
+      const float2 neg_m2 = make_float2(-m_use, -m_use);
+      float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+      // p = 2^(s*scale - m), packed in place: pair c/2 goes to t[c/2] (already consumed)
 #pragma unroll
-      for (int c = 0; c < kBN; ++c) {
-        s[c] = fast_exp2(fmaf(s[c], a.scale_log2, -m_use));
-        sum += s[c];
+      for (int c = 0; c < kBN; c += 2) {
+        const float2 x = __ffma2_rn(make_float2(__uint_as_float(t[c]), __uint_as_float(t[c + 1])), scale2, neg_m2);
+        const float2 e = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+        acc[(c >> 1) & 3] = __fadd2_rn(acc[(c >> 1) & 3], e);
+        t[c >> 1] = pack2<BF16>(e.x, e.y);
       }
-      l_run = l_run * alpha + sum;
-      m_run = m_new;
-      if (j > 0) {
-        ok = warp_wait(&bars[kBarODone], (j - 1) & 1, a.err);  // PV_{j-1} done: P tile free, O stable
-        if (!ok) break;
-        tc_fence_after();
-      }
-      // P row r -> swizzled K-major tile (keys 0-63 in the first atom column, 64-127 in the second)
+      const float2 sum2 = __fadd2_rn(__fadd2_rn(acc[0], acc[1]), __fadd2_rn(acc[2], acc[3]));
+      l_run = l_run * alpha + (sum2.x + sum2.y);
+      m_ref = m_new;
+      // P into the first BN/2 columns of this head's S region (the PV MMA's A operand)
 #pragma unroll
-      for (int at = 0; at < 2; ++at)
-#pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {
-          const float* v = s + at * 64 + ch * 8;
-          const uint4 w = make_uint4(pack2<BF16>(v[0], v[1]), pack2<BF16>(v[2], v[3]), pack2<BF16>(v[4], v[5]),
-                                     pack2<BF16>(v[6], v[7]));
-          *reinterpret_cast<uint4*>(sP + at * (kBM * 128) + swz128(r, ch)) = w;
-        }
-      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
-#pragma unroll
+      for (int c = 0; c < kBN / 64; ++c) tmem_st32(tS + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&t[32 * c]));
+      // S_g(j) completing implies PV_g(j-1) completed (MMAs execute in order), so O_g is stable here.
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+#pragma unroll 1
         for (int c = 0; c < kD / 32; ++c) {
-          uint32_t t[32];
-          tmem_ld32_wait(t_lane + kColO + c * 32, t);
+          uint32_t o[32];
+          tmem_ld32_wait(tO + c * 32, o);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) t[i] = __float_as_uint(__uint_as_float(t[i]) * alpha);
-          tmem_st16(t_lane + kColO + c * 32, *reinterpret_cast<uint32_t(*)[16]>(&t[0]));
-          tmem_st16(t_lane + kColO + c * 32 + 16, *reinterpret_cast<uint32_t(*)[16]>(&t[16]));
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(tO + c * 32, o);
         }
-        tc_wait_st();
       }
-      fence_proxy_async_smem();  // P stores -> visible to the tensor core
+      tc_wait_st();
       tc_fence_before();
-      mbar_arrive(&bars[kBarPFull]);
+      mbar_arrive(&bars[C::kBarPFull + g]);
     }
     // ---- epilogue
-    if (ok) ok = warp_wait(&bars[kBarODone], (n_kv - 1) & 1, a.err);
+    if (ok) ok = warp_wait(&bars[C::kBarODone], 0, a.err);
     if (ok) {
       tc_fence_after();
-      float o[kD];
-#pragma unroll
-      for (int c = 0; c < kD / 32; ++c) {
-        uint32_t t[32];
-        tmem_ld32_wait(t_lane + kColO + c * 32, t);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) o[c * 32 + i] = __uint_as_float(t[i]);
-      }
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-      if (m0 + r < qlen) {
-        const int64_t orow = (int64_t(qs) + m0 + r) * a.n_heads + h;
+      const int64_t orow = (int64_t(qs) + m0 + r) * a.n_heads + head0 + g;
+      const bool live = m0 + r < qlen;
+#pragma unroll 1
+      for (int c = 0; c < kD / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld32_wait(tO + c * 32, o);  // warp-collective: every lane loads, live rows store
+        if (!live) continue;
         if (a.out_f32) {
-          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + orow * kD);
+          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + orow * kD + c * 32);
 #pragma unroll
-          for (int i = 0; i < kD / 4; ++i)
-            dst[i] = make_float4(o[4 * i] * inv, o[4 * i + 1] * inv, o[4 * i + 2] * inv, o[4 * i + 3] * inv);
+          for (int i = 0; i < 8; ++i)
+            dst[i] = make_float4(__uint_as_float(o[4 * i]) * inv, __uint_as_float(o[4 * i + 1]) * inv,
+                                 __uint_as_float(o[4 * i + 2]) * inv, __uint_as_float(o[4 * i + 3]) * inv);
         } else {
-          uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.out) + orow * kD);
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.out) + orow * kD + c * 32);
 #pragma unroll
-          for (int i = 0; i < kD / 8; ++i)
-            dst[i] = make_uint4(pack2<BF16>(o[8 * i] * inv, o[8 * i + 1] * inv),
-                                pack2<BF16>(o[8 * i + 2] * inv, o[8 * i + 3] * inv),
-                                pack2<BF16>(o[8 * i + 4] * inv, o[8 * i + 5] * inv),
-                                pack2<BF16>(o[8 * i + 6] * inv, o[8 * i + 7] * inv));
+          for (int i = 0; i < 4; ++i)
+            dst[i] = make_uint4(pack2<BF16>(__uint_as_float(o[8 * i]) * inv, __uint_as_float(o[8 * i + 1]) * inv),
+                                pack2<BF16>(__uint_as_float(o[8 * i + 2]) * inv, __uint_as_float(o[8 * i + 3]) * inv),
+                                pack2<BF16>(__uint_as_float(o[8 * i + 4]) * inv, __uint_as_float(o[8 * i + 5]) * inv),
+                                pack2<BF16>(__uint_as_float(o[8 * i + 6]) * inv, __uint_as_float(o[8 * i + 7]) * inv));
         }
       }
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) {
+  if (warp == C::kWarpMma) {
     tc_fence_after();
-    tmem_dealloc(tmem, kTmemCols);
+    tmem_dealloc(tmem, C::kTmemCols);
   }
 }
 
-template <bool BF16>
+template <bool BF16, int NH, int BN>
 void launch_t(cudaStream_t st, const CUtensorMap& qmap, const CUtensorMap& kvmap, const PrefillArgs& a, int grid) {
+  using C = Cfg<NH, BN>;
   static std::atomic<uint64_t> configured{0};
   int dev = 0;
   check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
   const uint64_t bit = uint64_t(1) << (dev & 63);
   if (!(configured.load() & bit)) {
-    check_cuda(cudaFuncSetAttribute(prefill_kernel<BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes),
+    check_cuda(cudaFuncSetAttribute(prefill_kernel<BF16, NH, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    C::kSmemBytes),
                "prefill smem attribute");
     configured.fetch_or(bit);
   }
-  prefill_kernel<BF16><<<grid, kThreads, kSmemBytes, st>>>(qmap, kvmap, a);
+  prefill_kernel<BF16, NH, BN><<<grid, C::kThreads, C::kSmemBytes, st>>>(qmap, kvmap, a);
 }
 
 }  // namespace
@@ -384,6 +418,7 @@ void launch_t(cudaStream_t st, const CUtensorMap& qmap, const CUtensorMap& kvmap
 void launch_prefill(cudaStream_t st, const nbl_kv* kv, const void* q, int64_t n_q_rows, const int32_t* q_start,
                     const int32_t* q_len, const int32_t* kv_pos0, const int32_t* page_table, int32_t pt_stride,
                     int n_items, int n_heads, int max_q_len, void* out, int out_dtype, int* err) {
+  constexpr int NH = 2, BN = 64;  // heads per CTA, keys per K/V tile (see the file comment)
   const auto& c = kv->cfg;
   const bool bf16 = c.dtype == NBL_BF16;
   if (n_q_rows * n_heads >= (int64_t(1) << 31)) fail(NBL_E_INVALID, "prefill: q has more than 2^31 head rows");
@@ -407,12 +442,13 @@ void launch_prefill(cudaStream_t st, const nbl_kv* kv, const void* q, int64_t n_
   a.n_heads = n_heads;
   a.n_kv_heads = c.n_kv_heads;
   a.group = n_heads / c.n_kv_heads;
+  a.n_hgroups = (a.group + NH - 1) / NH;
   a.m_tiles = (max_q_len + kBM - 1) / kBM;
   a.scale_log2 = 1.4426950408889634f / 8.0f;  // log2(e) / sqrt(64)
-  const int64_t grid = int64_t(n_items) * n_heads * a.m_tiles;
+  const int64_t grid = int64_t(n_items) * c.n_kv_heads * a.n_hgroups * a.m_tiles;
   if (grid > 0x7fffffff) fail(NBL_E_INVALID, "prefill: items * heads * query tiles exceeds the grid limit");
-  if (bf16) launch_t<true>(st, qmap, kv->tmap, a, static_cast<int>(grid));
-  else launch_t<false>(st, qmap, kv->tmap, a, static_cast<int>(grid));
+  if (bf16) launch_t<true, NH, BN>(st, qmap, kv->tmap, a, static_cast<int>(grid));
+  else launch_t<false, NH, BN>(st, qmap, kv->tmap, a, static_cast<int>(grid));
   check_cuda(cudaGetLastError(), "prefill launch");
 }
 

@@ -107,6 +107,49 @@ def test_rope_kv_append_bit_exact(nbl_ctx, cfg):
         assert np.array_equal(pool[page, 1, :, slot, :], narrow(vi)), f"v token {i}"
 
 
+@pytest.mark.parametrize("neox,offset", [(False, 0), (True, 0), (False, 4), (False, 1), (True, 2), (True, 3)])
+def test_rope_kv_append_vector_and_scalar_paths(nbl_ctx, neox, offset):
+    """The 8-element vector path (16-byte-aligned rows) and the per-pair path (q/k/v that start off a 16-byte
+    boundary: `offset` shifts them by that many fp32 elements, 4 staying aligned) give the reference's bits, with
+    bias on every stream."""
+    import torch
+    import nibble_b200 as nb
+    H, KV, base, hd = 6, 2, 1e4, D
+    rng = np.random.default_rng(offset + (7 if neox else 0))
+    lens = [33, 5]
+    table, n_pages = make_page_tables(lens, 16, shuffle_seed=2)
+    kv = nbl_ctx.kv_pool(n_pages, KV, dtype=nb.BF16)
+    rows = np.concatenate([np.full(L, r) for r, L in enumerate(lens)]).astype(np.int32)
+    pos = np.concatenate([np.arange(L) for L in lens]).astype(np.int32)
+    n = len(rows)
+
+    def shifted(a):  # a device copy of `a` whose data pointer sits `offset` fp32 elements into its buffer
+        flat = torch.zeros(a.size + offset, device="cuda", dtype=torch.float32)
+        flat[offset:] = torch.from_numpy(a.ravel()).cuda()
+        return flat[offset:].view(a.shape)
+
+    q_in = rng.standard_normal((n, H, hd)).astype(np.float32)
+    k_in = rng.standard_normal((n, KV, hd)).astype(np.float32)
+    v_in = rng.standard_normal((n, KV, hd)).astype(np.float32)
+    bq, bk, bv = (rng.standard_normal(w * hd).astype(np.float32) for w in (H, KV, KV))
+    q_out = torch.empty((n, H, hd), device="cuda", dtype=torch.float32)
+    nbl_ctx.rope_kv_append(kv, shifted(q_in), shifted(k_in), shifted(v_in), q_out, dev(rows), dev(pos), dev(table),
+                           H, nb.RopeSpec(base, neox), bq=dev(bq), bk=dev(bk), bv=dev(bv))
+    nbl_ctx.check()
+    got_q = host(q_out)
+    pool = pool_bits(kv)
+    for i in range(n):
+        qi = oracle.add_bias(q_in[i], bq, 1).reshape(H, hd)
+        ki = oracle.add_bias(k_in[i], bk, 1).reshape(KV, hd)
+        vi = oracle.add_bias(v_in[i], bv, 1).reshape(KV, hd)
+        q_ref = oracle.rope(qi, H, hd, int(pos[i]), base, neox).reshape(H, hd)
+        k_ref = oracle.rope(ki, KV, hd, int(pos[i]), base, neox).reshape(KV, hd)
+        assert np.array_equal(got_q[i].view(np.uint32), q_ref.view(np.uint32)), f"q token {i}"
+        page, slot = table[rows[i], pos[i] // 16], pos[i] % 16
+        assert np.array_equal(pool[page, 0, :, slot, :], oracle.f32_to_bf16_bits(k_ref)), f"k token {i}"
+        assert np.array_equal(pool[page, 1, :, slot, :], oracle.f32_to_bf16_bits(vi)), f"v token {i}"
+
+
 # ---------------------------------------------------------------- decode
 DECODE_LENS = [1, 15, 16, 17, 33, 100, 257, 1000, 2049]
 
