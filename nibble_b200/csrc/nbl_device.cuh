@@ -77,7 +77,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   }
 }
 
-// ---------------------------------------------------------------- TMA (no multicast anywhere in this library)
+// ---------------------------------------------------------------- TMA (plain per-CTA tile loads only)
 // 2-D tiled load of the tensor-map box at (x, y) into shared memory, completing on `bar` (complete_tx).
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int32_t x, int32_t y,
                                             uint64_t* bar) {
