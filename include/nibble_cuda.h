@@ -155,6 +155,25 @@ NBL_API int nbl_attn_decode(nbl_ctx* ctx, const nbl_kv* kv, const float* q, cons
                     const int32_t* seq_lens, int32_t max_seq_len, int32_t n_rows, int32_t n_heads, float* out,
                     float* lse, int32_t n_splits);
 
+/* One decode step from host memory with the transfers overlapped -- nbl_write of the new tokens,
+ * nbl_rope_kv_append, nbl_attn_decode and nbl_read of the outputs in one call. Row r gets one new token: its
+ * q/k/v (q_in_h [n_rows, n_heads, head_dim], k_in_h / v_in_h [n_rows, n_kv_heads, head_dim], fp32 host memory;
+ * pinned memory lets the copies overlap) are biased (bq/bk/bv: fp32 device vectors or NULL), roped and appended
+ * at position seq_lens[r] - 1 (seq_lens counts the new token, so every seq_lens[r] >= 1), then row r attends keys
+ * 0..seq_lens[r]-1 and out_h[r] ([n_heads, head_dim] fp32 host) receives the result. page_table/seq_lens are
+ * device memory as for nbl_attn_decode. The rows are cut into n_chunks ranges (0 = chosen by the library): each
+ * range's upload runs on a copy stream while earlier ranges' append + decode run (on the context's stream and,
+ * when no split partials are needed, a second internal one so consecutive ranges overlap),
+ * and each range's results are copied back while the next range computes. Results equal the separate calls'
+ * (per-range split counts may differ, within the decode tolerance). Device staging (5 row-sized fp32 buffers)
+ * is context-owned and grown on demand. Returns once out_h is complete. No direct counterpart in the reference
+ * (its decode reads host-resident activations in place); this is the host-buffer form of the decode step. */
+NBL_API int nbl_decode_step_host(nbl_ctx* ctx, nbl_kv* kv, const float* q_in_h, const float* k_in_h,
+                                 const float* v_in_h, const float* bq, const float* bk, const float* bv,
+                                 const int32_t* page_table, int32_t pt_stride, const int32_t* seq_lens,
+                                 int32_t max_seq_len, int32_t n_rows, int32_t n_heads, const nbl_rope_params* rope,
+                                 float* out_h, int32_t n_chunks);
+
 /* Same arguments and results as nbl_attn_decode, but the call allocates no device memory: the split partials
  * live in a fixed 8 MiB array inside the library (held on every GPU that loads it, until the process exits)
  * instead of context scratch. For callers that may not allocate once running -- e.g. an engine that owns all

@@ -42,6 +42,11 @@ class RopeSpec:
 _DT = {"float32": F32, "float16": F16, "bfloat16": BF16}
 
 
+def torch_float32():
+    import torch
+    return torch.float32
+
+
 def _ptr(t) -> int | None:
     if t is None:
         return None
@@ -194,6 +199,20 @@ class Context:
         check(_abi.lib.nbl_attn_decode(self.handle, kv.handle, _ptr(q), _ptr(page_table), page_table.shape[-1],
                                        _ptr(seq_lens), max_seq_len, q.shape[0], q.shape[1], _ptr(out), _ptr(lse),
                                        n_splits))
+
+    def decode_step_host(self, kv: KVPool, q_in_h, k_in_h, v_in_h, page_table, seq_lens, max_seq_len: int,
+                         rope: RopeSpec, out_h, bq=None, bk=None, bv=None, n_chunks: int = 0):
+        """One decode step from host memory (see nbl_decode_step_host): q_in_h [rows, H, D], k_in_h/v_in_h
+        [rows, KVH, D] and out_h [rows, H, D] are fp32 host tensors (pinned for overlapped copies); page_table
+        and seq_lens (counting the new token) are device tensors."""
+        for t in (q_in_h, k_in_h, v_in_h, out_h):
+            if t.is_cuda or not t.is_contiguous() or t.dtype != torch_float32():
+                raise ValueError("host tensors must be contiguous float32 CPU tensors")
+        p, keep = rope._c()
+        check(_abi.lib.nbl_decode_step_host(
+            self.handle, kv.handle, q_in_h.data_ptr(), k_in_h.data_ptr(), v_in_h.data_ptr(), _ptr(bq), _ptr(bk),
+            _ptr(bv), _ptr(page_table), page_table.shape[-1], _ptr(seq_lens), max_seq_len, q_in_h.shape[0],
+            q_in_h.shape[1], C.byref(p), out_h.data_ptr(), n_chunks))
 
     def attn_prefill(self, kv: KVPool, q, q_start, q_len, kv_pos0, page_table, max_q_len: int, out):
         """Causal prefill: q [rows, n_heads, head_dim] (pool dtype), out [rows, n_heads, head_dim] fp32/pool dtype."""

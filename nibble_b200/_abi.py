@@ -65,6 +65,8 @@ SIGNATURES = {
                            C.POINTER(RopeParams)],
     "nbl_attn_decode": [_P, _P, _P, _P, _I32, _P, _I32, _I32, _I32, _P, _P, _I32],
     "nbl_attn_decode_static": [_P, _P, _P, _P, _I32, _P, _I32, _I32, _I32, _P, _P, _I32],
+    "nbl_decode_step_host": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I32, _P, _I32, _I32, _I32, C.POINTER(RopeParams),
+                             _P, _I32],
     "nbl_attn_prefill": [_P, _P, _P, _I32, _I64, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _P, _I32],
     "nbl_lse_merge": [_P, _P, _P, _I32, _I64, _I32, _P, _P],
 }

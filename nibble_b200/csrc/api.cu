@@ -195,6 +195,11 @@ int nbl_ctx_destroy(nbl_ctx* ctx) {
     for (auto& a : ctx->allocs) cudaFree(a.first);
     for (auto& t : ctx->rope_tables) cudaFree(t.dev);
     if (ctx->scratch) cudaFree(ctx->scratch);
+    if (ctx->io) cudaFree(ctx->io);
+    for (cudaEvent_t e : ctx->events) cudaEventDestroy(e);
+    if (ctx->up_stream) cudaStreamDestroy(ctx->up_stream);
+    if (ctx->down_stream) cudaStreamDestroy(ctx->down_stream);
+    if (ctx->aux_stream) cudaStreamDestroy(ctx->aux_stream);
     cudaFree(ctx->d_err);
     cudaStreamDestroy(ctx->own_stream);
     delete ctx;
@@ -461,6 +466,105 @@ int nbl_attn_decode(nbl_ctx* ctx, const nbl_kv* kv, const float* q, const int32_
     if (plan.scratch_bytes) ensure_scratch(ctx, plan.scratch_bytes);
     nbl::launch_decode(ctx->stream, kv, q, page_table, pt_stride, seq_lens, n_rows, n_heads, out, lse, plan,
                        ctx->scratch, ctx->d_err);
+  });
+}
+
+int nbl_decode_step_host(nbl_ctx* ctx, nbl_kv* kv, const float* q_in_h, const float* k_in_h, const float* v_in_h,
+                         const float* bq, const float* bk, const float* bv, const int32_t* page_table,
+                         int32_t pt_stride, const int32_t* seq_lens, int32_t max_seq_len, int32_t n_rows,
+                         int32_t n_heads, const nbl_rope_params* rope, float* out_h, int32_t n_chunks) {
+  return guarded([&] {
+    require(ctx && kv && q_in_h && k_in_h && v_in_h && page_table && seq_lens && rope && out_h,
+            "decode_step_host: NULL argument");
+    require(kv->ctx == ctx, "decode_step_host: pool belongs to another context");
+    require(kv->cfg.dtype == NBL_F16, "decode_step_host: the decode kernel reads an NBL_F16 pool");
+    require(n_rows >= 0 && pt_stride > 0 && max_seq_len >= 1 && n_chunks >= 0,
+            "decode_step_host: negative size, max_seq_len < 1 or pt_stride not positive");
+    const int kvh = kv->cfg.n_kv_heads;
+    require(n_heads > 0 && n_heads % kvh == 0 && n_heads / kvh <= 8,
+            "decode_step_host: n_heads must be a multiple of n_kv_heads with at most 8 query heads per KV head");
+    require(int64_t(max_seq_len) <= int64_t(pt_stride) * kv->cfg.page_size,
+            "decode_step_host: max_seq_len exceeds pt_stride * page_size");
+    if (n_rows == 0) return;
+    use_device(ctx);
+    const int64_t d = kv->cfg.head_dim;
+    const int64_t q_row = int64_t(n_heads) * d, kv_row = int64_t(kvh) * d;  // floats per row
+    const size_t need = static_cast<size_t>(n_rows) * static_cast<size_t>(3 * q_row + 2 * kv_row) * sizeof(float);
+    if (ctx->io_bytes < need) {
+      void* p = device_alloc(need, "decode_step_host staging");
+      if (ctx->io) {
+        nbl::check_cuda(cudaStreamSynchronize(ctx->stream), "staging sync");
+        cudaFree(ctx->io);
+      }
+      ctx->io = p;
+      ctx->io_bytes = need;
+    }
+    float* q_in = static_cast<float*>(ctx->io);
+    float* k_in = q_in + int64_t(n_rows) * q_row;
+    float* v_in = k_in + int64_t(n_rows) * kv_row;
+    float* q = v_in + int64_t(n_rows) * kv_row;
+    float* out = q + int64_t(n_rows) * q_row;
+    const auto& tab = rope_table(ctx, *rope, d, int64_t(pt_stride) * kv->cfg.page_size);
+    // Chunks: each keeps at least two waves of decode CTAs (2 per SM), at most 4.
+    int chunks = n_chunks;
+    if (chunks == 0) chunks = static_cast<int>(std::min<int64_t>(4, std::max<int64_t>(1, int64_t(n_rows) * kvh / (4 * ctx->num_sms))));
+    chunks = std::min(chunks, n_rows);
+    if (!ctx->up_stream) {
+      nbl::check_cuda(cudaStreamCreateWithFlags(&ctx->up_stream, cudaStreamNonBlocking), "copy stream");
+      nbl::check_cuda(cudaStreamCreateWithFlags(&ctx->down_stream, cudaStreamNonBlocking), "copy stream");
+      nbl::check_cuda(cudaStreamCreateWithFlags(&ctx->aux_stream, cudaStreamNonBlocking), "compute stream");
+    }
+    while (ctx->events.size() < size_t(2 * chunks + 1)) {
+      cudaEvent_t e;
+      nbl::check_cuda(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
+      ctx->events.push_back(e);
+    }
+    cudaEvent_t* ev_in = ctx->events.data() + 1;
+    cudaEvent_t* ev_out = ev_in + chunks;
+    std::vector<nbl::DecodePlan> plans(chunks);
+    size_t scratch = 0;
+    auto bounds = [&](int c) { return std::make_pair(int64_t(c) * n_rows / chunks, int64_t(c + 1) * n_rows / chunks); };
+    for (int c = 0; c < chunks; ++c) {
+      const auto [r0, r1] = bounds(c);
+      plans[c] = nbl::plan_decode(static_cast<int>(r1 - r0), kvh, n_heads / kvh, n_heads, max_seq_len,
+                                  kv->cfg.page_size, ctx->num_sms, 0);
+      scratch = std::max(scratch, plans[c].scratch_bytes);
+    }
+    if (scratch) ensure_scratch(ctx, scratch);
+    // Chunks touch disjoint rows and pages, so without split partials (which share the context scratch) odd
+    // chunks run on a second compute stream: one chunk's last wave overlaps the next chunk's first.
+    const bool two = scratch == 0 && chunks > 1;
+    // staging is free once earlier work on the compute stream is done
+    nbl::check_cuda(cudaEventRecord(ctx->events[0], ctx->stream), "cudaEventRecord");
+    nbl::check_cuda(cudaStreamWaitEvent(ctx->up_stream, ctx->events[0], 0), "cudaStreamWaitEvent");
+    for (int c = 0; c < chunks; ++c) {
+      const auto [r0, r1] = bounds(c);
+      const int64_t nr = r1 - r0;
+      nbl::check_cuda(cudaMemcpyAsync(q_in + r0 * q_row, q_in_h + r0 * q_row, nr * q_row * sizeof(float),
+                                      cudaMemcpyHostToDevice, ctx->up_stream), "q upload");
+      nbl::check_cuda(cudaMemcpyAsync(k_in + r0 * kv_row, k_in_h + r0 * kv_row, nr * kv_row * sizeof(float),
+                                      cudaMemcpyHostToDevice, ctx->up_stream), "k upload");
+      nbl::check_cuda(cudaMemcpyAsync(v_in + r0 * kv_row, v_in_h + r0 * kv_row, nr * kv_row * sizeof(float),
+                                      cudaMemcpyHostToDevice, ctx->up_stream), "v upload");
+      nbl::check_cuda(cudaEventRecord(ev_in[c], ctx->up_stream), "cudaEventRecord");
+    }
+    for (int c = 0; c < chunks; ++c) {
+      const auto [r0, r1] = bounds(c);
+      const int64_t nr = r1 - r0;
+      cudaStream_t cs = two && (c & 1) ? ctx->aux_stream : ctx->stream;
+      nbl::check_cuda(cudaStreamWaitEvent(cs, ev_in[c], 0), "cudaStreamWaitEvent");
+      nbl::launch_rope_kv_append(cs, kv, q_in + r0 * q_row, k_in + r0 * kv_row, v_in + r0 * kv_row, NBL_F32,
+                                 bq, bk, bv, q + r0 * q_row, NBL_F32, nullptr, nullptr, page_table, pt_stride, nr,
+                                 n_heads, rope->neox != 0, tab.dev, tab.n_pos, ctx->d_err, static_cast<int32_t>(r0),
+                                 seq_lens);
+      nbl::launch_decode(cs, kv, q + r0 * q_row, page_table + r0 * pt_stride, pt_stride, seq_lens + r0,
+                         static_cast<int>(nr), n_heads, out + r0 * q_row, nullptr, plans[c], ctx->scratch, ctx->d_err);
+      nbl::check_cuda(cudaEventRecord(ev_out[c], cs), "cudaEventRecord");
+      nbl::check_cuda(cudaStreamWaitEvent(ctx->down_stream, ev_out[c], 0), "cudaStreamWaitEvent");
+      nbl::check_cuda(cudaMemcpyAsync(out_h + r0 * q_row, out + r0 * q_row, nr * q_row * sizeof(float),
+                                      cudaMemcpyDeviceToHost, ctx->down_stream), "out download");
+    }
+    nbl::check_cuda(cudaStreamSynchronize(ctx->down_stream), "decode_step_host");
   });
 }
 

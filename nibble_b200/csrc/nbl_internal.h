@@ -49,6 +49,11 @@ struct nbl_ctx {
   int64_t reserved_ctx = 0, reserved_heads = 0;
   std::vector<nbl::RopeTable> rope_tables;
   std::vector<nbl_kv*> kvs;
+  // nbl_decode_step_host: staging for the step's inputs/outputs and the two copy streams with their events
+  void* io = nullptr;
+  size_t io_bytes = 0;
+  cudaStream_t up_stream = nullptr, down_stream = nullptr, aux_stream = nullptr;
+  std::vector<cudaEvent_t> events;
 };
 
 struct nbl_kv {
@@ -80,7 +85,8 @@ void launch_rope_kv_append(cudaStream_t st, const nbl_kv* kv, const void* q_in, 
                            int in_dtype, const float* bq, const float* bk, const float* bv, void* q_out,
                            int q_out_dtype, const int32_t* tok_row, const int32_t* tok_pos,
                            const int32_t* page_table, int32_t pt_stride, int64_t n_tok, int n_heads, bool neox,
-                           const float2* tab, int64_t tab_pos, int* err);
+                           const float2* tab, int64_t tab_pos, int* err,
+                           int32_t row_base = 0, const int32_t* lens = nullptr);
 // attn_f32.cu
 void launch_attention_f32(cudaStream_t st, const float* q, const float* k, const float* v, float* out, int64_t n,
                           int64_t pos0, int64_t n_heads, int64_t n_kv_heads, int64_t head_dim, float scale);

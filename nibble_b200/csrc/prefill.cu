@@ -123,6 +123,35 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// 2^x for two arguments on the FMA and integer pipes instead of the SFU (which issues 16 ex2 per clock per SM,
+// the softmax's bottleneck at head_dim 64). x = j + f with j = round(x) (adding 1.5 * 2^23 rounds to an integer
+// held in the low mantissa bits) and f in [-0.5, 0.5]; 2^f is a degree-3 polynomial whose coefficients are this
+// library's own minimax fit of relative error on that interval (7.5e-5 evaluated in fp32, below the bf16
+// rounding P gets anyway); 2^j is added to the exponent field. Arguments are clamped to >= -125 so the exponent
+// never underflows: masked scores (-inf) give 2^-125 ~ 2e-38 instead of 0, which no sum or bf16 product notices.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float kC0 = 0.9999280571937561f, kC1 = 0.6932609677314758f, kC2 = 0.2426111251115799f,
+                  kC3 = 0.0551716685295105f;
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  x = make_float2(fmaxf(x.x, -125.f), fmaxf(x.y, -125.f));
+  const float2 t = __fadd2_rn(x, make_float2(kRound, kRound));        // round(x) + kRound, exactly
+  const float2 j = __fadd2_rn(t, make_float2(-kRound, -kRound));      // round(x)
+  const float2 f = __ffma2_rn(j, make_float2(-1.f, -1.f), x);         // x - round(x), exactly
+  float2 p = __ffma2_rn(make_float2(kC3, kC3), f, make_float2(kC2, kC2));
+  p = __ffma2_rn(p, f, make_float2(kC1, kC1));
+  p = __ffma2_rn(p, f, make_float2(kC0, kC0));
+  // bits(t) << 23 == round(x) << 23 (mod 2^32): the low 9 bits of bits(t) hold round(x) + 2^22 mod 2^9 = round(x)
+  return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23)),
+                     __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
+}
+
+#ifndef PF_POLY
+#define PF_POLY 0
+#endif
+// Pairs of each 8 consecutive score pairs whose exponentials go to exp2_poly2 (the rest use ex2.approx).
+constexpr int kPolyPer8 = PF_POLY;
+__host__ __device__ constexpr bool poly_pair(int q) { return (q * kPolyPer8) % 8 < kPolyPer8; }
+
 template <bool BF16>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   if constexpr (BF16) {
@@ -334,7 +363,7 @@ __global__ void __launch_bounds__(Cfg<NH, BN>::kThreads, Cfg<NH, BN>::kCtasPerSm
 #pragma unroll
       for (int c = 0; c < kBN; c += 2) {
         const float2 x = __ffma2_rn(make_float2(__uint_as_float(t[c]), __uint_as_float(t[c + 1])), scale2, neg_m2);
-        const float2 e = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+        const float2 e = poly_pair(c >> 1) ? exp2_poly2(x) : make_float2(fast_exp2(x.x), fast_exp2(x.y));
         acc[(c >> 1) & 3] = __fadd2_rn(acc[(c >> 1) & 3], e);
         t[c >> 1] = pack2<BF16>(e.x, e.y);
       }

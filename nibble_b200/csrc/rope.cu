@@ -62,7 +62,9 @@ __device__ __forceinline__ void store_from_float(void* p, int64_t i, float v) {
 }
 
 // One CTA per token. Threads walk the token's q pairs, k pairs and v elements. The token's page slot is
-// resolved once; an out-of-range row/position/page id flags the error word and skips the K/V write.
+// resolved once; an out-of-range row/position/page id flags the error word and skips the K/V write. With
+// tok_row/tok_pos NULL the tokens are one new token per row: token t is row row_base + t at position
+// lens[row] - 1 (a decode step whose lengths already count the new token).
 template <int IN, int QOUT, int KV>
 __global__ void rope_kv_append_kernel(const void* __restrict__ q_in, const void* __restrict__ k_in,
                                       const void* __restrict__ v_in, const float* __restrict__ bq,
@@ -70,11 +72,12 @@ __global__ void rope_kv_append_kernel(const void* __restrict__ q_in, const void*
                                       const int32_t* __restrict__ tok_row, const int32_t* __restrict__ tok_pos,
                                       const int32_t* __restrict__ page_table, int32_t pt_stride, int n_heads,
                                       int n_kv_heads, int head_dim, int page_size, int64_t n_pages, bool neox,
-                                      const float2* __restrict__ tab, int64_t tab_pos, void* pool, int* err) {
+                                      const float2* __restrict__ tab, int64_t tab_pos, void* pool, int* err,
+                                      int32_t row_base, const int32_t* __restrict__ lens) {
   const int64_t r = blockIdx.x;
   const int half = head_dim / 2;
-  const int32_t pos = tok_pos[r];
-  const int32_t row = tok_row[r];
+  const int32_t row = tok_row ? tok_row[r] : row_base + static_cast<int32_t>(r);
+  const int32_t pos = tok_pos ? tok_pos[r] : lens[row] - 1;
   bool pos_ok = pos >= 0 && pos < tab_pos;
   int64_t page = -1;
   if (pos_ok && pos / page_size < pt_stride && row >= 0) {
@@ -226,8 +229,9 @@ __device__ __forceinline__ void store8(void* p, int64_t i, const float (&lo)[4],
 // (grid-stride, kTokGroup tokens at a time whose position, row and page slot are resolved in one round of loads);
 // for each token lane l takes 8-element chunks l, l+32, ... of its q heads, K heads and V heads in that order, so
 // the warp reads and writes consecutive 16-byte pieces of each row. A chunk holds four rotation pairs: elements
-// 8c..8c+7 (interleaved pairs) or 4c..4c+3 with their partners half+4c..half+4c+3 (NeoX). Checks and error flags
-// are those of the scalar kernel; the per-pair arithmetic is identical, so are the results.
+// 8c..8c+7 (interleaved pairs) or 4c..4c+3 with their partners half+4c..half+4c+3 (NeoX). Checks, error flags and
+// the NULL tok_row/tok_pos form are those of the scalar kernel; the per-pair arithmetic is identical, so are the
+// results.
 // Chunks per lane whose loads are issued together. One measured fastest on B200 (config-3 prefill append,
 // 3.7 GB: 0.75 ms with 1, 0.96 ms with 2, 1.5 ms with 4): the registers a second chunk costs lower occupancy more
 // than its extra load in flight gains.
@@ -240,7 +244,8 @@ __global__ void __launch_bounds__(256) rope_kv_append_vec_kernel(
     const float* __restrict__ bq, const float* __restrict__ bk, const float* __restrict__ bv, void* q_out,
     const int32_t* __restrict__ tok_row, const int32_t* __restrict__ tok_pos, const int32_t* __restrict__ page_table,
     int32_t pt_stride, int n_heads, int n_kv_heads, int head_dim, int page_size, int64_t n_pages,
-    const float2* __restrict__ tab, int64_t tab_pos, void* pool, int* err, int64_t n_tok) {
+    const float2* __restrict__ tab, int64_t tab_pos, void* pool, int* err, int64_t n_tok, int32_t row_base,
+    const int32_t* __restrict__ lens) {
   const int lane = threadIdx.x & 31;
   const int half = head_dim / 2;
   const int chunks = head_dim / 8;
@@ -256,8 +261,8 @@ __global__ void __launch_bounds__(256) rope_kv_append_vec_kernel(
     int64_t my_page = -1;
     if (lane < kTokGroup && t0 + lane < n_tok) {
       const int64_t t = t0 + lane;
-      my_pos = tok_pos[t];
-      const int32_t row = tok_row[t];
+      const int32_t row = tok_row ? tok_row[t] : row_base + static_cast<int32_t>(t);
+      my_pos = tok_pos ? tok_pos[t] : lens[row] - 1;
       if (my_pos >= 0 && my_pos < tab_pos) {
         if (my_pos / page_size < pt_stride && row >= 0) {
           my_page = page_table[int64_t(row) * pt_stride + my_pos / page_size];
@@ -373,11 +378,26 @@ int grid_for(int64_t total, int threads) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Resident CTAs of the vector kernel over the whole GPU, queried once per instance (one GPU type per process).
+template <int IN, int QOUT, int KV, bool NEOX>
+int64_t vec_resident() {
+  static const int64_t r = [] {
+    int dev = 0, sms = 148, per_sm = 1;
+    check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+    check_cuda(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "SM count");
+    check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rope_kv_append_vec_kernel<IN, QOUT, KV, NEOX>,
+                                                             256, 0),
+               "occupancy");
+    return int64_t(sms) * std::max(per_sm, 1);
+  }();
+  return r;
+}
+
 template <int IN, int QOUT, int KV>
 void launch_kv(cudaStream_t st, const nbl_kv* kv, const void* q_in, const void* k_in, const void* v_in,
                const float* bq, const float* bk, const float* bv, void* q_out, const int32_t* tok_row,
                const int32_t* tok_pos, const int32_t* page_table, int32_t pt_stride, int64_t n_tok, int n_heads,
-               bool neox, const float2* tab, int64_t tab_pos, int* err) {
+               bool neox, const float2* tab, int64_t tab_pos, int* err, int32_t row_base, const int32_t* lens) {
   const auto& c = kv->cfg;
   // vector path: whole 8-element chunks, 16-byte aligned rows and bias (every row offset is a multiple of
   // head_dim elements, so aligned bases keep every chunk aligned)
@@ -385,52 +405,50 @@ void launch_kv(cudaStream_t st, const nbl_kv* kv, const void* q_in, const void* 
                    aligned16(q_out) && aligned16(kv->pool) && (!bq || aligned16(bq)) && (!bk || aligned16(bk)) &&
                    (!bv || aligned16(bv));
   if (vec) {
-    int dev = 0, sms = 148;
-    check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
-    check_cuda(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "SM count");
     auto k = neox ? rope_kv_append_vec_kernel<IN, QOUT, KV, true> : rope_kv_append_vec_kernel<IN, QOUT, KV, false>;
-    int per_sm = 1;
-    check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, 256, 0), "occupancy");
-    // 8 warps (tokens at a time) per CTA; one wave of resident CTAs walks all tokens
-    const int64_t want = (n_tok + 7) / 8, cap = int64_t(sms) * std::max(per_sm, 1);
+    // 8 warps per CTA; one wave of resident CTAs walks all tokens
+    const int64_t want = (n_tok + 7) / 8;
+    const int64_t cap = neox ? vec_resident<IN, QOUT, KV, true>() : vec_resident<IN, QOUT, KV, false>();
     const int grid = static_cast<int>(std::max<int64_t>(1, std::min(want, cap)));
     k<<<grid, 256, 0, st>>>(q_in, k_in, v_in, bq, bk, bv, q_out, tok_row, tok_pos, page_table, pt_stride, n_heads,
-                            c.n_kv_heads, c.head_dim, c.page_size, c.n_pages, tab, tab_pos, kv->pool, err, n_tok);
+                            c.n_kv_heads, c.head_dim, c.page_size, c.n_pages, tab, tab_pos, kv->pool, err, n_tok,
+                            row_base, lens);
     return;
   }
   rope_kv_append_kernel<IN, QOUT, KV><<<dim3(static_cast<unsigned>(n_tok)), dim3(128), 0, st>>>(
       q_in, k_in, v_in, bq, bk, bv, q_out, tok_row, tok_pos, page_table, pt_stride, n_heads, c.n_kv_heads,
-      c.head_dim, c.page_size, c.n_pages, neox, tab, tab_pos, kv->pool, err);
+      c.head_dim, c.page_size, c.n_pages, neox, tab, tab_pos, kv->pool, err, row_base, lens);
 }
 
 template <int IN, int QOUT>
 void dispatch_kv(cudaStream_t st, const nbl_kv* kv, const void* q_in, const void* k_in, const void* v_in,
                  const float* bq, const float* bk, const float* bv, void* q_out, const int32_t* tok_row,
                  const int32_t* tok_pos, const int32_t* page_table, int32_t pt_stride, int64_t n_tok, int n_heads,
-                 bool neox, const float2* tab, int64_t tab_pos, int* err) {
+                 bool neox, const float2* tab, int64_t tab_pos, int* err, int32_t row_base, const int32_t* lens) {
   if (kv->cfg.dtype == NBL_F16)
     launch_kv<IN, QOUT, NBL_F16>(st, kv, q_in, k_in, v_in, bq, bk, bv, q_out, tok_row, tok_pos, page_table,
-                                 pt_stride, n_tok, n_heads, neox, tab, tab_pos, err);
+                                 pt_stride, n_tok, n_heads, neox, tab, tab_pos, err, row_base, lens);
   else
     launch_kv<IN, QOUT, NBL_BF16>(st, kv, q_in, k_in, v_in, bq, bk, bv, q_out, tok_row, tok_pos, page_table,
-                                  pt_stride, n_tok, n_heads, neox, tab, tab_pos, err);
+                                  pt_stride, n_tok, n_heads, neox, tab, tab_pos, err, row_base, lens);
 }
 
 template <int IN>
 void dispatch_qout(int q_out_dtype, cudaStream_t st, const nbl_kv* kv, const void* q_in, const void* k_in,
                    const void* v_in, const float* bq, const float* bk, const float* bv, void* q_out,
                    const int32_t* tok_row, const int32_t* tok_pos, const int32_t* page_table, int32_t pt_stride,
-                   int64_t n_tok, int n_heads, bool neox, const float2* tab, int64_t tab_pos, int* err) {
+                   int64_t n_tok, int n_heads, bool neox, const float2* tab, int64_t tab_pos, int* err,
+                   int32_t row_base, const int32_t* lens) {
   switch (q_out_dtype) {
     case NBL_F32:
       return dispatch_kv<IN, NBL_F32>(st, kv, q_in, k_in, v_in, bq, bk, bv, q_out, tok_row, tok_pos, page_table,
-                                      pt_stride, n_tok, n_heads, neox, tab, tab_pos, err);
+                                      pt_stride, n_tok, n_heads, neox, tab, tab_pos, err, row_base, lens);
     case NBL_F16:
       return dispatch_kv<IN, NBL_F16>(st, kv, q_in, k_in, v_in, bq, bk, bv, q_out, tok_row, tok_pos, page_table,
-                                      pt_stride, n_tok, n_heads, neox, tab, tab_pos, err);
+                                      pt_stride, n_tok, n_heads, neox, tab, tab_pos, err, row_base, lens);
     default:
       return dispatch_kv<IN, NBL_BF16>(st, kv, q_in, k_in, v_in, bq, bk, bv, q_out, tok_row, tok_pos, page_table,
-                                       pt_stride, n_tok, n_heads, neox, tab, tab_pos, err);
+                                       pt_stride, n_tok, n_heads, neox, tab, tab_pos, err, row_base, lens);
   }
 }
 
@@ -454,19 +472,19 @@ void launch_rope_kv_append(cudaStream_t st, const nbl_kv* kv, const void* q_in, 
                            int in_dtype, const float* bq, const float* bk, const float* bv, void* q_out,
                            int q_out_dtype, const int32_t* tok_row, const int32_t* tok_pos,
                            const int32_t* page_table, int32_t pt_stride, int64_t n_tok, int n_heads, bool neox,
-                           const float2* tab, int64_t tab_pos, int* err) {
+                           const float2* tab, int64_t tab_pos, int* err, int32_t row_base, const int32_t* lens) {
   switch (in_dtype) {
     case NBL_F32:
       dispatch_qout<NBL_F32>(q_out_dtype, st, kv, q_in, k_in, v_in, bq, bk, bv, q_out, tok_row, tok_pos, page_table,
-                             pt_stride, n_tok, n_heads, neox, tab, tab_pos, err);
+                             pt_stride, n_tok, n_heads, neox, tab, tab_pos, err, row_base, lens);
       break;
     case NBL_F16:
       dispatch_qout<NBL_F16>(q_out_dtype, st, kv, q_in, k_in, v_in, bq, bk, bv, q_out, tok_row, tok_pos, page_table,
-                             pt_stride, n_tok, n_heads, neox, tab, tab_pos, err);
+                             pt_stride, n_tok, n_heads, neox, tab, tab_pos, err, row_base, lens);
       break;
     default:
       dispatch_qout<NBL_BF16>(q_out_dtype, st, kv, q_in, k_in, v_in, bq, bk, bv, q_out, tok_row, tok_pos,
-                              page_table, pt_stride, n_tok, n_heads, neox, tab, tab_pos, err);
+                              page_table, pt_stride, n_tok, n_heads, neox, tab, tab_pos, err, row_base, lens);
   }
   check_cuda(cudaGetLastError(), "rope_kv_append launch");
 }

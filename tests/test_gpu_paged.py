@@ -179,6 +179,47 @@ def test_decode_matches_oracle(nbl_ctx, H, KV, n_splits):
         np.testing.assert_allclose(got_lse[r], ref_lse(q[r], k, v, H, KV), rtol=0, atol=2e-5)
 
 
+@pytest.mark.parametrize("n_chunks,bias", [(3, False), (0, True), (1, False)])
+def test_decode_step_host_matches_separate_calls(nbl_ctx, n_chunks, bias):
+    """nbl_decode_step_host (host q/k/v in, host out; uploads, append + decode and downloads overlapped over row
+    chunks) equals nbl_write + nbl_rope_kv_append + nbl_attn_decode + nbl_read on the same data, and the oracle."""
+    import torch
+    import nibble_b200 as nb
+    H, KV = 32, 8
+    rng = np.random.default_rng(n_chunks * 3 + int(bias))
+    lens = [int(x) for x in rng.integers(1, 3000, size=37)] + [1, 4097]  # counting the new token
+    rows = len(lens)
+    table, n_pages = make_page_tables(lens, 16, shuffle_seed=21)
+    kv = nbl_ctx.kv_pool(n_pages, KV)
+    fill_random(kv, seed=22)
+    q_in = torch.from_numpy(rng.standard_normal((rows, H, D)).astype(np.float32)).pin_memory()
+    k_in = torch.from_numpy(rng.standard_normal((rows, KV, D)).astype(np.float32)).pin_memory()
+    v_in = torch.from_numpy(rng.standard_normal((rows, KV, D)).astype(np.float32)).pin_memory()
+    bq, bk, bv = ((dev(rng.standard_normal(w * D).astype(np.float32)) if bias else None) for w in (H, KV, KV))
+    out_h = torch.full((rows, H, D), float("nan")).pin_memory()
+    t_table, t_lens = dev(table), dev(np.array(lens, np.int32))
+    spec = nb.RopeSpec(5e5, False)
+    nbl_ctx.decode_step_host(kv, q_in, k_in, v_in, t_table, t_lens, max(lens), spec, out_h, bq=bq, bk=bk, bv=bv,
+                             n_chunks=n_chunks)
+    nbl_ctx.check()
+    got = out_h.numpy().copy()
+    # the same step as separate calls (the append rewrites the same bits at the same slots)
+    q = torch.empty((rows, H, D), device="cuda")
+    out = torch.empty((rows, H, D), device="cuda")
+    nbl_ctx.rope_kv_append(kv, q_in.cuda(), k_in.cuda(), v_in.cuda(), q, dev(np.arange(rows, dtype=np.int32)),
+                           dev(np.array(lens, np.int32) - 1), t_table, H, spec, bq=bq, bk=bk, bv=bv)
+    nbl_ctx.attn_decode(kv, q, t_table, t_lens, max(lens), out)
+    nbl_ctx.check()
+    ref_sep = host(out)
+    np.testing.assert_allclose(got, ref_sep, rtol=1e-5, atol=1e-6)
+    pool = pool_bits(kv)
+    qr = host(q)
+    for r in (0, rows - 2, rows - 1):
+        k, v = oracle.gather_pages(pool, table[r], lens[r], KV, D, 16)
+        ref = oracle.attention(qr[r][None], k, v, 1, lens[r] - 1, H, KV, D)[0]
+        assert max_rel_err_per_head(got[r], ref) <= 1e-4
+
+
 def test_decode_empty_row_and_long_context(nbl_ctx):
     """A zero-length row yields out = 0, lse = -inf; a 131073-token row (config 4's length) takes the split-K
     path with the automatic split count and still matches."""
