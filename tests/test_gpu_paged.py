@@ -344,6 +344,8 @@ def _prefill_case(nbl_ctx, H, KV, pool_dtype, items, base, neox, seed):
     pool = pool_bits(kv)
     results = []
     for i, (ql, p0) in enumerate(items):
+        if ql == 0:
+            continue
         L = ql + p0
         s = starts[i]
         # reference path: bf16 inputs widened, RoPE in fp32, attention in fp32 (nibble's order)
@@ -367,6 +369,22 @@ def test_prefill_matches_oracle(nbl_ctx, H, KV, dt):
         assert np.abs(got - ref).max() <= 2e-2
         assert min_cosine_per_head(got, ref) >= 0.9999
         assert np.abs(got - ref_g).max() <= 1e-2  # only P's rounding to 16 bits separates these
+
+
+def test_prefill_many_works_per_cta(nbl_ctx):
+    """More works than the persistent grid holds (each CTA walks several, through both Q buffers and across the
+    K/V ring), with an odd group (Qwen's 14 / 2: the last head pair of a KV group has one head), empty items and
+    items that continue a cached prefix."""
+    import nibble_b200 as nb
+    rng = np.random.default_rng(5)
+    items = [(0, 0), (0, 40)] + [(int(q), int(p)) for q, p in zip(rng.integers(1, 300, 38), rng.integers(0, 200, 38))]
+    cases = _prefill_case(nbl_ctx, 14, 2, nb.BF16, items, 1e6, True, seed=31)
+    assert len(cases) == 38
+    for got, ref, ref_g in cases:
+        assert np.isfinite(got).all()
+        assert np.abs(got - ref).max() <= 2e-2
+        assert min_cosine_per_head(got, ref) >= 0.9999
+        assert np.abs(got - ref_g).max() <= 1e-2
 
 
 def test_prefill_tinyllama_full_tile_rows(nbl_ctx):
