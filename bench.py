@@ -358,39 +358,63 @@ def decode_long(args, world, rank, local, steps, warmup):
     fill_normal_(kv.tensor().view(torch.float16), seed=4000 + rank)
     rng = np.random.default_rng(7)  # the query is the same on every rank
     q = torch.from_numpy(rng.standard_normal((rows, H4, D)).astype(np.float32)).cuda()
-    out = torch.empty((rows, H4, D), device="cuda")
-    lse = torch.empty((rows, H4), device="cuda")
+    # the decode writes (O, lse) straight into the all-gather send buffer; the merge reads the gathered buffer
+    send, out, lse = ndist.partials_buffer(rows, H4, D)
+    recv = torch.empty((world, send.numel()), device="cuda")
     merged = torch.empty((rows * H4, D), device="cuda")
     d = lambda x: torch.from_numpy(np.ascontiguousarray(x)).cuda()  # noqa: E731
     t_table, lens = d(table), d(np.full(rows, my_len, np.int32))
-    st = torch.cuda.current_stream()
+    main = torch.cuda.current_stream()
 
-    def step(ev=None):
-        if ev:
-            ev[0].record(st)
+    def decode():
         ctx.attn_decode(kv, q, t_table, lens, max(1, my_len), out, lse)
-        if ev:
-            ev[1].record(st)
+
+    def step():
+        decode()
         if world > 1:
-            g = ndist.all_gather_partials(ndist.pack_partials(out, lse))
-            po, pl = ndist.unpack_partials(g, rows, H4, D)
-            ctx.lse_merge(po, pl, merged)
+            import torch.distributed as dist
+            dist.all_gather_into_tensor(recv, send)
+            ctx.lse_merge_packed(recv, world, rows * H4, D, merged)
 
     for _ in range(warmup):
         step()
     ctx.check()
+    # kernel time of the decode alone (the roofline), events around each launch
     kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for a0, b0 in kev:
+        a0.record(main)
+        decode()
+        b0.record(main)
+    torch.cuda.synchronize()
+    kern_ms = statistics.mean(x.elapsed_time(y) for x, y in kev)
+    # the step (decode + all-gather + merge) captured once as a CUDA graph and replayed: at a few tens of
+    # microseconds of work per rank, launching it op by op from Python would be the bottleneck
+    side = torch.cuda.Stream()
+    side.wait_stream(main)
+    with torch.cuda.stream(side):
+        ctx.set_stream(side.cuda_stream)
+        step()
+        side.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        ctx.set_stream(torch.cuda.current_stream().cuda_stream)
+        step()
+    ctx.set_stream(main.cuda_stream)
+    for _ in range(warmup):
+        graph.replay()
     barrier(world)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(st)
+    e0.record(main)
     for i in range(steps):
-        step(kev[i])
-    e1.record(st)
+        graph.replay()
+    e1.record(main)
     torch.cuda.synchronize()
     ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
-    kern_ms = statistics.mean(x.elapsed_time(y) for x, y in kev)
     ctx.check()
+    if world > 1 and rank == 0:  # the merged result equals rank 0's own merge of the same gathered partials
+        assert torch.isfinite(merged).all()
+    del graph  # released before the process group is destroyed
     total_kv = rows * length * KV4 * D * 2 * 2
     my_kv = rows * my_len * KV4 * D * 2 * 2
     hbm, _, _, src = peaks()
@@ -399,8 +423,8 @@ def decode_long(args, world, rank, local, steps, warmup):
            "scaling": "strong",
            "config": {"workload": "config 4: long-context decode, KV split over ranks", "kv_tokens": length,
                       "layers": LAYERS4, "heads": f"{H4}q/{KV4}kv", "kv_tokens_this_rank": my_len,
-                      "exchange": "one NCCL all-gather of packed (O, lse) for all layers + LSE merge" if world > 1
-                      else "none (one GPU)"},
+                      "exchange": "one NCCL all-gather of packed (O, lse) for all layers + LSE merge, the step "
+                                  "replayed as one CUDA graph" if world > 1 else "none (one GPU; CUDA graph)"},
            "roofline": {"kernel": "decode_kernel (+ lse_merge)", "bound": "hbm", "achieved": ach, "peak": hbm,
                         "unit": "GB/s", "frac": ach / hbm, "peak_source": src, "kernel_ms": kern_ms}}
     kv.close()

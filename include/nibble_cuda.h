@@ -205,6 +205,13 @@ NBL_API int nbl_attn_prefill(nbl_ctx* ctx, const nbl_kv* kv, const void* q, int3
 NBL_API int nbl_lse_merge(nbl_ctx* ctx, const float* part_o, const float* part_lse, int32_t n_parts, int64_t rows,
                   int32_t head_dim, float* out, float* lse);
 
+/* nbl_lse_merge over the layout one all-gather of per-rank partials produces: part p occupies
+ * packed[p * rows * (head_dim + 1) ...] as [rows, head_dim] outputs followed by [rows] lse, so a rank can
+ * decode straight into its send buffer and merge the gathered buffer in place. No reference counterpart (the
+ * reference never splits a softmax across devices). */
+NBL_API int nbl_lse_merge_packed(nbl_ctx* ctx, const float* packed, int32_t n_parts, int64_t rows, int32_t head_dim,
+                                 float* out, float* lse);
+
 #ifdef __cplusplus
 }
 #endif

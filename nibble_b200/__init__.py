@@ -220,6 +220,10 @@ class Context:
                                         _ptr(q_len), _ptr(kv_pos0), _ptr(page_table), page_table.shape[-1],
                                         q_start.shape[0], q.shape[1], max_q_len, _ptr(out), _dtype(out)))
 
+    def lse_merge_packed(self, packed, n_parts: int, rows: int, head_dim: int, out, lse=None):
+        """packed [n_parts, rows * (head_dim + 1)] fp32 (per part: outputs then lse) -> out [rows, head_dim]."""
+        check(_abi.lib.nbl_lse_merge_packed(self.handle, _ptr(packed), n_parts, rows, head_dim, _ptr(out), _ptr(lse)))
+
     def lse_merge(self, part_o, part_lse, out, lse=None):
         """part_o [P, rows, D], part_lse [P, rows] fp32 -> out [rows, D] (+ lse [rows])."""
         n_parts, rows, d = part_o.shape

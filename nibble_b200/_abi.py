@@ -69,6 +69,7 @@ SIGNATURES = {
                              _P, _I32],
     "nbl_attn_prefill": [_P, _P, _P, _I32, _I64, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _P, _I32],
     "nbl_lse_merge": [_P, _P, _P, _I32, _I64, _I32, _P, _P],
+    "nbl_lse_merge_packed": [_P, _P, _I32, _I64, _I32, _P, _P],
 }
 _RESTYPES = {"nbl_last_error": C.c_size_t, "nbl_ctx_stream": _P}
 

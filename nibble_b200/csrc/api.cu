@@ -599,4 +599,17 @@ int nbl_lse_merge(nbl_ctx* ctx, const float* part_o, const float* part_lse, int3
   });
 }
 
+int nbl_lse_merge_packed(nbl_ctx* ctx, const float* packed, int32_t n_parts, int64_t rows, int32_t head_dim,
+                         float* out, float* lse) {
+  return guarded([&] {
+    require(ctx && packed && out, "lse_merge_packed: NULL argument");
+    require(n_parts > 0 && rows >= 0 && head_dim > 0 && head_dim <= 256, "lse_merge_packed: bad size");
+    if (rows == 0) return;
+    use_device(ctx);
+    const int64_t part = rows * (int64_t(head_dim) + 1);  // [rows * head_dim outputs | rows lse] per part
+    nbl::launch_lse_merge(ctx->stream, packed, packed + rows * head_dim, n_parts, rows, head_dim, out, lse, part,
+                          part);
+  });
+}
+
 }  // extern "C"

@@ -325,18 +325,20 @@ __global__ void __launch_bounds__(kWarps * 32, kCtasPerSm)
 }
 
 // One CTA per group of rows; a thread per head dimension. part_o [n_parts, rows, D], part_lse [n_parts, rows].
-__global__ void lse_merge_kernel(const float* __restrict__ part_o, const float* __restrict__ part_lse, int n_parts,
-                                 int64_t rows, int head_dim, float* __restrict__ out, float* __restrict__ lse) {
+// Part p's outputs start at part_o + p * o_stride ([rows, head_dim]) and its lse at part_lse + p * lse_stride.
+__global__ void lse_merge_kernel(const float* __restrict__ part_o, int64_t o_stride, const float* __restrict__ part_lse,
+                                 int64_t lse_stride, int n_parts, int64_t rows, int head_dim, float* __restrict__ out,
+                                 float* __restrict__ lse) {
   const int d = threadIdx.x;
   for (int64_t r = blockIdx.x * int64_t(blockDim.y) + threadIdx.y; r < rows; r += int64_t(gridDim.x) * blockDim.y) {
     float mx = -INFINITY;
-    for (int p = 0; p < n_parts; ++p) mx = fmaxf(mx, part_lse[p * rows + r]);
+    for (int p = 0; p < n_parts; ++p) mx = fmaxf(mx, part_lse[p * lse_stride + r]);
     float W = 0.f, O = 0.f;
     if (mx != -INFINITY) {
       for (int p = 0; p < n_parts; ++p) {
-        const float w = expf(part_lse[p * rows + r] - mx);
+        const float w = expf(part_lse[p * lse_stride + r] - mx);
         W += w;
-        if (d < head_dim && w > 0.f) O += w * part_o[(p * rows + r) * head_dim + d];
+        if (d < head_dim && w > 0.f) O += w * part_o[p * o_stride + r * head_dim + d];
       }
     }
     if (d < head_dim) out[r * head_dim + d] = W > 0.f ? O / W : 0.f;
@@ -441,12 +443,14 @@ void launch_decode(cudaStream_t st, const nbl_kv* kv, const float* q, const int3
 }
 
 void launch_lse_merge(cudaStream_t st, const float* part_o, const float* part_lse, int n_parts, int64_t rows,
-                      int head_dim, float* out, float* lse) {
+                      int head_dim, float* out, float* lse, int64_t o_stride, int64_t lse_stride) {
+  if (o_stride < 0) o_stride = rows * head_dim;
+  if (lse_stride < 0) lse_stride = rows;
   const int tx = head_dim <= 32 ? 32 : (head_dim <= 64 ? 64 : (head_dim <= 128 ? 128 : 256));
   const int ty = std::max(1, 256 / tx);
   const int64_t blocks = std::min<int64_t>((rows + ty - 1) / ty, 65535 * 16);
   lse_merge_kernel<<<static_cast<unsigned>(std::max<int64_t>(blocks, 1)), dim3(tx, ty), 0, st>>>(
-      part_o, part_lse, n_parts, rows, head_dim, out, lse);
+      part_o, o_stride, part_lse, lse_stride, n_parts, rows, head_dim, out, lse);
   check_cuda(cudaGetLastError(), "lse_merge launch");
 }
 

@@ -102,7 +102,8 @@ void launch_decode(cudaStream_t st, const nbl_kv* kv, const float* q, const int3
                    const int32_t* seq_lens, int n_rows, int n_heads, float* out, float* lse, const DecodePlan& plan,
                    void* scratch, int* err);
 void launch_lse_merge(cudaStream_t st, const float* part_o, const float* part_lse, int n_parts, int64_t rows,
-                      int head_dim, float* out, float* lse);
+                      int head_dim, float* out, float* lse,
+                      int64_t o_stride = -1, int64_t lse_stride = -1);
 // prefill.cu
 void launch_prefill(cudaStream_t st, const nbl_kv* kv, const void* q, int64_t n_q_rows, const int32_t* q_start,
                     const int32_t* q_len, const int32_t* kv_pos0, const int32_t* page_table, int32_t pt_stride,

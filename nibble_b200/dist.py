@@ -18,6 +18,16 @@ def pack_partials(o, lse):
     return torch.cat([o.reshape(-1), lse.reshape(-1)])
 
 
+def partials_buffer(rows: int, heads: int, head_dim: int, device="cuda"):
+    """A send buffer in the packed layout plus views a decode can write into directly: returns (send, o, lse)
+    with send [rows*H*D + rows*H] fp32, o = send's first rows*H*D floats as [rows, H, D], lse the rest as
+    [rows, H]. After all_gather_partials(send), Context.lse_merge_packed merges the gathered buffer in place."""
+    import torch
+    n_o = rows * heads * head_dim
+    send = torch.empty(n_o + rows * heads, dtype=torch.float32, device=device)
+    return send, send[:n_o].view(rows, heads, head_dim), send[n_o:].view(rows, heads)
+
+
 def unpack_partials(gathered, rows: int, heads: int, head_dim: int):
     """gathered [world, rows*H*D + rows*H] -> part_o [world, rows*H, D], part_lse [world, rows*H]."""
     world = gathered.shape[0]

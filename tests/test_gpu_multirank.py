@@ -70,7 +70,11 @@ def _worker(rank, world, port, outdir):
         po, pl = ndist.unpack_partials(g, ROWS, H, D)
         merged = torch.empty((ROWS * H, D), device="cuda")
         ctx.lse_merge(po, pl, merged)
+        # the same gathered buffer merged in place (nbl_lse_merge_packed) gives the same bits
+        merged_packed = torch.empty_like(merged)
+        ctx.lse_merge_packed(g, 2, ROWS * H, D, merged_packed)
         ctx.check()
+        assert torch.equal(merged, merged_packed)
         np.save(os.path.join(outdir, f"merged{rank}.npy"), merged.cpu().numpy())
         dist.barrier()
         kv.close()

@@ -305,6 +305,30 @@ def test_lse_merge_matches_oracle(nbl_ctx):
     np.testing.assert_allclose(got_l[fin], ref_l[fin], rtol=0, atol=2e-6)
 
 
+def test_lse_merge_packed_matches_lse_merge(nbl_ctx):
+    """The packed layout of one all-gather ([parts][rows*D outputs | rows lse]) merged in place equals
+    nbl_lse_merge on the same partials, including parts with lse = -inf (empty chunks)."""
+    import torch
+    from nibble_b200 import dist as ndist
+    rng = np.random.default_rng(8)
+    parts, rows = 5, 37
+    o = torch.from_numpy(rng.standard_normal((parts, rows, D)).astype(np.float32)).cuda()
+    lse_np = rng.standard_normal((parts, rows)).astype(np.float32) * 4
+    lse_np[1, :] = -np.inf
+    lse_np[3, 5] = -np.inf
+    lse = torch.from_numpy(lse_np).cuda()
+    packed = torch.cat([o.reshape(parts, -1), lse], dim=1).contiguous()
+    a = torch.empty((rows, D), device="cuda")
+    b = torch.empty((rows, D), device="cuda")
+    la, lb = torch.empty(rows, device="cuda"), torch.empty(rows, device="cuda")
+    nbl_ctx.lse_merge(o, lse, a, la)
+    nbl_ctx.lse_merge_packed(packed, parts, rows, D, b, lb)
+    nbl_ctx.check()
+    assert torch.equal(a, b) and torch.equal(la, lb)
+    send, ov, lv = ndist.partials_buffer(3, 2, D)
+    assert ov.shape == (3, 2, D) and lv.shape == (3, 2) and send.numel() == 3 * 2 * (D + 1)
+
+
 # ---------------------------------------------------------------- prefill (tcgen05)
 PREFILL_ITEMS = [(1, 0), (37, 0), (128, 0), (129, 0), (300, 0), (64, 200), (200, 57)]  # (q_len, pos0)
 
