@@ -40,7 +40,9 @@ def _digest(extra: list[str]) -> str:
             h.update(name.encode() + b"\0" + f.read())
     with open(os.path.join(ROOT, "include", "nibble_cuda.h"), "rb") as f:
         h.update(f.read())
-    h.update(" ".join(ARCH + FLAGS + extra).encode())
+    # the flags name the repository's absolute path (-I): leave it out, so a tree copied elsewhere (the GPU box's
+    # snapshot) keeps the stamp of the library it ships with
+    h.update(" ".join(ARCH + FLAGS + extra).replace(ROOT, "<root>").encode())
     return h.hexdigest()
 
 

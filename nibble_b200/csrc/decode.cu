@@ -147,7 +147,7 @@ __global__ void __launch_bounds__(kWarps * 32, kCtasPerSm)
 
   for (int i = 0; i < my_n; ++i) {
     const int stage = i % kStages;
-    const bool ok = __all_sync(0xffffffffu, mbar_wait(&bars[stage], (i / kStages) & 1, a.err));
+    const bool ok = warp_wait_all(&bars[stage], (i / kStages) & 1, a.err);
     if (!ok) break;
     done = i + 1;
     const int pg0 = p_begin + (warp + kWarps * i) * kChunkPages;

@@ -62,8 +62,11 @@ constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s: legitimate waits here 
 // Waits for the phase with the given parity to complete. Gives up after kWaitLimitNs of wall-clock time, or at
 // once when another wait of this context has already timed out (kErrTimeout is sticky until nbl_ctx_check),
 // so one lost completion ends the whole launch in seconds. Returns false on giving up.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
-  if (mbar_try_wait(bar, parity)) return true;
+//
+// The polling loop with its timer sits in a separate non-inlined function: inlined, its reconvergence code made
+// every wait cost ~108 cycles even when the phase had already completed (measured on B200), against ~16 for
+// the bare try_wait and ~48 for this split form.
+static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, int* err) {
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -75,6 +78,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
       }
     }
   }
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+  bool ok = mbar_try_wait(bar, parity);
+  if (!ok) ok = mbar_wait_slow(bar, parity, err);
+  return ok;
+}
+static __device__ __noinline__ bool warp_wait_slow(uint64_t* bar, uint32_t parity, int* err) {
+  return __all_sync(0xffffffffu, mbar_wait_slow(bar, parity, err));
+}
+// The same wait executed by every lane of a warp; true only if all lanes saw the phase complete.
+__device__ __forceinline__ bool warp_wait_all(uint64_t* bar, uint32_t parity, int* err) {
+  if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
+  return warp_wait_slow(bar, parity, err);
 }
 
 // ---------------------------------------------------------------- TMA (plain per-CTA tile loads only)

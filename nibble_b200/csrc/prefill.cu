@@ -11,9 +11,9 @@
 // their K/V in L2. Warps, specialised:
 //   warps 0..7   softmax, one warpgroup per head: thread i of a warpgroup owns query row i = TMEM lane i (a warp
 //                reaches the lane quarter warp % 4). Per K/V tile it loads its S row (64 fp32) from TMEM in one
-//                instruction, masks causally, takes the row max with a tree, and keeps a reference max m_ref (log2
-//                domain) that only moves when the tile max exceeds it by more than 2^8, so the O accumulator in
-//                TMEM is rescaled rarely; p = 2^(s*scale - m_ref) via ex2.approx (one pair in eight on the FMA
+//                instruction, masks causally, takes the row max with 3-input max instructions, and keeps a
+//                reference max m_ref (log2 domain) that only moves when the tile max exceeds it by more than 2^8, so
+//                the O accumulator in TMEM is rescaled rarely; p = 2^(s*scale - m_ref) via ex2.approx (one pair in eight on the FMA
 //                pipe) with packed fp32x2 arguments, the row sum with packed adds; P is packed to bf16/fp16 pairs
 //                and stored into the first 32 columns of its S region as the A operand of the PV MMA. After a
 //                work's last tile it reads O out of TMEM (releasing it to the next work), normalises and stores.
@@ -214,6 +214,14 @@ __device__ __forceinline__ float2 exp2_poly2(float2 x) {
 // polynomial's extra instructions lengthen it).
 __host__ __device__ constexpr bool poly_pair(int q) { return q % 8 == 0; }
 
+// max(a, b, c) in one instruction (sm_100's three-input max: the row max over 64 scores takes 34 instructions
+// instead of 63).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 template <bool BF16>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   if constexpr (BF16) {
@@ -227,7 +235,7 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
 
 // Bounded wait executed by every lane of a warp; true only if all lanes saw the phase complete.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* err) {
-  return __all_sync(0xffffffffu, mbar_wait(bar, parity, err));
+  return warp_wait_all(bar, parity, err);
 }
 
 template <bool BF16, int NH, int BN>
@@ -432,15 +440,17 @@ __global__ void __launch_bounds__(Cfg<NH, BN>::kThreads, Cfg<NH, BN>::kCtasPerSm
           for (int c = 0; c < kBN; ++c)
             if (kbase + c > qpos) t[c] = __float_as_uint(-INFINITY);
         }
-        float mx[8];
+        // four chains of 3-input maxima over 16 columns each (c = i, i+4, ..., i+60)
+        float mx[4];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) mx[i] = __uint_as_float(t[i]);
+        for (int i = 0; i < 4; ++i) {
+          mx[i] = fmax3(__uint_as_float(t[i]), __uint_as_float(t[i + 4]), __uint_as_float(t[i + 8]));
 #pragma unroll
-        for (int c = 8; c < kBN; c += 8)
-#pragma unroll
-          for (int i = 0; i < 8; ++i) mx[i] = fmaxf(mx[i], __uint_as_float(t[c + i]));
-        const float m_tile = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                                   fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * scale;
+          for (int c = 12; c < 60; c += 8)
+            mx[i] = fmax3(mx[i], __uint_as_float(t[c + i]), __uint_as_float(t[c + 4 + i]));
+          mx[i] = fmaxf(mx[i], __uint_as_float(t[60 + i]));
+        }
+        const float m_tile = fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]) * scale;
         const bool need = m_tile > m_ref + kRescaleThreshold;  // false for m_tile = -inf
         const float m_new = need ? m_tile : m_ref;
         const float m_use = m_new == -INFINITY ? 0.f : m_new;
