@@ -48,6 +48,7 @@ typedef enum { NBL_F32 = 0, NBL_F16 = 1, NBL_BF16 = 2 } nbl_dtype;
 
 typedef struct nbl_ctx nbl_ctx; /* device, stream, scratch, RoPE tables, allocation registry */
 typedef struct nbl_kv nbl_kv;   /* one paged K/V pool */
+typedef struct nbl_weight nbl_weight; /* one weight tensor uploaded to the device */
 
 /* Rotary-embedding options; same fields and meaning as nibble::RopeParams (src/backend/backend.h:16-20).
  * freq_factors is HOST memory (head_dim/2 floats) or NULL. */
@@ -94,8 +95,9 @@ NBL_API int nbl_ctx_check(nbl_ctx* ctx);
 
 /* ---- Backend memory ops ---- */
 /* Backend::reserve (backend.h:42-45; CpuBackend::reserve cpu_backend.cpp:24-67): sizes the split-K scratch and
- * the RoPE tables for up to n_ctx positions and n_heads heads, so later attention calls within those limits
- * allocate nothing. max_rows/max_width are accepted for interface parity. */
+ * the RoPE tables for up to n_ctx positions and n_heads heads, the token-id staging for max_rows tokens, and
+ * (max_rows > 8) the SGEMM handle and its workspace, so later calls within those limits allocate nothing.
+ * max_width is accepted for interface parity. */
 NBL_API int nbl_reserve(nbl_ctx* ctx, int64_t n_ctx, int64_t n_heads, int64_t max_rows, int64_t max_width);
 /* Backend::alloc (backend.h:46-47): zeroed device block of n_floats floats (256-byte aligned). n_floats < 0 or
  * an allocation failure is an error. */
@@ -123,6 +125,39 @@ NBL_API int nbl_rope(nbl_ctx* ctx, float* x, int64_t n, int64_t n_heads, int64_t
  * attends to 0..pos0+t. n_heads % n_kv_heads == 0, head_dim <= 256 (any parity, as in the reference). */
 NBL_API int nbl_attention(nbl_ctx* ctx, const float* q, const float* k, const float* v, float* out, int64_t n, int64_t pos0,
                   int64_t n_heads, int64_t n_kv_heads, int64_t head_dim);
+
+/* ---- weights and the model's other ops (backend.h:54-70), fp32 device activations ---- */
+/* Uploads a host weight tensor of ne1 rows x ne0 elements, dtype NBL_F32 or NBL_F16, to device memory owned by
+ * the context: the device form of a weight Tensor view (src/tensor.h:57-70; nibble's are views of the mmap'd
+ * GGUF). An F16 matrix also gets an fp32 copy for multi-row matmuls. Freed by nbl_weight_destroy or with the
+ * context. Returns after the upload has completed (the host buffer may be released). */
+NBL_API int nbl_weight_create(nbl_ctx* ctx, const void* host, int32_t dtype, int64_t ne0, int64_t ne1,
+                              nbl_weight** out);
+NBL_API int nbl_weight_destroy(nbl_weight* w);
+/* The uploaded tensor: device address of its elements (in its own dtype), dtype and shape. Any out pointer may be
+ * NULL. An F32 vector's address is what nbl_add_bias takes. */
+NBL_API int nbl_weight_data(const nbl_weight* w, const void** dev, int32_t* dtype, int64_t* ne0, int64_t* ne1);
+/* Backend::embed (backend.h:54-55; cpu::embed ref_ops.cpp:80-98): out[t, :] = row ids[t] of table, widened to
+ * fp32 (bit-identical). ids is HOST memory (a std::span in the reference); an id outside [0, ne1) is
+ * NBL_E_INVALID with the reference's message and nothing is written. */
+NBL_API int nbl_embed(nbl_ctx* ctx, const nbl_weight* table, const int32_t* ids, int64_t n, float* out);
+/* Backend::matmul (backend.h:56; cpu::matmul_rows ref_ops.cpp:109-136): y[n, ne1] = x[n, ne0] . W^T in fp32
+ * arithmetic (F16 weights widened exactly). n <= 8 streams the weight once (GEMV kernel); larger n runs SGEMM
+ * (cuBLAS, no TF32). Results differ from the CPU's only by fp32 summation order. Backend::matmul_multi is one
+ * call per weight, as the reference's contract allows ("results equal separate calls"). */
+NBL_API int nbl_matmul(nbl_ctx* ctx, const nbl_weight* w, const float* x, float* y, int64_t n);
+/* Backend::rmsnorm (backend.h:61; cpu::rmsnorm ref_ops.cpp:138-148): y[t] = x[t] / sqrt(mean(x[t]^2) + eps) *
+ * weight, evaluated in double like the reference and rounded once to float. weight is an F32 vector (ne1 = 1)
+ * of width d = ne0; x, y are [n, d]. */
+NBL_API int nbl_rmsnorm(nbl_ctx* ctx, const float* x, const nbl_weight* weight, float* y, int64_t n, float eps);
+/* Backend::add (backend.h:62; ref_ops.cpp:151-153): x[i] += y[i] for i < count (bit-identical). */
+NBL_API int nbl_add(nbl_ctx* ctx, float* x, const float* y, int64_t count);
+/* Backend::copy (backend.h:65; CpuBackend::copy cpu_backend.cpp:260-264): dst[i] = src[i]; the ranges must not
+ * overlap (the reference's memmove allows it; its only caller, the Transformer, never overlaps). */
+NBL_API int nbl_copy(nbl_ctx* ctx, float* dst, const float* src, int64_t count);
+/* Backend::silu_mul (backend.h:70; ref_ops.cpp:217-222): gate[i] = g / (1 + e^-g) * up[i], g = gate[i], in
+ * float (within a few ulp of the reference: CUDA's expf against the C library's). */
+NBL_API int nbl_silu_mul(nbl_ctx* ctx, float* gate, const float* up, int64_t count);
 
 /* ---- paged K/V path (B200-native layout; the reference keeps fp32 flat caches) ---- */
 /* Allocates and zeroes a pool (see nbl_kv_config) and the TMA descriptors over it. */

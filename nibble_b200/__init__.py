@@ -16,7 +16,7 @@ from dataclasses import dataclass
 from . import _abi
 from ._abi import BF16, F16, F32, NibbleError, check
 
-__all__ = ["Context", "KVPool", "NibbleError", "RopeSpec", "F32", "F16", "BF16", "abi_version"]
+__all__ = ["Context", "KVPool", "Weight", "NibbleError", "RopeSpec", "F32", "F16", "BF16", "abi_version"]
 
 
 def abi_version() -> int:
@@ -92,6 +92,29 @@ class KVPool:
     def close(self):
         if self.handle:
             check(_abi.lib.nbl_kv_destroy(self.handle))
+            self.handle = None
+
+
+class Weight:
+    """A weight tensor uploaded to the device (nbl_weight): ne1 rows of ne0 elements, F32 or F16 -- the device form
+    of nibble's Tensor view (src/tensor.h:57-70)."""
+
+    def __init__(self, ctx: "Context", host, dtype: int | None = None):
+        """host: a C-contiguous numpy float32 / float16 array, 1-D (a vector) or 2-D [ne1, ne0]."""
+        import numpy as np
+        a = np.ascontiguousarray(host)
+        if dtype is None:
+            dtype = {np.dtype(np.float32): F32, np.dtype(np.float16): F16}.get(a.dtype)
+            if dtype is None:
+                raise ValueError(f"weights must be float32 or float16, got {a.dtype}")
+        ne1, ne0 = (1, a.shape[0]) if a.ndim == 1 else a.shape
+        h = C.c_void_p()
+        check(_abi.lib.nbl_weight_create(ctx.handle, a.ctypes.data, dtype, ne0, ne1, C.byref(h)))
+        self.ctx, self.handle, self.ne0, self.ne1, self.dtype = ctx, h, ne0, ne1, dtype
+
+    def close(self):
+        if self.handle:
+            check(_abi.lib.nbl_weight_destroy(self.handle))
             self.handle = None
 
 
@@ -176,6 +199,32 @@ class Context:
     def attention(self, q, k, v, out, n: int, pos0: int, n_heads: int, n_kv_heads: int, head_dim: int):
         check(_abi.lib.nbl_attention(self.handle, _ptr(q), _ptr(k), _ptr(v), _ptr(out), n, pos0, n_heads, n_kv_heads,
                                      head_dim))
+
+    # ---- the model's other Backend ops (backend.h:54-70) on fp32 device buffers
+    def weight(self, host, dtype: int | None = None) -> Weight:
+        return Weight(self, host, dtype)
+
+    def embed(self, table: Weight, ids, out):
+        """ids: host int32 array (a std::span in the reference); out [n, ne0] fp32."""
+        import numpy as np
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        check(_abi.lib.nbl_embed(self.handle, table.handle, ids.ctypes.data, ids.shape[0], _ptr(out)))
+
+    def matmul(self, w: Weight, x, y, n: int):
+        """y[n, ne1] = x[n, ne0] . W^T"""
+        check(_abi.lib.nbl_matmul(self.handle, w.handle, _ptr(x), _ptr(y), n))
+
+    def rmsnorm(self, x, weight: Weight, y, n: int, eps: float):
+        check(_abi.lib.nbl_rmsnorm(self.handle, _ptr(x), weight.handle, _ptr(y), n, eps))
+
+    def add(self, x, y, count: int):
+        check(_abi.lib.nbl_add(self.handle, _ptr(x), _ptr(y), count))
+
+    def copy(self, dst, src, count: int):
+        check(_abi.lib.nbl_copy(self.handle, _ptr(dst), _ptr(src), count))
+
+    def silu_mul(self, gate, up, count: int):
+        check(_abi.lib.nbl_silu_mul(self.handle, _ptr(gate), _ptr(up), count))
 
     # ---- paged path
     def kv_pool(self, n_pages: int, n_kv_heads: int, head_dim: int = 64, page_size: int = 16,

@@ -70,6 +70,15 @@ SIGNATURES = {
     "nbl_attn_prefill": [_P, _P, _P, _I32, _I64, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _P, _I32],
     "nbl_lse_merge": [_P, _P, _P, _I32, _I64, _I32, _P, _P],
     "nbl_lse_merge_packed": [_P, _P, _I32, _I64, _I32, _P, _P],
+    "nbl_weight_create": [_P, _P, _I32, _I64, _I64, C.POINTER(_P)],
+    "nbl_weight_destroy": [_P],
+    "nbl_weight_data": [_P, C.POINTER(_P), C.POINTER(_I32), C.POINTER(_I64), C.POINTER(_I64)],
+    "nbl_embed": [_P, _P, _P, _I64, _P],
+    "nbl_matmul": [_P, _P, _P, _P, _I64],
+    "nbl_rmsnorm": [_P, _P, _P, _P, _I64, C.c_float],
+    "nbl_add": [_P, _P, _P, _I64],
+    "nbl_copy": [_P, _P, _P, _I64],
+    "nbl_silu_mul": [_P, _P, _P, _I64],
 }
 _RESTYPES = {"nbl_last_error": C.c_size_t, "nbl_ctx_stream": _P}
 

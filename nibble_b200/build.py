@@ -19,8 +19,8 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libnibble_cuda.so")
 STAMP = LIB + ".stamp"
-SOURCES = ["api.cu", "rope.cu", "attn_f32.cu", "decode.cu", "decode_static.cu", "prefill.cu"]
-HEADERS = ["nbl_device.cuh", "nbl_internal.h", "nbl_errors.h"]
+SOURCES = ["api.cu", "rope.cu", "attn_f32.cu", "decode.cu", "decode_static.cu", "prefill.cu", "model_ops.cu"]
+HEADERS = ["nbl_device.cuh", "nbl_internal.h", "nbl_errors.h", "model_ops.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
          "--expt-relaxed-constexpr", "-I" + os.path.join(ROOT, "include")]
@@ -77,7 +77,7 @@ def build(force: bool = False, verbose: bool = False, extra: list[str] | None = 
     if failed:
         raise RuntimeError(f"nvcc failed for {', '.join(failed)}")
     tmp = LIB + ".tmp"
-    subprocess.run([cc, *ARCH, "-shared", "-o", tmp, *objs, "-lcudart_static", "-lrt", "-ldl", "-lpthread"],
+    subprocess.run([cc, *ARCH, "-shared", "-o", tmp, *objs, "-lcudart_static", "-lcublas", "-lrt", "-ldl", "-lpthread"],
                    check=True)
     os.replace(tmp, LIB)
     with open(STAMP, "w") as f:

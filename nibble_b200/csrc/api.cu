@@ -12,6 +12,7 @@
 #include <new>
 #include <string>
 
+#include "model_ops.h"
 #include "nbl_internal.h"
 
 namespace {
@@ -136,6 +137,52 @@ namespace {
 
 bool is_dtype(int32_t d) { return d == NBL_F32 || d == NBL_F16 || d == NBL_BF16; }
 
+constexpr size_t kCublasWorkspace = size_t(32) << 20;
+
+// The context's SGEMM handle with a fixed workspace (so a matmul allocates nothing), created once.
+cublasHandle_t cublas_handle(nbl_ctx* ctx) {
+  if (!ctx->cublas) {
+    cublasHandle_t h = nullptr;
+    if (cublasCreate(&h) != CUBLAS_STATUS_SUCCESS) nbl::fail(NBL_E_CUDA, "cublasCreate failed");
+    void* ws = nullptr;
+    try {
+      ws = device_alloc(kCublasWorkspace, "SGEMM workspace");
+      if (cublasSetWorkspace(h, ws, kCublasWorkspace) != CUBLAS_STATUS_SUCCESS ||
+          cublasSetMathMode(h, CUBLAS_DEFAULT_MATH) != CUBLAS_STATUS_SUCCESS)  // fp32 arithmetic, no TF32
+        nbl::fail(NBL_E_CUDA, "cublas workspace/math mode setup failed");
+    } catch (...) {
+      if (ws) cudaFree(ws);
+      cublasDestroy(h);
+      throw;
+    }
+    ctx->cublas = h;
+    ctx->cublas_ws = ws;
+  }
+  return static_cast<cublasHandle_t>(ctx->cublas);
+}
+
+// Grows the device token-id staging buffer to n ids.
+void ensure_ids(nbl_ctx* ctx, int64_t n) {
+  if (ctx->ids_cap >= n) return;
+  void* p = device_alloc(static_cast<size_t>(n) * sizeof(int32_t), "token ids");
+  if (ctx->ids) {
+    nbl::check_cuda(cudaStreamSynchronize(ctx->stream), "ids sync");
+    cudaFree(ctx->ids);
+  }
+  ctx->ids = static_cast<int32_t*>(p);
+  ctx->ids_cap = n;
+}
+
+void release_weight(nbl_weight* w) {
+  if (w->w.f32 && w->w.f32 != w->w.dev) cudaFree(w->w.f32);
+  cudaFree(w->w.dev);
+  delete w;
+}
+
+void require_weight(const nbl_ctx* ctx, const nbl_weight* w, const char* what) {
+  require(w != nullptr && w->ctx == ctx, std::string(what) + ": weight is NULL or belongs to another context");
+}
+
 }  // namespace
 
 extern "C" {
@@ -192,6 +239,10 @@ int nbl_ctx_destroy(nbl_ctx* ctx) {
       cudaFree(kv->pool);
       delete kv;
     }
+    for (nbl_weight* w : ctx->weights) release_weight(w);
+    if (ctx->cublas) cublasDestroy(static_cast<cublasHandle_t>(ctx->cublas));
+    if (ctx->cublas_ws) cudaFree(ctx->cublas_ws);
+    if (ctx->ids) cudaFree(ctx->ids);
     for (auto& a : ctx->allocs) cudaFree(a.first);
     for (auto& t : ctx->rope_tables) cudaFree(t.dev);
     if (ctx->scratch) cudaFree(ctx->scratch);
@@ -264,6 +315,8 @@ int nbl_reserve(nbl_ctx* ctx, int64_t n_ctx, int64_t n_heads, int64_t max_rows, 
     const auto plan = nbl::plan_decode(1, 1, 1, static_cast<int>(n_heads), static_cast<int>(std::min<int64_t>(n_ctx, INT32_MAX)),
                                        16, ctx->num_sms, 0);
     if (plan.scratch_bytes) ensure_scratch(ctx, plan.scratch_bytes);
+    if (max_rows > 0) ensure_ids(ctx, max_rows);
+    if (max_rows > nbl::kGemvMaxRows) cublas_handle(ctx);
   });
 }
 
@@ -609,6 +662,145 @@ int nbl_lse_merge_packed(nbl_ctx* ctx, const float* packed, int32_t n_parts, int
     const int64_t part = rows * (int64_t(head_dim) + 1);  // [rows * head_dim outputs | rows lse] per part
     nbl::launch_lse_merge(ctx->stream, packed, packed + rows * head_dim, n_parts, rows, head_dim, out, lse, part,
                           part);
+  });
+}
+
+// ---- weights and the model's other ops ----
+
+int nbl_weight_create(nbl_ctx* ctx, const void* host, int32_t dtype, int64_t ne0, int64_t ne1, nbl_weight** out) {
+  return guarded([&] {
+    require(ctx && host && out, "weight_create: ctx, host or out is NULL");
+    *out = nullptr;
+    require(dtype == NBL_F32 || dtype == NBL_F16, "weight_create: dtype must be NBL_F32 or NBL_F16");
+    require(ne0 > 0 && ne1 > 0, "weight_create: bad shape " + std::to_string(ne0) + " x " + std::to_string(ne1));
+    const size_t elem = dtype == NBL_F32 ? 4 : 2;
+    require(static_cast<uint64_t>(ne0) <= (uint64_t(1) << 40) / static_cast<uint64_t>(ne1),
+            "weight_create: tensor too large");
+    const size_t count = static_cast<size_t>(ne0) * static_cast<size_t>(ne1);
+    use_device(ctx);
+    auto* w = new nbl_weight();
+    w->ctx = ctx;
+    w->w.dtype = dtype;
+    w->w.ne0 = ne0;
+    w->w.ne1 = ne1;
+    try {
+      w->w.dev = device_alloc(count * elem, "weight");
+      nbl::check_cuda(cudaMemcpyAsync(w->w.dev, host, count * elem, cudaMemcpyHostToDevice, ctx->stream), "weight upload");
+      if (dtype == NBL_F32) {
+        w->w.f32 = static_cast<float*>(w->w.dev);
+      } else if (ne1 > 1) {  // matrices: an fp32 copy for the SGEMM path
+        w->w.f32 = static_cast<float*>(device_alloc(count * sizeof(float), "weight fp32 copy"));
+        nbl::launch_widen_f16(ctx->stream, w->w.dev, w->w.f32, static_cast<int64_t>(count), ctx->num_sms);
+        nbl::check_cuda(cudaGetLastError(), "widen launch");
+      }
+      nbl::check_cuda(cudaStreamSynchronize(ctx->stream), "weight upload");
+      ctx->weights.push_back(w);
+    } catch (...) {
+      release_weight(w);
+      throw;
+    }
+    *out = w;
+  });
+}
+
+int nbl_weight_destroy(nbl_weight* w) {
+  if (!w) return NBL_OK;
+  return guarded([&] {
+    nbl_ctx* ctx = w->ctx;
+    use_device(ctx);
+    nbl::check_cuda(cudaStreamSynchronize(ctx->stream), "weight destroy sync");
+    ctx->weights.erase(std::remove(ctx->weights.begin(), ctx->weights.end(), w), ctx->weights.end());
+    release_weight(w);
+  });
+}
+
+int nbl_weight_data(const nbl_weight* w, const void** dev, int32_t* dtype, int64_t* ne0, int64_t* ne1) {
+  return guarded([&] {
+    require(w != nullptr, "weight_data: weight is NULL");
+    if (dev) *dev = w->w.dev;
+    if (dtype) *dtype = w->w.dtype;
+    if (ne0) *ne0 = w->w.ne0;
+    if (ne1) *ne1 = w->w.ne1;
+  });
+}
+
+int nbl_embed(nbl_ctx* ctx, const nbl_weight* table, const int32_t* ids, int64_t n, float* out) {
+  return guarded([&] {
+    require(ctx && ids && out, "embed: ctx, ids or out is NULL");
+    require_weight(ctx, table, "embed");
+    require(n >= 0, "embed: n < 0");
+    for (int64_t t = 0; t < n; ++t)  // the reference's check and message (ref_ops.cpp:84-87)
+      if (ids[t] < 0 || ids[t] >= table->w.ne1)
+        nbl::fail(NBL_E_INVALID, "embed: token id " + std::to_string(ids[t]) + " out of range (n_vocab " +
+                                     std::to_string(table->w.ne1) + ")");
+    if (n == 0) return;
+    use_device(ctx);
+    ensure_ids(ctx, n);
+    nbl::check_cuda(cudaMemcpyAsync(ctx->ids, ids, static_cast<size_t>(n) * sizeof(int32_t), cudaMemcpyHostToDevice,
+                                    ctx->stream),
+                    "embed ids");
+    nbl::launch_embed(ctx->stream, table->w, ctx->ids, n, out, ctx->num_sms);
+    nbl::check_cuda(cudaGetLastError(), "embed launch");
+  });
+}
+
+int nbl_matmul(nbl_ctx* ctx, const nbl_weight* w, const float* x, float* y, int64_t n) {
+  return guarded([&] {
+    require(ctx && x && y, "matmul: ctx, x or y is NULL");
+    require_weight(ctx, w, "matmul");
+    require(n >= 0 && n <= INT32_MAX && w->w.ne0 <= INT32_MAX && w->w.ne1 <= INT32_MAX, "matmul: bad size");
+    if (n == 0) return;
+    use_device(ctx);
+    if (n <= nbl::kGemvMaxRows || !w->w.f32) {
+      nbl::launch_gemv(ctx->stream, w->w, x, y, n);
+      nbl::check_cuda(cudaGetLastError(), "matmul launch");
+    } else {
+      nbl::gemm_f32(cublas_handle(ctx), ctx->stream, w->w.f32, x, y, w->w.ne0, w->w.ne1, n);
+    }
+  });
+}
+
+int nbl_rmsnorm(nbl_ctx* ctx, const float* x, const nbl_weight* weight, float* y, int64_t n, float eps) {
+  return guarded([&] {
+    require(ctx && x && y, "rmsnorm: ctx, x or y is NULL");
+    require_weight(ctx, weight, "rmsnorm");
+    require(weight->w.dtype == NBL_F32 && weight->w.ne1 == 1, "rmsnorm: weight must be an F32 vector");
+    require(n >= 0 && n <= INT32_MAX, "rmsnorm: bad n");
+    if (n == 0) return;
+    use_device(ctx);
+    nbl::launch_rmsnorm(ctx->stream, x, static_cast<const float*>(weight->w.dev), y, n, weight->w.ne0, eps);
+    nbl::check_cuda(cudaGetLastError(), "rmsnorm launch");
+  });
+}
+
+int nbl_add(nbl_ctx* ctx, float* x, const float* y, int64_t count) {
+  return guarded([&] {
+    require(ctx && x && y && count >= 0, "add: NULL argument or count < 0");
+    if (count == 0) return;
+    use_device(ctx);
+    nbl::launch_add(ctx->stream, x, y, count, ctx->num_sms);
+    nbl::check_cuda(cudaGetLastError(), "add launch");
+  });
+}
+
+int nbl_copy(nbl_ctx* ctx, float* dst, const float* src, int64_t count) {
+  return guarded([&] {
+    require(ctx && dst && src && count >= 0, "copy: NULL argument or count < 0");
+    if (count == 0 || dst == src) return;
+    use_device(ctx);
+    nbl::check_cuda(cudaMemcpyAsync(dst, src, static_cast<size_t>(count) * sizeof(float), cudaMemcpyDeviceToDevice,
+                                    ctx->stream),
+                    "copy");
+  });
+}
+
+int nbl_silu_mul(nbl_ctx* ctx, float* gate, const float* up, int64_t count) {
+  return guarded([&] {
+    require(ctx && gate && up && count >= 0, "silu_mul: NULL argument or count < 0");
+    if (count == 0) return;
+    use_device(ctx);
+    nbl::launch_silu_mul(ctx->stream, gate, up, count, ctx->num_sms);
+    nbl::check_cuda(cudaGetLastError(), "silu_mul launch");
   });
 }
 

@@ -16,13 +16,7 @@ void check(int status) {
 
 CudaBackend::CudaBackend(int device) { check(nbl_ctx_create(device, &ctx_)); }
 
-CudaBackend::~CudaBackend() { nbl_ctx_destroy(ctx_); }
-
-void CudaBackend::unsupported(const char* op) {
-  throw Error(std::string("cuda backend: ") + op +
-              " is not implemented on the GPU in this build (attention path only: reserve, alloc, free, read, "
-              "add_bias, rope, attention)");
-}
+CudaBackend::~CudaBackend() { nbl_ctx_destroy(ctx_); }  // releases the uploaded weights too
 
 void CudaBackend::reserve(const ReserveParams& rp) {
   check(nbl_reserve(ctx_, rp.n_ctx, rp.n_heads, rp.max_rows, rp.max_width));
@@ -42,20 +36,44 @@ void CudaBackend::write(float* dst, const float* host_src, int64_t n) { check(nb
 
 void CudaBackend::synchronize() { check(nbl_ctx_check(ctx_)); }
 
-const float* CudaBackend::device_weight(const Tensor& t, int64_t n_floats) {
+const nbl_weight* CudaBackend::device_weight(const Tensor& t) {
   auto it = weights_.find(t.data);
   if (it != weights_.end()) return it->second;
-  float* d = alloc(n_floats);
-  write(d, static_cast<const float*>(t.data), n_floats);
-  weights_.emplace(t.data, d);
-  return d;
+  if (!t.data) throw Error("cuda backend: weight tensor has no data");
+  if (t.type != DType::F32 && t.type != DType::F16)
+    throw Error("cuda backend: unsupported weight dtype (only F32/F16 run on the GPU)");
+  nbl_weight* w = nullptr;
+  check(nbl_weight_create(ctx_, t.data, t.type == DType::F32 ? NBL_F32 : NBL_F16, t.ne[0], t.rows(), &w));
+  weights_.emplace(t.data, w);
+  return w;
 }
+
+// Backend::embed (src/backend/backend.h:54-55): ids stay host memory, as in the reference's span.
+void CudaBackend::embed(const Tensor& table, std::span<const int32_t> ids, float* out) {
+  check(nbl_embed(ctx_, device_weight(table), ids.data(), static_cast<int64_t>(ids.size()), out));
+}
+
+void CudaBackend::matmul(const Tensor& w, const float* x, float* y, int64_t n) {
+  check(nbl_matmul(ctx_, device_weight(w), x, y, n));
+}
+
+void CudaBackend::rmsnorm(const float* x, const Tensor& weight, float* y, int64_t n, float eps) {
+  if (weight.type != DType::F32) throw Error("rmsnorm: weight must be an F32 tensor");
+  check(nbl_rmsnorm(ctx_, x, device_weight(weight), y, n, eps));
+}
+
+void CudaBackend::add(float* x, const float* y, int64_t count) { check(nbl_add(ctx_, x, y, count)); }
+
+void CudaBackend::copy(float* dst, const float* src, int64_t count) { check(nbl_copy(ctx_, dst, src, count)); }
+
+void CudaBackend::silu_mul(float* gate, const float* up, int64_t count) { check(nbl_silu_mul(ctx_, gate, up, count)); }
 
 // Each of n rows += bias (F32 vector of width bias.ne[0]) -- CpuBackend::add_bias, cpu_backend.cpp:247-252.
 void CudaBackend::add_bias(float* x, const Tensor& bias, int64_t n) {
   if (bias.type != DType::F32 || !bias.data) throw Error("add_bias: bias must be an F32 tensor");
-  const int64_t width = bias.ne[0];
-  check(nbl_add_bias(ctx_, x, device_weight(bias, width), width, n));
+  const void* b = nullptr;
+  check(nbl_weight_data(device_weight(bias), &b, nullptr, nullptr, nullptr));
+  check(nbl_add_bias(ctx_, x, static_cast<const float*>(b), bias.ne[0], n));
 }
 
 void CudaBackend::rope(float* x, int64_t n, int64_t n_heads, int64_t head_dim, int64_t pos0, const RopeParams& p) {

@@ -6,20 +6,27 @@
 //     (CpuBackend::~CpuBackend, src/backend/cpu/cpu_backend.cpp:70-72);
 //   * input/resource faults throw nibble::Error with the C layer's message (include/nibble/error.h);
 //   * after reserve(), attention/rope within the reserved sizes allocate nothing.
-// Weights arrive as host Tensor views (the mmap'd GGUF); the ones this backend consumes (biases) are uploaded
-// once and cached by host address.
+// Weights arrive as host Tensor views (the mmap'd GGUF); each is uploaded once, on first use, and cached by host
+// address (nbl_weight_create), so the first forward pass after construction allocates the model's device weights
+// and later ones allocate nothing.
 //
-// Coverage: the attention path -- reserve, alloc, free, read, add_bias, rope, attention -- runs on the GPU. The
-// weight GEMMs and the remaining elementwise ops (embed, matmul, rmsnorm, add, copy, silu_mul) are not part of
-// this backend yet: supports() reports no weight type, so a model refuses to load on it instead of silently
-// running anything on the CPU, and those ops throw nibble::Error.
+// Coverage: every Backend op runs on the GPU for F32 and F16 weights -- embed, matmul (weight-streaming GEMV for
+// up to 8 rows, SGEMM above), rmsnorm, add, add_bias, rope, copy, attention, silu_mul -- so nibble's Transformer
+// (src/model/transformer.cpp) runs on it unchanged. supports() reports F32 and F16; the quantized types are not
+// part of this backend yet, so a quantized model refuses to load on it instead of running anything on the CPU.
 //
 // The paged fp16/bf16 fast path (fused append, split-K decode, tcgen05 prefill) is reached through handle()
 // and the nbl_* functions, with check() turning their statuses into nibble::Error.
 #include <unordered_map>
 
 #include "../../../include/nibble_cuda.h"
-#include "backend.h"
+#ifdef NBL_WITH_NIBBLE_TREE
+// Built inside a nibble tree (src/ and include/ on the include path): implement nibble's own interface header.
+#include "backend/backend.h"
+#include "nibble/error.h"
+#else
+#include "backend.h"  // this repository's restatement of src/backend/backend.h (identical declarations)
+#endif
 
 namespace nibble::cuda {
 
@@ -33,7 +40,7 @@ class CudaBackend final : public Backend {
   CudaBackend(const CudaBackend&) = delete;
   CudaBackend& operator=(const CudaBackend&) = delete;
 
-  bool supports(DType) const override { return false; }
+  bool supports(DType t) const override { return t == DType::F32 || t == DType::F16; }
   void reserve(const ReserveParams& rp) override;
   float* alloc(int64_t n_floats) override;
   void free(float* p) override;
@@ -43,12 +50,12 @@ class CudaBackend final : public Backend {
   void attention(const float* q, const float* k, const float* v, float* out, int64_t n, int64_t pos0, int64_t n_heads,
                  int64_t n_kv_heads, int64_t head_dim) override;
 
-  void embed(const Tensor&, std::span<const int32_t>, float*) override { unsupported("embed"); }
-  void matmul(const Tensor&, const float*, float*, int64_t) override { unsupported("matmul"); }
-  void rmsnorm(const float*, const Tensor&, float*, int64_t, float) override { unsupported("rmsnorm"); }
-  void add(float*, const float*, int64_t) override { unsupported("add"); }
-  void copy(float*, const float*, int64_t) override { unsupported("copy"); }
-  void silu_mul(float*, const float*, int64_t) override { unsupported("silu_mul"); }
+  void embed(const Tensor& table, std::span<const int32_t> ids, float* out) override;
+  void matmul(const Tensor& w, const float* x, float* y, int64_t n) override;
+  void rmsnorm(const float* x, const Tensor& weight, float* y, int64_t n, float eps) override;
+  void add(float* x, const float* y, int64_t count) override;
+  void copy(float* dst, const float* src, int64_t count) override;
+  void silu_mul(float* gate, const float* up, int64_t count) override;
 
   // Host -> device upload into a block from alloc() (tests and callers that stage inputs).
   void write(float* dst, const float* host_src, int64_t n);
@@ -57,11 +64,11 @@ class CudaBackend final : public Backend {
   nbl_ctx* handle() const { return ctx_; }
 
  private:
-  [[noreturn]] static void unsupported(const char* op);
-  const float* device_weight(const Tensor& t, int64_t n_floats);
+  // The device copy of a weight Tensor (uploaded on first use, cached by host address).
+  const nbl_weight* device_weight(const Tensor& t);
 
   nbl_ctx* ctx_ = nullptr;
-  std::unordered_map<const void*, float*> weights_;  // host weight address -> uploaded copy
+  std::unordered_map<const void*, nbl_weight*> weights_;  // host weight address -> uploaded tensor
 };
 
 }  // namespace nibble::cuda

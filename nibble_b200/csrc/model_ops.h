@@ -1,0 +1,35 @@
+// Device weights and the launches of the model's non-attention ops (model_ops.cu), shared with api.cu.
+#pragma once
+#include <cublas_v2.h>
+
+#include "nbl_internal.h"
+
+namespace nbl {
+
+// Activation rows up to which a matmul runs as the weight-streaming GEMV (decode); more rows use SGEMM.
+constexpr int64_t kGemvMaxRows = 8;
+
+// One weight tensor on the device: ne1 rows of ne0 elements (F32 or F16), plus an fp32 copy of an F16 matrix for
+// the SGEMM path (equal to `dev` for F32).
+struct Weight {
+  int32_t dtype = NBL_F32;
+  int64_t ne0 = 0, ne1 = 0;
+  void* dev = nullptr;
+  float* f32 = nullptr;
+};
+
+void launch_embed(cudaStream_t st, const Weight& table, const int32_t* ids, int64_t n, float* out, int num_sms);
+void launch_widen_f16(cudaStream_t st, const void* src, float* dst, int64_t count, int num_sms);
+void launch_gemv(cudaStream_t st, const Weight& w, const float* x, float* y, int64_t n);
+void gemm_f32(cublasHandle_t h, cudaStream_t st, const float* w_f32, const float* x, float* y, int64_t ne0, int64_t ne1,
+              int64_t n);
+void launch_rmsnorm(cudaStream_t st, const float* x, const float* w, float* y, int64_t n, int64_t d, float eps);
+void launch_add(cudaStream_t st, float* x, const float* y, int64_t count, int num_sms);
+void launch_silu_mul(cudaStream_t st, float* gate, const float* up, int64_t count, int num_sms);
+
+}  // namespace nbl
+
+struct nbl_weight {
+  nbl_ctx* ctx = nullptr;
+  nbl::Weight w;
+};

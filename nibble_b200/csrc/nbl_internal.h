@@ -54,6 +54,12 @@ struct nbl_ctx {
   size_t io_bytes = 0;
   cudaStream_t up_stream = nullptr, down_stream = nullptr, aux_stream = nullptr;
   std::vector<cudaEvent_t> events;
+  // the model's other ops (model_ops.cu): uploaded weights, the token-id staging buffer, the SGEMM handle
+  std::vector<nbl_weight*> weights;
+  int32_t* ids = nullptr;
+  int64_t ids_cap = 0;
+  void* cublas = nullptr;     // cublasHandle_t, created by nbl_reserve (max_rows > the GEMV limit) or first use
+  void* cublas_ws = nullptr;  // its fixed workspace
 };
 
 struct nbl_kv {

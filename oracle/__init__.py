@@ -34,11 +34,17 @@ _lib = None
 _ref = None
 
 
+MODEL_CHECK = os.path.join(HERE, "_ref", "nbl_model_check")
+
+
 def build(with_ref: bool | None = None) -> None:
-    """Compiles liboracle.so, and oracle/_ref when the reference tree is present (or with_ref is True)."""
+    """Compiles liboracle.so, and oracle/_ref when the reference tree is present (or with_ref is True): nibble's own
+    code, and -- once nibble_b200/libnibble_cuda.so exists -- the Transformer drop-in check binary."""
     targets = ["oracle"]
     if with_ref or (with_ref is None and os.path.isdir(os.path.join(REF_TREE, "src"))):
         targets.append("ref")
+        if os.path.exists(os.path.join(os.path.dirname(HERE), "nibble_b200", "libnibble_cuda.so")):
+            targets.append("model-check")
     subprocess.run(["make", "-s", "-C", HERE, f"REF={REF_TREE}", "-j8", *targets], check=True)
 
 
@@ -64,6 +70,12 @@ def _load_oracle():
     lib.orc_add_bias.argtypes = [_f32p, _f32p, _i64, _i64]
     lib.orc_gather_pages.argtypes = [_u16p, _i32p, _i64, _i64, _i64, _i64, C.c_int, _f32p, _f32p]
     lib.orc_lse_merge.argtypes = [_f32p, _f32p, _i64, _i64, _i64, _f32p, C.c_void_p]
+    lib.orc_embed.argtypes = [C.c_void_p, C.c_int, _i64, _i64, _i32p, _i64, _f32p]
+    lib.orc_embed.restype = C.c_int
+    lib.orc_matmul.argtypes = [C.c_void_p, C.c_int, _i64, _i64, _f32p, _f32p, _i64]
+    lib.orc_rmsnorm.argtypes = [_f32p, _f32p, _f32p, _i64, _i64, C.c_float]
+    lib.orc_add.argtypes = [_f32p, _f32p, _i64]
+    lib.orc_silu_mul.argtypes = [_f32p, _f32p, _i64]
     _lib = lib
     return lib
 
@@ -103,6 +115,14 @@ def _load_ref():
     lib.nref_backend_attention.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                            _i64, _i64, _i64, _i64, _i64]
     lib.nref_backend_rope.argtypes = [C.c_void_p, _f32p, _i64, _i64, _i64, _i64, C.c_float, C.c_int, C.c_void_p]
+    lib.nref_embed.argtypes = [C.c_void_p, C.c_int, _i64, _i64, _i32p, _i64, _f32p]
+    lib.nref_matmul.argtypes = [C.c_void_p, C.c_int, _i64, _i64, _f32p, _f32p, _i64]
+    lib.nref_rmsnorm.argtypes = [_f32p, _f32p, _f32p, _i64, _i64, C.c_float]
+    lib.nref_add.argtypes = [_f32p, _f32p, _i64]
+    lib.nref_silu_mul.argtypes = [_f32p, _f32p, _i64]
+    lib.nref_backend_matmul.argtypes = [C.c_void_p, C.c_void_p, C.c_int, _i64, _i64, _f32p, _f32p, _i64]
+    lib.nref_backend_rmsnorm.argtypes = [C.c_void_p, _f32p, _f32p, _f32p, _i64, _i64, C.c_float]
+    lib.nref_backend_silu_mul.argtypes = [C.c_void_p, _f32p, _f32p, _i64]
     _ref = lib
     return lib
 
@@ -198,7 +218,96 @@ def lse_merge(part_o, part_lse):
     return out, lse
 
 
+# ---------------------------------------------------------------- the model's other ops (backend.h:54-70)
+def _weight_arg(w):
+    """(pointer, dtype code, array kept alive) for an F32 or F16 (float16 or uint16 bits) weight array."""
+    w = np.ascontiguousarray(w)
+    if w.dtype == np.float32:
+        return w.ctypes.data, 0, w
+    if w.dtype in (np.float16, np.uint16):
+        return w.ctypes.data, 1, w
+    raise ValueError(f"weight dtype {w.dtype}")
+
+
+def embed(table, ids) -> np.ndarray:
+    """Rows ids of table [n_rows, ne0] (F32 or F16), widened to fp32 (ref_ops.cpp:80-98)."""
+    ptr, dt, keep = _weight_arg(table)
+    ids = _c(ids, np.int32)
+    out = np.empty((ids.size, keep.shape[-1]), np.float32)
+    if _load_oracle().orc_embed(ptr, dt, keep.shape[-1], keep.shape[0], ids, ids.size, out) != 0:
+        raise ValueError("embed: token id out of range")
+    return out
+
+
+def matmul(w, x, n) -> np.ndarray:
+    """y[n, ne1] = x[n, ne0] . W^T, float accumulation left to right (ref_ops.cpp:109-136)."""
+    ptr, dt, keep = _weight_arg(w)
+    ne1, ne0 = keep.shape
+    y = np.empty((n, ne1), np.float32)
+    _load_oracle().orc_matmul(ptr, dt, ne0, ne1, _c(x), y, n)
+    return y
+
+
+def rmsnorm(x, weight, n, eps) -> np.ndarray:
+    w = _c(weight)
+    y = np.empty((n, w.size), np.float32)
+    _load_oracle().orc_rmsnorm(_c(x), w, y, n, w.size, eps)
+    return y
+
+
+def add(x, y) -> np.ndarray:
+    z = _c(x).copy()
+    _load_oracle().orc_add(z, _c(y), z.size)
+    return z
+
+
+def silu_mul(gate, up) -> np.ndarray:
+    g = _c(gate).copy()
+    _load_oracle().orc_silu_mul(g, _c(up), g.size)
+    return g
+
+
 # ---------------------------------------------------------------- nibble's own code (oracle/_ref)
+def ref_embed(table, ids) -> np.ndarray:
+    """nibble::cpu::embed (src/backend/cpu/ref_ops.cpp:80)."""
+    ptr, dt, keep = _weight_arg(table)
+    ids = _c(ids, np.int32)
+    out = np.empty((ids.size, keep.shape[-1]), np.float32)
+    lib = _load_ref()
+    if lib.nref_embed(ptr, dt, keep.shape[-1], keep.shape[0], ids, ids.size, out) != 0:
+        raise ValueError(lib.nref_last_error().decode())
+    return out
+
+
+def ref_matmul(w, x, n) -> np.ndarray:
+    """nibble::cpu::matmul_rows, float weights (src/backend/cpu/ref_ops.cpp:109)."""
+    ptr, dt, keep = _weight_arg(w)
+    ne1, ne0 = keep.shape
+    y = np.empty((n, ne1), np.float32)
+    _load_ref().nref_matmul(ptr, dt, ne0, ne1, _c(x), y, n)
+    return y
+
+
+def ref_rmsnorm(x, weight, n, eps) -> np.ndarray:
+    w = _c(weight)
+    y = np.empty((n, w.size), np.float32)
+    _load_ref().nref_rmsnorm(_c(x), w, y, n, w.size, eps)
+    return y
+
+
+def ref_add(x, y) -> np.ndarray:
+    z = _c(x).copy()
+    _load_ref().nref_add(z, _c(y), z.size)
+    return z
+
+
+def ref_silu_mul(gate, up) -> np.ndarray:
+    g = _c(gate).copy()
+    _load_ref().nref_silu_mul(g, _c(up), g.size)
+    return g
+
+
+
 def ref_attention_scalar(q, k, v, n, pos0, n_heads, n_kv_heads, head_dim) -> np.ndarray:
     """nibble::cpu::attention_heads over all heads (src/backend/cpu/ref_ops.cpp:188)."""
     q, k, v = _c(q), _c(k), _c(v)

@@ -217,3 +217,50 @@ void orc_lse_merge(const float* part_o, const float* part_lse, int64_t n_parts, 
     if (lse_out) lse_out[r] = (float)(mx + log(wsum));
   }
 }
+
+/* ---- the model's other ops ---- */
+
+static float orc_weight_at(const void* w, int dtype, int64_t i) {
+  return dtype == 0 ? ((const float*)w)[i] : orc_fp16_to_fp32(((const uint16_t*)w)[i]);
+}
+
+int orc_embed(const void* table, int dtype, int64_t ne0, int64_t n_rows, const int32_t* ids, int64_t n, float* out) {
+  for (int64_t t = 0; t < n; ++t) {
+    const int64_t id = ids[t];
+    if (id < 0 || id >= n_rows) return -1;
+    for (int64_t k = 0; k < ne0; ++k) out[t * ne0 + k] = orc_weight_at(table, dtype, id * ne0 + k);
+  }
+  return 0;
+}
+
+void orc_matmul(const void* w, int dtype, int64_t ne0, int64_t ne1, const float* x, float* y, int64_t n) {
+  for (int64_t t = 0; t < n; ++t) {
+    const float* xt = x + t * ne0;
+    for (int64_t r = 0; r < ne1; ++r) {
+      float acc = 0;
+      for (int64_t k = 0; k < ne0; ++k) acc += xt[k] * orc_weight_at(w, dtype, r * ne0 + k);
+      y[t * ne1 + r] = acc;
+    }
+  }
+}
+
+void orc_rmsnorm(const float* x, const float* weight, float* y, int64_t n, int64_t d, float eps) {
+  for (int64_t t = 0; t < n; ++t) {
+    const float* xt = x + t * d;
+    double ss = 0;
+    for (int64_t i = 0; i < d; ++i) ss += (double)xt[i] * xt[i];
+    const double scale = 1.0 / sqrt(ss / (double)d + (double)eps);
+    for (int64_t i = 0; i < d; ++i) y[t * d + i] = (float)(xt[i] * scale * weight[i]);
+  }
+}
+
+void orc_add(float* x, const float* y, int64_t count) {
+  for (int64_t i = 0; i < count; ++i) x[i] += y[i];
+}
+
+void orc_silu_mul(float* gate, const float* up, int64_t count) {
+  for (int64_t i = 0; i < count; ++i) {
+    const float g = gate[i];
+    gate[i] = g / (1.0f + expf(-g)) * up[i];
+  }
+}

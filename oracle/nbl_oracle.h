@@ -66,6 +66,20 @@ void orc_gather_pages(const uint16_t* pool, const int32_t* page_table, int64_t l
 void orc_lse_merge(const float* part_o, const float* part_lse, int64_t n_parts, int64_t rows, int64_t head_dim,
                    float* out, float* lse_out);
 
+/* The model's other ops (src/backend/backend.h:54-70). dtype: 0 = F32, 1 = F16 (IEEE binary16 bits). */
+/* Embedding lookup: out[t, :] = row ids[t] of table [n_rows, ne0], widened (src/backend/cpu/ref_ops.cpp:80-98).
+ * Returns 0, or -1 (nothing written past the bad row) when an id is outside [0, n_rows). */
+int orc_embed(const void* table, int dtype, int64_t ne0, int64_t n_rows, const int32_t* ids, int64_t n, float* out);
+/* y[t, r] = sum_k x[t, k] * w[r, k] accumulated left to right in float, w [ne1, ne0] F32 or F16
+ * (src/backend/cpu/ref_ops.cpp:109-136, the float branch of matmul_rows). */
+void orc_matmul(const void* w, int dtype, int64_t ne0, int64_t ne1, const float* x, float* y, int64_t n);
+/* RMSNorm of n rows of width d with an F32 weight, in double (src/backend/cpu/ref_ops.cpp:138-148). */
+void orc_rmsnorm(const float* x, const float* weight, float* y, int64_t n, int64_t d, float eps);
+/* x[i] += y[i] (src/backend/cpu/ref_ops.cpp:151-153). */
+void orc_add(float* x, const float* y, int64_t count);
+/* gate[i] = g / (1 + e^-g) * up[i] in float (src/backend/cpu/ref_ops.cpp:217-222). */
+void orc_silu_mul(float* gate, const float* up, int64_t count);
+
 #ifdef __cplusplus
 }
 #endif

@@ -12,10 +12,13 @@
 //   nibble::cpu::CpuBackend        src/backend/cpu/cpu_backend.cpp:20 (ctor), :272 (attention) on a ThreadPool
 //   nibble::simd::select           src/backend/cpu/simd/dispatch.cpp:123 (the kernel tier the backend runs)
 //   nibble::fp16_to_fp32 / fp32_to_fp16   src/fp16.h:18, :46
+//   nibble::cpu::embed / matmul_rows / rmsnorm / add / silu_mul   src/backend/cpu/ref_ops.cpp:80, :109, :138, :151,
+//                                  :217 (the model's other ops, scalar), and the same ops through CpuBackend
 #include <cstdint>
 #include <cstring>
 #include <exception>
 #include <new>
+#include <span>
 #include <vector>
 
 #include "backend/cpu/cpu_backend.h"
@@ -119,6 +122,78 @@ int nref_backend_rope(void* h, float* x, int64_t n, int64_t n_heads, int64_t hea
   try {
     const nibble::RopeParams p{freq_base, neox != 0, freq_factors};
     static_cast<RefBackend*>(h)->be.rope(x, n, n_heads, head_dim, pos0, p);
+    return 0;
+  } catch (const std::exception& e) {
+    set_err(e.what());
+    return 1;
+  }
+}
+
+// ---- the model's other ops (dtype 0 = F32, 1 = F16) ----
+namespace {
+nibble::Tensor tensor_of(const void* data, int dtype, int64_t ne0, int64_t ne1) {
+  nibble::Tensor t;
+  t.type = dtype == 0 ? nibble::DType::F32 : nibble::DType::F16;
+  t.n_dims = ne1 > 1 ? 2 : 1;
+  t.ne = {ne0, ne1, 1, 1};
+  t.data = data;
+  return t;
+}
+}  // namespace
+
+int nref_embed(const void* table, int dtype, int64_t ne0, int64_t n_rows, const int32_t* ids, int64_t n, float* out) {
+  try {
+    nibble::cpu::embed(tensor_of(table, dtype, ne0, n_rows), std::span<const int32_t>(ids, static_cast<size_t>(n)), out);
+    return 0;
+  } catch (const std::exception& e) {
+    set_err(e.what());
+    return 1;
+  }
+}
+
+int nref_matmul(const void* w, int dtype, int64_t ne0, int64_t ne1, const float* x, float* y, int64_t n) {
+  try {
+    nibble::cpu::matmul_rows(tensor_of(w, dtype, ne0, ne1), x, y, n, 0, ne1, nullptr);
+    return 0;
+  } catch (const std::exception& e) {
+    set_err(e.what());
+    return 1;
+  }
+}
+
+void nref_rmsnorm(const float* x, const float* weight, float* y, int64_t n, int64_t d, float eps) {
+  nibble::cpu::rmsnorm(x, tensor_of(weight, 0, d, 1), y, n, eps);
+}
+
+void nref_add(float* x, const float* y, int64_t count) { nibble::cpu::add(x, y, count); }
+
+void nref_silu_mul(float* gate, const float* up, int64_t count) { nibble::cpu::silu_mul(gate, up, count); }
+
+// The same ops through CpuBackend (its SIMD tier where the build has one).
+int nref_backend_matmul(void* h, const void* w, int dtype, int64_t ne0, int64_t ne1, const float* x, float* y,
+                        int64_t n) {
+  try {
+    static_cast<RefBackend*>(h)->be.matmul(tensor_of(w, dtype, ne0, ne1), x, y, n);
+    return 0;
+  } catch (const std::exception& e) {
+    set_err(e.what());
+    return 1;
+  }
+}
+
+int nref_backend_rmsnorm(void* h, const float* x, const float* weight, float* y, int64_t n, int64_t d, float eps) {
+  try {
+    static_cast<RefBackend*>(h)->be.rmsnorm(x, tensor_of(weight, 0, d, 1), y, n, eps);
+    return 0;
+  } catch (const std::exception& e) {
+    set_err(e.what());
+    return 1;
+  }
+}
+
+int nref_backend_silu_mul(void* h, float* gate, const float* up, int64_t count) {
+  try {
+    static_cast<RefBackend*>(h)->be.silu_mul(gate, up, count);
     return 0;
   } catch (const std::exception& e) {
     set_err(e.what());

@@ -122,7 +122,7 @@ static void add_bias_case(CudaBackend& be) {
   be.free(dx);
 }
 
-// alloc is zeroed; free(nullptr) and freeing twice are tolerated; bad sizes and unsupported ops throw Error.
+// alloc is zeroed; free(nullptr) and freeing twice are tolerated; bad sizes and weights without data throw Error.
 static void contracts(CudaBackend& be) {
   float* p = be.alloc(100);
   std::vector<float> h(100, 1.f);
@@ -147,7 +147,9 @@ static void contracts(CudaBackend& be) {
     threw = true;
   }
   CHECK(threw);
-  CHECK(!be.supports(nibble::DType::F32));
+  // float weights run on the GPU; quantized ones are refused at load time rather than run on the CPU
+  CHECK(be.supports(nibble::DType::F32) && be.supports(nibble::DType::F16));
+  CHECK(!be.supports(nibble::DType::Q4_0) && !be.supports(nibble::DType::Q8_0) && !be.supports(nibble::DType::Q6_K));
   threw = false;
   try {
     be.attention(nullptr, nullptr, nullptr, nullptr, 1, 0, 6, 4, 16);

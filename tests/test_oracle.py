@@ -166,3 +166,59 @@ def test_oracle_bit_identical_to_reference(shape):
     for neox in (False, True):
         assert np.array_equal(oracle.rope(x, H, D, pos0 + 70000, 5e5, neox),
                               oracle.ref_rope(x, H, D, pos0 + 70000, 5e5, neox))
+
+
+# ---------------------------------------------------------------- the model's other ops (backend.h:54-70)
+# Known answers restated from the reference's own tests (tests/test_ref_ops.cpp:33-37, :98-103, :106-127).
+def test_rmsnorm_known_answer():
+    x = np.array([1, 2, 3, 4], np.float32)
+    y = oracle.rmsnorm(x, np.ones(4, np.float32), 1, 0.0)[0]
+    assert np.allclose(y, x / np.sqrt(7.5), rtol=1e-6, atol=1e-7)
+
+
+def test_silu_mul_known_answer():
+    g = oracle.silu_mul(np.array([0, 1], np.float32), np.array([2, 3], np.float32))
+    assert np.allclose(g, [0.0, 3.0 / (1.0 + np.exp(-1.0))], rtol=1e-6, atol=1e-7)
+
+
+def test_matmul_and_embed_known_answer():
+    w = np.array([[1, 2, 3], [4, 5, 6]], np.float32)
+    x = np.ones((1, 3), np.float32)
+    y = oracle.matmul(w, x, 1)[0]
+    assert np.allclose(y, [6, 15], rtol=1e-6)
+    wh = oracle.f32_to_fp16_bits(w)
+    assert np.array_equal(oracle.matmul(wh, x, 1)[0], y)
+    assert np.array_equal(oracle.embed(wh, np.array([1], np.int32))[0], [4, 5, 6])
+
+
+@pytest.mark.parametrize("dt", ["f32", "f16"])
+@pytest.mark.parametrize("shape", [(1, 3, 5), (5, 37, 72), (9, 64, 130), (3, 1, 1)])
+def test_model_ops_bit_identical_to_reference(dt, shape):
+    if not oracle.have_ref():
+        pytest.skip("oracle/_ref (nibble's own code) is not built here")
+    n, ne1, ne0 = shape
+    rng = np.random.default_rng(n * 1000 + ne1 + ne0)
+    w = (rng.standard_normal((ne1, ne0)) * 0.2).astype(np.float32)
+    if dt == "f16":
+        w = oracle.f32_to_fp16_bits(w)
+    x = rng.standard_normal((n, ne0)).astype(np.float32)
+    assert np.array_equal(oracle.matmul(w, x, n).view(np.uint32), oracle.ref_matmul(w, x, n).view(np.uint32))
+    ids = rng.integers(0, ne1, n).astype(np.int32)
+    assert np.array_equal(oracle.embed(w, ids).view(np.uint32), oracle.ref_embed(w, ids).view(np.uint32))
+    norm_w = rng.standard_normal(ne0).astype(np.float32)
+    for eps in (1e-6, 1e-5, 0.0):
+        assert np.array_equal(oracle.rmsnorm(x * 3, norm_w, n, eps).view(np.uint32),
+                              oracle.ref_rmsnorm(x * 3, norm_w, n, eps).view(np.uint32))
+    g = (rng.standard_normal(n * ne0) * 6).astype(np.float32)
+    u = rng.standard_normal(n * ne0).astype(np.float32)
+    assert np.array_equal(oracle.silu_mul(g, u).view(np.uint32), oracle.ref_silu_mul(g, u).view(np.uint32))
+    assert np.array_equal(oracle.add(g, u).view(np.uint32), oracle.ref_add(g, u).view(np.uint32))
+
+
+def test_embed_out_of_range_matches_reference_error():
+    w = np.zeros((7, 4), np.float32)
+    with pytest.raises(ValueError):
+        oracle.embed(w, np.array([7], np.int32))
+    if oracle.have_ref():
+        with pytest.raises(ValueError, match=r"embed: token id 7 out of range \(n_vocab 7\)"):
+            oracle.ref_embed(w, np.array([7], np.int32))
