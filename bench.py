@@ -12,6 +12,9 @@ Workloads (synthetic seeded inputs of the named shapes; n
   prefill         config 3: TinyLlama-1.1B attention (32 Q / 4 KV heads, theta 1e4), 8 sequences x 2048 bf16
                   tokens x 22 layers = 176 items; a step = fused RoPE/append of all tokens + tcgen05 causal prefill.
                   Metric: TFLOP/s with causal FLOPs 4 * H * D * sum(keys attended).
+  decode_long / decode_ragged   configs 4 and 5 (extra legs of the default run).
+  model_gemv      the weight matmuls of one decode token of a TinyLlama-1.1B-shaped F16 model (the rest of the
+                  Backend on the GPU; bounds a whole-model decode step). Metric: weight bytes / time (HBM GB/s).
 With N > 1 (torchrun, one rank per GPU, NCCL) every rank runs its own shard of the same per-GPU work ("weak"
 scaling: the sequences shard with no collective); value = all ranks' work / max-over-ranks device time.
 
@@ -432,6 +435,82 @@ def decode_long(args, world, rank, local, steps, warmup):
     return res
 
 
+# ---------------------------------------------------------------- the model's weight matmuls at decode
+E6, FF6, Q6, KV6, LAYERS6, VOCAB6 = 2048, 5632, 2048, 256, 22, 32000   # TinyLlama-1.1B
+
+
+def model_gemv(args, world, rank, local, steps, warmup):
+    """The weight matmuls of one decode token of a TinyLlama-1.1B-shaped model with F16 weights through
+    nbl_matmul (n = 1: the weight-streaming GEMV): per layer Q, K, V, O, gate, up and down projections, then the
+    output projection -- Q/K/V and gate/up as one multi-weight launch each (the Transformer's matmul_multi), 89
+    launches reading 2.07 GB of weights, replayed as one CUDA graph. This is what bounds
+    a decode step of the whole Transformer on CudaBackend (attention and the elementwise ops move a few MB).
+    Metric: weight bytes / step time (HBM GB/s); tokens/s = 1 / step time. Weights are random (synthetic)."""
+    import torch
+    import nibble_b200 as nb
+    ctx = nb.Context(local)
+    rng = np.random.default_rng(60 + rank)
+    pool = (rng.standard_normal(VOCAB6 * E6, dtype=np.float32) * 0.02).astype(np.float16)
+    shapes = []
+    for _ in range(LAYERS6):
+        shapes += [(Q6, E6), (KV6, E6), (KV6, E6), (E6, Q6), (FF6, E6), (FF6, E6), (E6, FF6)]
+    shapes.append((VOCAB6, E6))
+    weights = [ctx.weight(pool[: r * c].reshape(r, c)) for r, c in shapes]
+    del pool
+    x = {c: torch.randn(c, device="cuda") for c in (E6, FF6)}
+    y = {w: torch.empty(w, device="cuda") for w in (Q6, KV6, E6, FF6, VOCAB6)}
+    y["v"], y["u"] = torch.empty(KV6, device="cuda"), torch.empty(FF6, device="cuda")
+    wbytes = sum(r * c * 2 for r, c in shapes)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+
+    def step():  # as the Transformer calls them: matmul_multi for Q/K/V and for gate/up, matmul for O and down
+        for layer in range(LAYERS6):
+            wq, wk, wv, wo, wg, wu, wd = weights[7 * layer:7 * layer + 7]
+            ctx.matmul_multi([wq, wk, wv], x[E6], [y[Q6], y[KV6], y["v"]], 1)
+            ctx.matmul(wo, x[E6], y[E6], 1)
+            ctx.matmul_multi([wg, wu], x[E6], [y[FF6], y["u"]], 1)
+            ctx.matmul(wd, x[FF6], y[E6], 1)
+        ctx.matmul(weights[-1], x[E6], y[VOCAB6], 1)
+
+    with torch.cuda.stream(side):
+        ctx.set_stream(side.cuda_stream)
+        step()
+        side.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        ctx.set_stream(torch.cuda.current_stream().cuda_stream)
+        step()
+    main = torch.cuda.current_stream()
+    ctx.set_stream(main.cuda_stream)
+    for _ in range(warmup):
+        graph.replay()
+    ctx.check()
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(main)
+    for _ in range(steps):
+        graph.replay()
+    e1.record(main)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
+    ctx.check()
+    del graph
+    for w in weights:
+        w.close()
+    ctx.close()
+    hbm, _, _, src = peaks()
+    ach = wbytes / (ms * 1e-3) / 1e9
+    return {"metric": "model decode weight-matmul HBM GB/s", "value": world * ach, "unit": "GB/s", "ms_per_step": ms,
+            "tokens_per_s_per_gpu": 1e3 / ms, "scaling": "weak",
+            "config": {"workload": "TinyLlama-1.1B decode-step weight matmuls (F16 weights, n = 1)",
+                       "launches_per_step": 4 * LAYERS6 + 1, "weight_bytes": wbytes,
+                       "l2": "weights (2.07 GB) larger than L2; no flush needed"},
+            "roofline": {"kernel": "gemv_kernel", "bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s",
+                         "frac": ach / hbm, "peak_source": src}}
+
+
 # ---------------------------------------------------------------- config 5: ragged paged decode, LPT-balanced
 H5, KV5, SEQ5, LAYERS5, MAXLEN5 = 14, 2, 256, 24, 8192
 
@@ -582,7 +661,7 @@ def main():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["decode_batched", "prefill", "decode_long", "decode_ragged"],
+    ap.add_argument("--workload", choices=["decode_batched", "prefill", "decode_long", "decode_ragged", "model_gemv"],
                     default="decode_batched")
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-3 prefill leg of the default run")
     ap.add_argument("--no-extra", action="store_true", help="skip the config-4/5 legs of the default run")
@@ -607,6 +686,8 @@ def main():
         res = decode_long(args, world, rank, local, args.steps, args.warmup)
     elif args.workload == "decode_ragged":
         res = decode_ragged(args, world, rank, local, args.steps, args.warmup)
+    elif args.workload == "model_gemv":
+        res = model_gemv(args, world, rank, local, args.steps, args.warmup)
     else:
         res = decode_batched(args, world, rank, local)
         if not args.no_prefill:
@@ -614,6 +695,7 @@ def main():
         if not args.no_extra:
             res["decode_long"] = decode_long(args, world, rank, local, legs, 3)
             res["decode_ragged"] = decode_ragged(args, world, rank, local, legs, 3)
+            res["model_decode_gemv"] = model_gemv(args, world, rank, local, legs, 3)
     res.setdefault("scaling", "weak")
     res.update({"n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
                 "vs_baseline": None, "data": "synthetic (seeded N(0,1))"})

@@ -129,8 +129,9 @@ NBL_API int nbl_attention(nbl_ctx* ctx, const float* q, const float* k, const fl
 /* ---- weights and the model's other ops (backend.h:54-70), fp32 device activations ---- */
 /* Uploads a host weight tensor of ne1 rows x ne0 elements, dtype NBL_F32 or NBL_F16, to device memory owned by
  * the context: the device form of a weight Tensor view (src/tensor.h:57-70; nibble's are views of the mmap'd
- * GGUF). An F16 matrix also gets an fp32 copy for multi-row matmuls. Freed by nbl_weight_destroy or with the
- * context. Returns after the upload has completed (the host buffer may be released). */
+ * GGUF). An F16 matrix gets an fp32 copy on its first matmul with more than 8 rows (the SGEMM path; decode-only use
+ * never holds it). Freed by nbl_weight_destroy or with the context. Returns after the upload has completed (the
+ * host buffer may be released). */
 NBL_API int nbl_weight_create(nbl_ctx* ctx, const void* host, int32_t dtype, int64_t ne0, int64_t ne1,
                               nbl_weight** out);
 NBL_API int nbl_weight_destroy(nbl_weight* w);
@@ -146,6 +147,12 @@ NBL_API int nbl_embed(nbl_ctx* ctx, const nbl_weight* table, const int32_t* ids,
  * (cuBLAS, no TF32). Results differ from the CPU's only by fp32 summation order. Backend::matmul_multi is one
  * call per weight, as the reference's contract allows ("results equal separate calls"). */
 NBL_API int nbl_matmul(nbl_ctx* ctx, const nbl_weight* w, const float* x, float* y, int64_t n);
+/* Backend::matmul_multi (backend.h:57-60; CpuBackend::matmul_multi cpu_backend.cpp:146-233): ys[i] = x . ws[i]^T
+ * for `count` weights sharing one input x [n, ne0] (all ws[i] have the same ne0); results equal separate
+ * nbl_matmul calls. For n <= 8 and count <= 4 this is one GEMV launch over all the weights' rows (the model's
+ * Q/K/V and gate/up projections). ws and ys are HOST arrays of count entries. */
+NBL_API int nbl_matmul_multi(nbl_ctx* ctx, const nbl_weight* const* ws, int32_t count, const float* x,
+                             float* const* ys, int64_t n);
 /* Backend::rmsnorm (backend.h:61; cpu::rmsnorm ref_ops.cpp:138-148): y[t] = x[t] / sqrt(mean(x[t]^2) + eps) *
  * weight, evaluated in double like the reference and rounded once to float. weight is an F32 vector (ne1 = 1)
  * of width d = ne0; x, y are [n, d]. */

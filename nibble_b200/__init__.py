@@ -214,6 +214,13 @@ class Context:
         """y[n, ne1] = x[n, ne0] . W^T"""
         check(_abi.lib.nbl_matmul(self.handle, w.handle, _ptr(x), _ptr(y), n))
 
+    def matmul_multi(self, ws, x, ys, n: int):
+        """ys[i][n, ws[i].ne1] = x[n, ne0] . ws[i]^T for weights sharing one input (one launch for n <= 8)."""
+        count = len(ws)
+        warr = (C.c_void_p * count)(*[w.handle.value for w in ws])
+        yarr = (C.c_void_p * count)(*[_ptr(y) for y in ys])
+        check(_abi.lib.nbl_matmul_multi(self.handle, warr, count, _ptr(x), yarr, n))
+
     def rmsnorm(self, x, weight: Weight, y, n: int, eps: float):
         check(_abi.lib.nbl_rmsnorm(self.handle, _ptr(x), weight.handle, _ptr(y), n, eps))
 

@@ -75,6 +75,7 @@ SIGNATURES = {
     "nbl_weight_data": [_P, C.POINTER(_P), C.POINTER(_I32), C.POINTER(_I64), C.POINTER(_I64)],
     "nbl_embed": [_P, _P, _P, _I64, _P],
     "nbl_matmul": [_P, _P, _P, _P, _I64],
+    "nbl_matmul_multi": [_P, _P, _I32, _P, _P, _I64],
     "nbl_rmsnorm": [_P, _P, _P, _P, _I64, C.c_float],
     "nbl_add": [_P, _P, _P, _I64],
     "nbl_copy": [_P, _P, _P, _I64],

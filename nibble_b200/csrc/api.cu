@@ -179,6 +179,19 @@ void release_weight(nbl_weight* w) {
   delete w;
 }
 
+// The fp32 copy an F16 matrix needs for the SGEMM path, made on its first multi-row matmul (so decode-only use
+// never holds it). Allocates once per weight.
+const float* weight_f32(nbl_ctx* ctx, const nbl_weight* cw) {
+  auto* w = const_cast<nbl_weight*>(cw);
+  if (!w->w.f32) {
+    const int64_t count = w->w.ne0 * w->w.ne1;
+    w->w.f32 = static_cast<float*>(device_alloc(static_cast<size_t>(count) * sizeof(float), "weight fp32 copy"));
+    nbl::launch_widen_f16(ctx->stream, w->w.dev, w->w.f32, count, ctx->num_sms);
+    nbl::check_cuda(cudaGetLastError(), "widen launch");
+  }
+  return w->w.f32;
+}
+
 void require_weight(const nbl_ctx* ctx, const nbl_weight* w, const char* what) {
   require(w != nullptr && w->ctx == ctx, std::string(what) + ": weight is NULL or belongs to another context");
 }
@@ -686,13 +699,7 @@ int nbl_weight_create(nbl_ctx* ctx, const void* host, int32_t dtype, int64_t ne0
     try {
       w->w.dev = device_alloc(count * elem, "weight");
       nbl::check_cuda(cudaMemcpyAsync(w->w.dev, host, count * elem, cudaMemcpyHostToDevice, ctx->stream), "weight upload");
-      if (dtype == NBL_F32) {
-        w->w.f32 = static_cast<float*>(w->w.dev);
-      } else if (ne1 > 1) {  // matrices: an fp32 copy for the SGEMM path
-        w->w.f32 = static_cast<float*>(device_alloc(count * sizeof(float), "weight fp32 copy"));
-        nbl::launch_widen_f16(ctx->stream, w->w.dev, w->w.f32, static_cast<int64_t>(count), ctx->num_sms);
-        nbl::check_cuda(cudaGetLastError(), "widen launch");
-      }
+      if (dtype == NBL_F32) w->w.f32 = static_cast<float*>(w->w.dev);  // F16: fp32 copy on first SGEMM use
       nbl::check_cuda(cudaStreamSynchronize(ctx->stream), "weight upload");
       ctx->weights.push_back(w);
     } catch (...) {
@@ -751,11 +758,45 @@ int nbl_matmul(nbl_ctx* ctx, const nbl_weight* w, const float* x, float* y, int6
     require(n >= 0 && n <= INT32_MAX && w->w.ne0 <= INT32_MAX && w->w.ne1 <= INT32_MAX, "matmul: bad size");
     if (n == 0) return;
     use_device(ctx);
-    if (n <= nbl::kGemvMaxRows || !w->w.f32) {
-      nbl::launch_gemv(ctx->stream, w->w, x, y, n);
+    if (n <= nbl::kGemvMaxRows) {
+      nbl::launch_gemv(ctx->stream, w->w, x, y, n, ctx->num_sms);
       nbl::check_cuda(cudaGetLastError(), "matmul launch");
     } else {
-      nbl::gemm_f32(cublas_handle(ctx), ctx->stream, w->w.f32, x, y, w->w.ne0, w->w.ne1, n);
+      nbl::gemm_f32(cublas_handle(ctx), ctx->stream, weight_f32(ctx, w), x, y, w->w.ne0, w->w.ne1, n);
+    }
+  });
+}
+
+int nbl_matmul_multi(nbl_ctx* ctx, const nbl_weight* const* ws, int32_t count, const float* x, float* const* ys,
+                     int64_t n) {
+  return guarded([&] {
+    require(ctx && ws && ys && x, "matmul_multi: NULL argument");
+    require(count > 0, "matmul_multi: count must be positive");
+    require(n >= 0 && n <= INT32_MAX, "matmul_multi: bad n");
+    for (int32_t i = 0; i < count; ++i) {
+      require_weight(ctx, ws[i], "matmul_multi");
+      require(ys[i] != nullptr, "matmul_multi: output is NULL");
+      require(ws[i]->w.ne0 == ws[0]->w.ne0, "matmul_multi: weights differ in input width");
+      require(ws[i]->w.ne1 <= INT32_MAX, "matmul_multi: bad size");
+    }
+    if (n == 0) return;
+    use_device(ctx);
+    if (n <= nbl::kGemvMaxRows) {
+      for (int32_t i0 = 0; i0 < count; i0 += nbl::kMaxMulti) {
+        const int c = static_cast<int>(std::min<int32_t>(nbl::kMaxMulti, count - i0));
+        const nbl::Weight* w[nbl::kMaxMulti];
+        float* y[nbl::kMaxMulti];
+        for (int i = 0; i < c; ++i) {
+          w[i] = &ws[i0 + i]->w;
+          y[i] = ys[i0 + i];
+        }
+        nbl::launch_gemv_multi(ctx->stream, w, y, c, x, n, ctx->num_sms);
+      }
+      nbl::check_cuda(cudaGetLastError(), "matmul launch");
+    } else {
+      for (int32_t i = 0; i < count; ++i)
+        nbl::gemm_f32(cublas_handle(ctx), ctx->stream, weight_f32(ctx, ws[i]), x, ys[i], ws[i]->w.ne0, ws[i]->w.ne1,
+                      n);
     }
   });
 }

@@ -57,6 +57,17 @@ void CudaBackend::matmul(const Tensor& w, const float* x, float* y, int64_t n) {
   check(nbl_matmul(ctx_, device_weight(w), x, y, n));
 }
 
+void CudaBackend::matmul_multi(std::span<const Tensor* const> ws, const float* x, std::span<float* const> ys,
+                               int64_t n) {
+  if (ws.size() != ys.size()) throw Error("matmul_multi: weights and outputs differ in count");
+  std::vector<const nbl_weight*> dw(ws.size());
+  for (size_t i = 0; i < ws.size(); ++i) {
+    if (ws[i]->ne[0] != ws[0]->ne[0]) return Backend::matmul_multi(ws, x, ys, n);  // one matmul per weight
+    dw[i] = device_weight(*ws[i]);
+  }
+  check(nbl_matmul_multi(ctx_, dw.data(), static_cast<int32_t>(dw.size()), x, ys.data(), n));
+}
+
 void CudaBackend::rmsnorm(const float* x, const Tensor& weight, float* y, int64_t n, float eps) {
   if (weight.type != DType::F32) throw Error("rmsnorm: weight must be an F32 tensor");
   check(nbl_rmsnorm(ctx_, x, device_weight(weight), y, n, eps));

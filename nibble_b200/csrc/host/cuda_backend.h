@@ -52,6 +52,8 @@ class CudaBackend final : public Backend {
 
   void embed(const Tensor& table, std::span<const int32_t> ids, float* out) override;
   void matmul(const Tensor& w, const float* x, float* y, int64_t n) override;
+  // One launch for the weights sharing x at decode sizes (the reference's contract: equal to separate calls).
+  void matmul_multi(std::span<const Tensor* const> ws, const float* x, std::span<float* const> ys, int64_t n) override;
   void rmsnorm(const float* x, const Tensor& weight, float* y, int64_t n, float eps) override;
   void add(float* x, const float* y, int64_t count) override;
   void copy(float* dst, const float* src, int64_t count) override;

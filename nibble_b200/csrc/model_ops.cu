@@ -33,78 +33,162 @@ __global__ void embed_kernel(const T* __restrict__ table, const int32_t* __restr
 }
 
 // ---------------------------------------------------------------- matmul, decode-sized n (GEMV)
-// y[t][r] = sum_k x[t][k] * w[r][k] for t < NT. One warp per kRowsPerWarp weight rows; lane l reads 16-byte
-// chunks l, l+32, ... of each row (kVec elements), so a warp streams whole 512-byte segments. x (NT rows) is
-// read through the read-only cache: every warp of every CTA reads the same few KB.
-constexpr int kGemvThreads = 256;
-constexpr int kRowsPerWarp = 2;
+// y_j[t][r] = sum_k x[t][k] * w_j[r][k] for t < NT over up to kMaxMulti weights sharing x (Backend::matmul_multi:
+// the Q/K/V and gate/up projections) in one launch: their rows are numbered consecutively. A fixed grid (a few CTAs
+// per SM) of warps walks the rows with a grid stride; a row is cut into groups of 32 x kUnroll 16-byte chunks
+// (lane l takes chunks l, l + 32, ...), and the next (row, group)'s chunks are loaded before the current one is
+// used, so every warp keeps two groups (8 KB) of weight in flight and never waits on a CTA launch. x (NT rows)
+// is read through the read-only cache: every warp reads the same few KB.
+constexpr int kGemvThreads = 128;
+constexpr int kGemvCtasPerSm = 4;  // at most; 128 threads at 128 registers: the register file holds exactly 4 CTAs
+constexpr int kUnroll = 8;
 
-template <typename T, int NT>
-__global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const T* __restrict__ w, const float* __restrict__ x,
-                                                            float* __restrict__ y, int64_t ne0, int64_t ne1) {
-  constexpr int kVec = 16 / sizeof(T);  // weight elements per 16-byte load
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t r0 = (int64_t(blockIdx.x) * (kGemvThreads / 32) + warp) * kRowsPerWarp;
-  if (r0 >= ne1) return;
-  float acc[kRowsPerWarp][NT];
+template <int U, typename T>
+__device__ __forceinline__ void gemv_load(uint4 (&raw)[U], const T* wr, int64_t base, int lane, int64_t n_chunks) {
 #pragma unroll
-  for (int i = 0; i < kRowsPerWarp; ++i)
+  for (int u = 0; u < U; ++u) {
+    const int64_t c = base + lane + 32 * u;
+    raw[u] = c < n_chunks ? __ldg(reinterpret_cast<const uint4*>(wr) + c) : make_uint4(0, 0, 0, 0);
+  }
+}
+
+// Weight j of global row r (rows numbered consecutively over the batch): its row pointer, output column base and
+// row count. A static scan, so the parameter block is never indexed dynamically.
+template <typename T>
+__device__ __forceinline__ void gemv_row(const GemvBatch& b, int64_t r, int64_t ne0, const T*& wr, float*& ybase,
+                                         int64_t& local, int64_t& rows_j) {
+  int64_t begin = 0;
+  wr = static_cast<const T*>(b.w[0]);
+  ybase = b.y[0];
+  rows_j = b.row_end[0];
+  bool found = r < b.row_end[0];
 #pragma unroll
-    for (int t = 0; t < NT; ++t) acc[i][t] = 0.f;
-  const int64_t n_chunks = ne0 / kVec;
-#pragma unroll 2
-  for (int64_t c = lane; c < n_chunks; c += 32) {
-    float wv[kRowsPerWarp][kVec];
-#pragma unroll
-    for (int i = 0; i < kRowsPerWarp; ++i) {
-      const int64_t r = min(r0 + i, ne1 - 1);  // a missing last row re-reads a valid one; its sum is dropped
-      const uint4 raw = __ldg(reinterpret_cast<const uint4*>(w + r * ne0) + c);
-      if constexpr (sizeof(T) == 4) {
-        wv[i][0] = __uint_as_float(raw.x);
-        wv[i][1] = __uint_as_float(raw.y);
-        wv[i][2] = __uint_as_float(raw.z);
-        wv[i][3] = __uint_as_float(raw.w);
-      } else {
-        const uint32_t u[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&u[j]));
-          wv[i][2 * j] = f.x;
-          wv[i][2 * j + 1] = f.y;
-        }
-      }
+  for (int i = 1; i < kMaxMulti; ++i)
+    if (i < b.count && !found && r < b.row_end[i]) {
+      found = true;
+      wr = static_cast<const T*>(b.w[i]);
+      ybase = b.y[i];
+      begin = b.row_end[i - 1];
+      rows_j = b.row_end[i] - b.row_end[i - 1];
     }
+  local = r - begin;
+  wr += local * ne0;
+}
+
+// XREG (one activation row whose width fits one group, n_chunks <= 32 * kUnroll): each lane holds its slice of x --
+// the kVec elements of each of its chunks, at most 64 floats -- in registers, so only the weights pass through L1
+// (with x read through L1 as well, a 16-byte weight chunk costs 48 bytes of L1 traffic, and L1, not DRAM, limits
+// the large matrices).
+template <typename T, int NT, bool XREG>
+__global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvBatch b, const float* __restrict__ x,
+                                                            int64_t ne0) {
+  static_assert(!XREG || NT == 1, "x in registers holds one activation row");
+  constexpr int kVec = 16 / sizeof(T);  // weight elements per 16-byte load
+  constexpr int kGroup = 32 * kUnroll;  // chunks per (row, group) item
+  const int lane = threadIdx.x & 31;
+  // Let the next kernel in the stream launch now: a dependent GEMV starts streaming its own weights while this one
+  // finishes (it reads this one's output only after its griddepcontrol.wait).
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  int64_t total = b.row_end[0];
 #pragma unroll
-    for (int t = 0; t < NT; ++t) {
-      const float* xt = x + t * ne0 + c * kVec;
+  for (int i = 1; i < kMaxMulti; ++i)
+    if (i < b.count) total = b.row_end[i];
+  const int64_t n_warps = int64_t(gridDim.x) * (kGemvThreads / 32);
+  const int64_t n_chunks = ne0 / kVec;
+  const int64_t groups = (n_chunks + kGroup - 1) / kGroup;
+  int64_t r = int64_t(blockIdx.x) * (kGemvThreads / 32) + (threadIdx.x >> 5);
+  int64_t g = 0;
+  const T* wr = nullptr;
+  float* ybase = nullptr;
+  int64_t local = 0, rows_j = 0;
+  uint4 raw[kUnroll];
+  if (r < total) {
+    gemv_row<T>(b, r, ne0, wr, ybase, local, rows_j);
+    gemv_load<kUnroll>(raw, wr, 0, lane, n_chunks);  // independent of the previous kernel: before the wait
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // x (the previous kernel's output) is visible after this
+  float xr[XREG ? kUnroll : 1][XREG ? kVec : 1];
+  if constexpr (XREG) {
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t c = lane + 32 * u;
 #pragma unroll
       for (int v = 0; v < kVec; v += 4) {
-        const float4 xv = ldg4(xt + v);
-#pragma unroll
-        for (int i = 0; i < kRowsPerWarp; ++i) {
-          acc[i][t] = fmaf(xv.x, wv[i][v], acc[i][t]);
-          acc[i][t] = fmaf(xv.y, wv[i][v + 1], acc[i][t]);
-          acc[i][t] = fmaf(xv.z, wv[i][v + 2], acc[i][t]);
-          acc[i][t] = fmaf(xv.w, wv[i][v + 3], acc[i][t]);
-        }
+        const float4 xv = c < n_chunks ? ldg4(x + c * kVec + v) : make_float4(0.f, 0.f, 0.f, 0.f);
+        xr[u][v] = xv.x, xr[u][v + 1] = xv.y, xr[u][v + 2] = xv.z, xr[u][v + 3] = xv.w;
       }
     }
   }
+  float acc[NT];
 #pragma unroll
-  for (int i = 0; i < kRowsPerWarp; ++i)
+  for (int t = 0; t < NT; ++t) acc[t] = 0.f;
+  while (r < total) {
+    uint4 cur[kUnroll];
 #pragma unroll
-    for (int t = 0; t < NT; ++t) {
-      float s = acc[i][t];
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-      acc[i][t] = s;
+    for (int u = 0; u < kUnroll; ++u) cur[u] = raw[u];
+    const int64_t base = g * kGroup;
+    // the next item of this warp: the row's next group, or the first group of its next row
+    float* y_cur = ybase;
+    const int64_t local_cur = local, rows_cur = rows_j;
+    const bool row_done = g + 1 == groups;
+    int64_t r2 = r, g2 = g + 1;
+    if (row_done) {
+      r2 = r + n_warps;
+      g2 = 0;
     }
-  if (lane == 0)
+    if (r2 < total) {
+      if (row_done) gemv_row<T>(b, r2, ne0, wr, ybase, local, rows_j);
+      gemv_load<kUnroll>(raw, wr, g2 * kGroup, lane, n_chunks);
+    }
 #pragma unroll
-    for (int i = 0; i < kRowsPerWarp; ++i)
-      if (r0 + i < ne1)
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t c = base + lane + 32 * u;
+      if (c < n_chunks) {
+        float wv[kVec];
+        if constexpr (sizeof(T) == 4) {
+          wv[0] = __uint_as_float(cur[u].x);
+          wv[1] = __uint_as_float(cur[u].y);
+          wv[2] = __uint_as_float(cur[u].z);
+          wv[3] = __uint_as_float(cur[u].w);
+        } else {
+          const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&cur[u].x));
+          const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&cur[u].y));
+          const float2 f2 = __half22float2(*reinterpret_cast<const __half2*>(&cur[u].z));
+          const float2 f3 = __half22float2(*reinterpret_cast<const __half2*>(&cur[u].w));
+          wv[0] = f0.x, wv[1] = f0.y, wv[2] = f1.x, wv[3] = f1.y, wv[4] = f2.x, wv[5] = f2.y, wv[6] = f3.x, wv[7] = f3.y;
+        }
+        if constexpr (XREG) {
 #pragma unroll
-        for (int t = 0; t < NT; ++t) y[t * ne1 + r0 + i] = acc[i][t];
+          for (int v = 0; v < kVec; ++v) acc[0] = fmaf(xr[u][v], wv[v], acc[0]);
+        } else {
+#pragma unroll
+          for (int t = 0; t < NT; ++t) {
+            const float* xt = x + t * ne0 + c * kVec;
+#pragma unroll
+            for (int v = 0; v < kVec; v += 4) {
+              const float4 xv = ldg4(xt + v);
+              acc[t] = fmaf(xv.x, wv[v], acc[t]);
+              acc[t] = fmaf(xv.y, wv[v + 1], acc[t]);
+              acc[t] = fmaf(xv.z, wv[v + 2], acc[t]);
+              acc[t] = fmaf(xv.w, wv[v + 3], acc[t]);
+            }
+          }
+        }
+      }
+    }
+    if (row_done) {
+#pragma unroll
+      for (int t = 0; t < NT; ++t) {
+        float s = acc[t];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        if (lane == 0) y_cur[t * rows_cur + local_cur] = s;
+        acc[t] = 0.f;
+      }
+    }
+    r = r2;
+    g = g2;
+  }
 }
 
 // Any ne0 (no alignment assumptions): one warp per output row and activation row, scalar loads.
@@ -205,24 +289,45 @@ int elementwise_grid(int64_t count, int num_sms) {
   return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, int64_t(num_sms) * 8)));
 }
 
-template <typename T, int NT>
-void gemv_t(cudaStream_t st, const void* w, const float* x, float* y, int64_t ne0, int64_t ne1) {
-  const int64_t rows_per_cta = (kGemvThreads / 32) * kRowsPerWarp;
-  const int64_t grid = (ne1 + rows_per_cta - 1) / rows_per_cta;
-  gemv_kernel<T, NT><<<static_cast<unsigned>(grid), kGemvThreads, 0, st>>>(static_cast<const T*>(w), x, y, ne0, ne1);
+// Launched with programmatic stream serialization: the kernel may start while the previous one in the stream is
+// still running, and orders itself behind it with griddepcontrol.wait before reading x.
+template <typename T, int NT, bool XREG = false>
+void gemv_t(cudaStream_t st, const GemvBatch& b, const float* x, int64_t ne0, int num_sms) {
+  // resident CTAs per SM for this instantiation (its register count decides: 3 or 4)
+  static const int per_sm = [] {
+    int n = 0;
+    check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_kernel<T, NT, XREG>, kGemvThreads, 0),
+               "gemv occupancy");
+    return std::max(1, std::min(n, kGemvCtasPerSm));
+  }();
+  const int64_t warps_per_cta = kGemvThreads / 32;
+  const int64_t grid = std::min<int64_t>((b.row_end[b.count - 1] + warps_per_cta - 1) / warps_per_cta,
+                                         int64_t(num_sms) * per_sm);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(kGemvThreads);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  check_cuda(cudaLaunchKernelEx(&cfg, gemv_kernel<T, NT, XREG>, b, x, ne0), "gemv launch");
 }
 
 template <typename T>
-void gemv_dispatch(cudaStream_t st, const void* w, const float* x, float* y, int64_t ne0, int64_t ne1, int64_t n) {
+void gemv_dispatch(cudaStream_t st, const GemvBatch& b, const float* x, int64_t ne0, int64_t n, int sms) {
+  constexpr int64_t kVec = 16 / sizeof(T);
+  if (n == 1 && ne0 / kVec <= 32 * kUnroll) return gemv_t<T, 1, true>(st, b, x, ne0, sms);
   switch (n) {
-    case 1: return gemv_t<T, 1>(st, w, x, y, ne0, ne1);
-    case 2: return gemv_t<T, 2>(st, w, x, y, ne0, ne1);
-    case 3: return gemv_t<T, 3>(st, w, x, y, ne0, ne1);
-    case 4: return gemv_t<T, 4>(st, w, x, y, ne0, ne1);
-    case 5: return gemv_t<T, 5>(st, w, x, y, ne0, ne1);
-    case 6: return gemv_t<T, 6>(st, w, x, y, ne0, ne1);
-    case 7: return gemv_t<T, 7>(st, w, x, y, ne0, ne1);
-    default: return gemv_t<T, 8>(st, w, x, y, ne0, ne1);
+    case 1: return gemv_t<T, 1>(st, b, x, ne0, sms);
+    case 2: return gemv_t<T, 2>(st, b, x, ne0, sms);
+    case 3: return gemv_t<T, 3>(st, b, x, ne0, sms);
+    case 4: return gemv_t<T, 4>(st, b, x, ne0, sms);
+    case 5: return gemv_t<T, 5>(st, b, x, ne0, sms);
+    case 6: return gemv_t<T, 6>(st, b, x, ne0, sms);
+    case 7: return gemv_t<T, 7>(st, b, x, ne0, sms);
+    default: return gemv_t<T, 8>(st, b, x, ne0, sms);
   }
 }
 
@@ -248,20 +353,42 @@ bool gemv_vector_ok(const Weight& w, const float* x) {
          (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
 }
 
-void launch_gemv(cudaStream_t st, const Weight& w, const float* x, float* y, int64_t n) {
-  if (gemv_vector_ok(w, x)) {
-    for (int64_t t0 = 0; t0 < n; t0 += kGemvMaxRows) {
-      const int64_t nt = std::min<int64_t>(kGemvMaxRows, n - t0);
-      if (w.dtype == NBL_F32) gemv_dispatch<float>(st, w.dev, x + t0 * w.ne0, y + t0 * w.ne1, w.ne0, w.ne1, nt);
-      else gemv_dispatch<__half>(st, w.dev, x + t0 * w.ne0, y + t0 * w.ne1, w.ne0, w.ne1, nt);
+void launch_gemv_multi(cudaStream_t st, const Weight* const* ws, float* const* ys, int count, const float* x,
+                       int64_t n, int num_sms) {
+  const Weight& w0 = *ws[0];
+  bool vec = true;
+  for (int i = 0; i < count; ++i) vec = vec && gemv_vector_ok(*ws[i], x) && ws[i]->dtype == w0.dtype;
+  if (!vec) {
+    for (int i = 0; i < count; ++i) {
+      const Weight& w = *ws[i];
+      const dim3 grid(static_cast<unsigned>((w.ne1 + 7) / 8), static_cast<unsigned>(n));
+      if (w.dtype == NBL_F32)
+        gemv_scalar_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(w.dev), x, ys[i], w.ne0, w.ne1, n);
+      else
+        gemv_scalar_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half*>(w.dev), x, ys[i], w.ne0, w.ne1, n);
     }
-  } else {
-    const dim3 grid(static_cast<unsigned>((w.ne1 + 7) / 8), static_cast<unsigned>(n));
-    if (w.dtype == NBL_F32)
-      gemv_scalar_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(w.dev), x, y, w.ne0, w.ne1, n);
-    else
-      gemv_scalar_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half*>(w.dev), x, y, w.ne0, w.ne1, n);
+    return;
   }
+  for (int64_t t0 = 0; t0 < n; t0 += kGemvMaxRows) {
+    const int64_t nt = std::min<int64_t>(kGemvMaxRows, n - t0);
+    GemvBatch b{};
+    b.count = count;
+    int64_t rows = 0;
+    for (int i = 0; i < count; ++i) {
+      b.w[i] = ws[i]->dev;
+      b.y[i] = ys[i] + t0 * ws[i]->ne1;
+      rows += ws[i]->ne1;
+      b.row_end[i] = rows;
+    }
+    if (w0.dtype == NBL_F32) gemv_dispatch<float>(st, b, x + t0 * w0.ne0, w0.ne0, nt, num_sms);
+    else gemv_dispatch<__half>(st, b, x + t0 * w0.ne0, w0.ne0, nt, num_sms);
+  }
+}
+
+void launch_gemv(cudaStream_t st, const Weight& w, const float* x, float* y, int64_t n, int num_sms) {
+  const Weight* ws[1] = {&w};
+  float* ys[1] = {y};
+  launch_gemv_multi(st, ws, ys, 1, x, n, num_sms);
 }
 
 void gemm_f32(cublasHandle_t h, cudaStream_t st, const float* w_f32, const float* x, float* y, int64_t ne0, int64_t ne1,

@@ -10,7 +10,7 @@ namespace nbl {
 constexpr int64_t kGemvMaxRows = 8;
 
 // One weight tensor on the device: ne1 rows of ne0 elements (F32 or F16), plus an fp32 copy of an F16 matrix for
-// the SGEMM path (equal to `dev` for F32).
+// the SGEMM path (equal to `dev` for F32; made on an F16 matrix's first multi-row matmul).
 struct Weight {
   int32_t dtype = NBL_F32;
   int64_t ne0 = 0, ne1 = 0;
@@ -20,7 +20,18 @@ struct Weight {
 
 void launch_embed(cudaStream_t st, const Weight& table, const int32_t* ids, int64_t n, float* out, int num_sms);
 void launch_widen_f16(cudaStream_t st, const void* src, float* dst, int64_t count, int num_sms);
-void launch_gemv(cudaStream_t st, const Weight& w, const float* x, float* y, int64_t n);
+// Up to kMaxMulti weights sharing one input, run as one GEMV launch (rows numbered consecutively).
+constexpr int kMaxMulti = 4;
+struct GemvBatch {
+  const void* w[kMaxMulti];
+  float* y[kMaxMulti];
+  int64_t row_end[kMaxMulti];  // cumulative row counts
+  int count;
+};
+void launch_gemv(cudaStream_t st, const Weight& w, const float* x, float* y, int64_t n, int num_sms);
+// All weights share ne0; n rows of x. Weights of mixed dtype, or unaligned ones, run one scalar launch each.
+void launch_gemv_multi(cudaStream_t st, const Weight* const* ws, float* const* ys, int count, const float* x,
+                       int64_t n, int num_sms);
 void gemm_f32(cublasHandle_t h, cudaStream_t st, const float* w_f32, const float* x, float* y, int64_t ne0, int64_t ne1,
               int64_t n);
 void launch_rmsnorm(cudaStream_t st, const float* x, const float* w, float* y, int64_t n, int64_t d, float eps);

@@ -169,3 +169,24 @@ def test_weight_data_reports_the_upload(nbl_ctx):
     nbl_ctx.copy(back, p.value, 12)
     assert np.array_equal(host(back), w.ravel())
     wt.close()
+
+
+@pytest.mark.parametrize("dt", ["f32", "f16"])
+@pytest.mark.parametrize("n", [1, 4, 8, 20])
+def test_matmul_multi_equals_separate_calls(nbl_ctx, dt, n):
+    """Backend::matmul_multi's contract (backend.h:57-58): results equal separate matmul calls -- here bit for bit,
+    for a Q/K/V-like triple (one GEMV launch for n <= 8) and five weights (more than one launch holds)."""
+    import torch
+    rng = np.random.default_rng(n + 100 * (dt == "f16"))
+    ne0 = 256
+    for rows in ([256, 64, 64], [96, 32, 512, 8, 40]):
+        ws = [nbl_ctx.weight(_weights(rng, r, ne0, dt)) for r in rows]
+        x = dev(rng.standard_normal((n, ne0)).astype(np.float32))
+        ys = [torch.full((n, r), float("nan"), device="cuda") for r in rows]
+        nbl_ctx.matmul_multi(ws, x, ys, n)
+        for w, y, r in zip(ws, ys, rows):
+            single = torch.full((n, r), float("nan"), device="cuda")
+            nbl_ctx.matmul(w, x, single, n)
+            assert np.array_equal(host(y).view(np.uint32), host(single).view(np.uint32))
+        for w in ws:
+            w.close()
