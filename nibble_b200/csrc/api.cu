@@ -426,7 +426,7 @@ int nbl_attention(nbl_ctx* ctx, const float* q, const float* k, const float* v, 
                 std::to_string(head_dim) + " (n_heads must be a multiple of n_kv_heads; head_dim <= 256)");
     use_device(ctx);
     const float scale = 1.0f / std::sqrt(static_cast<float>(head_dim));
-    nbl::launch_attention_f32(ctx->stream, q, k, v, out, n, pos0, n_heads, n_kv_heads, head_dim, scale);
+    nbl::launch_attention_f32(ctx->stream, q, k, v, out, n, pos0, n_heads, n_kv_heads, head_dim, scale, ctx->num_sms);
   });
 }
 

@@ -4,17 +4,21 @@
 // head h / (n_heads / n_kv_heads).
 //
 // This is the drop-in path for a Transformer that keeps nibble's flat fp32 caches; the paged fp16/bf16 kernels
-// (decode.cu, prefill.cu) are the fast paths. One warp per (row, head): keys in chunks of 32 (one per lane)
-// with an online softmax, then the chunk's p_j * v_j accumulated with lanes over head dimensions. Scores are
-// q.k * (1/sqrtf(head_dim)) like the reference; exp is expf; sums are fp32 (the reference sums the softmax
-// denominator in double), so results agree to ~1e-6 relative.
+// (decode.cu, prefill.cu) are the fast paths. One CTA per (row, head); its warps take the row's keys in chunks of
+// 32 (warp w: chunks w, w + W, ...). A warp stages its chunk of K and V in shared memory with coalesced 16-byte
+// loads (K rows padded by one float, so lane i reading key i is conflict-free), each lane scores one key, an online
+// softmax keeps (m, l, o) per warp, and the chunk's p_j * v_j is accumulated with lanes over head dimensions. The
+// warps' states are merged at the end. Scores are q.k * (1/sqrtf(head_dim)) accumulated over d in
+// order like the reference; exp is expf; sums are fp32 (the reference sums the softmax denominator in double), so
+// results agree to ~1e-6 relative.
+#include <atomic>
+
 #include "nbl_device.cuh"
 #include "nbl_internal.h"
 
 namespace nbl {
 namespace {
 
-constexpr int kWarps = 4;
 constexpr int kMaxDimPerLane = 8;  // head_dim <= 256
 
 __device__ __forceinline__ float warp_max(float v) {
@@ -28,21 +32,50 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
-__global__ void __launch_bounds__(kWarps * 32) attention_f32_kernel(const float* __restrict__ q,
-                                                                    const float* __restrict__ k,
-                                                                    const float* __restrict__ v,
-                                                                    float* __restrict__ out, int64_t n, int64_t pos0,
-                                                                    int64_t n_heads, int64_t n_kv_heads, int head_dim,
-                                                                    float scale) {
-  extern __shared__ float q_smem[];
+// Shared memory: q [head_dim], per warp a K chunk [32][head_dim + 1], a V chunk [32][head_dim] and its final
+// (m, l, o[head_dim]).
+__host__ __device__ constexpr size_t attn_smem_floats(int warps, int head_dim) {
+  return size_t(head_dim) + size_t(warps) * (32 * (2 * head_dim + 1) + head_dim + 2);
+}
+
+// Copies `cnt` rows of head_dim floats (global row stride `stride`) into shared rows of stride ld, with 16-byte loads
+// when every row start is 16-byte aligned and head_dim % 4 == 0.
+__device__ __forceinline__ void stage_rows(float* dst, int ld, const float* src, int64_t stride, int cnt,
+                                           int head_dim, bool vec, int lane) {
+  if (vec) {
+    const int q4 = head_dim / 4;
+    for (int e = lane; e < cnt * q4; e += 32) {
+      const int row = e / q4, c = e - row * q4;
+      const float4 x = __ldg(reinterpret_cast<const float4*>(src + row * stride) + c);
+      float* o = dst + row * ld + 4 * c;
+      o[0] = x.x, o[1] = x.y, o[2] = x.z, o[3] = x.w;
+    }
+  } else {
+    for (int e = lane; e < cnt * head_dim; e += 32) {
+      const int row = e / head_dim, d = e - row * head_dim;
+      dst[row * ld + d] = __ldg(src + row * stride + d);
+    }
+  }
+}
+
+template <int W>
+__global__ void __launch_bounds__(W * 32) attention_f32_kernel(const float* __restrict__ q, const float* __restrict__ k,
+                                                               const float* __restrict__ v, float* __restrict__ out,
+                                                               int64_t n, int64_t pos0, int64_t n_heads,
+                                                               int64_t n_kv_heads, int head_dim, float scale,
+                                                               bool vec) {
+  extern __shared__ float smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t idx = int64_t(blockIdx.x) * kWarps + warp;
-  if (idx >= n * n_heads) return;
+  const int64_t idx = blockIdx.x;  // (row t, head h)
   const int64_t t = idx / n_heads, h = idx % n_heads;
   const int64_t kvh = h / (n_heads / n_kv_heads);
-  float* qw = q_smem + warp * head_dim;
-  for (int d = lane; d < head_dim; d += 32) qw[d] = q[idx * head_dim + d];
-  __syncwarp();
+  const int ldk = head_dim + 1;
+  float* q_s = smem;
+  float* k_s = smem + head_dim + size_t(warp) * 32 * (2 * head_dim + 1);
+  float* v_s = k_s + 32 * ldk;
+  float* st = smem + head_dim + size_t(W) * 32 * (2 * head_dim + 1);  // per warp: m, l, o[head_dim]
+  for (int d = threadIdx.x; d < head_dim; d += W * 32) q_s[d] = q[idx * head_dim + d];
+  __syncthreads();
 
   const int64_t len = pos0 + t + 1;
   const int64_t kv_stride = n_kv_heads * head_dim;
@@ -53,35 +86,28 @@ __global__ void __launch_bounds__(kWarps * 32) attention_f32_kernel(const float*
 #pragma unroll
   for (int i = 0; i < kMaxDimPerLane; ++i) o[i] = 0.f;
 
-  for (int64_t j0 = 0; j0 < len; j0 += 32) {
-    const int64_t j = j0 + lane;
+  for (int64_t j0 = int64_t(warp) * 32; j0 < len; j0 += W * 32) {
+    const int cnt = static_cast<int>(len - j0 < 32 ? len - j0 : 32);
+    stage_rows(k_s, ldk, kbase + j0 * kv_stride, kv_stride, cnt, head_dim, vec, lane);
+    stage_rows(v_s, head_dim, vbase + j0 * kv_stride, kv_stride, cnt, head_dim, vec, lane);
+    __syncwarp();
     float s = -INFINITY;
-    if (j < len) {
-      const float* kj = kbase + j * kv_stride;
+    if (lane < cnt) {
+      const float* kr = k_s + lane * ldk;  // row stride head_dim + 1: lanes hit distinct banks
       float dot = 0.f;
-      if ((head_dim & 1) == 0) {  // rows start on 8-byte boundaries: paired loads
-        const float2* k2 = reinterpret_cast<const float2*>(kj);
-        const float2* q2 = reinterpret_cast<const float2*>(qw);
-        for (int d = 0; d < head_dim / 2; ++d) {
-          const float2 kk = k2[d], qq = q2[d];
-          dot = fmaf(qq.x, kk.x, dot);
-          dot = fmaf(qq.y, kk.y, dot);
-        }
-      } else {
-        for (int d = 0; d < head_dim; ++d) dot = fmaf(qw[d], kj[d], dot);
-      }
+      for (int d = 0; d < head_dim; ++d) dot = fmaf(q_s[d], kr[d], dot);
       s = dot * scale;
     }
     const float m_new = fmaxf(m, warp_max(s));  // finite: lane 0's key is always valid
     const float alpha = expf(m - m_new);
-    const float p = (j < len) ? expf(s - m_new) : 0.f;
+    const float p = lane < cnt ? expf(s - m_new) : 0.f;
     l = l * alpha + p;
 #pragma unroll
     for (int i = 0; i < kMaxDimPerLane; ++i) o[i] *= alpha;
-    const int cnt = static_cast<int>(len - j0 < 32 ? len - j0 : 32);
+#pragma unroll 4
     for (int jj = 0; jj < cnt; ++jj) {
       const float pj = __shfl_sync(0xffffffffu, p, jj);
-      const float* vj = vbase + (j0 + jj) * kv_stride;
+      const float* vj = v_s + jj * head_dim;
 #pragma unroll
       for (int i = 0; i < kMaxDimPerLane; ++i) {
         const int d = lane + 32 * i;
@@ -89,25 +115,78 @@ __global__ void __launch_bounds__(kWarps * 32) attention_f32_kernel(const float*
       }
     }
     m = m_new;
+    __syncwarp();  // the chunk buffers are reused by the next chunk
   }
-  const float inv = 1.f / warp_sum(l);
+  // merge the warps: M = max m_w, out = sum_w o_w e^(m_w - M) / sum_w l_w e^(m_w - M)
+  float* my = st + size_t(warp) * (head_dim + 2);
+  const float lw = warp_sum(l);
+  if (lane == 0) {
+    my[0] = m;
+    my[1] = lw;
+  }
 #pragma unroll
   for (int i = 0; i < kMaxDimPerLane; ++i) {
     const int d = lane + 32 * i;
-    if (d < head_dim) out[idx * head_dim + d] = o[i] * inv;
+    if (d < head_dim) my[2 + d] = o[i];
   }
+  __syncthreads();
+  float big = -INFINITY;
+#pragma unroll
+  for (int w = 0; w < W; ++w) big = fmaxf(big, st[size_t(w) * (head_dim + 2)]);
+  float den = 0.f;
+#pragma unroll
+  for (int w = 0; w < W; ++w) {
+    const float mw = st[size_t(w) * (head_dim + 2)];
+    if (mw != -INFINITY) den += st[size_t(w) * (head_dim + 2) + 1] * expf(mw - big);
+  }
+  const float inv = 1.f / den;
+  for (int d = threadIdx.x; d < head_dim; d += W * 32) {
+    float acc = 0.f;
+#pragma unroll
+    for (int w = 0; w < W; ++w) {
+      const float mw = st[size_t(w) * (head_dim + 2)];
+      if (mw != -INFINITY) acc += st[size_t(w) * (head_dim + 2) + 2 + d] * expf(mw - big);
+    }
+    out[idx * head_dim + d] = acc * inv;
+  }
+}
+
+// The widest head each warp count is launched for (shared memory stays under ~140 KB).
+template <int W>
+constexpr int max_dim_for() { return W == 8 ? 64 : W == 4 ? 128 : 256; }
+
+template <int W>
+void launch_w(cudaStream_t st, const float* q, const float* k, const float* v, float* out, int64_t n, int64_t pos0,
+              int64_t n_heads, int64_t n_kv_heads, int64_t head_dim, float scale) {
+  const size_t smem = attn_smem_floats(W, static_cast<int>(head_dim)) * sizeof(float);
+  static std::atomic<uint64_t> configured{0};  // the attribute is per device: set it once on each
+  int dev = 0;
+  check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+  const uint64_t bit = uint64_t(1) << (dev & 63);
+  if (!(configured.load() & bit)) {
+    check_cuda(cudaFuncSetAttribute(attention_f32_kernel<W>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(attn_smem_floats(W, max_dim_for<W>()) * sizeof(float))),
+               "attention smem attribute");
+    configured.fetch_or(bit);
+  }
+  const bool vec = head_dim % 4 == 0 && ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15u) == 0;
+  attention_f32_kernel<W><<<static_cast<unsigned>(n * n_heads), W * 32, smem, st>>>(
+      q, k, v, out, n, pos0, n_heads, n_kv_heads, static_cast<int>(head_dim), scale, vec);
 }
 
 }  // namespace
 
 void launch_attention_f32(cudaStream_t st, const float* q, const float* k, const float* v, float* out, int64_t n,
-                          int64_t pos0, int64_t n_heads, int64_t n_kv_heads, int64_t head_dim, float scale) {
-  const int64_t pairs = n * n_heads;
-  const int64_t blocks = (pairs + kWarps - 1) / kWarps;
-  if (blocks > 0x7fffffff) fail(NBL_E_INVALID, "attention: n * n_heads too large");
-  const size_t smem = size_t(kWarps) * head_dim * sizeof(float);
-  attention_f32_kernel<<<static_cast<unsigned>(blocks), kWarps * 32, smem, st>>>(
-      q, k, v, out, n, pos0, n_heads, n_kv_heads, static_cast<int>(head_dim), scale);
+                          int64_t pos0, int64_t n_heads, int64_t n_kv_heads, int64_t head_dim, float scale,
+                          int num_sms) {
+  if (n * n_heads > 0x7fffffff) fail(NBL_E_INVALID, "attention: n * n_heads too large");
+  // Many (row, head) CTAs (prefill chunks): 2 warps each, small enough that several CTAs share an SM. Few (decode):
+  // as many warps as their K/V chunks fit in shared memory -- 8 up to head_dim 64, 4 up to 128, 2 up to 256.
+  if (n * n_heads >= 4 * int64_t(num_sms))
+    launch_w<2>(st, q, k, v, out, n, pos0, n_heads, n_kv_heads, head_dim, scale);
+  else if (head_dim <= max_dim_for<8>()) launch_w<8>(st, q, k, v, out, n, pos0, n_heads, n_kv_heads, head_dim, scale);
+  else if (head_dim <= max_dim_for<4>()) launch_w<4>(st, q, k, v, out, n, pos0, n_heads, n_kv_heads, head_dim, scale);
+  else launch_w<2>(st, q, k, v, out, n, pos0, n_heads, n_kv_heads, head_dim, scale);
   check_cuda(cudaGetLastError(), "attention launch");
 }
 

@@ -95,7 +95,8 @@ void launch_rope_kv_append(cudaStream_t st, const nbl_kv* kv, const void* q_in, 
                            int32_t row_base = 0, const int32_t* lens = nullptr);
 // attn_f32.cu
 void launch_attention_f32(cudaStream_t st, const float* q, const float* k, const float* v, float* out, int64_t n,
-                          int64_t pos0, int64_t n_heads, int64_t n_kv_heads, int64_t head_dim, float scale);
+                          int64_t pos0, int64_t n_heads, int64_t n_kv_heads, int64_t head_dim, float scale,
+                          int num_sms);
 // decode.cu
 struct DecodePlan {
   int n_splits = 1;

@@ -35,16 +35,17 @@ _ref = None
 
 
 MODEL_CHECK = os.path.join(HERE, "_ref", "nbl_model_check")
+MODEL_BENCH = os.path.join(HERE, "_ref", "nbl_model_bench")
 
 
 def build(with_ref: bool | None = None) -> None:
     """Compiles liboracle.so, and oracle/_ref when the reference tree is present (or with_ref is True): nibble's own
-    code, and -- once nibble_b200/libnibble_cuda.so exists -- the Transformer drop-in check binary."""
+    code, and -- once nibble_b200/libnibble_cuda.so exists -- the Transformer drop-in check and bench binaries."""
     targets = ["oracle"]
     if with_ref or (with_ref is None and os.path.isdir(os.path.join(REF_TREE, "src"))):
         targets.append("ref")
         if os.path.exists(os.path.join(os.path.dirname(HERE), "nibble_b200", "libnibble_cuda.so")):
-            targets.append("model-check")
+            targets += ["model-check", "model-bench"]
     subprocess.run(["make", "-s", "-C", HERE, f"REF={REF_TREE}", "-j8", *targets], check=True)
 
 

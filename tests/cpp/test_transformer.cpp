@@ -22,101 +22,12 @@
 
 #include "backend/cpu/cpu_backend.h"
 #include "cuda_backend.h"
-#include "fp16.h"
-#include "model/transformer.h"
+#include "random_model.h"
 #include "thread_pool.h"
 
 using namespace nibble;
 
 namespace {
-
-struct Model {
-  model::LlamaConfig c;
-  model::Weights w;
-  std::vector<std::vector<float>> f32;      // storage behind the F32 tensors
-  std::vector<std::vector<uint16_t>> f16;   // storage behind the F16 tensors
-};
-
-Tensor view(DType t, int n_dims, int64_t ne0, int64_t ne1, const void* data) {
-  Tensor x;
-  x.type = t;
-  x.n_dims = n_dims;
-  x.ne = {ne0, ne1, 1, 1};
-  x.data = data;
-  return x;
-}
-
-// A weight matrix [out rows][in] of N(0, 1/in) values, stored F16 or F32.
-Tensor matrix(Model& m, std::mt19937_64& rng, int64_t in, int64_t out, bool f16) {
-  std::normal_distribution<float> nd(0.f, 1.f / std::sqrt(static_cast<float>(in)));
-  std::vector<float> v(static_cast<size_t>(in * out));
-  for (float& x : v) x = nd(rng);
-  if (f16) {
-    std::vector<uint16_t> h(v.size());
-    for (size_t i = 0; i < v.size(); ++i) h[i] = fp32_to_fp16(v[i]);
-    m.f16.push_back(std::move(h));
-    return view(DType::F16, 2, in, out, m.f16.back().data());
-  }
-  m.f32.push_back(std::move(v));
-  return view(DType::F32, 2, in, out, m.f32.back().data());
-}
-
-Tensor vec(Model& m, std::mt19937_64& rng, int64_t n, float mean, float sd) {
-  std::normal_distribution<float> nd(mean, sd);
-  std::vector<float> v(static_cast<size_t>(n));
-  for (float& x : v) x = nd(rng);
-  m.f32.push_back(std::move(v));
-  return view(DType::F32, 1, n, 1, m.f32.back().data());
-}
-
-void build(Model& m, bool qwen, uint64_t seed) {
-  std::mt19937_64 rng(seed);
-  auto& c = m.c;
-  c.arch = qwen ? "qwen2" : "llama";
-  c.n_layers = 2;
-  c.n_embd = 256;
-  c.n_ff = 512;
-  c.n_heads = qwen ? 4 : 8;
-  c.n_kv_heads = 2;
-  c.head_dim = c.n_embd / c.n_heads;
-  c.n_vocab = 3000;
-  c.n_ctx_train = 4096;
-  c.rope_base = qwen ? 1e6f : 5e5f;
-  c.rms_eps = 1e-6f;
-  c.rope_neox = qwen;
-  c.qkv_bias = qwen;
-  m.f32.reserve(64);  // tensors keep pointers into these vectors: no reallocation of the outer vectors
-  m.f16.reserve(64);
-  const bool f16 = qwen;
-  const int64_t E = c.n_embd, Q = c.n_heads * c.head_dim, KV = c.n_kv_heads * c.head_dim;
-  m.w.token_embd = matrix(m, rng, E, c.n_vocab, f16);
-  m.w.output_norm = vec(m, rng, E, 1.f, 0.1f);
-  m.w.output = matrix(m, rng, E, c.n_vocab, f16);
-  if (!qwen) {
-    std::vector<float> ff(static_cast<size_t>(c.head_dim / 2));
-    for (size_t i = 0; i < ff.size(); ++i) ff[i] = i < ff.size() / 2 ? 1.f : 8.f;  // llama-3 style low/high bands
-    m.f32.push_back(std::move(ff));
-    m.w.rope_freqs = view(DType::F32, 1, c.head_dim / 2, 1, m.f32.back().data());
-  }
-  for (int64_t l = 0; l < c.n_layers; ++l) {
-    model::LayerWeights L;
-    L.attn_norm = vec(m, rng, E, 1.f, 0.1f);
-    L.wq = matrix(m, rng, E, Q, f16);
-    L.wk = matrix(m, rng, E, KV, f16);
-    L.wv = matrix(m, rng, E, KV, f16);
-    L.wo = matrix(m, rng, Q, E, f16);
-    L.ffn_norm = vec(m, rng, E, 1.f, 0.1f);
-    L.w_gate = matrix(m, rng, E, c.n_ff, f16);
-    L.w_up = matrix(m, rng, E, c.n_ff, f16);
-    L.w_down = matrix(m, rng, c.n_ff, E, f16);
-    if (qwen) {
-      L.bq = vec(m, rng, Q, 0.f, 0.5f);
-      L.bk = vec(m, rng, KV, 0.f, 0.5f);
-      L.bv = vec(m, rng, KV, 0.f, 0.5f);
-    }
-    m.w.layers.push_back(L);
-  }
-}
 
 int failures = 0;
 
@@ -137,8 +48,9 @@ void compare(const char* what, const std::vector<float>& gpu, const std::vector<
 }
 
 void run(bool qwen) {
-  Model m;
-  build(m, qwen, qwen ? 11 : 22);
+  nbl_test::Model m;
+  // qwen2-style: 4 heads of 64, F16 weights; llama-style: 8 heads of 32, F32 weights
+  nbl_test::build(m, {qwen, qwen, 2, 256, 512, qwen ? 4 : 8, 2, 3000}, qwen ? 11 : 22);
   const int64_t n_ctx = 256, max_batch = 32;
   ThreadPool pool(4);
   cpu::CpuBackend cpu_be(pool);

@@ -141,3 +141,20 @@ def test_config1_qwen_prefill_then_decode_every_step(nbl_ctx):
     for t in range(128, 256):
         step(t, 1)
     assert worst <= 1e-4
+
+
+@pytest.mark.parametrize("n,pos0,H,KV,D", [(1, 999, 8, 2, 256), (3, 500, 4, 4, 160), (2, 2000, 32, 4, 64),
+                                           (40, 0, 2, 1, 130), (1, 0, 4, 2, 64), (5, 31, 6, 3, 96)])
+def test_attention_wide_heads_and_long_context(nbl_ctx, n, pos0, H, KV, D):
+    """head_dim above 128 (the 4-warp configuration), contexts spanning many 32-key chunks per warp, a single key,
+    and keys that end inside a warp's first chunk; against the C oracle (nibble's scalar attention)."""
+    import torch
+    rng = np.random.default_rng(n * 7 + pos0 + D)
+    L = pos0 + n
+    q = rng.standard_normal((n, H, D)).astype(np.float32)
+    k = rng.standard_normal((L, KV, D)).astype(np.float32)
+    v = rng.standard_normal((L, KV, D)).astype(np.float32)
+    out = torch.full((n, H, D), float("nan"), device="cuda")
+    nbl_ctx.attention(dev(q), dev(k), dev(v), out, n, pos0, H, KV, D)
+    ref = oracle.attention(q, k, v, n, pos0, H, KV, D)
+    assert max_rel_err_per_head(host(out), ref) <= 1e-4
