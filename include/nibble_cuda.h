@@ -44,7 +44,9 @@ typedef enum {
   NBL_E_DEVICE = 5       /* a kernel found an out-of-range device-side index (see nbl_ctx_check) */
 } nbl_status;
 
-typedef enum { NBL_F32 = 0, NBL_F16 = 1, NBL_BF16 = 2 } nbl_dtype;
+/* Element types. The quantized weight types are GGUF's block formats byte for byte (src/quant.h:30-60):
+ * Q4_0 (18-byte blocks of 32), Q5_0 (22-byte blocks), Q8_0 (34-byte blocks). */
+typedef enum { NBL_F32 = 0, NBL_F16 = 1, NBL_BF16 = 2, NBL_Q4_0 = 3, NBL_Q5_0 = 4, NBL_Q8_0 = 5 } nbl_dtype;
 
 typedef struct nbl_ctx nbl_ctx; /* device, stream, scratch, RoPE tables, allocation registry */
 typedef struct nbl_kv nbl_kv;   /* one paged K/V pool */
@@ -127,25 +129,27 @@ NBL_API int nbl_attention(nbl_ctx* ctx, const float* q, const float* k, const fl
                   int64_t n_heads, int64_t n_kv_heads, int64_t head_dim);
 
 /* ---- weights and the model's other ops (backend.h:54-70), fp32 device activations ---- */
-/* Uploads a host weight tensor of ne1 rows x ne0 elements, dtype NBL_F32 or NBL_F16, to device memory owned by
- * the context: the device form of a weight Tensor view (src/tensor.h:57-70; nibble's are views of the mmap'd
- * GGUF). An F16 matrix gets an fp32 copy on its first matmul with more than 8 rows (the SGEMM path; decode-only use
+/* Uploads a host weight tensor of ne1 rows x ne0 elements, dtype NBL_F32, NBL_F16, NBL_Q4_0, NBL_Q5_0 or NBL_Q8_0
+ * (quantized: the GGUF block bytes row after row, ne0 % 32 == 0; they are repacked into an internal aligned
+ * layout), to device memory owned by the context: the device form of a weight Tensor view (src/tensor.h:57-70;
+ * nibble's are views of the mmap'd GGUF). An F16 matrix gets an fp32 copy on its first matmul with more than 8 rows (the SGEMM path; decode-only use
  * never holds it). Freed by nbl_weight_destroy or with the context. Returns after the upload has completed (the
  * host buffer may be released). */
 NBL_API int nbl_weight_create(nbl_ctx* ctx, const void* host, int32_t dtype, int64_t ne0, int64_t ne1,
                               nbl_weight** out);
 NBL_API int nbl_weight_destroy(nbl_weight* w);
-/* The uploaded tensor: device address of its elements (in its own dtype), dtype and shape. Any out pointer may be
- * NULL. An F32 vector's address is what nbl_add_bias takes. */
+/* The uploaded tensor: device address of its elements (F32/F16: in its own dtype; quantized: the internal
+ * layout), dtype and shape. Any out pointer may be NULL. An F32 vector's address is what nbl_add_bias takes. */
 NBL_API int nbl_weight_data(const nbl_weight* w, const void** dev, int32_t* dtype, int64_t* ne0, int64_t* ne1);
 /* Backend::embed (backend.h:54-55; cpu::embed ref_ops.cpp:80-98): out[t, :] = row ids[t] of table, widened to
  * fp32 (bit-identical). ids is HOST memory (a std::span in the reference); an id outside [0, ne1) is
  * NBL_E_INVALID with the reference's message and nothing is written. */
 NBL_API int nbl_embed(nbl_ctx* ctx, const nbl_weight* table, const int32_t* ids, int64_t n, float* out);
-/* Backend::matmul (backend.h:56; cpu::matmul_rows ref_ops.cpp:109-136): y[n, ne1] = x[n, ne0] . W^T in fp32
- * arithmetic (F16 weights widened exactly). n <= 8 streams the weight once (GEMV kernel); larger n runs SGEMM
- * (cuBLAS, no TF32). Results differ from the CPU's only by fp32 summation order. Backend::matmul_multi is one
- * call per weight, as the reference's contract allows ("results equal separate calls"). */
+/* Backend::matmul (backend.h:56; cpu::matmul_rows ref_ops.cpp:109-136): y[n, ne1] = x[n, ne0] . W^T.
+ * F32/F16 weights: fp32 arithmetic (F16 widened exactly); n <= 8 streams the weight once (GEMV kernel), larger n
+ * runs SGEMM (cuBLAS, no TF32); results differ from the CPU's only by fp32 summation order. Quantized weights: x is
+ * quantized to Q8_0 blocks and each output is the reference's sum of per-block terms (src/quant.cpp:310-366),
+ * bit-identical to nibble's CPU result, for any n (in chunks of 8 rows). */
 NBL_API int nbl_matmul(nbl_ctx* ctx, const nbl_weight* w, const float* x, float* y, int64_t n);
 /* Backend::matmul_multi (backend.h:57-60; CpuBackend::matmul_multi cpu_backend.cpp:146-233): ys[i] = x . ws[i]^T
  * for `count` weights sharing one input x [n, ne0] (all ws[i] have the same ne0); results equal separate

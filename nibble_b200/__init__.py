@@ -14,9 +14,10 @@ import ctypes as C
 from dataclasses import dataclass
 
 from . import _abi
-from ._abi import BF16, F16, F32, NibbleError, check
+from ._abi import BF16, F16, F32, Q4_0, Q5_0, Q8_0, NibbleError, check
 
-__all__ = ["Context", "KVPool", "Weight", "NibbleError", "RopeSpec", "F32", "F16", "BF16", "abi_version"]
+__all__ = ["Context", "KVPool", "Weight", "NibbleError", "RopeSpec", "F32", "F16", "BF16", "Q4_0", "Q5_0", "Q8_0",
+           "abi_version"]
 
 
 def abi_version() -> int:
@@ -99,15 +100,21 @@ class Weight:
     """A weight tensor uploaded to the device (nbl_weight): ne1 rows of ne0 elements, F32 or F16 -- the device form
     of nibble's Tensor view (src/tensor.h:57-70)."""
 
-    def __init__(self, ctx: "Context", host, dtype: int | None = None):
-        """host: a C-contiguous numpy float32 / float16 array, 1-D (a vector) or 2-D [ne1, ne0]."""
+    def __init__(self, ctx: "Context", host, dtype: int | None = None, ne0: int | None = None):
+        """host: a C-contiguous numpy float32 / float16 array, 1-D (a vector) or 2-D [ne1, ne0]; or, with dtype
+        Q4_0 / Q5_0 / Q8_0 and ne0 given, the GGUF block bytes as uint8 [ne1, row bytes]."""
         import numpy as np
         a = np.ascontiguousarray(host)
         if dtype is None:
             dtype = {np.dtype(np.float32): F32, np.dtype(np.float16): F16}.get(a.dtype)
             if dtype is None:
                 raise ValueError(f"weights must be float32 or float16, got {a.dtype}")
-        ne1, ne0 = (1, a.shape[0]) if a.ndim == 1 else a.shape
+        if dtype in (Q4_0, Q5_0, Q8_0):
+            if ne0 is None or a.ndim != 2:
+                raise ValueError("quantized weights take uint8 blocks [ne1, row bytes] and ne0")
+            ne1 = a.shape[0]
+        else:
+            ne1, ne0 = (1, a.shape[0]) if a.ndim == 1 else a.shape
         h = C.c_void_p()
         check(_abi.lib.nbl_weight_create(ctx.handle, a.ctypes.data, dtype, ne0, ne1, C.byref(h)))
         self.ctx, self.handle, self.ne0, self.ne1, self.dtype = ctx, h, ne0, ne1, dtype
@@ -201,8 +208,8 @@ class Context:
                                      head_dim))
 
     # ---- the model's other Backend ops (backend.h:54-70) on fp32 device buffers
-    def weight(self, host, dtype: int | None = None) -> Weight:
-        return Weight(self, host, dtype)
+    def weight(self, host, dtype: int | None = None, ne0: int | None = None) -> Weight:
+        return Weight(self, host, dtype, ne0)
 
     def embed(self, table: Weight, ids, out):
         """ids: host int32 array (a std::span in the reference); out [n, ne0] fp32."""

@@ -72,10 +72,16 @@ void ensure_scratch(nbl_ctx* ctx, size_t bytes) {
 // on the host in double with the reference's expression (src/backend/cpu/ref_ops.cpp:173-176) if needed.
 const nbl::RopeTable& rope_table(nbl_ctx* ctx, const nbl_rope_params& rp, int64_t head_dim, int64_t n_pos) {
   const int64_t half = head_dim / 2;
+  // the cache hit is the per-call path (every layer of every token): compare in place, allocate nothing
+  auto same_factors = [&](const nbl::RopeTable& t) {
+    if (!rp.freq_factors) return t.factors.empty();
+    return t.factors.size() == static_cast<size_t>(half) &&
+           std::memcmp(t.factors.data(), rp.freq_factors, static_cast<size_t>(half) * sizeof(float)) == 0;
+  };
+  for (auto& t : ctx->rope_tables)
+    if (t.base == rp.freq_base && t.head_dim == head_dim && t.n_pos >= n_pos && same_factors(t)) return t;
   std::vector<float> ff;
   if (rp.freq_factors) ff.assign(rp.freq_factors, rp.freq_factors + half);
-  for (auto& t : ctx->rope_tables)
-    if (t.base == rp.freq_base && t.head_dim == head_dim && t.factors == ff && t.n_pos >= n_pos) return t;
   // Build (grow to the larger of the request and the reserved context length).
   const int64_t want = std::max<int64_t>(n_pos, ctx->reserved_ctx);
   std::vector<float2> host(static_cast<size_t>(want * half));
@@ -173,6 +179,27 @@ void ensure_ids(nbl_ctx* ctx, int64_t n) {
   ctx->ids_cap = n;
 }
 
+// Quantizes n rows of x (width ne0, a multiple of 32) into the context's activation scratch; returns the int8
+// values [n][ne0] and the per-block scales [n][ne0 / 32] (16-byte aligned).
+std::pair<const int8_t*, const float*> quantize_activations(nbl_ctx* ctx, const float* x, int64_t n, int64_t ne0) {
+  const size_t vals = (static_cast<size_t>(n * ne0) + 255) & ~size_t(255);
+  const size_t need = vals + static_cast<size_t>(n * (ne0 / 32)) * sizeof(float);
+  if (ctx->qact_bytes < need) {
+    void* p = device_alloc(need, "quantized activations");
+    if (ctx->qact) {
+      nbl::check_cuda(cudaStreamSynchronize(ctx->stream), "activation scratch sync");
+      cudaFree(ctx->qact);
+    }
+    ctx->qact = p;
+    ctx->qact_bytes = need;
+  }
+  auto* qs = static_cast<int8_t*>(ctx->qact);
+  auto* d = reinterpret_cast<float*>(static_cast<char*>(ctx->qact) + vals);
+  nbl::launch_quantize_q8_0(ctx->stream, x, qs, d, n * ne0);
+  nbl::check_cuda(cudaGetLastError(), "activation quantize launch");
+  return {qs, d};
+}
+
 void release_weight(nbl_weight* w) {
   if (w->w.f32 && w->w.f32 != w->w.dev) cudaFree(w->w.f32);
   cudaFree(w->w.dev);
@@ -256,6 +283,7 @@ int nbl_ctx_destroy(nbl_ctx* ctx) {
     if (ctx->cublas) cublasDestroy(static_cast<cublasHandle_t>(ctx->cublas));
     if (ctx->cublas_ws) cudaFree(ctx->cublas_ws);
     if (ctx->ids) cudaFree(ctx->ids);
+    if (ctx->qact) cudaFree(ctx->qact);
     for (auto& a : ctx->allocs) cudaFree(a.first);
     for (auto& t : ctx->rope_tables) cudaFree(t.dev);
     if (ctx->scratch) cudaFree(ctx->scratch);
@@ -684,8 +712,10 @@ int nbl_weight_create(nbl_ctx* ctx, const void* host, int32_t dtype, int64_t ne0
   return guarded([&] {
     require(ctx && host && out, "weight_create: ctx, host or out is NULL");
     *out = nullptr;
-    require(dtype == NBL_F32 || dtype == NBL_F16, "weight_create: dtype must be NBL_F32 or NBL_F16");
+    require(dtype == NBL_F32 || dtype == NBL_F16 || nbl::is_quant(dtype),
+            "weight_create: dtype must be NBL_F32, NBL_F16, NBL_Q4_0, NBL_Q5_0 or NBL_Q8_0");
     require(ne0 > 0 && ne1 > 0, "weight_create: bad shape " + std::to_string(ne0) + " x " + std::to_string(ne1));
+    require(!nbl::is_quant(dtype) || ne0 % 32 == 0, "weight_create: a quantized row must be whole 32-element blocks");
     const size_t elem = dtype == NBL_F32 ? 4 : 2;
     require(static_cast<uint64_t>(ne0) <= (uint64_t(1) << 40) / static_cast<uint64_t>(ne1),
             "weight_create: tensor too large");
@@ -697,8 +727,38 @@ int nbl_weight_create(nbl_ctx* ctx, const void* host, int32_t dtype, int64_t ne0
     w->w.ne0 = ne0;
     w->w.ne1 = ne1;
     try {
-      w->w.dev = device_alloc(count * elem, "weight");
-      nbl::check_cuda(cudaMemcpyAsync(w->w.dev, host, count * elem, cudaMemcpyHostToDevice, ctx->stream), "weight upload");
+      if (nbl::is_quant(dtype)) {
+        // GGUF blocks -> [scales][values][high bits], each array 256-byte aligned, split on the host
+        const size_t nbk = count / 32, bb = static_cast<size_t>(nbl::quant_block_bytes(dtype));
+        const size_t qsb = static_cast<size_t>(nbl::quant_qs_bytes(dtype));
+        const size_t off_qs = (nbk * 2 + 255) & ~size_t(255);
+        const size_t off_qh = (off_qs + nbk * qsb + 255) & ~size_t(255);
+        const size_t total = off_qh + (dtype == NBL_Q5_0 ? nbk * 4 : 0);
+        std::vector<uint8_t> packed(total);
+        const auto* src = static_cast<const uint8_t*>(host);
+        for (size_t b = 0; b < nbk; ++b) {
+          const uint8_t* blk = src + b * bb;
+          std::memcpy(packed.data() + b * 2, blk, 2);  // fp16 scale
+          if (dtype == NBL_Q5_0) {
+            std::memcpy(packed.data() + off_qh + b * 4, blk + 2, 4);  // high bits
+            std::memcpy(packed.data() + off_qs + b * qsb, blk + 6, qsb);
+          } else {
+            std::memcpy(packed.data() + off_qs + b * qsb, blk + 2, qsb);
+          }
+        }
+        w->w.dev = device_alloc(total, "weight");
+        nbl::check_cuda(cudaMemcpyAsync(w->w.dev, packed.data(), total, cudaMemcpyHostToDevice, ctx->stream),
+                        "weight upload");
+        nbl::check_cuda(cudaStreamSynchronize(ctx->stream), "weight upload");  // `packed` is released below
+        auto* base = static_cast<uint8_t*>(w->w.dev);
+        w->w.q.d = reinterpret_cast<const uint16_t*>(base);
+        w->w.q.qs = base + off_qs;
+        w->w.q.qh = dtype == NBL_Q5_0 ? reinterpret_cast<const uint32_t*>(base + off_qh) : nullptr;
+      } else {
+        w->w.dev = device_alloc(count * elem, "weight");
+        nbl::check_cuda(cudaMemcpyAsync(w->w.dev, host, count * elem, cudaMemcpyHostToDevice, ctx->stream),
+                        "weight upload");
+      }
       if (dtype == NBL_F32) w->w.f32 = static_cast<float*>(w->w.dev);  // F16: fp32 copy on first SGEMM use
       nbl::check_cuda(cudaStreamSynchronize(ctx->stream), "weight upload");
       ctx->weights.push_back(w);
@@ -746,7 +806,8 @@ int nbl_embed(nbl_ctx* ctx, const nbl_weight* table, const int32_t* ids, int64_t
     nbl::check_cuda(cudaMemcpyAsync(ctx->ids, ids, static_cast<size_t>(n) * sizeof(int32_t), cudaMemcpyHostToDevice,
                                     ctx->stream),
                     "embed ids");
-    nbl::launch_embed(ctx->stream, table->w, ctx->ids, n, out, ctx->num_sms);
+    if (nbl::is_quant(table->w.dtype)) nbl::launch_embed_q(ctx->stream, table->w, ctx->ids, n, out);
+    else nbl::launch_embed(ctx->stream, table->w, ctx->ids, n, out, ctx->num_sms);
     nbl::check_cuda(cudaGetLastError(), "embed launch");
   });
 }
@@ -758,7 +819,13 @@ int nbl_matmul(nbl_ctx* ctx, const nbl_weight* w, const float* x, float* y, int6
     require(n >= 0 && n <= INT32_MAX && w->w.ne0 <= INT32_MAX && w->w.ne1 <= INT32_MAX, "matmul: bad size");
     if (n == 0) return;
     use_device(ctx);
-    if (n <= nbl::kGemvMaxRows) {
+    if (nbl::is_quant(w->w.dtype)) {
+      const auto a = quantize_activations(ctx, x, n, w->w.ne0);
+      const nbl::Weight* ws[1] = {&w->w};
+      float* ys[1] = {y};
+      nbl::launch_gemv_q(ctx->stream, ws, ys, 1, a.first, a.second, n, ctx->num_sms);
+      nbl::check_cuda(cudaGetLastError(), "matmul launch");
+    } else if (n <= nbl::kGemvMaxRows) {
       nbl::launch_gemv(ctx->stream, w->w, x, y, n, ctx->num_sms);
       nbl::check_cuda(cudaGetLastError(), "matmul launch");
     } else {
@@ -781,7 +848,41 @@ int nbl_matmul_multi(nbl_ctx* ctx, const nbl_weight* const* ws, int32_t count, c
     }
     if (n == 0) return;
     use_device(ctx);
-    if (n <= nbl::kGemvMaxRows) {
+    bool any_quant = false, all_quant_same = true;
+    for (int32_t i = 0; i < count; ++i) {
+      any_quant = any_quant || nbl::is_quant(ws[i]->w.dtype);
+      all_quant_same = all_quant_same && ws[i]->w.dtype == ws[0]->w.dtype && nbl::is_quant(ws[i]->w.dtype);
+    }
+    if (any_quant) {
+      // x quantized once for every quantized weight (CpuBackend::matmul_multi does the same)
+      const auto a = quantize_activations(ctx, x, n, ws[0]->w.ne0);
+      if (all_quant_same) {
+        for (int32_t i0 = 0; i0 < count; i0 += nbl::kMaxMulti) {
+          const int c = static_cast<int>(std::min<int32_t>(nbl::kMaxMulti, count - i0));
+          const nbl::Weight* w[nbl::kMaxMulti];
+          float* y[nbl::kMaxMulti];
+          for (int i = 0; i < c; ++i) {
+            w[i] = &ws[i0 + i]->w;
+            y[i] = ys[i0 + i];
+          }
+          nbl::launch_gemv_q(ctx->stream, w, y, c, a.first, a.second, n, ctx->num_sms);
+        }
+      } else {
+        for (int32_t i = 0; i < count; ++i) {
+          if (nbl::is_quant(ws[i]->w.dtype)) {
+            const nbl::Weight* w[1] = {&ws[i]->w};
+            float* y[1] = {ys[i]};
+            nbl::launch_gemv_q(ctx->stream, w, y, 1, a.first, a.second, n, ctx->num_sms);
+          } else if (n <= nbl::kGemvMaxRows) {
+            nbl::launch_gemv(ctx->stream, ws[i]->w, x, ys[i], n, ctx->num_sms);
+          } else {
+            nbl::gemm_f32(cublas_handle(ctx), ctx->stream, weight_f32(ctx, ws[i]), x, ys[i], ws[i]->w.ne0,
+                          ws[i]->w.ne1, n);
+          }
+        }
+      }
+      nbl::check_cuda(cudaGetLastError(), "matmul launch");
+    } else if (n <= nbl::kGemvMaxRows) {
       for (int32_t i0 = 0; i0 < count; i0 += nbl::kMaxMulti) {
         const int c = static_cast<int>(std::min<int32_t>(nbl::kMaxMulti, count - i0));
         const nbl::Weight* w[nbl::kMaxMulti];

@@ -40,10 +40,17 @@ const nbl_weight* CudaBackend::device_weight(const Tensor& t) {
   auto it = weights_.find(t.data);
   if (it != weights_.end()) return it->second;
   if (!t.data) throw Error("cuda backend: weight tensor has no data");
-  if (t.type != DType::F32 && t.type != DType::F16)
-    throw Error("cuda backend: unsupported weight dtype (only F32/F16 run on the GPU)");
+  int32_t dt;
+  switch (t.type) {
+    case DType::F32: dt = NBL_F32; break;
+    case DType::F16: dt = NBL_F16; break;
+    case DType::Q4_0: dt = NBL_Q4_0; break;
+    case DType::Q5_0: dt = NBL_Q5_0; break;
+    case DType::Q8_0: dt = NBL_Q8_0; break;
+    default: throw Error("cuda backend: unsupported weight dtype (F32/F16/Q4_0/Q5_0/Q8_0 run on the GPU)");
+  }
   nbl_weight* w = nullptr;
-  check(nbl_weight_create(ctx_, t.data, t.type == DType::F32 ? NBL_F32 : NBL_F16, t.ne[0], t.rows(), &w));
+  check(nbl_weight_create(ctx_, t.data, dt, t.ne[0], t.rows(), &w));
   weights_.emplace(t.data, w);
   return w;
 }

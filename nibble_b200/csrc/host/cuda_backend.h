@@ -10,10 +10,11 @@
 // address (nbl_weight_create), so the first forward pass after construction allocates the model's device weights
 // and later ones allocate nothing.
 //
-// Coverage: every Backend op runs on the GPU for F32 and F16 weights -- embed, matmul (weight-streaming GEMV for
-// up to 8 rows, SGEMM above), rmsnorm, add, add_bias, rope, copy, attention, silu_mul -- so nibble's Transformer
-// (src/model/transformer.cpp) runs on it unchanged. supports() reports F32 and F16; the quantized types are not
-// part of this backend yet, so a quantized model refuses to load on it instead of running anything on the CPU.
+// Coverage: every Backend op runs on the GPU for F32, F16, Q4_0, Q5_0 and Q8_0 weights -- embed, matmul
+// (weight-streaming GEMV for up to 8 rows, SGEMM above; the quantized types bit-identical to the CPU's block dots),
+// rmsnorm, add, add_bias, rope, copy, attention, silu_mul -- so nibble's Transformer (src/model/transformer.cpp) runs
+// on it unchanged. supports() is false for Q5_1 and the k-quants, so such a model refuses to load on it instead of
+// running anything on the CPU.
 //
 // The paged fp16/bf16 fast path (fused append, split-K decode, tcgen05 prefill) is reached through handle()
 // and the nbl_* functions, with check() turning their statuses into nibble::Error.
@@ -40,7 +41,9 @@ class CudaBackend final : public Backend {
   CudaBackend(const CudaBackend&) = delete;
   CudaBackend& operator=(const CudaBackend&) = delete;
 
-  bool supports(DType t) const override { return t == DType::F32 || t == DType::F16; }
+  bool supports(DType t) const override {
+    return t == DType::F32 || t == DType::F16 || t == DType::Q4_0 || t == DType::Q5_0 || t == DType::Q8_0;
+  }
   void reserve(const ReserveParams& rp) override;
   float* alloc(int64_t n_floats) override;
   void free(float* p) override;

@@ -9,13 +9,23 @@ namespace nbl {
 // Activation rows up to which a matmul runs as the weight-streaming GEMV (decode); more rows use SGEMM.
 constexpr int64_t kGemvMaxRows = 8;
 
-// One weight tensor on the device: ne1 rows of ne0 elements (F32 or F16), plus an fp32 copy of an F16 matrix for
-// the SGEMM path (equal to `dev` for F32; made on an F16 matrix's first multi-row matmul).
+// A quantized weight's device arrays (quant_ops.cu): fp16 scale bits [rows][blocks], value bytes
+// [rows][blocks][16 or 32] (16-byte aligned), Q5_0's high bits [rows][blocks].
+struct QWeightView {
+  const uint16_t* d = nullptr;
+  const uint8_t* qs = nullptr;
+  const uint32_t* qh = nullptr;
+};
+
+// One weight tensor on the device: ne1 rows of ne0 elements (F32, F16 or a quantized type), plus an fp32 copy of an
+// F16 matrix for the SGEMM path (equal to `dev` for F32; made on an F16 matrix's first multi-row matmul). For a
+// quantized type `dev` holds the arrays `q` points into.
 struct Weight {
   int32_t dtype = NBL_F32;
   int64_t ne0 = 0, ne1 = 0;
   void* dev = nullptr;
   float* f32 = nullptr;
+  QWeightView q;
 };
 
 void launch_embed(cudaStream_t st, const Weight& table, const int32_t* ids, int64_t n, float* out, int num_sms);
@@ -28,12 +38,29 @@ struct GemvBatch {
   int64_t row_end[kMaxMulti];  // cumulative row counts
   int count;
 };
+struct QBatch {
+  QWeightView w[kMaxMulti];
+  float* y[kMaxMulti];
+  int64_t row_end[kMaxMulti];  // cumulative row counts
+  int count;
+};
 void launch_gemv(cudaStream_t st, const Weight& w, const float* x, float* y, int64_t n, int num_sms);
 // All weights share ne0; n rows of x. Weights of mixed dtype, or unaligned ones, run one scalar launch each.
 void launch_gemv_multi(cudaStream_t st, const Weight* const* ws, float* const* ys, int count, const float* x,
                        int64_t n, int num_sms);
 void gemm_f32(cublasHandle_t h, cudaStream_t st, const float* w_f32, const float* x, float* y, int64_t ne0, int64_t ne1,
               int64_t n);
+// quant_ops.cu: the Q8_0-activation weight family (Q4_0, Q5_0, Q8_0)
+bool is_quant(int32_t dtype);
+int64_t quant_block_bytes(int32_t dtype);  // GGUF bytes per 32-element block
+int64_t quant_qs_bytes(int32_t dtype);     // value bytes per block in the device layout
+// x [n_elems / 32 blocks] -> int8 values and the fp32 value of each block's fp16 scale
+void launch_quantize_q8_0(cudaStream_t st, const float* x, int8_t* qs, float* d, int64_t n_elems);
+// weights of one quantized type sharing ne0 and the quantized activations (n rows, in chunks of 8)
+void launch_gemv_q(cudaStream_t st, const Weight* const* ws, float* const* ys, int count, const int8_t* aq,
+                   const float* ad, int64_t n, int num_sms);
+void launch_embed_q(cudaStream_t st, const Weight& table, const int32_t* ids, int64_t n, float* out);
+
 void launch_rmsnorm(cudaStream_t st, const float* x, const float* w, float* y, int64_t n, int64_t d, float eps);
 void launch_add(cudaStream_t st, float* x, const float* y, int64_t count, int num_sms);
 void launch_silu_mul(cudaStream_t st, float* gate, const float* up, int64_t count, int num_sms);

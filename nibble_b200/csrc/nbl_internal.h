@@ -58,6 +58,8 @@ struct nbl_ctx {
   std::vector<nbl_weight*> weights;
   int32_t* ids = nullptr;
   int64_t ids_cap = 0;
+  void* qact = nullptr;       // activations quantized for a quantized-weight matmul (int8 values, then fp32 scales)
+  size_t qact_bytes = 0;
   void* cublas = nullptr;     // cublasHandle_t, created by nbl_reserve (max_rows > the GEMV limit) or first use
   void* cublas_ws = nullptr;  // its fixed workspace
 };

@@ -77,6 +77,11 @@ def _load_oracle():
     lib.orc_rmsnorm.argtypes = [_f32p, _f32p, _f32p, _i64, _i64, C.c_float]
     lib.orc_add.argtypes = [_f32p, _f32p, _i64]
     lib.orc_silu_mul.argtypes = [_f32p, _f32p, _i64]
+    lib.orc_quantize_q8_0.argtypes = [_f32p, C.c_void_p, _i64]
+    lib.orc_dequantize_row.argtypes = [C.c_int, C.c_void_p, _f32p, _i64]
+    lib.orc_dequantize_row.restype = C.c_int
+    lib.orc_matmul_q.argtypes = [C.c_void_p, C.c_int, _i64, _i64, _f32p, _f32p, _i64]
+    lib.orc_matmul_q.restype = C.c_int
     _lib = lib
     return lib
 
@@ -124,6 +129,9 @@ def _load_ref():
     lib.nref_backend_matmul.argtypes = [C.c_void_p, C.c_void_p, C.c_int, _i64, _i64, _f32p, _f32p, _i64]
     lib.nref_backend_rmsnorm.argtypes = [C.c_void_p, _f32p, _f32p, _f32p, _i64, _i64, C.c_float]
     lib.nref_backend_silu_mul.argtypes = [C.c_void_p, _f32p, _f32p, _i64]
+    lib.nref_quantize_q8_0.argtypes = [_f32p, C.c_void_p, _i64]
+    lib.nref_dequantize_row.argtypes = [C.c_int, C.c_void_p, _f32p, _i64]
+    lib.nref_matmul_q.argtypes = [C.c_void_p, C.c_int, _i64, _i64, _f32p, _f32p, _i64]
     _ref = lib
     return lib
 
@@ -268,7 +276,77 @@ def silu_mul(gate, up) -> np.ndarray:
     return g
 
 
+# ---------------------------------------------------------------- quantized weights (Q8_0-activation family)
+Q4_0, Q5_0, Q8_0 = 2, 6, 8  # nibble DType ids (ggml's)
+BLOCK_BYTES = {Q4_0: 18, Q5_0: 22, Q8_0: 34}
+
+
+def quantize_q8_0(x) -> np.ndarray:
+    """fp32 [n] (n % 32 == 0) -> uint8 [n / 32 * 34] Q8_0 blocks (src/quant.cpp:37-51, :250-257)."""
+    x = _c(x).ravel()
+    out = np.empty(x.size // 32 * 34, np.uint8)
+    _load_oracle().orc_quantize_q8_0(x, out.ctypes.data, x.size)
+    return out
+
+
+def dequantize_rows(blocks, dtype, ne0, ne1) -> np.ndarray:
+    b = np.ascontiguousarray(blocks, dtype=np.uint8)
+    out = np.empty((ne1, ne0), np.float32)
+    rb = ne0 // 32 * BLOCK_BYTES[dtype]
+    for r in range(ne1):
+        if _load_oracle().orc_dequantize_row(dtype, b.ctypes.data + r * rb, out[r], ne0) != 0:
+            raise ValueError("dtype")
+    return out
+
+
+def matmul_q(blocks, dtype, ne0, ne1, x, n) -> np.ndarray:
+    b = np.ascontiguousarray(blocks, dtype=np.uint8)
+    y = np.empty((n, ne1), np.float32)
+    if _load_oracle().orc_matmul_q(b.ctypes.data, dtype, ne0, ne1, _c(x), y, n) != 0:
+        raise ValueError("dtype")
+    return y
+
+
+def random_q_blocks(rng, dtype, ne1, ne0, scale=0.02) -> np.ndarray:
+    """Random but well-formed weight blocks: random 4/5/8-bit values and fp16 scales of about `scale`."""
+    nb = ne0 // 32
+    bb = BLOCK_BYTES[dtype]
+    raw = rng.integers(0, 256, size=(ne1 * nb, bb), dtype=np.uint8)
+    d = f32_to_fp16_bits((scale * (0.5 + rng.random(ne1 * nb))).astype(np.float32))
+    raw[:, 0] = d & 0xFF
+    raw[:, 1] = d >> 8
+    return raw.reshape(ne1, nb * bb)
+
+
 # ---------------------------------------------------------------- nibble's own code (oracle/_ref)
+def ref_quantize_q8_0(x) -> np.ndarray:
+    x = _c(x).ravel()
+    out = np.empty(x.size // 32 * 34, np.uint8)
+    _load_ref().nref_quantize_q8_0(x, out.ctypes.data, x.size)
+    return out
+
+
+def ref_dequantize_rows(blocks, dtype, ne0, ne1) -> np.ndarray:
+    b = np.ascontiguousarray(blocks, dtype=np.uint8)
+    out = np.empty((ne1, ne0), np.float32)
+    rb = ne0 // 32 * BLOCK_BYTES[dtype]
+    lib = _load_ref()
+    for r in range(ne1):
+        if lib.nref_dequantize_row(dtype, b.ctypes.data + r * rb, out[r], ne0) != 0:
+            raise ValueError(lib.nref_last_error().decode())
+    return out
+
+
+def ref_matmul_q(blocks, dtype, ne0, ne1, x, n) -> np.ndarray:
+    b = np.ascontiguousarray(blocks, dtype=np.uint8)
+    y = np.empty((n, ne1), np.float32)
+    lib = _load_ref()
+    if lib.nref_matmul_q(b.ctypes.data, dtype, ne0, ne1, _c(x), y, n) != 0:
+        raise ValueError(lib.nref_last_error().decode())
+    return y
+
+
+
 def ref_embed(table, ids) -> np.ndarray:
     """nibble::cpu::embed (src/backend/cpu/ref_ops.cpp:80)."""
     ptr, dt, keep = _weight_arg(table)

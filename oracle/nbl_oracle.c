@@ -264,3 +264,101 @@ void orc_silu_mul(float* gate, const float* up, int64_t count) {
     gate[i] = g / (1.0f + expf(-g)) * up[i];
   }
 }
+
+/* ---- quantized weights (Q8_0-activation family) ---- */
+
+static uint16_t orc_rd16(const uint8_t* p) { return (uint16_t)(p[0] | (p[1] << 8)); }
+
+void orc_quantize_q8_0(const float* x, uint8_t* blocks, int64_t n) {
+  for (int64_t b = 0; b < n / 32; ++b) {
+    const float* xb = x + b * 32;
+    uint8_t* o = blocks + b * 34;
+    float amax = 0.f;
+    int has_nan = 0;
+    for (int j = 0; j < 32; ++j) {
+      amax = fmaxf(amax, fabsf(xb[j]));
+      has_nan |= isnan(xb[j]);
+    }
+    const float d = has_nan ? NAN : amax / 127.f;
+    const float id = d != 0.f ? 1.0f / d : 0.0f;
+    for (int j = 0; j < 32; ++j) {
+      const float r = roundf(xb[j] * id);
+      o[2 + j] = (uint8_t)(int8_t)(r != r ? 0 : (int)fminf(127.f, fmaxf(-127.f, r)));
+    }
+    const uint16_t h = orc_fp32_to_fp16(d);
+    o[0] = (uint8_t)(h & 0xFF);
+    o[1] = (uint8_t)(h >> 8);
+  }
+}
+
+static int64_t orc_block_bytes(int dtype) { return dtype == 2 ? 18 : dtype == 6 ? 22 : dtype == 8 ? 34 : 0; }
+
+int orc_dequantize_row(int dtype, const void* src, float* dst, int64_t n) {
+  const uint8_t* p = (const uint8_t*)src;
+  const int64_t bb = orc_block_bytes(dtype);
+  if (!bb) return -1;
+  for (int64_t b = 0; b < n / 32; ++b) {
+    const uint8_t* blk = p + b * bb;
+    const float d = orc_fp16_to_fp32(orc_rd16(blk));
+    if (dtype == 8) {
+      for (int j = 0; j < 32; ++j) dst[b * 32 + j] = (float)(int8_t)blk[2 + j] * d;
+    } else if (dtype == 2) {
+      for (int j = 0; j < 16; ++j) {
+        dst[b * 32 + j] = (float)((blk[2 + j] & 0x0F) - 8) * d;
+        dst[b * 32 + j + 16] = (float)((blk[2 + j] >> 4) - 8) * d;
+      }
+    } else {
+      const uint32_t qh = (uint32_t)blk[2] | ((uint32_t)blk[3] << 8) | ((uint32_t)blk[4] << 16) | ((uint32_t)blk[5] << 24);
+      for (int j = 0; j < 16; ++j) {
+        const int x0 = ((blk[6 + j] & 0x0F) | (((qh >> j) << 4) & 0x10)) - 16;
+        const int x1 = ((blk[6 + j] >> 4) | ((qh >> (j + 12)) & 0x10)) - 16;
+        dst[b * 32 + j] = (float)x0 * d;
+        dst[b * 32 + j + 16] = (float)x1 * d;
+      }
+    }
+  }
+  return 0;
+}
+
+int orc_matmul_q(const void* w, int dtype, int64_t ne0, int64_t ne1, const float* x, float* y, int64_t n) {
+  const int64_t bb = orc_block_bytes(dtype), nb = ne0 / 32;
+  if (!bb) return -1;
+  uint8_t* xa = (uint8_t*)malloc((size_t)(nb * 34));
+  if (!xa) return -1;
+  for (int64_t t = 0; t < n; ++t) {
+    orc_quantize_q8_0(x + t * ne0, xa, ne0);
+    for (int64_t r = 0; r < ne1; ++r) {
+      const uint8_t* wr = (const uint8_t*)w + r * nb * bb;
+      float sum = 0.f;
+      for (int64_t b = 0; b < nb; ++b) {
+        const uint8_t* bw = wr + b * bb;
+        const uint8_t* ba = xa + b * 34;
+        const int8_t* aq = (const int8_t*)(ba + 2);
+        const float dw = orc_fp16_to_fp32(orc_rd16(bw)), da = orc_fp16_to_fp32(orc_rd16(ba));
+        if (dtype == 8) {
+          int s = 0;
+          for (int j = 0; j < 32; ++j) s += (int8_t)bw[2 + j] * aq[j];
+          sum += (float)s * (dw * da);
+        } else if (dtype == 2) {
+          int s0 = 0, s1 = 0;
+          for (int j = 0; j < 16; ++j) {
+            s0 += ((bw[2 + j] & 0x0F) - 8) * aq[j];
+            s1 += ((bw[2 + j] >> 4) - 8) * aq[j + 16];
+          }
+          sum += (float)(s0 + s1) * dw * da;
+        } else {
+          const uint32_t qh = (uint32_t)bw[2] | ((uint32_t)bw[3] << 8) | ((uint32_t)bw[4] << 16) | ((uint32_t)bw[5] << 24);
+          int s0 = 0, s1 = 0;
+          for (int j = 0; j < 16; ++j) {
+            s0 += (((bw[6 + j] & 0x0F) | (((qh >> j) << 4) & 0x10)) - 16) * aq[j];
+            s1 += (((bw[6 + j] >> 4) | ((qh >> (j + 12)) & 0x10)) - 16) * aq[j + 16];
+          }
+          sum += (dw * da) * (float)(s0 + s1);
+        }
+      }
+      y[t * ne1 + r] = sum;
+    }
+  }
+  free(xa);
+  return 0;
+}

@@ -25,6 +25,7 @@
 #include "backend/cpu/ref_ops.h"
 #include "backend/cpu/simd/dispatch.h"
 #include "fp16.h"
+#include "quant.h"
 #include "thread_pool.h"
 
 namespace {
@@ -131,9 +132,10 @@ int nref_backend_rope(void* h, float* x, int64_t n, int64_t n_heads, int64_t hea
 
 // ---- the model's other ops (dtype 0 = F32, 1 = F16) ----
 namespace {
+// dtype: 0 = F32, 1 = F16, otherwise a quantized type's DType id (2 Q4_0, 6 Q5_0, 8 Q8_0, ...).
 nibble::Tensor tensor_of(const void* data, int dtype, int64_t ne0, int64_t ne1) {
   nibble::Tensor t;
-  t.type = dtype == 0 ? nibble::DType::F32 : nibble::DType::F16;
+  t.type = static_cast<nibble::DType>(dtype);
   t.n_dims = ne1 > 1 ? 2 : 1;
   t.ne = {ne0, ne1, 1, 1};
   t.data = data;
@@ -154,6 +156,38 @@ int nref_embed(const void* table, int dtype, int64_t ne0, int64_t n_rows, const 
 int nref_matmul(const void* w, int dtype, int64_t ne0, int64_t ne1, const float* x, float* y, int64_t n) {
   try {
     nibble::cpu::matmul_rows(tensor_of(w, dtype, ne0, ne1), x, y, n, 0, ne1, nullptr);
+    return 0;
+  } catch (const std::exception& e) {
+    set_err(e.what());
+    return 1;
+  }
+}
+
+// nibble::quantize_row_q8_0 (src/quant.cpp:250) into 34-byte blocks.
+void nref_quantize_q8_0(const float* x, void* blocks, int64_t n) {
+  nibble::quantize_row_q8_0(x, static_cast<nibble::BlockQ8_0*>(blocks), n);
+}
+
+// nibble::dequantize_row (src/quant.cpp:158) for any supported dtype id.
+int nref_dequantize_row(int dtype, const void* src, float* dst, int64_t n) {
+  try {
+    nibble::dequantize_row(static_cast<nibble::DType>(dtype), src, dst, n);
+    return 0;
+  } catch (const std::exception& e) {
+    set_err(e.what());
+    return 1;
+  }
+}
+
+// nibble::cpu::matmul_rows with a quantized weight: x quantized row by row to Q8_0 (quantize_rows_q8_0), then the
+// scalar block dots (Q8_0-activation weight types only).
+int nref_matmul_q(const void* w, int dtype, int64_t ne0, int64_t ne1, const float* x, float* y, int64_t n) {
+  try {
+    std::vector<nibble::BlockQ8_0> xq(static_cast<size_t>(n * (ne0 / 32)));
+    nibble::cpu::quantize_rows_q8_0(x, xq.data(), n, ne0);
+    nibble::QuantActs acts;
+    acts.q8_0 = xq.data();
+    nibble::cpu::matmul_rows(tensor_of(w, dtype, ne0, ne1), x, y, n, 0, ne1, &acts);
     return 0;
   } catch (const std::exception& e) {
     set_err(e.what());

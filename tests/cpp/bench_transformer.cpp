@@ -5,8 +5,8 @@
 // min / max tokens per second -- on a random in-memory model of a named shape (no model file exists here, so the
 // loader and tokenizer are not involved; the prompt is token i % n_vocab as in the reference).
 //
-//   nbl_model_bench [--backend cuda|cpu] [--shape tinyllama|qwen05] [-p 512] [-n 128] [-r 5] [-t threads]
-//                   [--out file.jsonl]
+//   nbl_model_bench [--backend cuda|cpu] [--shape tinyllama|qwen05] [--type F16|F32|Q4_0|Q5_0|Q8_0] [-p 512]
+//                   [-n 128] [-r 5] [-t threads] [--out file.jsonl]
 //
 // Prints the reference's table and, with --out, appends its JSON line per test with a "backend" field added.
 // Built by oracle/Makefile (target model-bench) where the reference tree is present.
@@ -53,22 +53,32 @@ std::string iso_now() {
   return b;
 }
 
-nbl_test::Shape shape_of(const std::string& name) {
-  if (name == "tinyllama") return {false, true, 22, 2048, 5632, 32, 4, 32000};  // TinyLlama-1.1B, llama, F16
-  if (name == "qwen05") return {true, true, 24, 896, 4864, 14, 2, 151936};     // Qwen2.5-0.5B, qwen2, F16
+nbl_test::Shape shape_of(const std::string& name, DType t) {
+  if (name == "tinyllama") return {false, t, 22, 2048, 5632, 32, 4, 32000};  // TinyLlama-1.1B, llama
+  if (name == "qwen05") return {true, t, 24, 896, 4864, 14, 2, 151936};     // Qwen2.5-0.5B, qwen2
   throw Error("unknown --shape '" + name + "' (tinyllama or qwen05)");
+}
+
+DType type_of(const std::string& name) {
+  if (name == "F32") return DType::F32;
+  if (name == "F16") return DType::F16;
+  if (name == "Q4_0") return DType::Q4_0;
+  if (name == "Q5_0") return DType::Q5_0;
+  if (name == "Q8_0") return DType::Q8_0;
+  throw Error("unknown --type '" + name + "' (F32, F16, Q4_0, Q5_0, Q8_0)");
 }
 
 }  // namespace
 
 int main(int argc, char** argv) {
-  std::string backend = "cuda", shape_name = "tinyllama", out_path;
+  std::string backend = "cuda", shape_name = "tinyllama", type_name = "F16", out_path;
   long p = 512, n = 128, r = 5;
   int threads = 0;
   for (int i = 1; i + 1 < argc; i += 2) {
     const std::string a = argv[i], v = argv[i + 1];
     if (a == "--backend") backend = v;
     else if (a == "--shape") shape_name = v;
+    else if (a == "--type") type_name = v;
     else if (a == "-p") p = std::stol(v);
     else if (a == "-n") n = std::stol(v);
     else if (a == "-r") r = std::stol(v);
@@ -80,7 +90,7 @@ int main(int argc, char** argv) {
     }
   }
   try {
-    const nbl_test::Shape shape = shape_of(shape_name);
+    const nbl_test::Shape shape = shape_of(shape_name, type_of(type_name));
     nbl_test::Model m;
     nbl_test::build(m, shape, 1234);
     if (threads <= 0) threads = static_cast<int>(std::max(1u, std::thread::hardware_concurrency()));
@@ -123,7 +133,7 @@ int main(int argc, char** argv) {
     const std::string date = iso_now();
     std::ofstream out;
     if (!out_path.empty()) out.open(out_path, std::ios::app);
-    const std::string model_name = "random " + shape_name + " F16";
+    const std::string model_name = "random " + shape_name + " " + type_name;
     for (int k = 0; k < 2; ++k) {
       const std::string test = (k == 0 ? "pp" + std::to_string(p) : "tg" + std::to_string(n));
       const Stats s = stats(k == 0 ? pp : tg);

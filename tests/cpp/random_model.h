@@ -1,6 +1,7 @@
 // A random decoder-only model held in memory: nibble's LlamaConfig and Weights (Tensor views into host vectors),
 // shaped like a qwen2 or llama GGUF model, for tests and measurements that run nibble's own Transformer without a
-// model file. Values: projections N(0, 1/in), norms N(1, 0.1), biases N(0, 0.5); F16 or F32 projection weights.
+// model file. Values: projections N(0, 1/in) (or quantized blocks of that spread), norms N(1, 0.1), biases
+// N(0, 0.5); F32, F16, Q4_0, Q5_0 or Q8_0 projection, embedding and output weights.
 #pragma once
 #include <cmath>
 #include <cstdint>
@@ -18,8 +19,8 @@ using nibble::Tensor;
 namespace model = nibble::model;
 
 struct Shape {
-  bool qwen;  // qwen2 (Q/K/V biases, NeoX rope, theta 1e6) or llama (interleaved rope, freq factors, theta 5e5)
-  bool f16;   // projection and embedding weights F16 (else F32)
+  bool qwen;    // qwen2 (Q/K/V biases, NeoX rope, theta 1e6) or llama (interleaved rope, freq factors, theta 5e5)
+  DType wtype;  // projection, embedding and output weights: F32, F16, Q4_0, Q5_0 or Q8_0
   int64_t n_layers, n_embd, n_ff, n_heads, n_kv_heads, n_vocab;
 };
 
@@ -27,7 +28,7 @@ struct Model {
   model::LlamaConfig c;
   model::Weights w;
   std::vector<std::vector<float>> f32;     // storage behind the F32 tensors
-  std::vector<std::vector<uint16_t>> f16;  // storage behind the F16 tensors
+  std::vector<std::vector<uint16_t>> f16;  // storage behind the F16 and quantized tensors
 };
 
 inline Tensor view(DType t, int n_dims, int64_t ne0, int64_t ne1, const void* data) {
@@ -56,9 +57,30 @@ struct Rng {
   }
 };
 
-inline Tensor matrix(Model& m, Rng& rng, int64_t in, int64_t out, bool f16) {
+// Quantized blocks (GGUF layout, 32 elements each): uniformly random value bits and an fp16 scale that gives the
+// row about the same spread as a float matrix of N(0, 1/in).
+inline Tensor quant_matrix(Model& m, Rng& rng, int64_t in, int64_t out, DType t) {
+  const int64_t bb = t == DType::Q4_0 ? 18 : t == DType::Q5_0 ? 22 : 34;
+  const float rms = t == DType::Q4_0 ? 4.6f : t == DType::Q5_0 ? 9.2f : 73.9f;  // of the block's integer values
+  const float sd = 1.f / std::sqrt(static_cast<float>(in)) / rms;
+  const int64_t nb = in / 32 * out;
+  std::vector<uint16_t> raw(static_cast<size_t>((nb * bb + 1) / 2));
+  auto* bytes = reinterpret_cast<uint8_t*>(raw.data());
+  for (int64_t b = 0; b < nb; ++b) {
+    uint8_t* blk = bytes + b * bb;
+    const uint16_t d = nibble::fp32_to_fp16(sd * (0.5f + static_cast<float>(rng.next() & 0xFFFF) / 65536.f));
+    blk[0] = static_cast<uint8_t>(d & 0xFF);
+    blk[1] = static_cast<uint8_t>(d >> 8);
+    for (int64_t i = 2; i < bb; ++i) blk[i] = static_cast<uint8_t>(rng.next());
+  }
+  m.f16.push_back(std::move(raw));
+  return view(t, 2, in, out, m.f16.back().data());
+}
+
+inline Tensor matrix(Model& m, Rng& rng, int64_t in, int64_t out, DType t) {
+  if (t != DType::F32 && t != DType::F16) return quant_matrix(m, rng, in, out, t);
   const float sd = 1.f / std::sqrt(static_cast<float>(in));
-  if (f16) {
+  if (t == DType::F16) {
     std::vector<uint16_t> h(static_cast<size_t>(in * out));
     for (auto& x : h) x = nibble::fp32_to_fp16(rng.normal(0.f, sd));
     m.f16.push_back(std::move(h));
@@ -95,9 +117,9 @@ inline void build(Model& m, const Shape& s, uint64_t seed) {
   c.rope_neox = s.qwen;
   c.qkv_bias = s.qwen;
   const int64_t E = c.n_embd, Q = c.n_heads * c.head_dim, KV = c.n_kv_heads * c.head_dim;
-  m.w.token_embd = matrix(m, rng, E, c.n_vocab, s.f16);
+  m.w.token_embd = matrix(m, rng, E, c.n_vocab, s.wtype);
   m.w.output_norm = vec(m, rng, E, 1.f, 0.1f);
-  m.w.output = matrix(m, rng, E, c.n_vocab, s.f16);
+  m.w.output = matrix(m, rng, E, c.n_vocab, s.wtype);
   if (!s.qwen) {
     std::vector<float> ff(static_cast<size_t>(c.head_dim / 2));
     for (size_t i = 0; i < ff.size(); ++i) ff[i] = i < ff.size() / 2 ? 1.f : 8.f;  // llama-3 style low/high bands
@@ -107,14 +129,14 @@ inline void build(Model& m, const Shape& s, uint64_t seed) {
   for (int64_t l = 0; l < c.n_layers; ++l) {
     model::LayerWeights L;
     L.attn_norm = vec(m, rng, E, 1.f, 0.1f);
-    L.wq = matrix(m, rng, E, Q, s.f16);
-    L.wk = matrix(m, rng, E, KV, s.f16);
-    L.wv = matrix(m, rng, E, KV, s.f16);
-    L.wo = matrix(m, rng, Q, E, s.f16);
+    L.wq = matrix(m, rng, E, Q, s.wtype);
+    L.wk = matrix(m, rng, E, KV, s.wtype);
+    L.wv = matrix(m, rng, E, KV, s.wtype);
+    L.wo = matrix(m, rng, Q, E, s.wtype);
     L.ffn_norm = vec(m, rng, E, 1.f, 0.1f);
-    L.w_gate = matrix(m, rng, E, c.n_ff, s.f16);
-    L.w_up = matrix(m, rng, E, c.n_ff, s.f16);
-    L.w_down = matrix(m, rng, c.n_ff, E, s.f16);
+    L.w_gate = matrix(m, rng, E, c.n_ff, s.wtype);
+    L.w_up = matrix(m, rng, E, c.n_ff, s.wtype);
+    L.w_down = matrix(m, rng, c.n_ff, E, s.wtype);
     if (s.qwen) {
       L.bq = vec(m, rng, Q, 0.f, 0.5f);
       L.bk = vec(m, rng, KV, 0.f, 0.5f);

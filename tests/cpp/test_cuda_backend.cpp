@@ -147,9 +147,10 @@ static void contracts(CudaBackend& be) {
     threw = true;
   }
   CHECK(threw);
-  // float weights run on the GPU; quantized ones are refused at load time rather than run on the CPU
+  // float and Q8_0-activation quantized weights run on the GPU; the others are refused at load time
   CHECK(be.supports(nibble::DType::F32) && be.supports(nibble::DType::F16));
-  CHECK(!be.supports(nibble::DType::Q4_0) && !be.supports(nibble::DType::Q8_0) && !be.supports(nibble::DType::Q6_K));
+  CHECK(be.supports(nibble::DType::Q4_0) && be.supports(nibble::DType::Q5_0) && be.supports(nibble::DType::Q8_0));
+  CHECK(!be.supports(nibble::DType::Q5_1) && !be.supports(nibble::DType::Q4_K) && !be.supports(nibble::DType::Q6_K));
   threw = false;
   try {
     be.attention(nullptr, nullptr, nullptr, nullptr, 1, 0, 6, 4, 16);

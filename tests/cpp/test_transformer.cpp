@@ -7,9 +7,10 @@
 // reference's; only the Backend object differs. Built by oracle/Makefile (target model-check) where the
 // reference tree is present; tests/test_gpu_transformer.py runs it on a GPU.
 //
-// Two model variants: "qwen2"-style (Q/K/V biases, NeoX rope, theta 1e6) with F16 projection weights, and
-// "llama"-style (no biases, interleaved rope with per-pair frequency factors, theta 5e5) with F32 weights. The
-// prompt is longer than max_batch, so prefill runs in chunks (SGEMM-sized and GEMV-sized) before the decode steps.
+// Model variants: "qwen2"-style (Q/K/V biases, NeoX rope, theta 1e6) with F16, Q4_0 and Q5_0 weights, and
+// "llama"-style (no biases, interleaved rope with per-pair frequency factors, theta 5e5) with F32 and Q8_0 weights.
+// The prompt is longer than max_batch, so prefill runs in chunks (SGEMM-sized and GEMV-sized) before the decode
+// steps.
 //
 // Tolerance: per logit vector, max |gpu - cpu| <= 1e-4 * max |cpu| (the reference's own model-level bound against
 // a naive fp64 forward, tests/test_model.cpp:110-151), and the same argmax.
@@ -47,15 +48,26 @@ void compare(const char* what, const std::vector<float>& gpu, const std::vector<
   if (!ok) ++failures;
 }
 
-void run(bool qwen) {
+const char* type_name(DType t) {
+  switch (t) {
+    case DType::F32: return "F32";
+    case DType::F16: return "F16";
+    case DType::Q4_0: return "Q4_0";
+    case DType::Q5_0: return "Q5_0";
+    case DType::Q8_0: return "Q8_0";
+    default: return "?";
+  }
+}
+
+void run(bool qwen, DType wtype) {
   nbl_test::Model m;
-  // qwen2-style: 4 heads of 64, F16 weights; llama-style: 8 heads of 32, F32 weights
-  nbl_test::build(m, {qwen, qwen, 2, 256, 512, qwen ? 4 : 8, 2, 3000}, qwen ? 11 : 22);
+  // qwen2-style: 4 heads of 64; llama-style: 8 heads of 32
+  nbl_test::build(m, {qwen, wtype, 2, 256, 512, qwen ? 4 : 8, 2, 3000}, (qwen ? 11 : 22) + static_cast<int>(wtype));
   const int64_t n_ctx = 256, max_batch = 32;
   ThreadPool pool(4);
   cpu::CpuBackend cpu_be(pool);
   cuda::CudaBackend gpu_be(0);
-  if (!gpu_be.supports(qwen ? DType::F16 : DType::F32)) {
+  if (!gpu_be.supports(wtype)) {
     std::printf("CudaBackend does not support the weight type\n");
     ++failures;
     return;
@@ -66,7 +78,7 @@ void run(bool qwen) {
   std::vector<int32_t> prompt(70);
   for (auto& id : prompt) id = static_cast<int32_t>(rng() % static_cast<uint64_t>(m.c.n_vocab));
   std::vector<float> lc(static_cast<size_t>(m.c.n_vocab)), lg(lc.size());
-  const std::string tag = qwen ? "qwen2/F16" : "llama/F32";
+  const std::string tag = std::string(qwen ? "qwen2/" : "llama/") + type_name(wtype);
   // prefill in chunks of 32, 32 and 6 rows
   t_cpu.forward(prompt, 0, lc.data());
   t_gpu.forward(prompt, 0, lg.data());
@@ -110,8 +122,11 @@ void run(bool qwen) {
 
 int main() {
   try {
-    run(true);
-    run(false);
+    run(true, DType::F16);
+    run(false, DType::F32);
+    run(true, DType::Q4_0);
+    run(false, DType::Q8_0);
+    run(true, DType::Q5_0);
   } catch (const std::exception& e) {
     std::printf("exception: %s\n", e.what());
     return 2;

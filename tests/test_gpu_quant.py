@@ -1,0 +1,80 @@
+"""Quantized weights on the GPU (Q4_0, Q5_0, Q8_0: the types whose activations are Q8_0 blocks) against the C
+oracle, which test_oracle.py pins bit-exactly to nibble's own quantizer, block dots and dequantization
+(src/quant.cpp). The reference quantizes each activation row, adds per-block float terms in block order, and
+dequantizes embedding rows with one float product per element; the GPU does the same operations, so every result
+here is required to be bit-identical."""
+import numpy as np
+import pytest
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+TYPES = {"q4_0": (oracle.Q4_0, 3), "q5_0": (oracle.Q5_0, 4), "q8_0": (oracle.Q8_0, 5)}  # oracle id, ABI code
+
+
+def dev(a):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def host(t):
+    import torch
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+@pytest.mark.parametrize("name", sorted(TYPES))
+@pytest.mark.parametrize("n", [1, 3, 8, 9, 20])
+def test_quant_matmul_bit_exact(nbl_ctx, name, n):
+    """n <= 8 is one launch; larger n runs in chunks of 8 activation rows. Widths of 96 (3 blocks), 2048 (two full
+    rounds of 32 blocks) and 5632 (176 blocks: a partial last round)."""
+    import torch
+    odt, cdt = TYPES[name]
+    rng = np.random.default_rng(n * 10 + cdt)
+    for ne1, ne0 in [(37, 96), (300, 2048), (64, 5632)]:
+        w = oracle.random_q_blocks(rng, odt, ne1, ne0)
+        x = (rng.standard_normal((n, ne0)) * 2).astype(np.float32)
+        wt = nbl_ctx.weight(w, cdt, ne0)
+        y = torch.full((n, ne1), float("nan"), device="cuda")
+        nbl_ctx.matmul(wt, dev(x), y, n)
+        ref = oracle.matmul_q(w, odt, ne0, ne1, x, n)
+        assert np.array_equal(host(y).view(np.uint32), ref.view(np.uint32)), (ne1, ne0)
+        wt.close()
+
+
+@pytest.mark.parametrize("name", sorted(TYPES))
+def test_quant_matmul_multi_and_zero_blocks(nbl_ctx, name):
+    """matmul_multi over three weights of one type (one launch) equals the oracle; an all-zero activation block
+    (scale 0) and a tiny-magnitude block quantize like the reference."""
+    import torch
+    odt, cdt = TYPES[name]
+    rng = np.random.default_rng(cdt)
+    ne0 = 256
+    x = rng.standard_normal((2, ne0)).astype(np.float32)
+    x[0, :32] = 0.0
+    x[1, 32:64] *= 1e-30
+    ws = [oracle.random_q_blocks(rng, odt, r, ne0) for r in (128, 16, 16)]
+    wts = [nbl_ctx.weight(w, cdt, ne0) for w in ws]
+    ys = [torch.full((2, w.shape[0]), float("nan"), device="cuda") for w in ws]
+    nbl_ctx.matmul_multi(wts, dev(x), ys, 2)
+    for w, y in zip(ws, ys):
+        ref = oracle.matmul_q(w, odt, ne0, w.shape[0], x, 2)
+        assert np.array_equal(host(y).view(np.uint32), ref.view(np.uint32))
+    for wt in wts:
+        wt.close()
+
+
+@pytest.mark.parametrize("name", sorted(TYPES))
+def test_quant_embed_bit_exact(nbl_ctx, name):
+    import torch
+    odt, cdt = TYPES[name]
+    rng = np.random.default_rng(40 + cdt)
+    table = oracle.random_q_blocks(rng, odt, 500, 192, scale=0.5)
+    ids = np.array([0, 499, 7, 7, 250], np.int32)
+    t = nbl_ctx.weight(table, cdt, 192)
+    out = torch.full((ids.size, 192), float("nan"), device="cuda")
+    nbl_ctx.embed(t, ids, out)
+    ref = oracle.dequantize_rows(table, odt, 192, 500)[ids]
+    assert np.array_equal(host(out).view(np.uint32), ref.view(np.uint32))
+    t.close()

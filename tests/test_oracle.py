@@ -222,3 +222,35 @@ def test_embed_out_of_range_matches_reference_error():
     if oracle.have_ref():
         with pytest.raises(ValueError, match=r"embed: token id 7 out of range \(n_vocab 7\)"):
             oracle.ref_embed(w, np.array([7], np.int32))
+
+
+# ---------------------------------------------------------------- quantized weights (Q8_0-activation family)
+@pytest.mark.parametrize("dtype", [oracle.Q4_0, oracle.Q5_0, oracle.Q8_0])
+def test_quant_oracle_bit_identical_to_reference(dtype):
+    """Activation quantizer, row dequantization and the quantized matmul against nibble's own scalar code
+    (src/quant.cpp via oracle/_ref), including an all-zero block and one of tiny magnitude."""
+    if not oracle.have_ref():
+        pytest.skip("oracle/_ref (nibble's own code) is not built here")
+    rng = np.random.default_rng(dtype)
+    x = (rng.standard_normal(32 * 9) * 3).astype(np.float32)
+    x[:32] = 0.0
+    x[32:64] *= 1e-30
+    assert np.array_equal(oracle.quantize_q8_0(x), oracle.ref_quantize_q8_0(x))
+    w = oracle.random_q_blocks(rng, dtype, 23, 160)
+    a = oracle.dequantize_rows(w, dtype, 160, 23)
+    b = oracle.ref_dequantize_rows(w, dtype, 160, 23)
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    xs = x[:160 * 1].reshape(1, 160).repeat(3, axis=0) * np.array([[1.0], [0.5], [-2.0]], np.float32)
+    y = oracle.matmul_q(w, dtype, 160, 23, xs, 3)
+    yr = oracle.ref_matmul_q(w, dtype, 160, 23, xs, 3)
+    assert np.array_equal(y.view(np.uint32), yr.view(np.uint32))
+
+
+def test_quantize_q8_0_known_answer():
+    """One block: d = max|x| / 127 and q = round(x / d), half away from zero (src/quant.cpp:37-51)."""
+    x = np.zeros(32, np.float32)
+    x[0], x[1], x[2], x[3] = 127.0, -63.5, 0.4, -127.0
+    blk = oracle.quantize_q8_0(x)
+    d = oracle.fp16_bits_to_f32(np.array([int(blk[0]) | (int(blk[1]) << 8)], np.uint16))[0]
+    q = blk[2:].view(np.int8)
+    assert d == 1.0 and list(q[:4]) == [127, -64, 0, -127] and not q[4:].any()
