@@ -15,6 +15,9 @@ Workloads (synthetic seeded inputs of the named shapes; n
   decode_long / decode_ragged   configs 4 and 5 (extra legs of the default run).
   model_gemv      the weight matmuls of one decode token of a TinyLlama-1.1B-shaped F16 model (the rest of the
                   Backend on the GPU; bounds a whole-model decode step). Metric: weight bytes / time (HBM GB/s).
+  model_gemv_q4_0 the same with Q4_0 weights (nibble's quantized matmul, bit-identical to its CPU kernels).
+  model_qgemm     the weight matmuls of a 512-token prefill of the Q4_0 model on the tcgen05 kind::i8 path.
+                  Metric: tokens/s of the matmul part.
 With N > 1 (torchrun, one rank per GPU, NCCL) every rank runs its own shard of the same per-GPU work ("weak"
 scaling: the sequences shard with no collective); value = all ranks' work / max-over-ranks device time.
 
@@ -439,28 +442,45 @@ def decode_long(args, world, rank, local, steps, warmup):
 E6, FF6, Q6, KV6, LAYERS6, VOCAB6 = 2048, 5632, 2048, 256, 22, 32000   # TinyLlama-1.1B
 
 
-def model_gemv(args, world, rank, local, steps, warmup):
-    """The weight matmuls of one decode token of a TinyLlama-1.1B-shaped model with F16 weights through
-    nbl_matmul (n = 1: the weight-streaming GEMV): per layer Q, K, V, O, gate, up and down projections, then the
-    output projection -- Q/K/V and gate/up as one multi-weight launch each (the Transformer's matmul_multi), 89
-    launches reading 2.07 GB of weights, replayed as one CUDA graph. This is what bounds
-    a decode step of the whole Transformer on CudaBackend (attention and the elementwise ops move a few MB).
-    Metric: weight bytes / step time (HBM GB/s); tokens/s = 1 / step time. Weights are random (synthetic)."""
+Q4_0_CODE, Q4_0_BLOCK = 3, 18  # nbl_dtype NBL_Q4_0; GGUF bytes per 32-element block
+
+
+def tinyllama_weights(ctx, rng, wtype, with_output=True):
+    """Random (synthetic) TinyLlama-1.1B weight matrices in nibble's order per layer (Q, K, V, O, gate, up, down)
+    plus the output projection: F16 values ~ N(0, 0.02), or Q4_0 blocks of random 4-bit values with fp16 scale
+    0.01. Returns (weights, shapes, device bytes read by one pass over them)."""
+    shapes = []
+    for _ in range(LAYERS6):
+        shapes += [(Q6, E6), (KV6, E6), (KV6, E6), (E6, Q6), (FF6, E6), (FF6, E6), (E6, FF6)]
+    if with_output:
+        shapes.append((VOCAB6, E6))
+    if wtype == "F16":
+        pool = (rng.standard_normal(VOCAB6 * E6, dtype=np.float32) * 0.02).astype(np.float16)
+        weights = [ctx.weight(pool[: r * c].reshape(r, c)) for r, c in shapes]
+        return weights, shapes, sum(r * c * 2 for r, c in shapes)
+    nbk = VOCAB6 * E6 // 32
+    pool = rng.integers(0, 256, size=(nbk, Q4_0_BLOCK), dtype=np.uint8)
+    pool[:, :2] = np.frombuffer(np.float16(0.01).tobytes(), np.uint8)
+    weights = [ctx.weight(pool[: r * c // 32].reshape(r, c // 32 * Q4_0_BLOCK), Q4_0_CODE, c) for r, c in shapes]
+    return weights, shapes, sum(r * c // 32 * Q4_0_BLOCK for r, c in shapes)
+
+
+def model_gemv(args, world, rank, local, steps, warmup, wtype="F16"):
+    """The weight matmuls of one decode token of a TinyLlama-1.1B-shaped model through nbl_matmul (n = 1): per
+    layer Q, K, V, O, gate, up and down projections, then the output projection -- Q/K/V and gate/up as one
+    multi-weight call each (the Transformer's matmul_multi), 89 calls, replayed as one CUDA graph. F16 weights
+    (2.07 GB) run the weight-streaming GEMV; Q4_0 weights (0.58 GB) run nibble's quantized matmul (activations
+    quantized to Q8_0, block dots summed in the reference's order: one quantize and one GEMV launch per call).
+    This is what bounds a decode step of the whole Transformer on CudaBackend. Metric: weight bytes / step time
+    (HBM GB/s); tokens/s = 1 / step time. Weights are random (synthetic)."""
     import torch
     import nibble_b200 as nb
     ctx = nb.Context(local)
     rng = np.random.default_rng(60 + rank)
-    pool = (rng.standard_normal(VOCAB6 * E6, dtype=np.float32) * 0.02).astype(np.float16)
-    shapes = []
-    for _ in range(LAYERS6):
-        shapes += [(Q6, E6), (KV6, E6), (KV6, E6), (E6, Q6), (FF6, E6), (FF6, E6), (E6, FF6)]
-    shapes.append((VOCAB6, E6))
-    weights = [ctx.weight(pool[: r * c].reshape(r, c)) for r, c in shapes]
-    del pool
+    weights, shapes, wbytes = tinyllama_weights(ctx, rng, wtype)
     x = {c: torch.randn(c, device="cuda") for c in (E6, FF6)}
     y = {w: torch.empty(w, device="cuda") for w in (Q6, KV6, E6, FF6, VOCAB6)}
     y["v"], y["u"] = torch.empty(KV6, device="cuda"), torch.empty(FF6, device="cuda")
-    wbytes = sum(r * c * 2 for r, c in shapes)
     side = torch.cuda.Stream()
     side.wait_stream(torch.cuda.current_stream())
 
@@ -502,13 +522,95 @@ def model_gemv(args, world, rank, local, steps, warmup):
     ctx.close()
     hbm, _, _, src = peaks()
     ach = wbytes / (ms * 1e-3) / 1e9
+    calls = 4 * LAYERS6 + 1
     return {"metric": "model decode weight-matmul HBM GB/s", "value": world * ach, "unit": "GB/s", "ms_per_step": ms,
             "tokens_per_s_per_gpu": 1e3 / ms, "scaling": "weak",
-            "config": {"workload": "TinyLlama-1.1B decode-step weight matmuls (F16 weights, n = 1)",
-                       "launches_per_step": 4 * LAYERS6 + 1, "weight_bytes": wbytes,
-                       "l2": "weights (2.07 GB) larger than L2; no flush needed"},
-            "roofline": {"kernel": "gemv_kernel", "bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s",
-                         "frac": ach / hbm, "peak_source": src}}
+            "gpu_launches_per_step": calls if wtype == "F16" else 2 * calls,
+            "config": {"workload": f"TinyLlama-1.1B decode-step weight matmuls ({wtype} weights, n = 1)",
+                       "launches_per_step": calls if wtype == "F16" else 2 * calls, "weight_bytes": wbytes,
+                       "l2": f"weights ({wbytes / 1e9:.2f} GB) larger than L2; no flush needed"},
+            "roofline": {"kernel": "gemv_kernel" if wtype == "F16" else "quantize_rows_kernel + gemv_q_kernel",
+                         "bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
+                         "peak_source": src}}
+
+
+def model_qgemm(args, world, rank, local, steps, warmup, n=512):
+    """The weight matmuls of one 512-token prefill of a TinyLlama-1.1B-shaped Q4_0 model through nbl_matmul (the
+    tensor-core path for more than 8 activation rows): per layer Q/K/V and gate/up as matmul_multi, O and down as
+    matmul -- 88 calls (the output projection runs on the last row only), replayed as one CUDA graph. Each call
+    quantizes its activation rows to Q8_0 and runs qgemm_kernel: one tcgen05 kind::i8 MMA per 32-element block into
+    TMEM, the reference's per-block float terms added in block order by the epilogue warps. Metric: activation rows
+    (tokens) per second of the matmul part; the kernel's own rate is given as int8 TOPS (2 * n * rows * ne0 per
+    second) and as block terms per second against the epilogue's issue bound."""
+    import torch
+    import nibble_b200 as nb
+    ctx = nb.Context(local)
+    rng = np.random.default_rng(70 + rank)
+    weights, shapes, wbytes = tinyllama_weights(ctx, rng, "Q4_0", with_output=False)
+    x = {c: torch.randn(n, c, device="cuda") for c in (E6, FF6)}
+    y = {w: torch.empty(n, w, device="cuda") for w in (Q6, KV6, E6, FF6)}
+    y["v"], y["u"] = torch.empty(n, KV6, device="cuda"), torch.empty(n, FF6, device="cuda")
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+
+    def step():
+        for layer in range(LAYERS6):
+            wq, wk, wv, wo, wg, wu, wd = weights[7 * layer:7 * layer + 7]
+            ctx.matmul_multi([wq, wk, wv], x[E6], [y[Q6], y[KV6], y["v"]], n)
+            ctx.matmul(wo, x[E6], y[E6], n)
+            ctx.matmul_multi([wg, wu], x[E6], [y[FF6], y["u"]], n)
+            ctx.matmul(wd, x[FF6], y[E6], n)
+
+    with torch.cuda.stream(side):  # the first pass makes the int8 operands and the activation scratch
+        ctx.set_stream(side.cuda_stream)
+        step()
+        side.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        ctx.set_stream(torch.cuda.current_stream().cuda_stream)
+        step()
+    main = torch.cuda.current_stream()
+    ctx.set_stream(main.cuda_stream)
+    for _ in range(warmup):
+        graph.replay()
+    ctx.check()
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(main)
+    for _ in range(steps):
+        graph.replay()
+    e1.record(main)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
+    ctx.check()
+    del graph
+    for w in weights:
+        w.close()
+    ctx.close()
+    macs = n * sum(r * c for r, c in shapes)
+    terms = macs // 32
+    clock = gpu_clock_mhz(local)
+    issue_bound = 148 * 128 / 4 * clock * 1e6  # 4 FP32-pipe issue slots per output and block, 128 lanes per SM
+    return {"metric": "model prefill weight-matmul tokens/s", "value": world * n / (ms * 1e-3), "unit": "tokens/s",
+            "ms_per_step": ms, "scaling": "weak", "gpu_launches_per_step": 8 * LAYERS6,
+            "config": {"workload": f"TinyLlama-1.1B {n}-token prefill weight matmuls (Q4_0 weights)",
+                       "calls_per_step": 4 * LAYERS6, "launches_per_step": 8 * LAYERS6, "weight_bytes": wbytes,
+                       "l2": "activations and each weight matrix are re-read from L2 by the tiles sharing them"},
+            "int8_tops": 2 * macs / (ms * 1e-3) / 1e12,
+            "roofline": {"kernel": "qgemm_kernel", "bound": "issue (fp32 epilogue)", "achieved": terms / (ms * 1e-3),
+                         "peak": issue_bound, "unit": "block terms/s", "frac": terms / (ms * 1e-3) / issue_bound,
+                         "peak_source": f"148 SMs x 32 terms/clk at the SM clock sampled ({clock:.0f} MHz)"}}
+
+
+def gpu_clock_mhz(local):
+    """Current SM clock of this GPU from nvidia-smi (MHz); 1965 if it cannot be read."""
+    try:
+        out = subprocess.run(["nvidia-smi", "-i", str(local), "--query-gpu=clocks.sm", "--format=csv,noheader,nounits"],
+                             capture_output=True, text=True, timeout=10).stdout.strip()
+        return float(out.splitlines()[0])
+    except Exception:
+        return 1965.0
 
 
 # ---------------------------------------------------------------- config 5: ragged paged decode, LPT-balanced
@@ -661,7 +763,8 @@ def main():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["decode_batched", "prefill", "decode_long", "decode_ragged", "model_gemv"],
+    ap.add_argument("--workload", choices=["decode_batched", "prefill", "decode_long", "decode_ragged", "model_gemv",
+                                           "model_gemv_q4_0", "model_qgemm"],
                     default="decode_batched")
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-3 prefill leg of the default run")
     ap.add_argument("--no-extra", action="store_true", help="skip the config-4/5 legs of the default run")
@@ -688,6 +791,10 @@ def main():
         res = decode_ragged(args, world, rank, local, args.steps, args.warmup)
     elif args.workload == "model_gemv":
         res = model_gemv(args, world, rank, local, args.steps, args.warmup)
+    elif args.workload == "model_gemv_q4_0":
+        res = model_gemv(args, world, rank, local, args.steps, args.warmup, wtype="Q4_0")
+    elif args.workload == "model_qgemm":
+        res = model_qgemm(args, world, rank, local, args.steps, args.warmup)
     else:
         res = decode_batched(args, world, rank, local)
         if not args.no_prefill:
@@ -696,11 +803,13 @@ def main():
             res["decode_long"] = decode_long(args, world, rank, local, legs, 3)
             res["decode_ragged"] = decode_ragged(args, world, rank, local, legs, 3)
             res["model_decode_gemv"] = model_gemv(args, world, rank, local, legs, 3)
+            res["model_decode_gemv_q4_0"] = model_gemv(args, world, rank, local, legs, 3, wtype="Q4_0")
+            res["model_prefill_qgemm_q4_0"] = model_qgemm(args, world, rank, local, legs, 3)
     res.setdefault("scaling", "weak")
     res.update({"n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
                 "vs_baseline": None, "data": "synthetic (seeded N(0,1))"})
     res["gpu_launches"] = res.pop("gpu_launches_per_step", 2) * args.steps
-    if rank == 0 and world == 1 and args.cpu_seconds > 0:
+    if rank == 0 and world == 1 and args.cpu_seconds > 0 and args.workload == "decode_batched":
         res["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
     if world > 1:
         import torch.distributed as dist

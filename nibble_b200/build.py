@@ -19,11 +19,14 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libnibble_cuda.so")
 STAMP = LIB + ".stamp"
-SOURCES = ["api.cu", "rope.cu", "attn_f32.cu", "decode.cu", "decode_static.cu", "prefill.cu", "model_ops.cu", "quant_ops.cu"]
-HEADERS = ["nbl_device.cuh", "nbl_internal.h", "nbl_errors.h", "model_ops.h"]
+SOURCES = ["api.cu", "rope.cu", "attn_f32.cu", "decode.cu", "decode_static.cu", "prefill.cu", "model_ops.cu", "quant_ops.cu", "quant_gemm.cu"]
+HEADERS = ["nbl_device.cuh", "nbl_internal.h", "nbl_errors.h", "model_ops.h", "quant_common.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
          "--expt-relaxed-constexpr", "-I" + os.path.join(ROOT, "include")]
+# Per-file additions: quant_gemm.cu must keep every multiply and add separately rounded (the reference's
+# arithmetic), so nothing in it may be contracted into a fused multiply-add.
+FILE_FLAGS = {"quant_gemm.cu": ["-fmad=false"]}
 
 
 def nvcc() -> str:
@@ -43,6 +46,7 @@ def _digest(extra: list[str]) -> str:
     # the flags name the repository's absolute path (-I): leave it out, so a tree copied elsewhere (the GPU box's
     # snapshot) keeps the stamp of the library it ships with
     h.update(" ".join(ARCH + FLAGS + extra).replace(ROOT, "<root>").encode())
+    h.update(repr(sorted(FILE_FLAGS.items())).encode())
     return h.hexdigest()
 
 
@@ -61,7 +65,7 @@ def build(force: bool = False, verbose: bool = False, extra: list[str] | None = 
     procs = []
     for name in SOURCES:
         obj = os.path.join(objdir, name.replace(".cu", ".o"))
-        cmd = [cc, *ARCH, *FLAGS, *extra, "-c", os.path.join(CSRC, name), "-o", obj]
+        cmd = [cc, *ARCH, *FLAGS, *FILE_FLAGS.get(name, []), *extra, "-c", os.path.join(CSRC, name), "-o", obj]
         if verbose:
             cmd += ["-Xptxas", "-v"]
             print(" ".join(cmd), file=sys.stderr)

@@ -129,10 +129,10 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 }  // namespace
 
 void nbl::encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, void* base, const cuuint64_t* dims,
-                      const cuuint64_t* strides_bytes, const cuuint32_t* box) {
+                      const cuuint64_t* strides_bytes, const cuuint32_t* box, CUtensorMapSwizzle swizzle) {
   const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
   const CUresult r = tensor_map_encoder()(map, dtype, static_cast<cuuint32_t>(rank), base, dims, strides_bytes, box,
-                                          estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                          estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) nbl::fail(NBL_E_CUDA, "cuTensorMapEncodeTiled failed (CUresult " + std::to_string(r) + ")");
 }
@@ -179,28 +179,8 @@ void ensure_ids(nbl_ctx* ctx, int64_t n) {
   ctx->ids_cap = n;
 }
 
-// Quantizes n rows of x (width ne0, a multiple of 32) into the context's activation scratch; returns the int8
-// values [n][ne0] and the per-block scales [n][ne0 / 32] (16-byte aligned).
-std::pair<const int8_t*, const float*> quantize_activations(nbl_ctx* ctx, const float* x, int64_t n, int64_t ne0) {
-  const size_t vals = (static_cast<size_t>(n * ne0) + 255) & ~size_t(255);
-  const size_t need = vals + static_cast<size_t>(n * (ne0 / 32)) * sizeof(float);
-  if (ctx->qact_bytes < need) {
-    void* p = device_alloc(need, "quantized activations");
-    if (ctx->qact) {
-      nbl::check_cuda(cudaStreamSynchronize(ctx->stream), "activation scratch sync");
-      cudaFree(ctx->qact);
-    }
-    ctx->qact = p;
-    ctx->qact_bytes = need;
-  }
-  auto* qs = static_cast<int8_t*>(ctx->qact);
-  auto* d = reinterpret_cast<float*>(static_cast<char*>(ctx->qact) + vals);
-  nbl::launch_quantize_q8_0(ctx->stream, x, qs, d, n * ne0);
-  nbl::check_cuda(cudaGetLastError(), "activation quantize launch");
-  return {qs, d};
-}
-
 void release_weight(nbl_weight* w) {
+  nbl::release_qgemm(w->w.qg);
   if (w->w.f32 && w->w.f32 != w->w.dev) cudaFree(w->w.f32);
   cudaFree(w->w.dev);
   delete w;
@@ -217,6 +197,43 @@ const float* weight_f32(nbl_ctx* ctx, const nbl_weight* cw) {
     nbl::check_cuda(cudaGetLastError(), "widen launch");
   }
   return w->w.f32;
+}
+
+// A quantized matmul of n activation rows for weights of one quantized type sharing ne0 (count <= kMaxMulti):
+// the GEMV for up to kGemvMaxRows rows, else the tensor-core GEMM (its weight operands made on first use, the
+// activation scratch grown to fit).
+void quant_matmul(nbl_ctx* ctx, const nbl_weight* const* cws, float* const* ys, int count, const float* x,
+                  int64_t n) {
+  const nbl::Weight* ws[nbl::kMaxMulti];
+  for (int i = 0; i < count; ++i) ws[i] = &cws[i]->w;
+  if (n <= nbl::kGemvMaxRows) {
+    const size_t need = nbl::gemv_q_act_bytes(ws[0]->ne0);
+    if (ctx->qgemv_act_bytes < need) {
+      if (ctx->qgemv_act) {
+        nbl::check_cuda(cudaStreamSynchronize(ctx->stream), "quant gemv scratch");
+        cudaFree(ctx->qgemv_act);
+        ctx->qgemv_act = nullptr;
+        ctx->qgemv_act_bytes = 0;
+      }
+      ctx->qgemv_act = device_alloc(need, "quant gemv activations");
+      ctx->qgemv_act_bytes = need;
+    }
+    nbl::launch_gemv_q(ctx->stream, ws, ys, count, x, n, ctx->qgemv_act, ctx->num_sms);
+    return;
+  }
+  for (int i = 0; i < count; ++i) nbl::prepare_qgemm(ctx->stream, const_cast<nbl_weight*>(cws[i])->w, ctx->num_sms);
+  const size_t need = nbl::qgemm_act_bytes(n, ws[0]->ne0);
+  if (ctx->qgemm_act_bytes < need) {
+    if (ctx->qgemm_act) {
+      nbl::check_cuda(cudaStreamSynchronize(ctx->stream), "quant gemm scratch");
+      cudaFree(ctx->qgemm_act);
+      ctx->qgemm_act = nullptr;
+      ctx->qgemm_act_bytes = 0;
+    }
+    ctx->qgemm_act = device_alloc(need, "quant gemm activations");
+    ctx->qgemm_act_bytes = need;
+  }
+  nbl::launch_qgemm(ctx->stream, ws, ys, count, x, n, ctx->qgemm_act, ctx->num_sms, ctx->d_err);
 }
 
 void require_weight(const nbl_ctx* ctx, const nbl_weight* w, const char* what) {
@@ -283,7 +300,8 @@ int nbl_ctx_destroy(nbl_ctx* ctx) {
     if (ctx->cublas) cublasDestroy(static_cast<cublasHandle_t>(ctx->cublas));
     if (ctx->cublas_ws) cudaFree(ctx->cublas_ws);
     if (ctx->ids) cudaFree(ctx->ids);
-    if (ctx->qact) cudaFree(ctx->qact);
+    if (ctx->qgemm_act) cudaFree(ctx->qgemm_act);
+    if (ctx->qgemv_act) cudaFree(ctx->qgemv_act);
     for (auto& a : ctx->allocs) cudaFree(a.first);
     for (auto& t : ctx->rope_tables) cudaFree(t.dev);
     if (ctx->scratch) cudaFree(ctx->scratch);
@@ -820,10 +838,7 @@ int nbl_matmul(nbl_ctx* ctx, const nbl_weight* w, const float* x, float* y, int6
     if (n == 0) return;
     use_device(ctx);
     if (nbl::is_quant(w->w.dtype)) {
-      const auto a = quantize_activations(ctx, x, n, w->w.ne0);
-      const nbl::Weight* ws[1] = {&w->w};
-      float* ys[1] = {y};
-      nbl::launch_gemv_q(ctx->stream, ws, ys, 1, a.first, a.second, n, ctx->num_sms);
+      quant_matmul(ctx, &w, &y, 1, x, n);
       nbl::check_cuda(cudaGetLastError(), "matmul launch");
     } else if (n <= nbl::kGemvMaxRows) {
       nbl::launch_gemv(ctx->stream, w->w, x, y, n, ctx->num_sms);
@@ -854,25 +869,14 @@ int nbl_matmul_multi(nbl_ctx* ctx, const nbl_weight* const* ws, int32_t count, c
       all_quant_same = all_quant_same && ws[i]->w.dtype == ws[0]->w.dtype && nbl::is_quant(ws[i]->w.dtype);
     }
     if (any_quant) {
-      // x quantized once for every quantized weight (CpuBackend::matmul_multi does the same)
-      const auto a = quantize_activations(ctx, x, n, ws[0]->w.ne0);
       if (all_quant_same) {
-        for (int32_t i0 = 0; i0 < count; i0 += nbl::kMaxMulti) {
-          const int c = static_cast<int>(std::min<int32_t>(nbl::kMaxMulti, count - i0));
-          const nbl::Weight* w[nbl::kMaxMulti];
-          float* y[nbl::kMaxMulti];
-          for (int i = 0; i < c; ++i) {
-            w[i] = &ws[i0 + i]->w;
-            y[i] = ys[i0 + i];
-          }
-          nbl::launch_gemv_q(ctx->stream, w, y, c, a.first, a.second, n, ctx->num_sms);
-        }
+        for (int32_t i0 = 0; i0 < count; i0 += nbl::kMaxMulti)
+          quant_matmul(ctx, ws + i0, ys + i0, static_cast<int>(std::min<int32_t>(nbl::kMaxMulti, count - i0)), x,
+                       n);
       } else {
         for (int32_t i = 0; i < count; ++i) {
           if (nbl::is_quant(ws[i]->w.dtype)) {
-            const nbl::Weight* w[1] = {&ws[i]->w};
-            float* y[1] = {ys[i]};
-            nbl::launch_gemv_q(ctx->stream, w, y, 1, a.first, a.second, n, ctx->num_sms);
+            quant_matmul(ctx, ws + i, ys + i, 1, x, n);
           } else if (n <= nbl::kGemvMaxRows) {
             nbl::launch_gemv(ctx->stream, ws[i]->w, x, ys[i], n, ctx->num_sms);
           } else {

@@ -17,6 +17,16 @@ struct QWeightView {
   const uint32_t* qh = nullptr;
 };
 
+// The operands of the tensor-core path of a quantized matmul (quant_gemm.cu), made on the weight's first multi-row
+// matmul: its values as int8 [rows][ne0] (Q8_0's device values themselves; an unpacked copy for Q4_0 and Q5_0) and
+// its block scales as fp32 [blocks][rows padded to 4], with their TMA descriptors.
+struct QGemmOperand {
+  CUtensorMap vmap, smap;
+  const int8_t* vals = nullptr;
+  int8_t* owned = nullptr;
+  float* scales_t = nullptr;
+};
+
 // One weight tensor on the device: ne1 rows of ne0 elements (F32, F16 or a quantized type), plus an fp32 copy of an
 // F16 matrix for the SGEMM path (equal to `dev` for F32; made on an F16 matrix's first multi-row matmul). For a
 // quantized type `dev` holds the arrays `q` points into.
@@ -26,6 +36,7 @@ struct Weight {
   void* dev = nullptr;
   float* f32 = nullptr;
   QWeightView q;
+  QGemmOperand* qg = nullptr;
 };
 
 void launch_embed(cudaStream_t st, const Weight& table, const int32_t* ids, int64_t n, float* out, int num_sms);
@@ -54,12 +65,20 @@ void gemm_f32(cublasHandle_t h, cudaStream_t st, const float* w_f32, const float
 bool is_quant(int32_t dtype);
 int64_t quant_block_bytes(int32_t dtype);  // GGUF bytes per 32-element block
 int64_t quant_qs_bytes(int32_t dtype);     // value bytes per block in the device layout
-// x [n_elems / 32 blocks] -> int8 values and the fp32 value of each block's fp16 scale
-void launch_quantize_q8_0(cudaStream_t st, const float* x, int8_t* qs, float* d, int64_t n_elems);
-// weights of one quantized type sharing ne0 and the quantized activations (n rows, in chunks of 8)
-void launch_gemv_q(cudaStream_t st, const Weight* const* ws, float* const* ys, int count, const int8_t* aq,
-                   const float* ad, int64_t n, int num_sms);
+// Weights of one quantized type sharing ne0 and the fp32 activations x (n rows, in chunks of kGemvMaxRows, each
+// quantized to Q8_0 blocks into `act` -- gemv_q_act_bytes(ne0) -- by a launch of its own).
+size_t gemv_q_act_bytes(int64_t ne0);
+void launch_gemv_q(cudaStream_t st, const Weight* const* ws, float* const* ys, int count, const float* x, int64_t n,
+                   void* act, int num_sms);
 void launch_embed_q(cudaStream_t st, const Weight& table, const int32_t* ids, int64_t n, float* out);
+// quant_gemm.cu: the same matmul for more than kGemvMaxRows activation rows, on the tensor cores. prepare_qgemm
+// makes a weight's operands (once); launch_qgemm quantizes x into `act` (qgemm_act_bytes) and runs weights of one
+// quantized type sharing ne0 (count <= kMaxMulti, each prepared).
+void prepare_qgemm(cudaStream_t st, Weight& w, int num_sms);
+void release_qgemm(QGemmOperand* g);
+size_t qgemm_act_bytes(int64_t n, int64_t ne0);
+void launch_qgemm(cudaStream_t st, const Weight* const* ws, float* const* ys, int count, const float* x, int64_t n,
+                  void* act, int num_sms, int* err);
 
 void launch_rmsnorm(cudaStream_t st, const float* x, const float* w, float* y, int64_t n, int64_t d, float eps);
 void launch_add(cudaStream_t st, float* x, const float* y, int64_t count, int num_sms);

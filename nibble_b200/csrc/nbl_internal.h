@@ -58,10 +58,12 @@ struct nbl_ctx {
   std::vector<nbl_weight*> weights;
   int32_t* ids = nullptr;
   int64_t ids_cap = 0;
-  void* qact = nullptr;       // activations quantized for a quantized-weight matmul (int8 values, then fp32 scales)
-  size_t qact_bytes = 0;
   void* cublas = nullptr;     // cublasHandle_t, created by nbl_reserve (max_rows > the GEMV limit) or first use
   void* cublas_ws = nullptr;  // its fixed workspace
+  void* qgemm_act = nullptr;  // activations quantized for the quantized tensor-core matmul
+  size_t qgemm_act_bytes = 0;
+  void* qgemv_act = nullptr;  // activations quantized for the quantized GEMV (up to 8 rows)
+  size_t qgemv_act_bytes = 0;
 };
 
 struct nbl_kv {
@@ -80,9 +82,11 @@ namespace nbl {
 int record_error(int status, const std::string& msg);
 
 // Encodes a tiled TMA descriptor (driver entry point resolved once through the runtime; no libcuda link).
-// dims/strides in elements/bytes as cuTensorMapEncodeTiled takes them; 128-byte swizzle, zero OOB fill.
+// dims/strides in elements/bytes as cuTensorMapEncodeTiled takes them; 128-byte swizzle unless told otherwise, zero
+// OOB fill.
 void encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, void* base, const cuuint64_t* dims,
-                 const cuuint64_t* strides_bytes, const cuuint32_t* box);
+                 const cuuint64_t* strides_bytes, const cuuint32_t* box,
+                 CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B);
 
 // ---- launches (defined in the kernel .cu files; all asynchronous on `st`) ----
 // rope.cu

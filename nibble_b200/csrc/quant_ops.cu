@@ -6,63 +6,26 @@
 // max|x| / 127 rounded to fp16, q = roundf(x / d)), takes the integer dot of each weight block with the activation
 // block, turns it into a float term with the two fp16 scales (the operation order differs per type and is kept
 // exactly: Q4_0 sumi * d_w * d_a, Q8_0 sumi * (d_w * d_a), Q5_0 (d_w * d_a) * sumi), and adds the terms to the row's
-// sum in block order. Here the activation quantizer runs one warp per block, the integer dots run four products per
-// dp4a instruction, every float operation is an uncontracted _rn intrinsic, and one row's terms are added in block
-// order (lanes hold consecutive blocks; their terms are broadcast to the whole warp one block at a time), so every
-// output equals the CPU's bit for bit.
+// sum in block order. Here the activation rows are quantized once per call (one warp per block, the same
+// arithmetic, so the same bits), the integer dots run four products per dp4a instruction, every float operation is
+// an uncontracted _rn intrinsic, and one row's terms are added in block order (lanes hold consecutive blocks; their
+// terms are broadcast to the whole warp one block at a time), so every output equals the CPU's bit for bit.
 //
 // Device layouts (made at upload, nbl_weight_create): the GGUF blocks of a row are split into aligned arrays --
 // fp16 scale bits [rows][blocks], the value bytes [rows][blocks][16 or 32] (16-byte aligned per block) and, for
-// Q5_0, the 32 high bits [rows][blocks] -- so a lane reads its block with one or two 16-byte loads. Activations are
-// quantized into int8 values [n][ne0] and the fp32 value of each block's fp16-rounded scale [n][ne0 / 32].
+// Q5_0, the 32 high bits [rows][blocks] -- so a lane reads its block with one or two 16-byte loads. Quantized
+// activations are int8 values [n][ne0] and the fp32 value of each block's fp16-rounded scale [n][blocks].
 #include <algorithm>
+#include <atomic>
 
 #include "model_ops.h"
 #include "nbl_device.cuh"
+#include "quant_common.cuh"
 
 namespace nbl {
 namespace {
 
-// ---------------------------------------------------------------- activations to Q8_0
-// One warp per 32-element block: amax by a max reduction (fmaxf skips NaN like std::fmax; a NaN anywhere makes d
-// NaN), d = amax / 127, q = roundf(x * (1 / d)) clamped to [-127, 127] (NaN -> 0); the scale is kept as the fp32
-// value of its fp16 rounding, which is what the dot products read.
-__global__ void quantize_q8_0_kernel(const float* __restrict__ x, int8_t* __restrict__ qs, float* __restrict__ d,
-                                     int64_t n_blocks) {
-  const int lane = threadIdx.x & 31;
-  const int64_t b = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-  if (b >= n_blocks) return;
-  const float v = x[b * 32 + lane];
-  float amax = fabsf(v);
-  bool nan = v != v;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-  nan = __any_sync(0xffffffffu, nan);
-  const float dd = nan ? __int_as_float(0x7fc00000) : __fdiv_rn(amax, 127.f);
-  const float id = dd != 0.f ? __fdiv_rn(1.0f, dd) : 0.f;
-  const float r = roundf(__fmul_rn(v, id));
-  qs[b * 32 + lane] = static_cast<int8_t>(r != r ? 0 : static_cast<int>(fminf(127.f, fmaxf(-127.f, r))));
-  if (lane == 0) d[b] = __half2float(__float2half_rn(dd));
-}
-
 // ---------------------------------------------------------------- block dots
-// The 4-bit / 5-bit value bytes of a Q4_0 / Q5_0 block widened to the int8 values dp4a takes, in element order:
-// lo[i] holds elements 4i..4i+3 (low nibbles of bytes 4i..4i+3), hi[i] elements 16+4i..16+4i+3.
-__device__ __forceinline__ void unpack_nibbles(const uint4 q, int (&lo)[4], int (&hi)[4]) {
-  const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    lo[i] = static_cast<int>(w[i] & 0x0F0F0F0Fu);
-    hi[i] = static_cast<int>((w[i] >> 4) & 0x0F0F0F0Fu);
-  }
-}
-
-// Spreads bits [first, first + 4) of qh to bit 4 of four bytes (the fifth bit of four Q5_0 elements).
-__device__ __forceinline__ int high_bits4(uint32_t qh, int first) {
-  const uint32_t b = qh >> first;
-  return static_cast<int>(((b & 1u) << 4) | ((b & 2u) << 11) | ((b & 4u) << 18) | ((b & 8u) << 25));
-}
-
 template <int T>
 struct QTraits;
 template <>
@@ -111,26 +74,45 @@ __device__ __forceinline__ float block_term(const uint8_t* wq, uint32_t qh, floa
 }
 
 constexpr int kQThreads = 128;
+constexpr int kQRegBlocks = 8;  // single-row decode: a lane keeps up to 8 activation blocks (ne0 <= 8192) in registers
 
-// y_j[t][r] over up to kMaxMulti weights of type T sharing the quantized activations (rows numbered
-// consecutively, as in the float GEMV). One warp per weight row with a grid stride; lane l takes blocks l, l + 32, ...
-// For each round of 32 blocks the lanes' terms are added to the row's sum in block order.
-template <int T, int NT>
+// The activation rows of a GEMV quantized to Q8_0 blocks once per call (one warp per block, the reference's
+// arithmetic): int8 values [n][ne0] and the fp32 value of each block's fp16 scale [n][ne0 / 32]. Launched with
+// programmatic stream serialization: it waits for x, then lets the GEMV launch and start streaming its weights.
+__global__ void quantize_rows_kernel(const float* __restrict__ x, int8_t* __restrict__ q, float* __restrict__ d,
+                                     int64_t n_blocks) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const int lane = threadIdx.x & 31;
+  const int64_t blk = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  if (blk >= n_blocks) return;
+  const float dd = quantize_block(x[blk * 32 + lane], &q[blk * 32 + lane]);
+  if (lane == 0) d[blk] = dd;
+}
+
+// y_j[t][r] over up to kMaxMulti weights of type T (rows numbered consecutively, as in the float GEMV), from the NT
+// quantized activation rows (aq, ad). One warp per weight row, grid-stride, lane l taking blocks l, l + 32, ...;
+// each round of 32 block terms is added to the row's sum in block order. The warp's first row is prefetched into
+// L2 before the kernel waits for the quantizer. REG (NT == 1, at most kQRegBlocks blocks per lane): each lane
+// keeps its activation blocks in registers across rows.
+template <int T, int NT, bool REG>
 __global__ void __launch_bounds__(kQThreads) gemv_q_kernel(const QBatch b, const int8_t* __restrict__ aq,
                                                            const float* __restrict__ ad, int64_t ne0) {
   constexpr int kQs = QTraits<T>::kQsBytes;
-  const int lane = threadIdx.x & 31;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t nb = ne0 / 32;
   int64_t total = b.row_end[0];
 #pragma unroll
   for (int i = 1; i < kMaxMulti; ++i)
     if (i < b.count) total = b.row_end[i];
   const int64_t n_warps = int64_t(gridDim.x) * (kQThreads / 32);
-  for (int64_t r = int64_t(blockIdx.x) * (kQThreads / 32) + (threadIdx.x >> 5); r < total; r += n_warps) {
-    // this row's weight j (a static scan of the parameter block)
-    QWeightView w = b.w[0];
-    float* y = b.y[0];
-    int64_t begin = 0, rows_j = b.row_end[0];
+  const int64_t r0 = int64_t(blockIdx.x) * (kQThreads / 32) + warp;
+  // this row's weight j (a static scan of the parameter block)
+  auto locate = [&](int64_t r, QWeightView& w, float*& y, int64_t& lr, int64_t& rows_j) {
+    w = b.w[0];
+    y = b.y[0];
+    int64_t begin = 0;
+    rows_j = b.row_end[0];
     bool found = r < b.row_end[0];
 #pragma unroll
     for (int i = 1; i < kMaxMulti; ++i)
@@ -141,11 +123,45 @@ __global__ void __launch_bounds__(kQThreads) gemv_q_kernel(const QBatch b, const
         begin = b.row_end[i - 1];
         rows_j = b.row_end[i] - b.row_end[i - 1];
       }
-    const int64_t lr = r - begin;
+    lr = r - begin;
+  };
+  if (r0 < total) {
+    QWeightView w;
+    float* y;
+    int64_t lr, rows_j;
+    locate(r0, w, y, lr, rows_j);
+    for (int64_t blk = lane; blk < nb; blk += 32)
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(w.qs + (lr * nb + blk) * kQs));
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // the quantized activations
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  int areg[REG ? kQRegBlocks : 1][8];
+  float dreg[REG ? kQRegBlocks : 1];
+  if constexpr (REG) {
+#pragma unroll
+    for (int i = 0; i < kQRegBlocks; ++i) {
+      const int64_t blk = lane + 32 * i;
+      if (blk < nb) {
+        const uint4 a0 = *reinterpret_cast<const uint4*>(aq + blk * 32);
+        const uint4 a1 = *reinterpret_cast<const uint4*>(aq + blk * 32 + 16);
+        areg[i][0] = int(a0.x), areg[i][1] = int(a0.y), areg[i][2] = int(a0.z), areg[i][3] = int(a0.w);
+        areg[i][4] = int(a1.x), areg[i][5] = int(a1.y), areg[i][6] = int(a1.z), areg[i][7] = int(a1.w);
+        dreg[i] = ad[blk];
+      }
+    }
+  }
+  for (int64_t r = r0; r < total; r += n_warps) {
+    QWeightView w;
+    float* y;
+    int64_t lr, rows_j;
+    locate(r, w, y, lr, rows_j);
     float sum[NT];
 #pragma unroll
     for (int t = 0; t < NT; ++t) sum[t] = 0.f;
-    for (int64_t k0 = 0; k0 < nb; k0 += 32) {
+#pragma unroll(REG ? kQRegBlocks : 1)
+    for (int round = 0; round < (REG ? kQRegBlocks : 1 << 30); ++round) {
+      const int64_t k0 = int64_t(round) * 32;
+      if (k0 >= nb) break;
       const int64_t blk = k0 + lane;
       float term[NT];
       if (blk < nb) {
@@ -153,12 +169,16 @@ __global__ void __launch_bounds__(kQThreads) gemv_q_kernel(const QBatch b, const
         const float dw = __half2float(__ushort_as_half(w.d[wb]));
         const uint32_t qh = T == NBL_Q5_0 ? w.qh[wb] : 0u;
         const uint8_t* wq = w.qs + wb * kQs;
+        if constexpr (REG) {
+          term[0] = block_term<T>(wq, qh, dw, areg[round], dreg[round]);
+        } else {
 #pragma unroll
-        for (int t = 0; t < NT; ++t) {
-          const uint4 a0 = *reinterpret_cast<const uint4*>(aq + t * ne0 + blk * 32);
-          const uint4 a1 = *reinterpret_cast<const uint4*>(aq + t * ne0 + blk * 32 + 16);
-          const int av[8] = {int(a0.x), int(a0.y), int(a0.z), int(a0.w), int(a1.x), int(a1.y), int(a1.z), int(a1.w)};
-          term[t] = block_term<T>(wq, qh, dw, av, ad[t * nb + blk]);
+          for (int t = 0; t < NT; ++t) {
+            const uint4 a0 = *reinterpret_cast<const uint4*>(aq + t * ne0 + blk * 32);
+            const uint4 a1 = *reinterpret_cast<const uint4*>(aq + t * ne0 + blk * 32 + 16);
+            const int av[8] = {int(a0.x), int(a0.y), int(a0.z), int(a0.w), int(a1.x), int(a1.y), int(a1.z), int(a1.w)};
+            term[t] = block_term<T>(wq, qh, dw, av, ad[t * nb + blk]);
+          }
         }
       } else {
 #pragma unroll
@@ -203,25 +223,45 @@ __global__ void embed_q_kernel(const QWeightView w, const int32_t* __restrict__ 
   }
 }
 
-template <int T, int NT>
+cudaLaunchAttribute pdl_attr() {
+  cudaLaunchAttribute a;
+  a.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  a.val.programmaticStreamSerializationAllowed = 1;
+  return a;
+}
+
+// Both launches use programmatic stream serialization (each kernel waits for its predecessor before reading).
+template <int T, int NT, bool REG>
 void gemv_q_t(cudaStream_t st, const QBatch& b, const int8_t* aq, const float* ad, int64_t ne0, int num_sms) {
-  int64_t total = b.row_end[b.count - 1];
-  const int64_t grid = std::min<int64_t>((total + kQThreads / 32 - 1) / (kQThreads / 32), int64_t(num_sms) * 8);
-  gemv_q_kernel<T, NT><<<static_cast<unsigned>(grid), kQThreads, 0, st>>>(b, aq, ad, ne0);
+  const int64_t total = b.row_end[b.count - 1];
+  int per_sm = 0;
+  check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_q_kernel<T, NT, REG>, kQThreads, 0),
+             "quant gemv occupancy");
+  const int64_t grid = std::min<int64_t>((total + kQThreads / 32 - 1) / (kQThreads / 32),
+                                         int64_t(num_sms) * std::max(1, std::min(per_sm, 8)));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(kQThreads);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1] = {pdl_attr()};
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  check_cuda(cudaLaunchKernelEx(&cfg, gemv_q_kernel<T, NT, REG>, b, aq, ad, ne0), "quant gemv launch");
 }
 
 template <int T>
 void gemv_q_dispatch(cudaStream_t st, const QBatch& b, const int8_t* aq, const float* ad, int64_t ne0, int64_t n,
                      int sms) {
+  if (n == 1 && ne0 / 32 <= 32 * kQRegBlocks) return gemv_q_t<T, 1, true>(st, b, aq, ad, ne0, sms);
   switch (n) {
-    case 1: return gemv_q_t<T, 1>(st, b, aq, ad, ne0, sms);
-    case 2: return gemv_q_t<T, 2>(st, b, aq, ad, ne0, sms);
-    case 3: return gemv_q_t<T, 3>(st, b, aq, ad, ne0, sms);
-    case 4: return gemv_q_t<T, 4>(st, b, aq, ad, ne0, sms);
-    case 5: return gemv_q_t<T, 5>(st, b, aq, ad, ne0, sms);
-    case 6: return gemv_q_t<T, 6>(st, b, aq, ad, ne0, sms);
-    case 7: return gemv_q_t<T, 7>(st, b, aq, ad, ne0, sms);
-    default: return gemv_q_t<T, 8>(st, b, aq, ad, ne0, sms);
+    case 1: return gemv_q_t<T, 1, false>(st, b, aq, ad, ne0, sms);
+    case 2: return gemv_q_t<T, 2, false>(st, b, aq, ad, ne0, sms);
+    case 3: return gemv_q_t<T, 3, false>(st, b, aq, ad, ne0, sms);
+    case 4: return gemv_q_t<T, 4, false>(st, b, aq, ad, ne0, sms);
+    case 5: return gemv_q_t<T, 5, false>(st, b, aq, ad, ne0, sms);
+    case 6: return gemv_q_t<T, 6, false>(st, b, aq, ad, ne0, sms);
+    case 7: return gemv_q_t<T, 7, false>(st, b, aq, ad, ne0, sms);
+    default: return gemv_q_t<T, 8, false>(st, b, aq, ad, ne0, sms);
   }
 }
 
@@ -235,18 +275,29 @@ int64_t quant_block_bytes(int32_t dtype) {
 
 int64_t quant_qs_bytes(int32_t dtype) { return dtype == NBL_Q8_0 ? 32 : 16; }
 
-void launch_quantize_q8_0(cudaStream_t st, const float* x, int8_t* qs, float* d, int64_t n_elems) {
-  const int64_t blocks = n_elems / 32;
-  const int64_t grid = (blocks * 32 + 255) / 256;
-  quantize_q8_0_kernel<<<static_cast<unsigned>(grid), 256, 0, st>>>(x, qs, d, blocks);
+size_t gemv_q_act_bytes(int64_t ne0) {
+  return static_cast<size_t>(kGemvMaxRows * ne0) + static_cast<size_t>(kGemvMaxRows * (ne0 / 32)) * sizeof(float);
 }
 
-void launch_gemv_q(cudaStream_t st, const Weight* const* ws, float* const* ys, int count, const int8_t* aq,
-                   const float* ad, int64_t n, int num_sms) {
+void launch_gemv_q(cudaStream_t st, const Weight* const* ws, float* const* ys, int count, const float* x, int64_t n,
+                   void* act, int num_sms) {
   const Weight& w0 = *ws[0];
   const int64_t ne0 = w0.ne0, nb = ne0 / 32;
+  int8_t* aq = static_cast<int8_t*>(act);
+  float* ad = reinterpret_cast<float*>(aq + kGemvMaxRows * ne0);
   for (int64_t t0 = 0; t0 < n; t0 += kGemvMaxRows) {
     const int64_t nt = std::min<int64_t>(kGemvMaxRows, n - t0);
+    {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(static_cast<unsigned>((nt * nb + 7) / 8));
+      cfg.blockDim = dim3(256);
+      cfg.stream = st;
+      cudaLaunchAttribute attr[1] = {pdl_attr()};
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      check_cuda(cudaLaunchKernelEx(&cfg, quantize_rows_kernel, x + t0 * ne0, aq, ad, nt * nb),
+                 "quantize activations launch");
+    }
     QBatch b{};
     b.count = count;
     int64_t rows = 0;
@@ -256,12 +307,10 @@ void launch_gemv_q(cudaStream_t st, const Weight* const* ws, float* const* ys, i
       rows += ws[i]->ne1;
       b.row_end[i] = rows;
     }
-    const int8_t* a = aq + t0 * ne0;
-    const float* d = ad + t0 * nb;
     switch (w0.dtype) {
-      case NBL_Q4_0: gemv_q_dispatch<NBL_Q4_0>(st, b, a, d, ne0, nt, num_sms); break;
-      case NBL_Q5_0: gemv_q_dispatch<NBL_Q5_0>(st, b, a, d, ne0, nt, num_sms); break;
-      default: gemv_q_dispatch<NBL_Q8_0>(st, b, a, d, ne0, nt, num_sms); break;
+      case NBL_Q4_0: gemv_q_dispatch<NBL_Q4_0>(st, b, aq, ad, ne0, nt, num_sms); break;
+      case NBL_Q5_0: gemv_q_dispatch<NBL_Q5_0>(st, b, aq, ad, ne0, nt, num_sms); break;
+      default: gemv_q_dispatch<NBL_Q8_0>(st, b, aq, ad, ne0, nt, num_sms); break;
     }
   }
 }

@@ -27,7 +27,7 @@ def host(t):
 @pytest.mark.parametrize("name", sorted(TYPES))
 @pytest.mark.parametrize("n", [1, 3, 8, 9, 20])
 def test_quant_matmul_bit_exact(nbl_ctx, name, n):
-    """n <= 8 is one launch; larger n runs in chunks of 8 activation rows. Widths of 96 (3 blocks), 2048 (two full
+    """n <= 8 is the GEMV (one launch); 9 and 20 rows the tensor-core GEMM. Widths of 96 (3 blocks), 2048 (two full
     rounds of 32 blocks) and 5632 (176 blocks: a partial last round)."""
     import torch
     odt, cdt = TYPES[name]
@@ -61,6 +61,51 @@ def test_quant_matmul_multi_and_zero_blocks(nbl_ctx, name):
     for w, y in zip(ws, ys):
         ref = oracle.matmul_q(w, odt, ne0, w.shape[0], x, 2)
         assert np.array_equal(host(y).view(np.uint32), ref.view(np.uint32))
+    for wt in wts:
+        wt.close()
+
+
+@pytest.mark.parametrize("name", sorted(TYPES))
+@pytest.mark.parametrize("n", [9, 127, 128, 257])
+def test_quant_gemm_bit_exact(nbl_ctx, name, n):
+    """More than 8 activation rows run on the tensor cores (one kind::i8 MMA per block, terms added in block
+    order by the epilogue). Shapes cover a width below one 128-byte stage (32), a block count that is not a
+    multiple of the 4 blocks per stage (160 = 5 blocks), weight-row counts that are not a multiple of the 128-row
+    tile, and token counts on both sides of the 128-row token tile."""
+    import torch
+    odt, cdt = TYPES[name]
+    rng = np.random.default_rng(n * 7 + cdt)
+    for ne1, ne0 in [(129, 32), (200, 160), (300, 1024)]:
+        w = oracle.random_q_blocks(rng, odt, ne1, ne0)
+        x = (rng.standard_normal((n, ne0)) * 3).astype(np.float32)
+        x[n // 2, :32] = 0.0  # a zero block: scale 0, terms +0
+        wt = nbl_ctx.weight(w, cdt, ne0)
+        y = torch.full((n, ne1), float("nan"), device="cuda")
+        nbl_ctx.matmul(wt, dev(x), y, n)
+        ref = oracle.matmul_q(w, odt, ne0, ne1, x, n)
+        got = host(y)
+        assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), (
+            ne1, ne0, int((got.view(np.uint32) != ref.view(np.uint32)).sum()))
+        wt.close()
+
+
+@pytest.mark.parametrize("name", sorted(TYPES))
+def test_quant_gemm_multi(nbl_ctx, name):
+    """matmul_multi on the tensor-core path: five weights of one type (a group of four in one launch, then one),
+    with row counts that end mid-tile, and the same weights again so the cached operands are reused."""
+    import torch
+    odt, cdt = TYPES[name]
+    rng = np.random.default_rng(90 + cdt)
+    ne0, n = 512, 45
+    ws = [oracle.random_q_blocks(rng, odt, r, ne0) for r in (256, 100, 100, 640, 33)]
+    wts = [nbl_ctx.weight(w, cdt, ne0) for w in ws]
+    for rep in range(2):
+        x = (rng.standard_normal((n, ne0)) * (rep + 1)).astype(np.float32)
+        ys = [torch.full((n, w.shape[0]), float("nan"), device="cuda") for w in ws]
+        nbl_ctx.matmul_multi(wts, dev(x), ys, n)
+        for w, y in zip(ws, ys):
+            ref = oracle.matmul_q(w, odt, ne0, w.shape[0], x, n)
+            assert np.array_equal(host(y).view(np.uint32), ref.view(np.uint32)), (rep, w.shape)
     for wt in wts:
         wt.close()
 
