@@ -7,9 +7,9 @@
 // (Q4_0: sumi * d_w * d_a; Q8_0: sumi * (d_w * d_a); Q5_0: (d_w * d_a) * sumi). The integer dots are exact, so
 // they can come from anywhere; the float ops and their order cannot change.
 //
-// So here the tensor core computes the integer dots and nothing else: for a tile of 128 weight rows x 128
-// activation rows, one tcgen05.mma kind::i8 (K = 32 = one block) per block writes that block's 128 x 128 int32
-// dots into its own TMEM buffer (4 buffers of 128 columns, a ring), and 16 epilogue warps read each buffer back
+// So here the tensor core computes the integer dots and nothing else: for a tile of 128 weight rows x BN (128 or
+// 64) activation rows, one tcgen05.mma kind::i8 (K = 32 = one block) per block writes that block's 128 x BN int32
+// dots into its own TMEM buffer (4 buffers of BN columns, a ring), and the epilogue warps read each buffer back
 // and add the block's terms to per-output running sums, in block order, with the reference's rounding: every
 // multiply and add rounded on its own. (The exact int-to-float conversion and the first product run as packed
 // f32x2 operations; the product that feeds the add and the add itself are the scalar _rn intrinsics, since the
@@ -19,8 +19,8 @@
 // Operands (made once per weight, on its first multi-row matmul): the weight's values as int8 [rows][ne0] (Q8_0's
 // device values as they are; Q4_0 and Q5_0 unpacked to value - 8 / value - 16) and its scales as fp32
 // [blocks][rows]; the activations quantized per call into int8 [n][ne0] and fp32 scales [blocks][n]. All four
-// arrive by TMA: per stage, 4 blocks (128 bytes of K) of 128 weight rows and of 128 activation rows (128-byte
-// swizzle, the canonical K-major layout the MMA reads) plus the 4 x 128 scales of each side.
+// arrive by TMA: per stage, 4 blocks (128 bytes of K) of 128 weight rows and of BN activation rows (128-byte
+// swizzle, the canonical K-major layout the MMA reads) plus the 4 x 128 and 4 x BN scales.
 #include <algorithm>
 #include <atomic>
 
@@ -32,25 +32,32 @@ namespace nbl {
 namespace {
 
 constexpr int kBM = 128;                     // weight rows per tile: MMA M, TMEM lanes
-constexpr int kBN = 128;                     // activation rows per tile: MMA N, int32 TMEM columns per buffer
 constexpr int kBlocksPerStage = 4;           // 4 blocks of 32 int8 = one 128-byte swizzle row
 constexpr int kStages = 4;
-constexpr int kTmemBufs = 4;                 // kTmemBufs * kBN = 512 columns
-constexpr int kGroups = 4;                   // column groups of the epilogue
-constexpr int kGroupCols = kBN / kGroups;    // 32 activation rows per epilogue warp
-constexpr int kEpiWarps = 4 * kGroups;       // each TMEM lane quarter x each column group
+constexpr int kTmemBufs = 4;                 // a ring of kTmemBufs int32 accumulators of BN columns
+constexpr int kGroupCols = 32;               // activation rows per epilogue warp
 constexpr int kWarpTma = 0, kWarpMma = 1, kWarpEpi0 = 2;
-constexpr int kThreads = 32 * (kWarpEpi0 + kEpiWarps);
-constexpr uint32_t kABytes = kBM * 128, kBBytes = kBN * 128;
-constexpr uint32_t kDaBytes = kBlocksPerStage * kBN * 4, kDwBytes = kBlocksPerStage * kBM * 4;
-constexpr uint32_t kStageBytes = kABytes + kBBytes + kDaBytes + kDwBytes;
-static_assert(kStageBytes % 1024 == 0, "stages must keep the 1024-byte alignment of the swizzled tiles");
-constexpr uint32_t kOffBar = kStages * kStageBytes;
 // barriers: full[kStages], empty[kStages], tfull[kTmemBufs], tempty[kTmemBufs], drain; then the TMEM address
 constexpr int kBarFull = 0, kBarEmpty = kStages, kBarTFull = 2 * kStages, kBarTEmpty = 2 * kStages + kTmemBufs,
               kBarDrain = 2 * kStages + 2 * kTmemBufs, kNumBars = kBarDrain + 1;
-constexpr uint32_t kOffTmemSlot = kOffBar + kNumBars * 8;
-constexpr uint32_t kSmemBytes = kOffTmemSlot + 16;
+
+// The layout of one CTA for BN activation rows per tile: BN = 128 runs one CTA per SM with 16 epilogue warps;
+// BN = 64 (small matrices: more tiles to spread over the SMs) runs two CTAs per SM with 8 epilogue warps each.
+template <int BN>
+struct GCfg {
+  static constexpr int kGroups = BN / kGroupCols;     // column groups of the epilogue
+  static constexpr int kEpiWarps = 4 * kGroups;        // each TMEM lane quarter x each column group
+  static constexpr int kThreads = 32 * (kWarpEpi0 + kEpiWarps);
+  static constexpr int kCtasPerSm = 128 / BN;
+  static constexpr uint32_t kTmemCols = kTmemBufs * BN;
+  static constexpr uint32_t kABytes = kBM * 128, kBBytes = BN * 128;
+  static constexpr uint32_t kDaBytes = kBlocksPerStage * BN * 4, kDwBytes = kBlocksPerStage * kBM * 4;
+  static constexpr uint32_t kStageBytes = kABytes + kBBytes + kDaBytes + kDwBytes;
+  static_assert(kStageBytes % 1024 == 0, "stages must keep the 1024-byte alignment of the swizzled tiles");
+  static constexpr uint32_t kOffBar = kStages * kStageBytes;
+  static constexpr uint32_t kOffTmemSlot = kOffBar + kNumBars * 8;
+  static constexpr uint32_t kSmemBytes = kOffTmemSlot + 16;
+};
 
 // Instruction descriptor for kind::i8: signed 8-bit A and B, s32 accumulator, both operands K-major.
 __host__ __device__ constexpr uint32_t make_idesc_i8(int m, int n) {
@@ -113,8 +120,8 @@ __device__ __forceinline__ uint64_t exact_float2(uint32_t s0, uint32_t s1) {
 struct QGemmMaps {
   CUtensorMap wv[kMaxMulti];  // weight values, int8 [rows][ne0], box 128 x 128, 128-byte swizzle
   CUtensorMap wd[kMaxMulti];  // weight scales, fp32 [blocks][rows], box 4 x 128
-  CUtensorMap av;             // activation values, int8 [n][ne0], box 128 x 128, 128-byte swizzle
-  CUtensorMap ad;             // activation scales, fp32 [blocks][n], box 4 x 128
+  CUtensorMap av;             // activation values, int8 [n][ne0], box 128 x BN, 128-byte swizzle
+  CUtensorMap ad;             // activation scales, fp32 [blocks][n], box 4 x BN
 };
 struct QGemmArgs {
   float* y[kMaxMulti];
@@ -127,6 +134,7 @@ struct QGemmArgs {
 struct Tile {
   int j, row0, tok0;
 };
+template <int BN>
 __device__ __forceinline__ Tile tile_of(const QGemmArgs& a, int t) {
   int j = 0, begin = 0;
 #pragma unroll
@@ -136,7 +144,7 @@ __device__ __forceinline__ Tile tile_of(const QGemmArgs& a, int t) {
       begin = a.tiles_end[i - 1];
     }
   const int local = t - begin;
-  return {j, (local / a.n_tt) * kBM, (local % a.n_tt) * kBN};
+  return {j, (local / a.n_tt) * kBM, (local % a.n_tt) * BN};
 }
 template <typename T>
 __device__ __forceinline__ T pick(const T (&v)[kMaxMulti], int j) {
@@ -147,17 +155,20 @@ __device__ __forceinline__ T pick(const T (&v)[kMaxMulti], int j) {
   return r;
 }
 
-template <int T>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int T, int BN>
+__global__ void __launch_bounds__(GCfg<BN>::kThreads, GCfg<BN>::kCtasPerSm)
     qgemm_kernel(const __grid_constant__ QGemmMaps maps, const QGemmArgs a) {
+  using C = GCfg<BN>;
+  constexpr int kEpiWarps = C::kEpiWarps;
+  constexpr uint32_t kABytes = C::kABytes, kBBytes = C::kBBytes, kDaBytes = C::kDaBytes, kStageBytes = C::kStageBytes;
   extern __shared__ __align__(1024) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (smem_u32(smem) & 1023u) {  // swizzled tiles need 1024-byte alignment; never expected to trip
     if (threadIdx.x == 0) flag_error(a.err, kErrSmemAlign);
     return;
   }
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffTmemSlot);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kOffTmemSlot);
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&bars[kBarFull + s], 1);
@@ -171,7 +182,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_barrier_init();
   }
   if (warp == kWarpMma) {
-    tmem_alloc(tmem_slot, kTmemBufs * kBN);
+    tmem_alloc(tmem_slot, C::kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -188,7 +199,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int kt = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < a.n_tiles && ok; t += gridDim.x) {
-        const Tile tl = tile_of(a, t);
+        const Tile tl = tile_of<BN>(a, t);
         const CUtensorMap* wv = &maps.wv[0];
         const CUtensorMap* wd = &maps.wd[0];
 #pragma unroll
@@ -215,7 +226,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == kWarpMma) {
     // ================= MMA issuer: one kind::i8 MMA per block into the next TMEM buffer of the ring
     if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc_i8(kBM, kBN);
+      constexpr uint32_t idesc = make_idesc_i8(kBM, BN);
       int kt = 0, kb = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < a.n_tiles && ok; t += gridDim.x) {
@@ -234,7 +245,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               break;
             }
             tc_fence_after();
-            tc_mma_i8(tmem + buf * kBN, make_sdesc(a_addr + i * 32, 16, 1024, 2),
+            tc_mma_i8(tmem + buf * BN, make_sdesc(a_addr + i * 32, 16, 1024, 2),
                       make_sdesc(b_addr + i * 32, 16, 1024, 2), idesc);
             tc_commit(&bars[kBarTFull + buf]);
           }
@@ -254,7 +265,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int kt = 0, kb = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < a.n_tiles && ok; t += gridDim.x) {
-      const Tile tl = tile_of(a, t);
+      const Tile tl = tile_of<BN>(a, t);
       float sum[kGroupCols];
 #pragma unroll
       for (int c = 0; c < kGroupCols; ++c) sum[c] = 0.f;
@@ -265,7 +276,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         const float* da_s = reinterpret_cast<const float*>(smem + s * kStageBytes + kABytes + kBBytes);
-        const float* dw_s = da_s + kBlocksPerStage * kBN;
+        const float* dw_s = da_s + kBlocksPerStage * BN;
         for (int i = 0; i < kBlocksPerStage && kc * kBlocksPerStage + i < a.nb; ++i, ++kb) {
           const int buf = kb % kTmemBufs;
           if (!warp_wait_all(&bars[kBarTFull + buf], (kb / kTmemBufs) & 1, a.err)) {
@@ -274,14 +285,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_after();
           uint32_t raw[kGroupCols];
-          tmem_ld32(tmem + t_lane + buf * kBN + group * kGroupCols, raw);
+          tmem_ld32(tmem + t_lane + buf * BN + group * kGroupCols, raw);
           tc_wait_ld();
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&bars[kBarTEmpty + buf]);
           const float dw = dw_s[i * kBM + r_in];
           const uint64_t dw2 = f2(dw, dw);
-          const float4* da4 = reinterpret_cast<const float4*>(da_s + i * kBN + group * kGroupCols);
+          const float4* da4 = reinterpret_cast<const float4*>(da_s + i * BN + group * kGroupCols);
 #pragma unroll
           for (int c4 = 0; c4 < kGroupCols / 4; ++c4) {
             const float4 d = da4[c4];
@@ -322,7 +333,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == kWarpMma) {
     tc_fence_after();
-    tmem_dealloc(tmem, kTmemBufs * kBN);
+    tmem_dealloc(tmem, C::kTmemCols);
   }
 }
 
@@ -376,32 +387,42 @@ __global__ void scales_t_kernel(const uint16_t* __restrict__ d, float* __restric
 
 int64_t pad4(int64_t v) { return (v + 3) / 4 * 4; }
 
-void encode_values(CUtensorMap* m, const void* base, int64_t ne0, int64_t rows) {
+void encode_values(CUtensorMap* m, const void* base, int64_t ne0, int64_t rows, int box_rows) {
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(ne0), static_cast<cuuint64_t>(rows)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ne0)};
-  const cuuint32_t box[2] = {128, kBM};
+  const cuuint32_t box[2] = {128, static_cast<cuuint32_t>(box_rows)};
   encode_tmap(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box);
 }
-void encode_scales(CUtensorMap* m, const float* base, int64_t rows, int64_t nb) {
+void encode_scales(CUtensorMap* m, const float* base, int64_t rows, int64_t nb, int box_rows) {
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(nb)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(pad4(rows) * 4)};
-  const cuuint32_t box[2] = {kBM, kBlocksPerStage};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_rows), kBlocksPerStage};
   encode_tmap(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box,
               CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
-template <int T>
+template <int T, int BN>
 void launch_t(cudaStream_t st, const QGemmMaps& maps, const QGemmArgs& a, int grid) {
+  using C = GCfg<BN>;
   static std::atomic<uint64_t> configured{0};
   int dev = 0;
   check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
   const uint64_t bit = uint64_t(1) << (dev & 63);
   if (!(configured.load() & bit)) {
-    check_cuda(cudaFuncSetAttribute(qgemm_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes),
+    check_cuda(cudaFuncSetAttribute(qgemm_kernel<T, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes),
                "quant gemm smem attribute");
     configured.fetch_or(bit);
   }
-  qgemm_kernel<T><<<grid, kThreads, kSmemBytes, st>>>(maps, a);
+  qgemm_kernel<T, BN><<<grid, C::kThreads, C::kSmemBytes, st>>>(maps, a);
+}
+
+template <int BN>
+void launch_bn(cudaStream_t st, int32_t dtype, const QGemmMaps& maps, const QGemmArgs& a, int grid) {
+  switch (dtype) {
+    case NBL_Q4_0: launch_t<NBL_Q4_0, BN>(st, maps, a, grid); break;
+    case NBL_Q5_0: launch_t<NBL_Q5_0, BN>(st, maps, a, grid); break;
+    default: launch_t<NBL_Q8_0, BN>(st, maps, a, grid); break;
+  }
 }
 
 }  // namespace
@@ -425,8 +446,8 @@ void prepare_qgemm(cudaStream_t st, Weight& w, int num_sms) {
     const int64_t blocks = std::min<int64_t>((w.ne1 * nb + 255) / 256, int64_t(num_sms) * 16);
     scales_t_kernel<<<blocks, 256, 0, st>>>(w.q.d, g->scales_t, w.ne1, nb, pad4(w.ne1));
     check_cuda(cudaGetLastError(), "quant gemm scales");
-    encode_values(&g->vmap, g->vals, w.ne0, w.ne1);
-    encode_scales(&g->smap, g->scales_t, w.ne1, nb);
+    encode_values(&g->vmap, g->vals, w.ne0, w.ne1, kBM);
+    encode_scales(&g->smap, g->scales_t, w.ne1, nb, kBM);
   } catch (...) {
     release_qgemm(g);
     throw;
@@ -459,8 +480,12 @@ void launch_qgemm(cudaStream_t st, const Weight* const* ws, float* const* ys, in
   a.count = count;
   a.n = static_cast<int>(n);
   a.nb = static_cast<int>(nb);
-  a.n_tt = static_cast<int>((n + kBN - 1) / kBN);
   a.err = err;
+  // 128 activation rows per tile, or 64 (two CTAs per SM) when 128 would leave fewer than two tiles per SM
+  int64_t row_tiles = 0;
+  for (int i = 0; i < count; ++i) row_tiles += (ws[i]->ne1 + kBM - 1) / kBM;
+  const int bn = row_tiles * ((n + 127) / 128) < 2 * int64_t(num_sms) ? 64 : 128;
+  a.n_tt = static_cast<int>((n + bn - 1) / bn);
   int tiles = 0;
   for (int i = 0; i < count; ++i) {
     maps.wv[i] = ws[i]->qg->vmap;
@@ -478,14 +503,11 @@ void launch_qgemm(cudaStream_t st, const Weight* const* ws, float* const* ys, in
     a.tiles_end[i] = tiles;
   }
   a.n_tiles = tiles;
-  encode_values(&maps.av, aq, ne0, n);
-  encode_scales(&maps.ad, ad, n, nb);
-  const int grid = static_cast<int>(std::min<int64_t>(tiles, num_sms));
-  switch (ws[0]->dtype) {
-    case NBL_Q4_0: launch_t<NBL_Q4_0>(st, maps, a, grid); break;
-    case NBL_Q5_0: launch_t<NBL_Q5_0>(st, maps, a, grid); break;
-    default: launch_t<NBL_Q8_0>(st, maps, a, grid); break;
-  }
+  encode_values(&maps.av, aq, ne0, n, bn);
+  encode_scales(&maps.ad, ad, n, nb, bn);
+  const int grid = static_cast<int>(std::min<int64_t>(tiles, int64_t(num_sms) * (128 / bn)));
+  if (bn == 64) launch_bn<64>(st, ws[0]->dtype, maps, a, grid);
+  else launch_bn<128>(st, ws[0]->dtype, maps, a, grid);
   check_cuda(cudaGetLastError(), "quant gemm launch");
 }
 

@@ -90,6 +90,25 @@ def test_quant_gemm_bit_exact(nbl_ctx, name, n):
 
 
 @pytest.mark.parametrize("name", sorted(TYPES))
+def test_quant_gemm_large_grid(nbl_ctx, name):
+    """Enough tiles (75 weight-row tiles x 4 activation-row tiles of 128) for the one-CTA-per-SM layout with
+    128-row activation tiles; the smaller cases above run the two-CTAs-per-SM layout with 64-row tiles."""
+    import torch
+    odt, cdt = TYPES[name]
+    rng = np.random.default_rng(70 + cdt)
+    ne1, ne0, n = 9600, 96, 400
+    w = oracle.random_q_blocks(rng, odt, ne1, ne0)
+    x = (rng.standard_normal((n, ne0)) * 3).astype(np.float32)
+    wt = nbl_ctx.weight(w, cdt, ne0)
+    y = torch.full((n, ne1), float("nan"), device="cuda")
+    nbl_ctx.matmul(wt, dev(x), y, n)
+    ref = oracle.matmul_q(w, odt, ne0, ne1, x, n)
+    got = host(y)
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), int((got.view(np.uint32) != ref.view(np.uint32)).sum())
+    wt.close()
+
+
+@pytest.mark.parametrize("name", sorted(TYPES))
 def test_quant_gemm_multi(nbl_ctx, name):
     """matmul_multi on the tensor-core path: five weights of one type (a group of four in one launch, then one),
     with row counts that end mid-tile, and the same weights again so the cached operands are reused."""
