@@ -67,10 +67,11 @@ class CudaBackend final : public Backend {
   // Waits for queued work; throws Error if a kernel flagged an out-of-range device-side index.
   void synchronize();
   nbl_ctx* handle() const { return ctx_; }
+  // The device copy of a weight Tensor (uploaded on first use, cached by host address); shared with code that runs
+  // the same model through the nbl_* calls directly (BatchedDecoder).
+  const nbl_weight* device_weight(const Tensor& t);
 
  private:
-  // The device copy of a weight Tensor (uploaded on first use, cached by host address).
-  const nbl_weight* device_weight(const Tensor& t);
 
   nbl_ctx* ctx_ = nullptr;
   std::unordered_map<const void*, nbl_weight*> weights_;  // host weight address -> uploaded tensor
