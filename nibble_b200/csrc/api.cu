@@ -181,6 +181,8 @@ void ensure_ids(nbl_ctx* ctx, int64_t n) {
 
 void release_weight(nbl_weight* w) {
   nbl::release_qgemm(w->w.qg);
+  if (w->w.tf_hi) cudaFree(w->w.tf_hi);
+  if (w->w.tf_lo) cudaFree(w->w.tf_lo);
   if (w->w.f32 && w->w.f32 != w->w.dev) cudaFree(w->w.f32);
   cudaFree(w->w.dev);
   delete w;
@@ -197,6 +199,48 @@ const float* weight_f32(nbl_ctx* ctx, const nbl_weight* cw) {
     nbl::check_cuda(cudaGetLastError(), "widen launch");
   }
   return w->w.f32;
+}
+
+// Grows a context-owned scratch buffer to `need` bytes (waiting for queued work before freeing the old one).
+void grow_scratch(nbl_ctx* ctx, void*& buf, size_t& bytes, size_t need, const char* what) {
+  if (bytes >= need) return;
+  if (buf) {
+    nbl::check_cuda(cudaStreamSynchronize(ctx->stream), what);
+    cudaFree(buf);
+    buf = nullptr;
+    bytes = 0;
+  }
+  buf = device_alloc(need, what);
+  bytes = need;
+}
+
+// A float-weight matmul of n > kGemvMaxRows activation rows: the tf32-split tensor-core GEMM (its weight operand
+// made on first use: the fp32 widening of an F16 matrix, or the two tf32 terms of an F32 one) from kFgemmMinRows
+// rows on, SGEMM below that and for row widths TMA cannot tile.
+constexpr int64_t kFgemmMinRows = 128;
+void float_gemm(nbl_ctx* ctx, const nbl_weight* cw, const float* x, float* y, int64_t n) {
+  auto* w = const_cast<nbl_weight*>(cw);
+  // below ~128 rows the tiles cover too few SMs (no split-K yet) and SGEMM measured faster (batched decode steps)
+  if (!nbl::fgemm_supported(w->w.ne0) || n < kFgemmMinRows) {
+    nbl::gemm_f32(cublas_handle(ctx), ctx->stream, weight_f32(ctx, w), x, y, w->w.ne0, w->w.ne1, n);
+    return;
+  }
+  const float* hi;
+  const float* lo = nullptr;
+  if (w->w.dtype == NBL_F16) {
+    hi = weight_f32(ctx, w);
+  } else {
+    if (!w->w.tf_hi) {
+      const int64_t count = w->w.ne0 * w->w.ne1;
+      w->w.tf_hi = static_cast<float*>(device_alloc(static_cast<size_t>(count) * sizeof(float), "weight tf32 terms"));
+      w->w.tf_lo = static_cast<float*>(device_alloc(static_cast<size_t>(count) * sizeof(float), "weight tf32 terms"));
+      nbl::split_tf32(ctx->stream, static_cast<const float*>(w->w.dev), w->w.tf_hi, w->w.tf_lo, count, ctx->num_sms);
+    }
+    hi = w->w.tf_hi;
+    lo = w->w.tf_lo;
+  }
+  grow_scratch(ctx, ctx->fgemm_act, ctx->fgemm_act_bytes, nbl::fgemm_act_bytes(n, w->w.ne0), "float gemm activations");
+  nbl::launch_fgemm(ctx->stream, hi, lo, w->w.ne0, w->w.ne1, x, y, n, ctx->fgemm_act, ctx->num_sms, ctx->d_err);
 }
 
 // A quantized matmul of n activation rows for weights of one quantized type sharing ne0 (count <= kMaxMulti):
@@ -222,17 +266,8 @@ void quant_matmul(nbl_ctx* ctx, const nbl_weight* const* cws, float* const* ys, 
     return;
   }
   for (int i = 0; i < count; ++i) nbl::prepare_qgemm(ctx->stream, const_cast<nbl_weight*>(cws[i])->w, ctx->num_sms);
-  const size_t need = nbl::qgemm_act_bytes(n, ws[0]->ne0);
-  if (ctx->qgemm_act_bytes < need) {
-    if (ctx->qgemm_act) {
-      nbl::check_cuda(cudaStreamSynchronize(ctx->stream), "quant gemm scratch");
-      cudaFree(ctx->qgemm_act);
-      ctx->qgemm_act = nullptr;
-      ctx->qgemm_act_bytes = 0;
-    }
-    ctx->qgemm_act = device_alloc(need, "quant gemm activations");
-    ctx->qgemm_act_bytes = need;
-  }
+  grow_scratch(ctx, ctx->qgemm_act, ctx->qgemm_act_bytes, nbl::qgemm_act_bytes(n, ws[0]->ne0),
+               "quant gemm activations");
   nbl::launch_qgemm(ctx->stream, ws, ys, count, x, n, ctx->qgemm_act, ctx->num_sms, ctx->d_err);
 }
 
@@ -301,6 +336,7 @@ int nbl_ctx_destroy(nbl_ctx* ctx) {
     if (ctx->cublas_ws) cudaFree(ctx->cublas_ws);
     if (ctx->ids) cudaFree(ctx->ids);
     if (ctx->qgemm_act) cudaFree(ctx->qgemm_act);
+    if (ctx->fgemm_act) cudaFree(ctx->fgemm_act);
     if (ctx->qgemv_act) cudaFree(ctx->qgemv_act);
     for (auto& a : ctx->allocs) cudaFree(a.first);
     for (auto& t : ctx->rope_tables) cudaFree(t.dev);
@@ -844,7 +880,7 @@ int nbl_matmul(nbl_ctx* ctx, const nbl_weight* w, const float* x, float* y, int6
       nbl::launch_gemv(ctx->stream, w->w, x, y, n, ctx->num_sms);
       nbl::check_cuda(cudaGetLastError(), "matmul launch");
     } else {
-      nbl::gemm_f32(cublas_handle(ctx), ctx->stream, weight_f32(ctx, w), x, y, w->w.ne0, w->w.ne1, n);
+      float_gemm(ctx, w, x, y, n);
     }
   });
 }
@@ -880,8 +916,7 @@ int nbl_matmul_multi(nbl_ctx* ctx, const nbl_weight* const* ws, int32_t count, c
           } else if (n <= nbl::kGemvMaxRows) {
             nbl::launch_gemv(ctx->stream, ws[i]->w, x, ys[i], n, ctx->num_sms);
           } else {
-            nbl::gemm_f32(cublas_handle(ctx), ctx->stream, weight_f32(ctx, ws[i]), x, ys[i], ws[i]->w.ne0,
-                          ws[i]->w.ne1, n);
+            float_gemm(ctx, ws[i], x, ys[i], n);
           }
         }
       }
@@ -899,9 +934,7 @@ int nbl_matmul_multi(nbl_ctx* ctx, const nbl_weight* const* ws, int32_t count, c
       }
       nbl::check_cuda(cudaGetLastError(), "matmul launch");
     } else {
-      for (int32_t i = 0; i < count; ++i)
-        nbl::gemm_f32(cublas_handle(ctx), ctx->stream, weight_f32(ctx, ws[i]), x, ys[i], ws[i]->w.ne0, ws[i]->w.ne1,
-                      n);
+      for (int32_t i = 0; i < count; ++i) float_gemm(ctx, ws[i], x, ys[i], n);
     }
   });
 }

@@ -62,6 +62,8 @@ struct nbl_ctx {
   void* cublas_ws = nullptr;  // its fixed workspace
   void* qgemm_act = nullptr;  // activations quantized for the quantized tensor-core matmul
   size_t qgemm_act_bytes = 0;
+  void* fgemm_act = nullptr;  // activations split into tf32 terms for the float tensor-core matmul
+  size_t fgemm_act_bytes = 0;
   void* qgemv_act = nullptr;  // activations quantized for the quantized GEMV (up to 8 rows)
   size_t qgemv_act_bytes = 0;
 };

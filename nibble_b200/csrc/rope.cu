@@ -236,7 +236,7 @@ __device__ __forceinline__ void store8(void* p, int64_t i, const float (&lo)[4],
 // 3.7 GB: 0.75 ms with 1, 0.96 ms with 2, 1.5 ms with 4): the registers a second chunk costs lower occupancy more
 // than its extra load in flight gains.
 constexpr int kInFlight = 1;
-constexpr int kTokGroup = 8;  // tokens whose metadata one warp resolves at once (<= 32)
+constexpr int kTokGroup = 8;  // most tokens whose metadata one warp resolves at once (<= 32)
 
 template <int IN, int QOUT, int KV, bool NEOX>
 __global__ void __launch_bounds__(256) rope_kv_append_vec_kernel(
@@ -245,7 +245,7 @@ __global__ void __launch_bounds__(256) rope_kv_append_vec_kernel(
     const int32_t* __restrict__ tok_row, const int32_t* __restrict__ tok_pos, const int32_t* __restrict__ page_table,
     int32_t pt_stride, int n_heads, int n_kv_heads, int head_dim, int page_size, int64_t n_pages,
     const float2* __restrict__ tab, int64_t tab_pos, void* pool, int* err, int64_t n_tok, int32_t row_base,
-    const int32_t* __restrict__ lens) {
+    const int32_t* __restrict__ lens, int tok_group) {
   const int lane = threadIdx.x & 31;
   const int half = head_dim / 2;
   const int chunks = head_dim / 8;
@@ -253,13 +253,14 @@ __global__ void __launch_bounds__(256) rope_kv_append_vec_kernel(
   const int units = q_units + 2 * k_units;
   const int64_t block = int64_t(n_kv_heads) * page_size * head_dim;
   const int64_t warps = int64_t(gridDim.x) * (blockDim.x >> 5);
-  // Tokens are taken kTokGroup at a time per warp: lane i < kTokGroup resolves token t0 + i (position check,
-  // page lookup, error flags) in one round of loads, then the warp walks the group reading the results by shuffle.
-  for (int64_t t0 = (blockIdx.x * int64_t(blockDim.x >> 5) + (threadIdx.x >> 5)) * kTokGroup; t0 < n_tok;
-       t0 += warps * kTokGroup) {
+  // Tokens are taken tok_group (1..kTokGroup) at a time per warp: lane i < tok_group resolves token t0 + i
+  // (position check, page lookup, error flags) in one round of loads, then the warp walks the group reading the
+  // results by shuffle. Few tokens run one per warp, so a small launch spreads over as many warps as it has tokens.
+  for (int64_t t0 = (blockIdx.x * int64_t(blockDim.x >> 5) + (threadIdx.x >> 5)) * tok_group; t0 < n_tok;
+       t0 += warps * tok_group) {
     int32_t my_pos = -1;
     int64_t my_page = -1;
-    if (lane < kTokGroup && t0 + lane < n_tok) {
+    if (lane < tok_group && t0 + lane < n_tok) {
       const int64_t t = t0 + lane;
       const int32_t row = tok_row ? tok_row[t] : row_base + static_cast<int32_t>(t);
       my_pos = tok_pos ? tok_pos[t] : lens[row] - 1;
@@ -278,7 +279,7 @@ __global__ void __launch_bounds__(256) rope_kv_append_vec_kernel(
         my_pos = -1;  // skipped entirely
       }
     }
-    const int n_here = static_cast<int>(std::min<int64_t>(kTokGroup, n_tok - t0));
+    const int n_here = static_cast<int>(std::min<int64_t>(tok_group, n_tok - t0));
 #pragma unroll 1
     for (int ti = 0; ti < n_here; ++ti) {
       const int64_t r = t0 + ti;
@@ -406,13 +407,15 @@ void launch_kv(cudaStream_t st, const nbl_kv* kv, const void* q_in, const void* 
                    (!bv || aligned16(bv));
   if (vec) {
     auto k = neox ? rope_kv_append_vec_kernel<IN, QOUT, KV, true> : rope_kv_append_vec_kernel<IN, QOUT, KV, false>;
-    // 8 warps per CTA; one wave of resident CTAs walks all tokens
-    const int64_t want = (n_tok + 7) / 8;
+    // 8 warps per CTA; one wave of resident CTAs walks all tokens, each warp tok_group tokens at a time (as few
+    // as the resident warps allow, at most kTokGroup)
     const int64_t cap = neox ? vec_resident<IN, QOUT, KV, true>() : vec_resident<IN, QOUT, KV, false>();
+    const int tok_group = static_cast<int>(std::min<int64_t>(kTokGroup, std::max<int64_t>(1, (n_tok + 8 * cap - 1) / (8 * cap))));
+    const int64_t want = (n_tok + 8 * tok_group - 1) / (8 * tok_group);
     const int grid = static_cast<int>(std::max<int64_t>(1, std::min(want, cap)));
     k<<<grid, 256, 0, st>>>(q_in, k_in, v_in, bq, bk, bv, q_out, tok_row, tok_pos, page_table, pt_stride, n_heads,
                             c.n_kv_heads, c.head_dim, c.page_size, c.n_pages, tab, tab_pos, kv->pool, err, n_tok,
-                            row_base, lens);
+                            row_base, lens, tok_group);
     return;
   }
   rope_kv_append_kernel<IN, QOUT, KV><<<dim3(static_cast<unsigned>(n_tok)), dim3(128), 0, st>>>(

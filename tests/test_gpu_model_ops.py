@@ -37,9 +37,10 @@ def _summation_bound(w, x):
 
 
 @pytest.mark.parametrize("dt", ["f32", "f16"])
-@pytest.mark.parametrize("n", [1, 2, 3, 5, 8, 9, 33, 130])
+@pytest.mark.parametrize("n", [1, 2, 3, 5, 8, 9, 33, 128, 130])
 def test_matmul_matches_oracle(nbl_ctx, dt, n):
-    """n <= 8 runs the weight-streaming GEMV (one instantiation per n), n > 8 the SGEMM path."""
+    """n <= 8 runs the weight-streaming GEMV (one instantiation per n), 9..127 SGEMM, n >= 128 the tensor-core GEMM
+    (kind::tf32 on operands split into tf32 terms); all within the bound of the reference's fp32 sum."""
     import torch
     rng = np.random.default_rng(n * 7 + (dt == "f16"))
     for ne1, ne0 in [(37, 72), (1000, 256), (96, 2048)]:
@@ -52,6 +53,24 @@ def test_matmul_matches_oracle(nbl_ctx, dt, n):
         ref = oracle.matmul(w.view(np.uint16) if dt == "f16" else w, x, n)
         assert np.all(np.abs(got - ref) <= _summation_bound(w, x) + 1e-30), (ne1, ne0)
         wt.close()
+
+
+@pytest.mark.parametrize("dt", ["f32", "f16"])
+def test_matmul_gemm_large_grid(nbl_ctx, dt):
+    """Enough tiles (32 weight-row tiles x 5 activation-row tiles of 128) for the 128-row activation tiles of the
+    tensor-core GEMM (the cases above use 64-row tiles), with a K tail (ne0 = 4 mod 32) and a 4-row weight tail."""
+    import torch
+    rng = np.random.default_rng(55 + (dt == "f16"))
+    ne1, ne0, n = 4100, 260, 640
+    w = _weights(rng, ne1, ne0, dt)
+    x = rng.standard_normal((n, ne0)).astype(np.float32)
+    wt = nbl_ctx.weight(w)
+    y = torch.full((n, ne1), float("nan"), device="cuda")
+    nbl_ctx.matmul(wt, dev(x), y, n)
+    got = host(y)
+    ref = oracle.matmul(w.view(np.uint16) if dt == "f16" else w, x, n)
+    assert np.all(np.abs(got - ref) <= _summation_bound(w, x) + 1e-30)
+    wt.close()
 
 
 @pytest.mark.parametrize("dt", ["f32", "f16"])
