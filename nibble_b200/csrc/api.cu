@@ -215,12 +215,11 @@ void grow_scratch(nbl_ctx* ctx, void*& buf, size_t& bytes, size_t need, const ch
 }
 
 // A float-weight matmul of n > kGemvMaxRows activation rows: the tf32-split tensor-core GEMM (its weight operand
-// made on first use: the fp32 widening of an F16 matrix, or the two tf32 terms of an F32 one) from kFgemmMinRows
-// rows on, SGEMM below that and for row widths TMA cannot tile.
-constexpr int64_t kFgemmMinRows = 128;
+// made on first use: the fp32 widening of an F16 matrix, or the two tf32 terms of an F32 one), or SGEMM for row
+// widths TMA cannot tile.
+constexpr int64_t kFgemmMinRows = nbl::kGemvMaxRows + 1;
 void float_gemm(nbl_ctx* ctx, const nbl_weight* cw, const float* x, float* y, int64_t n) {
   auto* w = const_cast<nbl_weight*>(cw);
-  // below ~128 rows the tiles cover too few SMs (no split-K yet) and SGEMM measured faster (batched decode steps)
   if (!nbl::fgemm_supported(w->w.ne0) || n < kFgemmMinRows) {
     nbl::gemm_f32(cublas_handle(ctx), ctx->stream, weight_f32(ctx, w), x, y, w->w.ne0, w->w.ne1, n);
     return;
@@ -239,7 +238,8 @@ void float_gemm(nbl_ctx* ctx, const nbl_weight* cw, const float* x, float* y, in
     hi = w->w.tf_hi;
     lo = w->w.tf_lo;
   }
-  grow_scratch(ctx, ctx->fgemm_act, ctx->fgemm_act_bytes, nbl::fgemm_act_bytes(n, w->w.ne0), "float gemm activations");
+  grow_scratch(ctx, ctx->fgemm_act, ctx->fgemm_act_bytes, nbl::fgemm_act_bytes(n, w->w.ne1, w->w.ne0),
+               "float gemm activations");
   nbl::launch_fgemm(ctx->stream, hi, lo, w->w.ne0, w->w.ne1, x, y, n, ctx->fgemm_act, ctx->num_sms, ctx->d_err);
 }
 

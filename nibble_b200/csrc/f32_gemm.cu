@@ -82,10 +82,28 @@ struct FGemmMaps {
   CUtensorMap b_hi, b_lo;  // activations fp32 [n][ne0], box 32 x BN
 };
 struct FGemmArgs {
-  float* y;
+  float* y;        // [n][rows], or the split-K partials [k_splits][n][rows]
   int rows, n, ne0, n_tt, n_tiles;
+  int k_splits, kc_per_split;  // K split into k_splits ranges of kc_per_split stages (1: no split)
   int* err;
 };
+
+// Tile t -> weight-row tile, activation tile, K split (the splits of one output tile adjacent).
+struct FTile {
+  int row0, tok0, kc0, kc1;
+  float* dst;
+};
+template <int BN>
+__device__ __forceinline__ FTile ftile_of(const FGemmArgs& a, int t, int n_kc) {
+  const int ks = t % a.k_splits, ot = t / a.k_splits;
+  FTile f;
+  f.row0 = (ot / a.n_tt) * kBM;
+  f.tok0 = (ot % a.n_tt) * BN;
+  f.kc0 = ks * a.kc_per_split;
+  f.kc1 = min(n_kc, f.kc0 + a.kc_per_split);
+  f.dst = a.y + static_cast<int64_t>(ks) * a.n * a.rows;
+  return f;
+}
 
 template <int TERMS, int BN>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -130,8 +148,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       int kt = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < a.n_tiles && ok; t += gridDim.x) {
-        const int row0 = (t / a.n_tt) * kBM, tok0 = (t % a.n_tt) * BN;
-        for (int kc = 0; kc < n_kc; ++kc, ++kt) {
+        const FTile f = ftile_of<BN>(a, t, n_kc);
+        const int row0 = f.row0, tok0 = f.tok0;
+        for (int kc = f.kc0; kc < f.kc1; ++kc, ++kt) {
           const int s = kt % kStages;
           if (kt >= kStages && !mbar_wait(&bars[C::kBarEmpty + s], ((kt / kStages) & 1) ^ 1, a.err)) {
             ok = false;
@@ -158,7 +177,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (tc >= kAccs && !mbar_wait(&bars[C::kBarTEmpty + acc], ((tc / kAccs) & 1) ^ 1, a.err)) break;
         tc_fence_after();
         const uint32_t d = tmem + acc * BN;
-        for (int kc = 0; kc < n_kc; ++kc, ++kt) {
+        const FTile f = ftile_of<BN>(a, t, n_kc);
+        for (int kc = f.kc0; kc < f.kc1; ++kc, ++kt) {
           const int s = kt % kStages;
           if (!mbar_wait(&bars[C::kBarFull + s], (kt / kStages) & 1, a.err)) {
             ok = false;
@@ -171,7 +191,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int kk = 0; kk < kKStage / kKMma; ++kk) {
             const uint32_t off = kk * kKMma * 4;  // 32 bytes per K-step inside the 128-byte swizzle row
             tc_mma_tf32(d, make_sdesc(ah + off, 16, 1024, 2), make_sdesc(bh + off, 16, 1024, 2), idesc,
-                        (kc > 0 || kk > 0) ? 1u : 0u);
+                        (kc > f.kc0 || kk > 0) ? 1u : 0u);
             tc_mma_tf32(d, make_sdesc(ah + off, 16, 1024, 2), make_sdesc(bl + off, 16, 1024, 2), idesc, 1u);
             if constexpr (TERMS == 3)
               tc_mma_tf32(d, make_sdesc(al + off, 16, 1024, 2), make_sdesc(bh + off, 16, 1024, 2), idesc, 1u);
@@ -192,7 +212,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int acc = tc % kAccs;
       if (!warp_wait_all(&bars[C::kBarTFull + acc], (tc / kAccs) & 1, a.err)) break;
       tc_fence_after();
-      const int row = (t / a.n_tt) * kBM + quarter * 32 + lane, tok0 = (t % a.n_tt) * BN;
+      const FTile f = ftile_of<BN>(a, t, (a.ne0 + kKStage - 1) / kKStage);
+      const int row = f.row0 + quarter * 32 + lane, tok0 = f.tok0;
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
         uint32_t v[32];
@@ -202,7 +223,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             const int tok = tok0 + c0 + j;
-            if (tok < a.n) a.y[static_cast<int64_t>(tok) * a.rows + row] = __uint_as_float(v[j]);
+            if (tok < a.n) f.dst[static_cast<int64_t>(tok) * a.rows + row] = __uint_as_float(v[j]);
           }
         }
       }
@@ -235,6 +256,15 @@ __global__ void split_tf32_kernel(const float* __restrict__ x, float* __restrict
   }
 }
 
+// y[i] = sum over the K splits of partial[s][i], in split order.
+__global__ void splitk_sum_kernel(const float* __restrict__ partial, float* __restrict__ y, int64_t count, int splits) {
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < count; i += int64_t(gridDim.x) * blockDim.x) {
+    float acc = partial[i];
+    for (int s = 1; s < splits; ++s) acc = __fadd_rn(acc, partial[s * count + i]);
+    y[i] = acc;
+  }
+}
+
 void encode_rows(CUtensorMap* m, const float* base, int64_t ne0, int64_t rows, int box_rows) {
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(ne0), static_cast<cuuint64_t>(rows)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ne0) * 4};
@@ -262,7 +292,13 @@ void launch_t(cudaStream_t st, const FGemmMaps& maps, const FGemmArgs& a, int gr
 
 bool fgemm_supported(int64_t ne0) { return ne0 % 4 == 0; }
 
-size_t fgemm_act_bytes(int64_t n, int64_t ne0) { return static_cast<size_t>(2 * n * ne0) * sizeof(float); }
+constexpr int kMaxSplits = 16;
+constexpr int kMinStagesPerSplit = 8;  // 256 K per split at least
+
+size_t fgemm_act_bytes(int64_t n, int64_t rows, int64_t ne0) {
+  // the two activation terms, then room for the split-K partials
+  return static_cast<size_t>(2 * n * ne0 + kMaxSplits * n * rows) * sizeof(float);
+}
 
 void split_tf32(cudaStream_t st, const float* x, float* hi, float* lo, int64_t count, int num_sms) {
   const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((count + 255) / 256, int64_t(num_sms) * 8));
@@ -274,16 +310,25 @@ void launch_fgemm(cudaStream_t st, const float* w_hi, const float* w_lo, int64_t
                   float* y, int64_t n, void* act, int num_sms, int* err) {
   float* xh = static_cast<float*>(act);
   float* xl = xh + n * ne0;
+  float* partial = xl + n * ne0;
   split_tf32(st, x, xh, xl, n * ne0, num_sms);
   const int64_t row_tiles = (rows + kBM - 1) / kBM;
   const int bn = row_tiles * ((n + 127) / 128) < num_sms ? 64 : 128;
   FGemmArgs a{};
-  a.y = y;
   a.rows = static_cast<int>(rows);
   a.n = static_cast<int>(n);
   a.ne0 = static_cast<int>(ne0);
   a.n_tt = static_cast<int>((n + bn - 1) / bn);
-  a.n_tiles = static_cast<int>(row_tiles) * a.n_tt;
+  // too few output tiles to cover the SMs: split K (partials summed in split order by a second launch)
+  const int64_t out_tiles = row_tiles * a.n_tt, n_kc = (ne0 + kKStage - 1) / kKStage;
+  int splits = 1;
+  if (out_tiles < num_sms)
+    splits = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>({(num_sms + out_tiles - 1) / out_tiles,
+                                                                       n_kc / kMinStagesPerSplit, kMaxSplits})));
+  a.kc_per_split = static_cast<int>((n_kc + splits - 1) / splits);
+  a.k_splits = static_cast<int>((n_kc + a.kc_per_split - 1) / a.kc_per_split);
+  a.n_tiles = static_cast<int>(out_tiles) * a.k_splits;
+  a.y = a.k_splits > 1 ? partial : y;
   a.err = err;
   FGemmMaps maps;
   encode_rows(&maps.a_hi, w_hi, ne0, rows, kBM);
@@ -299,6 +344,12 @@ void launch_fgemm(cudaStream_t st, const float* w_hi, const float* w_lo, int64_t
     else launch_t<2, 128>(st, maps, a, grid);
   }
   check_cuda(cudaGetLastError(), "float gemm launch");
+  if (a.k_splits > 1) {
+    const int64_t count = n * rows;
+    const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((count + 255) / 256, int64_t(num_sms) * 8));
+    splitk_sum_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(partial, y, count, a.k_splits);
+    check_cuda(cudaGetLastError(), "float gemm split-K sum");
+  }
 }
 
 }  // namespace nbl

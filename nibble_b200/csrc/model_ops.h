@@ -64,10 +64,10 @@ void gemm_f32(cublasHandle_t h, cudaStream_t st, const float* w_f32, const float
               int64_t n);
 // f32_gemm.cu: the float matmul for more than kGemvMaxRows rows on the tensor cores (kind::tf32 with the operands
 // split into tf32 terms: fp32 accuracy). w_hi: an F16 matrix widened to fp32 (exact in tf32, w_lo = NULL) or the
-// tf32 high term of an F32 matrix (w_lo its low term). x is split into act (fgemm_act_bytes). Rows of ne0 % 4 != 0
-// cannot be TMA-tiled (fgemm_supported).
+// tf32 high term of an F32 matrix (w_lo its low term). x is split into act (fgemm_act_bytes, which also holds the
+// partials when K is split across CTAs). Rows of ne0 % 4 != 0 cannot be TMA-tiled (fgemm_supported).
 bool fgemm_supported(int64_t ne0);
-size_t fgemm_act_bytes(int64_t n, int64_t ne0);
+size_t fgemm_act_bytes(int64_t n, int64_t rows, int64_t ne0);
 void split_tf32(cudaStream_t st, const float* x, float* hi, float* lo, int64_t count, int num_sms);
 void launch_fgemm(cudaStream_t st, const float* w_hi, const float* w_lo, int64_t ne0, int64_t rows, const float* x,
                   float* y, int64_t n, void* act, int num_sms, int* err);
