@@ -18,6 +18,7 @@ Workloads (synthetic seeded inputs of the named shapes; n
   model_gemv_q4_0 the same with Q4_0 weights (nibble's quantized matmul, bit-identical to its CPU kernels).
   model_qgemm     the weight matmuls of a 512-token prefill of the Q4_0 model on the tcgen05 kind::i8 path.
                   Metric: tokens/s of the matmul part.
+  model_fgemm     the same for the F16 model on the tcgen05 kind::tf32 path (operands split into tf32 terms).
 With N > 1 (torchrun, one rank per GPU, NCCL) every rank runs its own shard of the same per-GPU work ("weak"
 scaling: the sequences shard with no collective); value = all ranks' work / max-over-ranks device time.
 
@@ -534,19 +535,21 @@ def model_gemv(args, world, rank, local, steps, warmup, wtype="F16"):
                          "peak_source": src}}
 
 
-def model_qgemm(args, world, rank, local, steps, warmup, n=512):
-    """The weight matmuls of one 512-token prefill of a TinyLlama-1.1B-shaped Q4_0 model through nbl_matmul (the
-    tensor-core path for more than 8 activation rows): per layer Q/K/V and gate/up as matmul_multi, O and down as
-    matmul -- 88 calls (the output projection runs on the last row only), replayed as one CUDA graph. Each call
-    quantizes its activation rows to Q8_0 and runs qgemm_kernel: one tcgen05 kind::i8 MMA per 32-element block into
-    TMEM, the reference's per-block float terms added in block order by the epilogue warps. Metric: activation rows
-    (tokens) per second of the matmul part; the kernel's own rate is given as int8 TOPS (2 * n * rows * ne0 per
-    second) and as block terms per second against the epilogue's issue bound."""
+def model_qgemm(args, world, rank, local, steps, warmup, n=512, wtype="Q4_0"):
+    """The weight matmuls of one 512-token prefill of a TinyLlama-1.1B-shaped model through nbl_matmul (the
+    tensor-core paths for more than 8 activation rows): per layer Q/K/V and gate/up as matmul_multi, O and down as
+    matmul -- 88 calls (the output projection runs on the last row only), replayed as one CUDA graph.
+    Q4_0: each call quantizes its activation rows to Q8_0 and runs qgemm_kernel: one tcgen05 kind::i8 MMA per
+    32-element block into TMEM, the reference's per-block float terms added in block order by the epilogue warps;
+    the kernel's rate is given as int8 TOPS and as block terms per second against the epilogue's issue bound.
+    F16: each call splits its activations into two tf32 terms and runs fgemm_kernel (tcgen05 kind::tf32, two MMAs
+    per K-step, fp32 accuracy); the rate is useful TFLOP/s against the tf32 peak for two MMAs per step (a quarter
+    of the measured dense bf16 rate). Metric: activation rows (tokens) per second of the matmul part."""
     import torch
     import nibble_b200 as nb
     ctx = nb.Context(local)
     rng = np.random.default_rng(70 + rank)
-    weights, shapes, wbytes = tinyllama_weights(ctx, rng, "Q4_0", with_output=False)
+    weights, shapes, wbytes = tinyllama_weights(ctx, rng, wtype, with_output=False)
     x = {c: torch.randn(n, c, device="cuda") for c in (E6, FF6)}
     y = {w: torch.empty(n, w, device="cuda") for w in (Q6, KV6, E6, FF6)}
     y["v"], y["u"] = torch.empty(n, KV6, device="cuda"), torch.empty(n, FF6, device="cuda")
@@ -589,18 +592,26 @@ def model_qgemm(args, world, rank, local, steps, warmup, n=512):
         w.close()
     ctx.close()
     macs = n * sum(r * c for r, c in shapes)
+    res = {"metric": "model prefill weight-matmul tokens/s", "value": world * n / (ms * 1e-3), "unit": "tokens/s",
+           "ms_per_step": ms, "scaling": "weak", "gpu_launches_per_step": 8 * LAYERS6,
+           "config": {"workload": f"TinyLlama-1.1B {n}-token prefill weight matmuls ({wtype} weights)",
+                      "calls_per_step": 4 * LAYERS6, "launches_per_step": 8 * LAYERS6, "weight_bytes": wbytes,
+                      "l2": "activations and each weight matrix are re-read from L2 by the tiles sharing them"}}
+    if wtype == "F16":
+        _, bf16, _, src = peaks()
+        tflops = 2 * macs / (ms * 1e-3) / 1e12
+        res["roofline"] = {"kernel": "fgemm_kernel<2, BN>", "bound": "tensor (kind::tf32, 2 MMAs per K-step)",
+                           "achieved": tflops, "peak": bf16 / 4, "unit": "TFLOP/s (useful)", "frac": tflops / (bf16 / 4),
+                           "peak_source": f"{src} dense bf16 / 4: tf32 runs at half the bf16 rate, two MMAs per step"}
+        return res
     terms = macs // 32
     clock = gpu_clock_mhz(local)
     issue_bound = 148 * 128 / 4 * clock * 1e6  # 4 FP32-pipe issue slots per output and block, 128 lanes per SM
-    return {"metric": "model prefill weight-matmul tokens/s", "value": world * n / (ms * 1e-3), "unit": "tokens/s",
-            "ms_per_step": ms, "scaling": "weak", "gpu_launches_per_step": 8 * LAYERS6,
-            "config": {"workload": f"TinyLlama-1.1B {n}-token prefill weight matmuls (Q4_0 weights)",
-                       "calls_per_step": 4 * LAYERS6, "launches_per_step": 8 * LAYERS6, "weight_bytes": wbytes,
-                       "l2": "activations and each weight matrix are re-read from L2 by the tiles sharing them"},
-            "int8_tops": 2 * macs / (ms * 1e-3) / 1e12,
-            "roofline": {"kernel": "qgemm_kernel", "bound": "issue (fp32 epilogue)", "achieved": terms / (ms * 1e-3),
-                         "peak": issue_bound, "unit": "block terms/s", "frac": terms / (ms * 1e-3) / issue_bound,
-                         "peak_source": f"148 SMs x 32 terms/clk at the SM clock sampled ({clock:.0f} MHz)"}}
+    res["int8_tops"] = 2 * macs / (ms * 1e-3) / 1e12
+    res["roofline"] = {"kernel": "qgemm_kernel", "bound": "issue (fp32 epilogue)", "achieved": terms / (ms * 1e-3),
+                       "peak": issue_bound, "unit": "block terms/s", "frac": terms / (ms * 1e-3) / issue_bound,
+                       "peak_source": f"148 SMs x 32 terms/clk at the SM clock sampled ({clock:.0f} MHz)"}
+    return res
 
 
 def gpu_clock_mhz(local):
@@ -764,7 +775,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["decode_batched", "prefill", "decode_long", "decode_ragged", "model_gemv",
-                                           "model_gemv_q4_0", "model_qgemm"],
+                                           "model_gemv_q4_0", "model_qgemm", "model_fgemm"],
                     default="decode_batched")
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-3 prefill leg of the default run")
     ap.add_argument("--no-extra", action="store_true", help="skip the config-4/5 legs of the default run")
@@ -795,6 +806,8 @@ def main():
         res = model_gemv(args, world, rank, local, args.steps, args.warmup, wtype="Q4_0")
     elif args.workload == "model_qgemm":
         res = model_qgemm(args, world, rank, local, args.steps, args.warmup)
+    elif args.workload == "model_fgemm":
+        res = model_qgemm(args, world, rank, local, args.steps, args.warmup, wtype="F16")
     else:
         res = decode_batched(args, world, rank, local)
         if not args.no_prefill:
@@ -805,6 +818,7 @@ def main():
             res["model_decode_gemv"] = model_gemv(args, world, rank, local, legs, 3)
             res["model_decode_gemv_q4_0"] = model_gemv(args, world, rank, local, legs, 3, wtype="Q4_0")
             res["model_prefill_qgemm_q4_0"] = model_qgemm(args, world, rank, local, legs, 3)
+            res["model_prefill_fgemm_f16"] = model_qgemm(args, world, rank, local, legs, 3, wtype="F16")
     res.setdefault("scaling", "weak")
     res.update({"n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
                 "vs_baseline": None, "data": "synthetic (seeded N(0,1))"})
