@@ -214,33 +214,53 @@ void grow_scratch(nbl_ctx* ctx, void*& buf, size_t& bytes, size_t need, const ch
   bytes = need;
 }
 
-// A float-weight matmul of n > kGemvMaxRows activation rows: the tf32-split tensor-core GEMM (its weight operand
-// made on first use: the fp32 widening of an F16 matrix, or the two tf32 terms of an F32 one), or SGEMM for row
-// widths TMA cannot tile.
-constexpr int64_t kFgemmMinRows = nbl::kGemvMaxRows + 1;
-void float_gemm(nbl_ctx* ctx, const nbl_weight* cw, const float* x, float* y, int64_t n) {
+// The tensor-core GEMM's operand of a float weight, made on its first multi-row matmul: the fp32 widening of an
+// F16 matrix (hi, lo = NULL), or the two tf32 terms of an F32 matrix.
+void fgemm_operand(nbl_ctx* ctx, const nbl_weight* cw, const float** hi, const float** lo) {
   auto* w = const_cast<nbl_weight*>(cw);
-  if (!nbl::fgemm_supported(w->w.ne0) || n < kFgemmMinRows) {
-    nbl::gemm_f32(cublas_handle(ctx), ctx->stream, weight_f32(ctx, w), x, y, w->w.ne0, w->w.ne1, n);
+  if (w->w.dtype == NBL_F16) {
+    *hi = weight_f32(ctx, w);
+    *lo = nullptr;
     return;
   }
-  const float* hi;
-  const float* lo = nullptr;
-  if (w->w.dtype == NBL_F16) {
-    hi = weight_f32(ctx, w);
-  } else {
-    if (!w->w.tf_hi) {
-      const int64_t count = w->w.ne0 * w->w.ne1;
-      w->w.tf_hi = static_cast<float*>(device_alloc(static_cast<size_t>(count) * sizeof(float), "weight tf32 terms"));
-      w->w.tf_lo = static_cast<float*>(device_alloc(static_cast<size_t>(count) * sizeof(float), "weight tf32 terms"));
-      nbl::split_tf32(ctx->stream, static_cast<const float*>(w->w.dev), w->w.tf_hi, w->w.tf_lo, count, ctx->num_sms);
-    }
-    hi = w->w.tf_hi;
-    lo = w->w.tf_lo;
+  if (!w->w.tf_hi) {
+    const int64_t count = w->w.ne0 * w->w.ne1;
+    w->w.tf_hi = static_cast<float*>(device_alloc(static_cast<size_t>(count) * sizeof(float), "weight tf32 terms"));
+    w->w.tf_lo = static_cast<float*>(device_alloc(static_cast<size_t>(count) * sizeof(float), "weight tf32 terms"));
+    nbl::split_tf32(ctx->stream, static_cast<const float*>(w->w.dev), w->w.tf_hi, w->w.tf_lo, count, ctx->num_sms);
   }
-  grow_scratch(ctx, ctx->fgemm_act, ctx->fgemm_act_bytes, nbl::fgemm_act_bytes(n, w->w.ne1, w->w.ne0),
-               "float gemm activations");
-  nbl::launch_fgemm(ctx->stream, hi, lo, w->w.ne0, w->w.ne1, x, y, n, ctx->fgemm_act, ctx->num_sms, ctx->d_err);
+  *hi = w->w.tf_hi;
+  *lo = w->w.tf_lo;
+}
+
+// Float-weight matmuls of n > kGemvMaxRows activation rows for weights sharing x: groups of up to kMaxMulti
+// weights of one float type whose rows TMA can tile run as one tf32-split tensor-core GEMM launch; a row width TMA
+// cannot tile (ne0 % 4 != 0) runs SGEMM.
+void float_gemm(nbl_ctx* ctx, const nbl_weight* const* ws, float* const* ys, int count, const float* x, int64_t n) {
+  for (int i0 = 0; i0 < count;) {
+    const nbl::Weight& w0 = ws[i0]->w;
+    if (!nbl::fgemm_supported(w0.ne0)) {
+      nbl::gemm_f32(cublas_handle(ctx), ctx->stream, weight_f32(ctx, ws[i0]), x, ys[i0], w0.ne0, w0.ne1, n);
+      ++i0;
+      continue;
+    }
+    int c = 1;
+    while (c < nbl::kMaxMulti && i0 + c < count && ws[i0 + c]->w.dtype == w0.dtype && ws[i0 + c]->w.ne0 == w0.ne0)
+      ++c;
+    const float* hi[nbl::kMaxMulti];
+    const float* lo[nbl::kMaxMulti];
+    int64_t rows[nbl::kMaxMulti];
+    int64_t total = 0;
+    for (int i = 0; i < c; ++i) {
+      fgemm_operand(ctx, ws[i0 + i], &hi[i], &lo[i]);
+      rows[i] = ws[i0 + i]->w.ne1;
+      total += rows[i];
+    }
+    grow_scratch(ctx, ctx->fgemm_act, ctx->fgemm_act_bytes, nbl::fgemm_act_bytes(n, total, w0.ne0),
+                 "float gemm activations");
+    nbl::launch_fgemm(ctx->stream, hi, lo, rows, ys + i0, c, w0.ne0, x, n, ctx->fgemm_act, ctx->num_sms, ctx->d_err);
+    i0 += c;
+  }
 }
 
 // A quantized matmul of n activation rows for weights of one quantized type sharing ne0 (count <= kMaxMulti):
@@ -880,7 +900,7 @@ int nbl_matmul(nbl_ctx* ctx, const nbl_weight* w, const float* x, float* y, int6
       nbl::launch_gemv(ctx->stream, w->w, x, y, n, ctx->num_sms);
       nbl::check_cuda(cudaGetLastError(), "matmul launch");
     } else {
-      float_gemm(ctx, w, x, y, n);
+      float_gemm(ctx, &w, &y, 1, x, n);
     }
   });
 }
@@ -916,7 +936,7 @@ int nbl_matmul_multi(nbl_ctx* ctx, const nbl_weight* const* ws, int32_t count, c
           } else if (n <= nbl::kGemvMaxRows) {
             nbl::launch_gemv(ctx->stream, ws[i]->w, x, ys[i], n, ctx->num_sms);
           } else {
-            float_gemm(ctx, ws[i], x, ys[i], n);
+            float_gemm(ctx, ws + i, ys + i, 1, x, n);
           }
         }
       }
@@ -934,7 +954,7 @@ int nbl_matmul_multi(nbl_ctx* ctx, const nbl_weight* const* ws, int32_t count, c
       }
       nbl::check_cuda(cudaGetLastError(), "matmul launch");
     } else {
-      for (int32_t i = 0; i < count; ++i) float_gemm(ctx, ws[i], x, ys[i], n);
+      float_gemm(ctx, ws, ys, count, x, n);
     }
   });
 }

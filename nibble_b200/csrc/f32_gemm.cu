@@ -16,7 +16,8 @@
 // tcgen05.mma kind::tf32 into the tile's TMEM accumulator (two accumulators, so a tile's epilogue overlaps the next
 // tile's MMAs); four epilogue warps move the accumulator to y with tcgen05.ld, each thread one weight row (stores
 // coalesced across the warp). Persistent CTAs walk the tiles with the activation tiles of one weight-row tile
-// adjacent, so the weight tile is read from L2 by all of them.
+// adjacent, so the weight tile is read from L2 by all of them. Up to kMaxMulti weights sharing x (matmul_multi's
+// Q/K/V, gate/up) run as one launch, their row tiles numbered consecutively.
 #include <algorithm>
 #include <atomic>
 
@@ -78,30 +79,47 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 }
 
 struct FGemmMaps {
-  CUtensorMap a_hi, a_lo;  // weights fp32 [rows][ne0] (a_lo only for F32 weights), box 32 x 128
-  CUtensorMap b_hi, b_lo;  // activations fp32 [n][ne0], box 32 x BN
+  CUtensorMap a_hi[kMaxMulti], a_lo[kMaxMulti];  // weights fp32 [rows][ne0] (a_lo: F32 weights), box 32 x 128
+  CUtensorMap b_hi, b_lo;                        // activations fp32 [n][ne0], box 32 x BN
 };
 struct FGemmArgs {
-  float* y;        // [n][rows], or the split-K partials [k_splits][n][rows]
-  int rows, n, ne0, n_tt, n_tiles;
-  int k_splits, kc_per_split;  // K split into k_splits ranges of kc_per_split stages (1: no split)
+  float* dst[kMaxMulti];        // y_j [n][rows_j], or weight j's split-K partials [k_splits][n][rows_j]
+  int rows[kMaxMulti];
+  int tiles_end[kMaxMulti];     // cumulative tile counts (output tiles x K splits) per weight
+  int k_splits[kMaxMulti];      // weight j's K split into k_splits ranges of kc_per_split stages (1: no split)
+  int kc_per_split[kMaxMulti];
+  int count, n, ne0, n_tt, n_tiles;
   int* err;
 };
 
-// Tile t -> weight-row tile, activation tile, K split (the splits of one output tile adjacent).
+// Tile t -> weight j, weight-row tile, activation tile, K split (the splits of one output tile adjacent).
 struct FTile {
-  int row0, tok0, kc0, kc1;
+  int j, rows, row0, tok0, kc0, kc1;
   float* dst;
 };
 template <int BN>
 __device__ __forceinline__ FTile ftile_of(const FGemmArgs& a, int t, int n_kc) {
-  const int ks = t % a.k_splits, ot = t / a.k_splits;
   FTile f;
+  f.j = 0;
+  int begin = 0;
+#pragma unroll
+  for (int i = 1; i < kMaxMulti; ++i)
+    if (i < a.count && t >= a.tiles_end[i - 1]) {
+      f.j = i;
+      begin = a.tiles_end[i - 1];
+    }
+  float* dst = a.dst[0];
+  f.rows = a.rows[0];
+  int splits = a.k_splits[0], per = a.kc_per_split[0];
+#pragma unroll
+  for (int i = 1; i < kMaxMulti; ++i)
+    if (f.j == i) dst = a.dst[i], f.rows = a.rows[i], splits = a.k_splits[i], per = a.kc_per_split[i];
+  const int local = t - begin, ks = local % splits, ot = local / splits;
   f.row0 = (ot / a.n_tt) * kBM;
   f.tok0 = (ot % a.n_tt) * BN;
-  f.kc0 = ks * a.kc_per_split;
-  f.kc1 = min(n_kc, f.kc0 + a.kc_per_split);
-  f.dst = a.y + static_cast<int64_t>(ks) * a.n * a.rows;
+  f.kc0 = ks * per;
+  f.kc1 = min(n_kc, f.kc0 + per);
+  f.dst = dst + static_cast<int64_t>(ks) * a.n * f.rows;
   return f;
 }
 
@@ -150,6 +168,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int t = blockIdx.x; t < a.n_tiles && ok; t += gridDim.x) {
         const FTile f = ftile_of<BN>(a, t, n_kc);
         const int row0 = f.row0, tok0 = f.tok0;
+        const CUtensorMap* ahi = &maps.a_hi[0];
+        const CUtensorMap* alo = &maps.a_lo[0];
+#pragma unroll
+        for (int i = 1; i < kMaxMulti; ++i)
+          if (f.j == i) ahi = &maps.a_hi[i], alo = &maps.a_lo[i];
         for (int kc = f.kc0; kc < f.kc1; ++kc, ++kt) {
           const int s = kt % kStages;
           if (kt >= kStages && !mbar_wait(&bars[C::kBarEmpty + s], ((kt / kStages) & 1) ^ 1, a.err)) {
@@ -158,8 +181,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           uint64_t* full = &bars[C::kBarFull + s];
           mbar_arrive_expect_tx(full, C::kStageBytes);
-          tma_load_2d(a_tile(s, 0), &maps.a_hi, kc * kKStage, row0, full);
-          if constexpr (TERMS == 3) tma_load_2d(a_tile(s, 1), &maps.a_lo, kc * kKStage, row0, full);
+          tma_load_2d(a_tile(s, 0), ahi, kc * kKStage, row0, full);
+          if constexpr (TERMS == 3) tma_load_2d(a_tile(s, 1), alo, kc * kKStage, row0, full);
           tma_load_2d(b_tile(s, 0), &maps.b_hi, kc * kKStage, tok0, full);
           tma_load_2d(b_tile(s, 1), &maps.b_lo, kc * kKStage, tok0, full);
         }
@@ -219,11 +242,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t v[32];
         tmem_ld32(tmem + t_lane + acc * BN + c0, v);
         tc_wait_ld();
-        if (row < a.rows) {
+        if (row < f.rows) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             const int tok = tok0 + c0 + j;
-            if (tok < a.n) f.dst[static_cast<int64_t>(tok) * a.rows + row] = __uint_as_float(v[j]);
+            if (tok < a.n) f.dst[static_cast<int64_t>(tok) * f.rows + row] = __uint_as_float(v[j]);
           }
         }
       }
@@ -306,37 +329,57 @@ void split_tf32(cudaStream_t st, const float* x, float* hi, float* lo, int64_t c
   check_cuda(cudaGetLastError(), "tf32 split launch");
 }
 
-void launch_fgemm(cudaStream_t st, const float* w_hi, const float* w_lo, int64_t ne0, int64_t rows, const float* x,
-                  float* y, int64_t n, void* act, int num_sms, int* err) {
+void launch_fgemm(cudaStream_t st, const float* const* w_hi, const float* const* w_lo, const int64_t* rows,
+                  float* const* ys, int count, int64_t ne0, const float* x, int64_t n, void* act, int num_sms,
+                  int* err) {
   float* xh = static_cast<float*>(act);
   float* xl = xh + n * ne0;
   float* partial = xl + n * ne0;
   split_tf32(st, x, xh, xl, n * ne0, num_sms);
-  const int64_t row_tiles = (rows + kBM - 1) / kBM;
-  const int bn = row_tiles * ((n + 127) / 128) < num_sms ? 64 : 128;
+  // the tile shape and each weight's K split depend on n and that weight alone, never on the group, so a
+  // matmul_multi launch gives every weight the bits a separate call gives it
+  const int bn = n <= 64 ? 64 : 128;
   FGemmArgs a{};
-  a.rows = static_cast<int>(rows);
+  a.count = count;
   a.n = static_cast<int>(n);
   a.ne0 = static_cast<int>(ne0);
   a.n_tt = static_cast<int>((n + bn - 1) / bn);
-  // too few output tiles to cover the SMs: split K (partials summed in split order by a second launch)
-  const int64_t out_tiles = row_tiles * a.n_tt, n_kc = (ne0 + kKStage - 1) / kKStage;
-  int splits = 1;
-  if (out_tiles < num_sms)
-    splits = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>({(num_sms + out_tiles - 1) / out_tiles,
-                                                                       n_kc / kMinStagesPerSplit, kMaxSplits})));
-  a.kc_per_split = static_cast<int>((n_kc + splits - 1) / splits);
-  a.k_splits = static_cast<int>((n_kc + a.kc_per_split - 1) / a.kc_per_split);
-  a.n_tiles = static_cast<int>(out_tiles) * a.k_splits;
-  a.y = a.k_splits > 1 ? partial : y;
+  // a weight whose output tiles cannot cover the SMs alone splits K (partials summed in split order by a second
+  // launch)
+  const int64_t n_kc = (ne0 + kKStage - 1) / kKStage;
   a.err = err;
   FGemmMaps maps;
-  encode_rows(&maps.a_hi, w_hi, ne0, rows, kBM);
-  encode_rows(&maps.a_lo, w_lo ? w_lo : w_hi, ne0, rows, kBM);
+  int tiles = 0;
+  int64_t part_off = 0;
+  for (int i = 0; i < kMaxMulti; ++i) {
+    const int w = i < count ? i : 0;
+    if (i < count) {
+      const int64_t out_tiles = (rows[i] + kBM - 1) / kBM * a.n_tt;
+      int splits = 1;
+      if (out_tiles < num_sms)
+        splits = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>({(num_sms + out_tiles - 1) / out_tiles,
+                                                                           n_kc / kMinStagesPerSplit, kMaxSplits})));
+      a.kc_per_split[i] = static_cast<int>((n_kc + splits - 1) / splits);
+      a.k_splits[i] = static_cast<int>((n_kc + a.kc_per_split[i] - 1) / a.kc_per_split[i]);
+      a.rows[i] = static_cast<int>(rows[i]);
+      a.dst[i] = a.k_splits[i] > 1 ? partial + part_off : ys[i];
+      if (a.k_splits[i] > 1) part_off += static_cast<int64_t>(a.k_splits[i]) * n * rows[i];
+      tiles += static_cast<int>(out_tiles) * a.k_splits[i];
+    } else {
+      a.rows[i] = 0;
+      a.dst[i] = nullptr;
+      a.k_splits[i] = 1;
+      a.kc_per_split[i] = static_cast<int>(n_kc);
+    }
+    a.tiles_end[i] = tiles;
+    encode_rows(&maps.a_hi[i], w_hi[w], ne0, rows[w], kBM);
+    encode_rows(&maps.a_lo[i], w_lo[w] ? w_lo[w] : w_hi[w], ne0, rows[w], kBM);
+  }
+  a.n_tiles = tiles;
   encode_rows(&maps.b_hi, xh, ne0, n, bn);
   encode_rows(&maps.b_lo, xl, ne0, n, bn);
   const int grid = static_cast<int>(std::min<int64_t>(a.n_tiles, num_sms));
-  if (w_lo) {
+  if (w_lo[0]) {
     if (bn == 64) launch_t<3, 64>(st, maps, a, grid);
     else launch_t<3, 128>(st, maps, a, grid);
   } else {
@@ -344,11 +387,14 @@ void launch_fgemm(cudaStream_t st, const float* w_hi, const float* w_lo, int64_t
     else launch_t<2, 128>(st, maps, a, grid);
   }
   check_cuda(cudaGetLastError(), "float gemm launch");
-  if (a.k_splits > 1) {
-    const int64_t count = n * rows;
-    const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((count + 255) / 256, int64_t(num_sms) * 8));
-    splitk_sum_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(partial, y, count, a.k_splits);
+  part_off = 0;
+  for (int i = 0; i < count; ++i) {
+    if (a.k_splits[i] == 1) continue;
+    const int64_t cnt = n * rows[i];
+    const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((cnt + 255) / 256, int64_t(num_sms) * 8));
+    splitk_sum_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(partial + part_off, ys[i], cnt, a.k_splits[i]);
     check_cuda(cudaGetLastError(), "float gemm split-K sum");
+    part_off += static_cast<int64_t>(a.k_splits[i]) * cnt;
   }
 }
 

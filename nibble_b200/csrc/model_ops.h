@@ -63,14 +63,17 @@ void launch_gemv_multi(cudaStream_t st, const Weight* const* ws, float* const* y
 void gemm_f32(cublasHandle_t h, cudaStream_t st, const float* w_f32, const float* x, float* y, int64_t ne0, int64_t ne1,
               int64_t n);
 // f32_gemm.cu: the float matmul for more than kGemvMaxRows rows on the tensor cores (kind::tf32 with the operands
-// split into tf32 terms: fp32 accuracy). w_hi: an F16 matrix widened to fp32 (exact in tf32, w_lo = NULL) or the
-// tf32 high term of an F32 matrix (w_lo its low term). x is split into act (fgemm_act_bytes, which also holds the
-// partials when K is split across CTAs). Rows of ne0 % 4 != 0 cannot be TMA-tiled (fgemm_supported).
+// split into tf32 terms: fp32 accuracy), for up to kMaxMulti weights sharing x and ne0 in one launch. w_hi[i]: an
+// F16 matrix widened to fp32 (exact in tf32, w_lo[i] = NULL) or the tf32 high term of an F32 matrix (w_lo[i] its
+// low term); all weights of one launch are of one kind. x is split into act (fgemm_act_bytes over the weights'
+// total rows; it also holds the partials when K is split across CTAs). Rows of ne0 % 4 != 0 cannot be TMA-tiled
+// (fgemm_supported).
 bool fgemm_supported(int64_t ne0);
 size_t fgemm_act_bytes(int64_t n, int64_t rows, int64_t ne0);
 void split_tf32(cudaStream_t st, const float* x, float* hi, float* lo, int64_t count, int num_sms);
-void launch_fgemm(cudaStream_t st, const float* w_hi, const float* w_lo, int64_t ne0, int64_t rows, const float* x,
-                  float* y, int64_t n, void* act, int num_sms, int* err);
+void launch_fgemm(cudaStream_t st, const float* const* w_hi, const float* const* w_lo, const int64_t* rows,
+                  float* const* ys, int count, int64_t ne0, const float* x, int64_t n, void* act, int num_sms,
+                  int* err);
 // quant_ops.cu: the Q8_0-activation weight family (Q4_0, Q5_0, Q8_0)
 bool is_quant(int32_t dtype);
 int64_t quant_block_bytes(int32_t dtype);  // GGUF bytes per 32-element block

@@ -191,6 +191,25 @@ def test_weight_data_reports_the_upload(nbl_ctx):
 
 
 @pytest.mark.parametrize("dt", ["f32", "f16"])
+def test_matmul_multi_equals_separate_calls_large(nbl_ctx, dt):
+    """Two weights large enough that their joint launch takes 128-row activation tiles while each alone takes 64
+    (and the first alone splits K): still bit for bit equal to the separate calls."""
+    import torch
+    rng = np.random.default_rng(7 + (dt == "f16"))
+    ne0, n, rows = 512, 256, [8192, 8192, 100]
+    ws = [nbl_ctx.weight(_weights(rng, r, ne0, dt)) for r in rows]
+    x = dev(rng.standard_normal((n, ne0)).astype(np.float32))
+    ys = [torch.full((n, r), float("nan"), device="cuda") for r in rows]
+    nbl_ctx.matmul_multi(ws, x, ys, n)
+    for w, y, r in zip(ws, ys, rows):
+        single = torch.full((n, r), float("nan"), device="cuda")
+        nbl_ctx.matmul(w, x, single, n)
+        assert np.array_equal(host(y).view(np.uint32), host(single).view(np.uint32)), r
+    for w in ws:
+        w.close()
+
+
+@pytest.mark.parametrize("dt", ["f32", "f16"])
 @pytest.mark.parametrize("n", [1, 4, 8, 20])
 def test_matmul_multi_equals_separate_calls(nbl_ctx, dt, n):
     """Backend::matmul_multi's contract (backend.h:57-58): results equal separate matmul calls -- here bit for bit,
