@@ -66,6 +66,24 @@ def test_quant_matmul_multi_and_zero_blocks(nbl_ctx, name):
 
 
 @pytest.mark.parametrize("name", sorted(TYPES))
+def test_quant_gemv_wide_rows(nbl_ctx, name):
+    """Wide rows: 256 and 640 blocks per row (several rounds of 32 block terms per lane), with 3 and 8 activation
+    rows."""
+    import torch
+    odt, cdt = TYPES[name]
+    rng = np.random.default_rng(33 + cdt)
+    for ne1, ne0, n in [(40, 8192, 3), (24, 20480, 8)]:
+        w = oracle.random_q_blocks(rng, odt, ne1, ne0)
+        x = (rng.standard_normal((n, ne0)) * 2).astype(np.float32)
+        wt = nbl_ctx.weight(w, cdt, ne0)
+        y = torch.full((n, ne1), float("nan"), device="cuda")
+        nbl_ctx.matmul(wt, dev(x), y, n)
+        ref = oracle.matmul_q(w, odt, ne0, ne1, x, n)
+        assert np.array_equal(host(y).view(np.uint32), ref.view(np.uint32)), (ne1, ne0, n)
+        wt.close()
+
+
+@pytest.mark.parametrize("name", sorted(TYPES))
 @pytest.mark.parametrize("n", [9, 127, 128, 257])
 def test_quant_gemm_bit_exact(nbl_ctx, name, n):
     """More than 8 activation rows run on the tensor cores (one kind::i8 MMA per block, terms added in block
