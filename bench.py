@@ -18,7 +18,7 @@ Workloads (synthetic seeded inputs of the named shapes; n
   model_gemv_q4_0 the same with Q4_0 weights (nibble's quantized matmul, bit-identical to its CPU kernels).
   model_qgemm     the weight matmuls of a 512-token prefill of the Q4_0 model on the tcgen05 kind::i8 path.
                   Metric: tokens/s of the matmul part.
-  model_fgemm     the same for the F16 model on the tcgen05 kind::tf32 path (operands split into tf32 terms).
+  model_fgemm     the same for the F16 model on the tcgen05 kind::f16 path (activations split into two fp16 terms).
 With N > 1 (torchrun, one rank per GPU, NCCL) every rank runs its own shard of the same per-GPU work ("weak"
 scaling: the sequences shard with no collective); value = all ranks' work / max-over-ranks device time.
 
@@ -542,9 +542,10 @@ def model_qgemm(args, world, rank, local, steps, warmup, n=512, wtype="Q4_0"):
     Q4_0: each call quantizes its activation rows to Q8_0 and runs qgemm_kernel: one tcgen05 kind::i8 MMA per
     32-element block into TMEM, the reference's per-block float terms added in block order by the epilogue warps;
     the kernel's rate is given as int8 TOPS and as block terms per second against the epilogue's issue bound.
-    F16: each call splits its activations into two tf32 terms and runs fgemm_kernel (tcgen05 kind::tf32, two MMAs
-    per K-step, fp32 accuracy); the rate is useful TFLOP/s against the tf32 peak for two MMAs per step (a quarter
-    of the measured dense bf16 rate). Metric: activation rows (tokens) per second of the matmul part."""
+    F16: each call scales each activation row by a power of two, splits it into two fp16 terms and runs
+    fgemm_kernel on the F16 weights as they are (tcgen05 kind::f16, two MMAs per K-step, fp32 accuracy); the rate is
+    useful TFLOP/s against the peak for two MMAs per step (half the measured dense bf16 rate). Metric: activation
+    rows (tokens) per second of the matmul part."""
     import torch
     import nibble_b200 as nb
     ctx = nb.Context(local)
@@ -600,9 +601,9 @@ def model_qgemm(args, world, rank, local, steps, warmup, n=512, wtype="Q4_0"):
     if wtype == "F16":
         _, bf16, _, src = peaks()
         tflops = 2 * macs / (ms * 1e-3) / 1e12
-        res["roofline"] = {"kernel": "fgemm_kernel<2, BN>", "bound": "tensor (kind::tf32, 2 MMAs per K-step)",
-                           "achieved": tflops, "peak": bf16 / 4, "unit": "TFLOP/s (useful)", "frac": tflops / (bf16 / 4),
-                           "peak_source": f"{src} dense bf16 / 4: tf32 runs at half the bf16 rate, two MMAs per step"}
+        res["roofline"] = {"kernel": "fgemm_kernel<2, BN>", "bound": "tensor (kind::f16, 2 MMAs per K-step)",
+                           "achieved": tflops, "peak": bf16 / 2, "unit": "TFLOP/s (useful)", "frac": tflops / (bf16 / 2),
+                           "peak_source": f"{src} dense bf16 / 2: two fp16 MMAs per K-step"}
         return res
     terms = macs // 32
     clock = gpu_clock_mhz(local)

@@ -214,12 +214,12 @@ void grow_scratch(nbl_ctx* ctx, void*& buf, size_t& bytes, size_t need, const ch
   bytes = need;
 }
 
-// The tensor-core GEMM's operand of a float weight, made on its first multi-row matmul: the fp32 widening of an
-// F16 matrix (hi, lo = NULL), or the two tf32 terms of an F32 matrix.
-void fgemm_operand(nbl_ctx* ctx, const nbl_weight* cw, const float** hi, const float** lo) {
+// The tensor-core GEMM's operand of a float weight: an F16 matrix as uploaded (hi, lo = NULL), or the two tf32
+// terms of an F32 matrix (made on its first multi-row matmul).
+void fgemm_operand(nbl_ctx* ctx, const nbl_weight* cw, const void** hi, const float** lo) {
   auto* w = const_cast<nbl_weight*>(cw);
   if (w->w.dtype == NBL_F16) {
-    *hi = weight_f32(ctx, w);
+    *hi = w->w.dev;
     *lo = nullptr;
     return;
   }
@@ -234,12 +234,12 @@ void fgemm_operand(nbl_ctx* ctx, const nbl_weight* cw, const float** hi, const f
 }
 
 // Float-weight matmuls of n > kGemvMaxRows activation rows for weights sharing x: groups of up to kMaxMulti
-// weights of one float type whose rows TMA can tile run as one tf32-split tensor-core GEMM launch; a row width TMA
-// cannot tile (ne0 % 4 != 0) runs SGEMM.
+// weights of one float type whose rows TMA can tile run as one tensor-core GEMM launch; a row width TMA cannot
+// tile runs SGEMM.
 void float_gemm(nbl_ctx* ctx, const nbl_weight* const* ws, float* const* ys, int count, const float* x, int64_t n) {
   for (int i0 = 0; i0 < count;) {
     const nbl::Weight& w0 = ws[i0]->w;
-    if (!nbl::fgemm_supported(w0.ne0)) {
+    if (!nbl::fgemm_supported(w0.dtype, w0.ne0)) {
       nbl::gemm_f32(cublas_handle(ctx), ctx->stream, weight_f32(ctx, ws[i0]), x, ys[i0], w0.ne0, w0.ne1, n);
       ++i0;
       continue;
@@ -247,7 +247,7 @@ void float_gemm(nbl_ctx* ctx, const nbl_weight* const* ws, float* const* ys, int
     int c = 1;
     while (c < nbl::kMaxMulti && i0 + c < count && ws[i0 + c]->w.dtype == w0.dtype && ws[i0 + c]->w.ne0 == w0.ne0)
       ++c;
-    const float* hi[nbl::kMaxMulti];
+    const void* hi[nbl::kMaxMulti];
     const float* lo[nbl::kMaxMulti];
     int64_t rows[nbl::kMaxMulti];
     int64_t total = 0;

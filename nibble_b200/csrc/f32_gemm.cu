@@ -2,18 +2,19 @@
 // fp32 accuracy: y[t][r] = sum_k w[r][k] * x[t][k], the reference's matmul (ref_ops.cpp:109-136 and the tiled SIMD
 // GEMM of cpu_backend.cpp:146-233 for F16 / F32 weights), accumulated in fp32.
 //
-// The tensor core's fp32-class input is tf32 (11 significant bits), so each operand is split into terms that are
-// exact in tf32 and the products that matter are summed in one fp32 accumulator:
-//   F16 weights are exact in tf32 (11 significant bits, and every fp16 exponent fits), x = x_hi + x_lo with
-//   x_hi = tf32(x), x_lo = tf32(x - x_hi) (|x - x_hi - x_lo| <= 2^-24 |x|):  w * x_hi + w * x_lo   (2 MMAs per step);
-//   F32 weights likewise split, w_hi * x_hi + w_hi * x_lo + w_lo * x_hi        (3 MMAs per step; the dropped
-//   w_lo * x_lo is below 2^-22 of the product).
-// Each product of tf32 values is exact in fp32, so the result carries fp32 accumulation error only, like the
+// The tensor core takes 11-significant-bit inputs (fp16, tf32), so the fp32 activations are split into two terms
+// exact in the operand type and the products are summed in one fp32 accumulator:
+//   F16 weights are read as they are (kind::f16); each activation row is scaled by a power of two so its largest
+//   magnitude is below 2^14 and split into fp16 t1 + t2 (the remainder below 2^-22 of an element), w * t1 + w * t2
+//   per K-step (2 MMAs), the accumulator multiplied back by the power of two (exact);
+//   F32 weights and the activations are split into tf32 terms, w_hi * x_hi + w_hi * x_lo + w_lo * x_hi (kind::tf32,
+//   3 MMAs per step; the dropped w_lo * x_lo is below 2^-22 of the product).
+// Each product of 11-bit values is exact in fp32, so the result carries fp32 accumulation error only, like the
 // reference's (a different summation order).
 //
-// Kernel: a tile is 128 weight rows (MMA M, TMEM lanes) x BN activation rows (MMA N). Per stage TMA brings 32 fp32
-// of K (one 128-byte swizzle row) of every operand term; one elected thread issues 4 K-steps (K = 8) x the terms of
-// tcgen05.mma kind::tf32 into the tile's TMEM accumulator (two accumulators, so a tile's epilogue overlaps the next
+// Kernel: a tile is 128 weight rows (MMA M, TMEM lanes) x BN activation rows (MMA N). Per stage TMA brings one
+// 128-byte swizzle row of K (64 fp16 or 32 fp32) of every operand term; one elected thread issues 4 K-steps x the
+// terms of tcgen05.mma into the tile's TMEM accumulator (two accumulators, so a tile's epilogue overlaps the next
 // tile's MMAs); four epilogue warps move the accumulator to y with tcgen05.ld, each thread one weight row (stores
 // coalesced across the warp). Persistent CTAs walk the tiles with the activation tiles of one weight-row tile
 // adjacent, so the weight tile is read from L2 by all of them. Up to kMaxMulti weights sharing x (matmul_multi's
@@ -28,15 +29,20 @@ namespace nbl {
 namespace {
 
 constexpr int kBM = 128;
-constexpr int kKStage = 32;  // fp32 elements of K per stage: one 128-byte swizzle row
-constexpr int kKMma = 8;     // K of one kind::tf32 MMA
 constexpr int kAccs = 2;     // TMEM accumulators (tiles in flight)
+// Two operand modes. TERMS == 3: F32 weights, tf32 terms (4-byte elements, 32 of K per 128-byte swizzle row, K = 8
+// per kind::tf32 MMA). TERMS == 2: F16 weights read as they are and fp16 activation terms (2-byte elements, 64 of
+// K per row, K = 16 per kind::f16 MMA). A K-step is 32 bytes of a row in both.
+template <int TERMS>
+constexpr int kKStageOf = TERMS == 3 ? 32 : 64;
+template <int TERMS>
+constexpr int kKMmaOf = TERMS == 3 ? 8 : 16;
 constexpr int kWarpTma = 0, kWarpMma = 1, kWarpEpi0 = 2, kEpiWarps = 4;
 constexpr int kThreads = 32 * (kWarpEpi0 + kEpiWarps);
 
 template <int TERMS, int BN>
 struct FCfg {
-  static constexpr int kATerms = TERMS == 3 ? 2 : 1;  // weight terms in shared memory (hi, lo)
+  static constexpr int kATerms = TERMS == 3 ? 2 : 1;  // weight terms in shared memory (hi, lo; or the F16 weight)
   static constexpr int kStages = TERMS == 3 ? 3 : 4;
   static constexpr uint32_t kATile = kBM * 128, kBTile = BN * 128;
   static constexpr uint32_t kStageBytes = kATerms * kATile + 2 * kBTile;
@@ -84,6 +90,7 @@ struct FGemmMaps {
 };
 struct FGemmArgs {
   float* dst[kMaxMulti];        // y_j [n][rows_j], or weight j's split-K partials [k_splits][n][rows_j]
+  const float* scale;           // TERMS == 2: the power of two each activation row was scaled down by
   int rows[kMaxMulti];
   int tiles_end[kMaxMulti];     // cumulative tile counts (output tiles x K splits) per weight
   int k_splits[kMaxMulti];      // weight j's K split into k_splits ranges of kc_per_split stages (1: no split)
@@ -156,6 +163,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  constexpr int kKStage = kKStageOf<TERMS>, kKMma = kKMmaOf<TERMS>;
   const int n_kc = (a.ne0 + kKStage - 1) / kKStage;
   // stage s: [A_hi][A_lo (TERMS == 3)][B_hi][B_lo]
   auto a_tile = [&](int s, int term) { return smem + s * C::kStageBytes + term * C::kATile; };
@@ -192,7 +200,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == kWarpMma) {
     if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc_tf32(kBM, BN);
+      constexpr uint32_t idesc = TERMS == 3 ? make_idesc_tf32(kBM, BN) : make_idesc_f16(kBM, BN, false, false, false);
       int kt = 0, tc = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < a.n_tiles && ok; t += gridDim.x, ++tc) {
@@ -212,12 +220,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t bh = smem_u32(b_tile(s, 0)), bl = smem_u32(b_tile(s, 1));
 #pragma unroll
           for (int kk = 0; kk < kKStage / kKMma; ++kk) {
-            const uint32_t off = kk * kKMma * 4;  // 32 bytes per K-step inside the 128-byte swizzle row
-            tc_mma_tf32(d, make_sdesc(ah + off, 16, 1024, 2), make_sdesc(bh + off, 16, 1024, 2), idesc,
-                        (kc > f.kc0 || kk > 0) ? 1u : 0u);
-            tc_mma_tf32(d, make_sdesc(ah + off, 16, 1024, 2), make_sdesc(bl + off, 16, 1024, 2), idesc, 1u);
-            if constexpr (TERMS == 3)
+            const uint32_t off = kk * 32;  // 32 bytes per K-step inside the 128-byte swizzle row
+            const uint32_t first = (kc > f.kc0 || kk > 0) ? 1u : 0u;
+            if constexpr (TERMS == 3) {
+              tc_mma_tf32(d, make_sdesc(ah + off, 16, 1024, 2), make_sdesc(bh + off, 16, 1024, 2), idesc, first);
+              tc_mma_tf32(d, make_sdesc(ah + off, 16, 1024, 2), make_sdesc(bl + off, 16, 1024, 2), idesc, 1u);
               tc_mma_tf32(d, make_sdesc(al + off, 16, 1024, 2), make_sdesc(bh + off, 16, 1024, 2), idesc, 1u);
+            } else {
+              tc_mma_ss(d, make_sdesc(ah + off, 16, 1024, 2), make_sdesc(bh + off, 16, 1024, 2), idesc, first);
+              tc_mma_ss(d, make_sdesc(ah + off, 16, 1024, 2), make_sdesc(bl + off, 16, 1024, 2), idesc, 1u);
+            }
           }
           tc_commit(&bars[C::kBarEmpty + s]);
         }
@@ -235,7 +247,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int acc = tc % kAccs;
       if (!warp_wait_all(&bars[C::kBarTFull + acc], (tc / kAccs) & 1, a.err)) break;
       tc_fence_after();
-      const FTile f = ftile_of<BN>(a, t, (a.ne0 + kKStage - 1) / kKStage);
+      const FTile f = ftile_of<BN>(a, t, n_kc);
       const int row = f.row0 + quarter * 32 + lane, tok0 = f.tok0;
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
@@ -246,7 +258,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             const int tok = tok0 + c0 + j;
-            if (tok < a.n) f.dst[static_cast<int64_t>(tok) * f.rows + row] = __uint_as_float(v[j]);
+            if (tok < a.n) {
+              float r = __uint_as_float(v[j]);
+              if constexpr (TERMS == 2) r = __fmul_rn(r, a.scale[tok]);  // a power of two: exact
+              f.dst[static_cast<int64_t>(tok) * f.rows + row] = r;
+            }
           }
         }
       }
@@ -279,6 +295,40 @@ __global__ void split_tf32_kernel(const float* __restrict__ x, float* __restrict
   }
 }
 
+// One activation row (a CTA each) scaled by a power of two so its largest magnitude lies in [2^13, 2^14), then split
+// into two fp16 terms: x * 2^-s = t1 + t2 + r with t1 = fp16(x * 2^-s), t2 = fp16(x * 2^-s - t1) (the difference
+// is exact in fp32) and |r| <= 2^-12 |x * 2^-s - t1|, below 2^-22 of the element or 2^-38 of the row's largest one
+// where t2 is subnormal. scale[row] = 2^s undoes the scaling exactly in the epilogue.
+__global__ void split_f16_rows_kernel(const float* __restrict__ x, __half* __restrict__ t1, __half* __restrict__ t2,
+                                      float* __restrict__ scale, int64_t ne0) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const float* p = x + row * ne0;
+  float m = 0.f;
+  for (int64_t i = threadIdx.x; i < ne0; i += blockDim.x) m = fmaxf(m, fabsf(p[i]));
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    m = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (threadIdx.x == 0) red[0] = m;
+  }
+  __syncthreads();
+  m = red[0];
+  int e = 0;
+  if (m > 0.f && m <= 3.4e38f) frexpf(m, &e);  // m = f * 2^e, f in [0.5, 1)
+  const int sh = m > 0.f && m <= 3.4e38f ? e - 14 : 0;
+  const float down = ldexpf(1.f, -sh);
+  if (threadIdx.x == 0) scale[row] = ldexpf(1.f, sh);
+  for (int64_t i = threadIdx.x; i < ne0; i += blockDim.x) {
+    const float v = __fmul_rn(p[i], down);
+    const __half h1 = __float2half_rn(v);
+    t1[row * ne0 + i] = h1;
+    t2[row * ne0 + i] = __float2half_rn(__fsub_rn(v, __half2float(h1)));
+  }
+}
+
 // y[i] = sum over the K splits of partial[s][i], in split order.
 __global__ void splitk_sum_kernel(const float* __restrict__ partial, float* __restrict__ y, int64_t count, int splits) {
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < count; i += int64_t(gridDim.x) * blockDim.x) {
@@ -288,11 +338,13 @@ __global__ void splitk_sum_kernel(const float* __restrict__ partial, float* __re
   }
 }
 
-void encode_rows(CUtensorMap* m, const float* base, int64_t ne0, int64_t rows, int box_rows) {
+// Rows of 4-byte (tf32 terms) or 2-byte (fp16) elements; a box is one 128-byte swizzle row of K x box_rows.
+void encode_rows(CUtensorMap* m, const void* base, int elem, int64_t ne0, int64_t rows, int box_rows) {
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(ne0), static_cast<cuuint64_t>(rows)};
-  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ne0) * 4};
-  const cuuint32_t box[2] = {kKStage, static_cast<cuuint32_t>(box_rows)};
-  encode_tmap(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box);
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ne0) * elem};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / elem), static_cast<cuuint32_t>(box_rows)};
+  encode_tmap(m, elem == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+              const_cast<void*>(base), dims, strides, box);
 }
 
 template <int TERMS, int BN>
@@ -311,16 +363,20 @@ void launch_t(cudaStream_t st, const FGemmMaps& maps, const FGemmArgs& a, int gr
   fgemm_kernel<TERMS, BN><<<grid, kThreads, C::kSmemBytes, st>>>(maps, a);
 }
 
+int64_t pad_rows(int64_t n) { return (n + 63) / 64 * 64; }  // keeps the partials 256-byte aligned
+
 }  // namespace
 
-bool fgemm_supported(int64_t ne0) { return ne0 % 4 == 0; }
+// TMA rows must be whole 16-byte multiples: 4 fp32 (tf32 terms of an F32 matrix) or 8 fp16 (an F16 matrix).
+bool fgemm_supported(int32_t dtype, int64_t ne0) { return ne0 % (dtype == NBL_F16 ? 8 : 4) == 0; }
 
 constexpr int kMaxSplits = 16;
-constexpr int kMinStagesPerSplit = 8;  // 256 K per split at least
+constexpr int kMinStagesPerSplit = 8;  // 8 128-byte rows of K per split at least
 
 size_t fgemm_act_bytes(int64_t n, int64_t rows, int64_t ne0) {
-  // the two activation terms, then room for the split-K partials
-  return static_cast<size_t>(2 * n * ne0 + kMaxSplits * n * rows) * sizeof(float);
+  // the two activation terms (fp32 for F32 weights; fp16 for F16 weights, which use half), the activation rows'
+  // scales, then room for the split-K partials
+  return static_cast<size_t>(2 * n * ne0 + pad_rows(n) + kMaxSplits * n * rows) * sizeof(float);
 }
 
 void split_tf32(cudaStream_t st, const float* x, float* hi, float* lo, int64_t count, int num_sms) {
@@ -329,13 +385,23 @@ void split_tf32(cudaStream_t st, const float* x, float* hi, float* lo, int64_t c
   check_cuda(cudaGetLastError(), "tf32 split launch");
 }
 
-void launch_fgemm(cudaStream_t st, const float* const* w_hi, const float* const* w_lo, const int64_t* rows,
+void launch_fgemm(cudaStream_t st, const void* const* w_hi, const float* const* w_lo, const int64_t* rows,
                   float* const* ys, int count, int64_t ne0, const float* x, int64_t n, void* act, int num_sms,
                   int* err) {
-  float* xh = static_cast<float*>(act);
-  float* xl = xh + n * ne0;
-  float* partial = xl + n * ne0;
-  split_tf32(st, x, xh, xl, n * ne0, num_sms);
+  const bool f16 = w_lo[0] == nullptr;  // F16 weights as they are; else the tf32 terms of F32 weights
+  const int elem = f16 ? 2 : 4;
+  float* xh = static_cast<float*>(act);  // activation term 1, then term 2, of elem bytes each
+  void* b1 = xh;
+  void* b2 = static_cast<uint8_t*>(act) + static_cast<size_t>(n * ne0) * elem;
+  float* scale = xh + 2 * n * ne0;
+  float* partial = scale + pad_rows(n);
+  if (f16) {
+    split_f16_rows_kernel<<<static_cast<unsigned>(n), 256, 0, st>>>(x, static_cast<__half*>(b1),
+                                                                      static_cast<__half*>(b2), scale, ne0);
+    check_cuda(cudaGetLastError(), "fp16 split launch");
+  } else {
+    split_tf32(st, x, static_cast<float*>(b1), static_cast<float*>(b2), n * ne0, num_sms);
+  }
   // the tile shape and each weight's K split depend on n and that weight alone, never on the group, so a
   // matmul_multi launch gives every weight the bits a separate call gives it
   const int bn = n <= 64 ? 64 : 128;
@@ -344,9 +410,10 @@ void launch_fgemm(cudaStream_t st, const float* const* w_hi, const float* const*
   a.n = static_cast<int>(n);
   a.ne0 = static_cast<int>(ne0);
   a.n_tt = static_cast<int>((n + bn - 1) / bn);
+  a.scale = scale;
   // a weight whose output tiles cannot cover the SMs alone splits K (partials summed in split order by a second
   // launch)
-  const int64_t n_kc = (ne0 + kKStage - 1) / kKStage;
+  const int64_t k_row = 128 / elem, n_kc = (ne0 + k_row - 1) / k_row;
   a.err = err;
   FGemmMaps maps;
   int tiles = 0;
@@ -372,14 +439,14 @@ void launch_fgemm(cudaStream_t st, const float* const* w_hi, const float* const*
       a.kc_per_split[i] = static_cast<int>(n_kc);
     }
     a.tiles_end[i] = tiles;
-    encode_rows(&maps.a_hi[i], w_hi[w], ne0, rows[w], kBM);
-    encode_rows(&maps.a_lo[i], w_lo[w] ? w_lo[w] : w_hi[w], ne0, rows[w], kBM);
+    encode_rows(&maps.a_hi[i], w_hi[w], elem, ne0, rows[w], kBM);
+    encode_rows(&maps.a_lo[i], w_lo[w] ? static_cast<const void*>(w_lo[w]) : w_hi[w], elem, ne0, rows[w], kBM);
   }
   a.n_tiles = tiles;
-  encode_rows(&maps.b_hi, xh, ne0, n, bn);
-  encode_rows(&maps.b_lo, xl, ne0, n, bn);
+  encode_rows(&maps.b_hi, b1, elem, ne0, n, bn);
+  encode_rows(&maps.b_lo, b2, elem, ne0, n, bn);
   const int grid = static_cast<int>(std::min<int64_t>(a.n_tiles, num_sms));
-  if (w_lo[0]) {
+  if (!f16) {
     if (bn == 64) launch_t<3, 64>(st, maps, a, grid);
     else launch_t<3, 128>(st, maps, a, grid);
   } else {

@@ -62,16 +62,15 @@ void launch_gemv_multi(cudaStream_t st, const Weight* const* ws, float* const* y
                        int64_t n, int num_sms);
 void gemm_f32(cublasHandle_t h, cudaStream_t st, const float* w_f32, const float* x, float* y, int64_t ne0, int64_t ne1,
               int64_t n);
-// f32_gemm.cu: the float matmul for more than kGemvMaxRows rows on the tensor cores (kind::tf32 with the operands
-// split into tf32 terms: fp32 accuracy), for up to kMaxMulti weights sharing x and ne0 in one launch. w_hi[i]: an
-// F16 matrix widened to fp32 (exact in tf32, w_lo[i] = NULL) or the tf32 high term of an F32 matrix (w_lo[i] its
-// low term); all weights of one launch are of one kind. x is split into act (fgemm_act_bytes over the weights'
-// total rows; it also holds the partials when K is split across CTAs). Rows of ne0 % 4 != 0 cannot be TMA-tiled
-// (fgemm_supported).
-bool fgemm_supported(int64_t ne0);
+// f32_gemm.cu: the float matmul for more than kGemvMaxRows rows on the tensor cores at fp32 accuracy (activations
+// split into two 11-bit terms), for up to kMaxMulti weights of one type sharing x and ne0 in one launch. F16 weights:
+// w_hi[i] = the device fp16 matrix, w_lo[i] = NULL (kind::f16); F32 weights: w_hi[i] / w_lo[i] = the matrix's two
+// tf32 terms (kind::tf32). act holds the activation terms, their scales and the split-K partials
+// (fgemm_act_bytes over the weights' total rows). Row widths TMA cannot tile are refused (fgemm_supported).
+bool fgemm_supported(int32_t dtype, int64_t ne0);
 size_t fgemm_act_bytes(int64_t n, int64_t rows, int64_t ne0);
 void split_tf32(cudaStream_t st, const float* x, float* hi, float* lo, int64_t count, int num_sms);
-void launch_fgemm(cudaStream_t st, const float* const* w_hi, const float* const* w_lo, const int64_t* rows,
+void launch_fgemm(cudaStream_t st, const void* const* w_hi, const float* const* w_lo, const int64_t* rows,
                   float* const* ys, int count, int64_t ne0, const float* x, int64_t n, void* act, int num_sms,
                   int* err);
 // quant_ops.cu: the Q8_0-activation weight family (Q4_0, Q5_0, Q8_0)
