@@ -158,3 +158,20 @@ def test_attention_wide_heads_and_long_context(nbl_ctx, n, pos0, H, KV, D):
     nbl_ctx.attention(dev(q), dev(k), dev(v), out, n, pos0, H, KV, D)
     ref = oracle.attention(q, k, v, n, pos0, H, KV, D)
     assert max_rel_err_per_head(host(out), ref) <= 1e-4
+
+
+@pytest.mark.parametrize("n,pos0,H,KV,D", [(16, 0, 8, 2, 64), (100, 37, 4, 1, 128), (300, 500, 14, 2, 64),
+                                           (65, 3, 6, 3, 128), (64, 0, 32, 4, 64)])
+def test_attention_query_tiles(nbl_ctx, n, pos0, H, KV, D):
+    """Prefill chunks of 16 rows or more with head_dim 64 or 128 run 64-query tiles: a partial last tile, keys
+    before the chunk (pos0 > 0), GQA ratios 4, 7, 2 and 8; against the C oracle (nibble's scalar attention)."""
+    import torch
+    rng = np.random.default_rng(n + pos0 + D + H)
+    L = pos0 + n
+    q = rng.standard_normal((n, H, D)).astype(np.float32)
+    k = rng.standard_normal((L, KV, D)).astype(np.float32)
+    v = rng.standard_normal((L, KV, D)).astype(np.float32)
+    out = torch.full((n, H, D), float("nan"), device="cuda")
+    nbl_ctx.attention(dev(q), dev(k), dev(v), out, n, pos0, H, KV, D)
+    ref = oracle.attention(q, k, v, n, pos0, H, KV, D)
+    assert max_rel_err_per_head(host(out), ref) <= 1e-4
