@@ -153,7 +153,8 @@ __global__ void __launch_bounds__(W * 32) attention_f32_kernel(const float* __re
 }
 
 // ---------------------------------------------------------------- query tiles (prefill chunks)
-// A CTA takes 64 query rows of one head and walks their keys in chunks of 64 staged in shared memory, so each K/V
+// A CTA takes 64 query rows of one head (and, when there are more tiles than SMs, then the mirror tile from the end
+// of the chunk, so that every CTA has about the same causal work) and walks their keys in chunks of 64 staged in shared memory, so each K/V
 // row is read once per 64 queries instead of once per query. Thread (ty, tx) (16 x 16) owns query rows ty + 16 i and,
 // for the scores, key columns tx + 16 j (i, j < 4): each score is the same in-order fmaf chain over d as above, built
 // from 16-byte shared loads (K rows padded to head_dim + 4 floats, so eight lanes reading eight rows miss no bank).
@@ -169,7 +170,7 @@ __host__ __device__ constexpr size_t tiled_smem_floats() {
 template <int D>
 __global__ void __launch_bounds__(kTileThreads) attention_f32_tiled_kernel(
     const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v, float* __restrict__ out,
-    int64_t n, int64_t pos0, int64_t n_heads, int64_t n_kv_heads, float scale) {
+    int64_t n, int64_t pos0, int64_t n_heads, int64_t n_kv_heads, float scale, bool paired) {
   constexpr int LD = D + 4, LP = kTileK + 4, C4 = D / 64;  // C4: float4 column groups of o per thread
   extern __shared__ __align__(16) float tsm[];
   float* qs = tsm;                    // [64][LD]
@@ -178,121 +179,128 @@ __global__ void __launch_bounds__(kTileThreads) attention_f32_tiled_kernel(
   float* ps = vs + kTileK * D;        // [64][LP]
   const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
   const int64_t h = blockIdx.y, kvh = h / (n_heads / n_kv_heads);
-  const int64_t q0 = int64_t(blockIdx.x) * kTileQ;
   const int64_t q_stride = n_heads * D, kv_stride = n_kv_heads * D;
-  // the query tile (rows past n read as zero and are never written)
-  for (int e = tid; e < kTileQ * D / 4; e += kTileThreads) {
-    const int r = e / (D / 4), c = e - r * (D / 4);
-    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (q0 + r < n) x = __ldg(reinterpret_cast<const float4*>(q + (q0 + r) * q_stride + h * D) + c);
-    *reinterpret_cast<float4*>(qs + r * LD + 4 * c) = x;
-  }
-  float m[4], l[4], o[4][C4][4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    m[i] = -INFINITY;
-    l[i] = 0.f;
-#pragma unroll
-    for (int c = 0; c < C4; ++c)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) o[i][c][e] = 0.f;
-  }
-  const int64_t last = (q0 + kTileQ < n ? q0 + kTileQ : n) - 1;
-  const int64_t keys = pos0 + last + 1;  // the tile's longest causal range
-  for (int64_t j0 = 0; j0 < keys; j0 += kTileK) {
-    __syncthreads();  // the previous chunk's K, V and p are no longer read
-    for (int e = tid; e < kTileK * D / 4; e += kTileThreads) {
+  // tiles x and n_tiles - 1 - x: under the causal mask their key counts add up to the same total for every CTA
+  const int64_t n_tiles = (n + kTileQ - 1) / kTileQ;
+  for (int which = 0; which < 2; ++which) {
+    const int64_t tile = which == 0 ? int64_t(blockIdx.x) : n_tiles - 1 - int64_t(blockIdx.x);
+    if (which == 1 && (!paired || tile <= int64_t(blockIdx.x))) break;
+    const int64_t q0 = tile * kTileQ;
+    __syncthreads();  // the previous tile's shared data is no longer read
+    // the query tile (rows past n read as zero and are never written)
+    for (int e = tid; e < kTileQ * D / 4; e += kTileThreads) {
       const int r = e / (D / 4), c = e - r * (D / 4);
-      float4 kx = make_float4(0.f, 0.f, 0.f, 0.f), vx = kx;
-      if (j0 + r < keys) {
-        kx = __ldg(reinterpret_cast<const float4*>(k + (j0 + r) * kv_stride + kvh * D) + c);
-        vx = __ldg(reinterpret_cast<const float4*>(v + (j0 + r) * kv_stride + kvh * D) + c);
-      }
-      *reinterpret_cast<float4*>(ks + r * LD + 4 * c) = kx;
-      *reinterpret_cast<float4*>(vs + r * D + 4 * c) = vx;
+      float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (q0 + r < n) x = __ldg(reinterpret_cast<const float4*>(q + (q0 + r) * q_stride + h * D) + c);
+      *reinterpret_cast<float4*>(qs + r * LD + 4 * c) = x;
     }
-    __syncthreads();
-    float sc[4][4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) sc[i][j] = 0.f;
-#pragma unroll 4
-    for (int d = 0; d < D; d += 4) {
-      float4 qa[4], kb[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) qa[i] = *reinterpret_cast<const float4*>(qs + (ty + 16 * i) * LD + d);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) kb[j] = *reinterpret_cast<const float4*>(ks + (tx + 16 * j) * LD + d);
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          sc[i][j] = fmaf(qa[i].x, kb[j].x, sc[i][j]);
-          sc[i][j] = fmaf(qa[i].y, kb[j].y, sc[i][j]);
-          sc[i][j] = fmaf(qa[i].z, kb[j].z, sc[i][j]);
-          sc[i][j] = fmaf(qa[i].w, kb[j].w, sc[i][j]);
-        }
-    }
+    float m[4], l[4], o[4][C4][4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const int64_t qpos = pos0 + q0 + ty + 16 * i;  // keys 0..qpos
-      float mx = -INFINITY;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int64_t key = j0 + tx + 16 * j;
-        sc[i][j] = key <= qpos ? sc[i][j] * scale : -INFINITY;
-        mx = fmaxf(mx, sc[i][j]);
-      }
-#pragma unroll
-      for (int off = 8; off; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-      const float m_new = fmaxf(m[i], mx);  // finite: key 0 lies in every row's first chunk
-      const float alpha = expf(m[i] - m_new);
-      float rs = 0.f;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float p = sc[i][j] == -INFINITY ? 0.f : expf(sc[i][j] - m_new);
-        ps[(ty + 16 * i) * LP + tx + 16 * j] = p;
-        rs += p;
-      }
-#pragma unroll
-      for (int off = 8; off; off >>= 1) rs += __shfl_xor_sync(0xffffffffu, rs, off);
-      l[i] = l[i] * alpha + rs;
-      m[i] = m_new;
+      m[i] = -INFINITY;
+      l[i] = 0.f;
 #pragma unroll
       for (int c = 0; c < C4; ++c)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) o[i][c][e] *= alpha;
+        for (int e = 0; e < 4; ++e) o[i][c][e] = 0.f;
     }
-    __syncthreads();
-    const int jn = keys - j0 < kTileK ? static_cast<int>(keys - j0) : kTileK;
+    const int64_t last = (q0 + kTileQ < n ? q0 + kTileQ : n) - 1;
+    const int64_t keys = pos0 + last + 1;  // the tile's longest causal range
+    for (int64_t j0 = 0; j0 < keys; j0 += kTileK) {
+      __syncthreads();  // the previous chunk's K, V and p are no longer read
+      for (int e = tid; e < kTileK * D / 4; e += kTileThreads) {
+        const int r = e / (D / 4), c = e - r * (D / 4);
+        float4 kx = make_float4(0.f, 0.f, 0.f, 0.f), vx = kx;
+        if (j0 + r < keys) {
+          kx = __ldg(reinterpret_cast<const float4*>(k + (j0 + r) * kv_stride + kvh * D) + c);
+          vx = __ldg(reinterpret_cast<const float4*>(v + (j0 + r) * kv_stride + kvh * D) + c);
+        }
+        *reinterpret_cast<float4*>(ks + r * LD + 4 * c) = kx;
+        *reinterpret_cast<float4*>(vs + r * D + 4 * c) = vx;
+      }
+      __syncthreads();
+      float sc[4][4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) sc[i][j] = 0.f;
 #pragma unroll 4
-    for (int j = 0; j < jn; ++j) {
-      float pr[4];
+      for (int d = 0; d < D; d += 4) {
+        float4 qa[4], kb[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) pr[i] = ps[(ty + 16 * i) * LP + j];
+        for (int i = 0; i < 4; ++i) qa[i] = *reinterpret_cast<const float4*>(qs + (ty + 16 * i) * LD + d);
 #pragma unroll
-      for (int c = 0; c < C4; ++c) {
-        const float4 vv = *reinterpret_cast<const float4*>(vs + j * D + 64 * c + 4 * tx);
+        for (int j = 0; j < 4; ++j) kb[j] = *reinterpret_cast<const float4*>(ks + (tx + 16 * j) * LD + d);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          o[i][c][0] = fmaf(pr[i], vv.x, o[i][c][0]);
-          o[i][c][1] = fmaf(pr[i], vv.y, o[i][c][1]);
-          o[i][c][2] = fmaf(pr[i], vv.z, o[i][c][2]);
-          o[i][c][3] = fmaf(pr[i], vv.w, o[i][c][3]);
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            sc[i][j] = fmaf(qa[i].x, kb[j].x, sc[i][j]);
+            sc[i][j] = fmaf(qa[i].y, kb[j].y, sc[i][j]);
+            sc[i][j] = fmaf(qa[i].z, kb[j].z, sc[i][j]);
+            sc[i][j] = fmaf(qa[i].w, kb[j].w, sc[i][j]);
+          }
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int64_t qpos = pos0 + q0 + ty + 16 * i;  // keys 0..qpos
+        float mx = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int64_t key = j0 + tx + 16 * j;
+          sc[i][j] = key <= qpos ? sc[i][j] * scale : -INFINITY;
+          mx = fmaxf(mx, sc[i][j]);
+        }
+#pragma unroll
+        for (int off = 8; off; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+        const float m_new = fmaxf(m[i], mx);  // finite: key 0 lies in every row's first chunk
+        const float alpha = expf(m[i] - m_new);
+        float rs = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float p = sc[i][j] == -INFINITY ? 0.f : expf(sc[i][j] - m_new);
+          ps[(ty + 16 * i) * LP + tx + 16 * j] = p;
+          rs += p;
+        }
+#pragma unroll
+        for (int off = 8; off; off >>= 1) rs += __shfl_xor_sync(0xffffffffu, rs, off);
+        l[i] = l[i] * alpha + rs;
+        m[i] = m_new;
+#pragma unroll
+        for (int c = 0; c < C4; ++c)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) o[i][c][e] *= alpha;
+      }
+      __syncthreads();
+      const int jn = keys - j0 < kTileK ? static_cast<int>(keys - j0) : kTileK;
+#pragma unroll 4
+      for (int j = 0; j < jn; ++j) {
+        float pr[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) pr[i] = ps[(ty + 16 * i) * LP + j];
+#pragma unroll
+        for (int c = 0; c < C4; ++c) {
+          const float4 vv = *reinterpret_cast<const float4*>(vs + j * D + 64 * c + 4 * tx);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            o[i][c][0] = fmaf(pr[i], vv.x, o[i][c][0]);
+            o[i][c][1] = fmaf(pr[i], vv.y, o[i][c][1]);
+            o[i][c][2] = fmaf(pr[i], vv.z, o[i][c][2]);
+            o[i][c][3] = fmaf(pr[i], vv.w, o[i][c][3]);
+          }
         }
       }
     }
-  }
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int64_t row = q0 + ty + 16 * i;
-    if (row < n) {
-      const float inv = 1.f / l[i];
+    for (int i = 0; i < 4; ++i) {
+      const int64_t row = q0 + ty + 16 * i;
+      if (row < n) {
+        const float inv = 1.f / l[i];
 #pragma unroll
-      for (int c = 0; c < C4; ++c) {
-        const float4 y = make_float4(o[i][c][0] * inv, o[i][c][1] * inv, o[i][c][2] * inv, o[i][c][3] * inv);
-        *reinterpret_cast<float4*>(out + row * q_stride + h * D + 64 * c + 4 * tx) = y;
+        for (int c = 0; c < C4; ++c) {
+          const float4 y = make_float4(o[i][c][0] * inv, o[i][c][1] * inv, o[i][c][2] * inv, o[i][c][3] * inv);
+          *reinterpret_cast<float4*>(out + row * q_stride + h * D + 64 * c + 4 * tx) = y;
+        }
       }
     }
   }
@@ -300,7 +308,7 @@ __global__ void __launch_bounds__(kTileThreads) attention_f32_tiled_kernel(
 
 template <int D>
 void launch_tiled(cudaStream_t st, const float* q, const float* k, const float* v, float* out, int64_t n,
-                  int64_t pos0, int64_t n_heads, int64_t n_kv_heads, float scale) {
+                  int64_t pos0, int64_t n_heads, int64_t n_kv_heads, float scale, int num_sms) {
   const size_t smem = tiled_smem_floats<D>() * sizeof(float);
   static std::atomic<uint64_t> configured{0};
   int dev = 0;
@@ -312,8 +320,12 @@ void launch_tiled(cudaStream_t st, const float* q, const float* k, const float* 
                "attention smem attribute");
     configured.fetch_or(bit);
   }
-  const dim3 grid(static_cast<unsigned>((n + kTileQ - 1) / kTileQ), static_cast<unsigned>(n_heads));
-  attention_f32_tiled_kernel<D><<<grid, kTileThreads, smem, st>>>(q, k, v, out, n, pos0, n_heads, n_kv_heads, scale);
+  // pairs of tiles per CTA only when one tile per CTA would be more CTAs than SMs (otherwise the pairs idle SMs)
+  const int64_t n_tiles = (n + kTileQ - 1) / kTileQ;
+  const bool paired = n_tiles * n_heads > num_sms;
+  const dim3 grid(static_cast<unsigned>(paired ? (n_tiles + 1) / 2 : n_tiles), static_cast<unsigned>(n_heads));
+  attention_f32_tiled_kernel<D><<<grid, kTileThreads, smem, st>>>(q, k, v, out, n, pos0, n_heads, n_kv_heads, scale,
+                                                                   paired);
 }
 
 // The widest head each warp count is launched for (shared memory stays under ~140 KB).
@@ -349,8 +361,8 @@ void launch_attention_f32(cudaStream_t st, const float* q, const float* k, const
   const bool aligned = ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
                          reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(out)) & 15u) == 0;
   if (n >= 16 && aligned && n_heads <= 65535 && (head_dim == 64 || head_dim == 128)) {
-    if (head_dim == 64) launch_tiled<64>(st, q, k, v, out, n, pos0, n_heads, n_kv_heads, scale);
-    else launch_tiled<128>(st, q, k, v, out, n, pos0, n_heads, n_kv_heads, scale);
+    if (head_dim == 64) launch_tiled<64>(st, q, k, v, out, n, pos0, n_heads, n_kv_heads, scale, num_sms);
+    else launch_tiled<128>(st, q, k, v, out, n, pos0, n_heads, n_kv_heads, scale, num_sms);
     check_cuda(cudaGetLastError(), "attention launch");
     return;
   }
