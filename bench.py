@@ -3,7 +3,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
 
-Workloads (synthetic seeded inputs of the named shapes; no dataset is involved):
+Workloads (the benchmark configurations 1-5, synthetic seeded inputs of their shapes; no dataset is involved):
   decode_batched  config 2 (the headline): Llama-3.2-1B attention (32 Q / 8 KV heads, head_dim 64, interleaved
                   RoPE theta 5e5); per GPU 64 sequences x 16 layers = 1024 independent rows, each a 4096-token
                   fp16 paged cache plus one new token. A step = fused bias/RoPE/append of the 1024 new tokens +

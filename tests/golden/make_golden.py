@@ -11,7 +11,7 @@ Each fixture stores the seeded inputs and the reference's outputs:
   fp16.npz             : every fp16 bit pattern -> fp32 (src/fp16.h:18), and a float sample -> fp16 (fp16.h:46)
 
 The attention shapes are the reference's own test cases (tests/test_ops.cpp:200-201,
-tests/test_cpu_backend.cpp:66) plus BASELINE-shaped small cases (Qwen2.5 / Llama-3.2 / TinyLlama head layouts).
+tests/test_cpu_backend.cpp:66) plus small cases shaped like the benchmark models (Qwen2.5 / Llama-3.2 / TinyLlama head layouts).
 """
 from __future__ import annotations
 

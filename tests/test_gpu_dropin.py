@@ -3,7 +3,7 @@ C ABI: nbl_rope, nbl_add_bias, nbl_attention, nbl_alloc/free/read/write, against
 (nibble's own outputs) and the C oracle.
 
 Tolerances: RoPE bit-identical (same double-precision angles, uncontracted float rotation); attention max
-relative error per head <= 1e-4 against the fp32 CPU result (BASELINE decode tolerance), and max abs error
+relative error per head <= 1e-4 against the fp32 CPU result (the decode tolerance of the attention path), and max abs error
 <= 2e-5 * max(1, q scale).
 """
 import glob
@@ -98,7 +98,7 @@ def test_attention_rejects_bad_geometry(nbl_ctx):
 
 
 def test_config1_qwen_prefill_then_decode_every_step(nbl_ctx):
-    """Qwen2.5-0.5B attention shape, one layer, fp32 on the reference's own layout. Prefill
+    """Benchmark config 1: Qwen2.5-0.5B attention shape, one layer, fp32 on the reference's own layout. Prefill
     128 tokens, then 128 single-token decode steps; every step is checked against nibble's scalar attention
     (through the oracle, which tests/test_oracle.py pins bit-exactly to it). The op sequence is the
     Transformer's: K/V rows written into the cache at pos0, rope(q), rope(k cache rows), attention."""

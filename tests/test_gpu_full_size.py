@@ -1,4 +1,4 @@
-"""Parity at BASELINE's full sizes: the exact bench steps of configs 2, 3 and 5 (same shapes, page layouts and
+"""Parity at the benchmark configurations' full sizes: the exact bench steps of configs 2, 3 and 5 (same shapes, page layouts and
 seeds as bench.py), checked on sampled rows against the CPU oracle.
 
 The oracle cannot redo a whole step in seconds, so each test runs the full-size step on the GPU and recomputes a

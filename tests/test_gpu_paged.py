@@ -1,7 +1,7 @@
 """GPU parity of the paged K/V path through the C ABI: fused bias->RoPE->append, split-K flash-decode, LSE merge
 and the tcgen05 prefill, against the C oracle (pinned bit-exactly to nibble's scalar code by test_oracle.py).
 
-Tolerances (BASELINE):
+Tolerances (those of the attention path):
   * append: bit-identical (q_out fp32 = cpu::rope(q + bq); pool K = fp16/bf16 RNE of cpu::rope(k + bk)).
   * decode (fp32 accumulate over the fp16 cache): max relative error per head <= 1e-4 against the fp32 CPU
     result on the same fp16 values widened.
