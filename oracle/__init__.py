@@ -81,6 +81,8 @@ def _load_oracle():
     lib.orc_add.argtypes = [_f32p, _f32p, _i64]
     lib.orc_silu_mul.argtypes = [_f32p, _f32p, _i64]
     lib.orc_quantize_q8_0.argtypes = [_f32p, C.c_void_p, _i64]
+    lib.orc_quantize_q8_1.argtypes = [_f32p, C.c_void_p, _i64]
+    lib.orc_quantize_q8_K.argtypes = [_f32p, C.c_void_p, _i64]
     lib.orc_dequantize_row.argtypes = [C.c_int, C.c_void_p, _f32p, _i64]
     lib.orc_dequantize_row.restype = C.c_int
     lib.orc_matmul_q.argtypes = [C.c_void_p, C.c_int, _i64, _i64, _f32p, _f32p, _i64]
@@ -133,6 +135,8 @@ def _load_ref():
     lib.nref_backend_rmsnorm.argtypes = [C.c_void_p, _f32p, _f32p, _f32p, _i64, _i64, C.c_float]
     lib.nref_backend_silu_mul.argtypes = [C.c_void_p, _f32p, _f32p, _i64]
     lib.nref_quantize_q8_0.argtypes = [_f32p, C.c_void_p, _i64]
+    lib.nref_quantize_q8_1.argtypes = [_f32p, C.c_void_p, _i64]
+    lib.nref_quantize_q8_K.argtypes = [_f32p, C.c_void_p, _i64]
     lib.nref_dequantize_row.argtypes = [C.c_int, C.c_void_p, _f32p, _i64]
     lib.nref_matmul_q.argtypes = [C.c_void_p, C.c_int, _i64, _i64, _f32p, _f32p, _i64]
     _ref = lib
@@ -280,8 +284,13 @@ def silu_mul(gate, up) -> np.ndarray:
 
 
 # ---------------------------------------------------------------- quantized weights (Q8_0-activation family)
-Q4_0, Q5_0, Q8_0 = 2, 6, 8  # nibble DType ids (ggml's)
-BLOCK_BYTES = {Q4_0: 18, Q5_0: 22, Q8_0: 34}
+Q4_0, Q5_0, Q5_1, Q8_0, Q4_K, Q5_K, Q6_K = 2, 6, 7, 8, 12, 13, 14  # nibble DType ids (ggml's)
+BLOCK_BYTES = {Q4_0: 18, Q5_0: 22, Q5_1: 24, Q8_0: 34, Q4_K: 144, Q5_K: 176, Q6_K: 210}
+BLOCK_ELEMS = {Q4_0: 32, Q5_0: 32, Q5_1: 32, Q8_0: 32, Q4_K: 256, Q5_K: 256, Q6_K: 256}
+
+
+def row_bytes(dtype, ne0) -> int:
+    return ne0 // BLOCK_ELEMS[dtype] * BLOCK_BYTES[dtype]
 
 
 def quantize_q8_0(x) -> np.ndarray:
@@ -292,10 +301,26 @@ def quantize_q8_0(x) -> np.ndarray:
     return out
 
 
+def quantize_q8_1(x) -> np.ndarray:
+    """fp32 [n] (n % 32 == 0) -> uint8 [n / 32 * 36] Q8_1 blocks (src/quant.cpp:260-273)."""
+    x = _c(x).ravel()
+    out = np.empty(x.size // 32 * 36, np.uint8)
+    _load_oracle().orc_quantize_q8_1(x, out.ctypes.data, x.size)
+    return out
+
+
+def quantize_q8_K(x) -> np.ndarray:
+    """fp32 [n] (n % 256 == 0) -> uint8 [n / 256 * 292] Q8_K blocks (src/quant.cpp:276-307)."""
+    x = _c(x).ravel()
+    out = np.empty(x.size // 256 * 292, np.uint8)
+    _load_oracle().orc_quantize_q8_K(x, out.ctypes.data, x.size)
+    return out
+
+
 def dequantize_rows(blocks, dtype, ne0, ne1) -> np.ndarray:
     b = np.ascontiguousarray(blocks, dtype=np.uint8)
     out = np.empty((ne1, ne0), np.float32)
-    rb = ne0 // 32 * BLOCK_BYTES[dtype]
+    rb = row_bytes(dtype, ne0)
     for r in range(ne1):
         if _load_oracle().orc_dequantize_row(dtype, b.ctypes.data + r * rb, out[r], ne0) != 0:
             raise ValueError("dtype")
@@ -311,13 +336,27 @@ def matmul_q(blocks, dtype, ne0, ne1, x, n) -> np.ndarray:
 
 
 def random_q_blocks(rng, dtype, ne1, ne0, scale=0.02) -> np.ndarray:
-    """Random but well-formed weight blocks: random 4/5/8-bit values and fp16 scales of about `scale`."""
-    nb = ne0 // 32
+    """Random but well-formed weight blocks: random value bytes (and random packed sub-block scales for the
+    k-quants) with fp16 scales of about `scale` (Q5_1's minimum and Q4_K / Q5_K's dmin of about -8 / 4 scales)."""
+    nb = ne0 // BLOCK_ELEMS[dtype]
     bb = BLOCK_BYTES[dtype]
     raw = rng.integers(0, 256, size=(ne1 * nb, bb), dtype=np.uint8)
-    d = f32_to_fp16_bits((scale * (0.5 + rng.random(ne1 * nb))).astype(np.float32))
-    raw[:, 0] = d & 0xFF
-    raw[:, 1] = d >> 8
+
+    def put(off, vals):
+        h = f32_to_fp16_bits(vals.astype(np.float32))
+        raw[:, off] = h & 0xFF
+        raw[:, off + 1] = h >> 8
+
+    mag = scale * (0.5 + rng.random(ne1 * nb))
+    if dtype in (Q4_K, Q5_K):
+        put(0, mag / 32)
+        put(2, mag / 16 * rng.random(ne1 * nb))
+    elif dtype == Q6_K:
+        put(208, mag / 64)
+    else:
+        put(0, mag)
+        if dtype == Q5_1:
+            put(2, -8 * mag * rng.random(ne1 * nb))
     return raw.reshape(ne1, nb * bb)
 
 
@@ -329,10 +368,24 @@ def ref_quantize_q8_0(x) -> np.ndarray:
     return out
 
 
+def ref_quantize_q8_1(x) -> np.ndarray:
+    x = _c(x).ravel()
+    out = np.empty(x.size // 32 * 36, np.uint8)
+    _load_ref().nref_quantize_q8_1(x, out.ctypes.data, x.size)
+    return out
+
+
+def ref_quantize_q8_K(x) -> np.ndarray:
+    x = _c(x).ravel()
+    out = np.empty(x.size // 256 * 292, np.uint8)
+    _load_ref().nref_quantize_q8_K(x, out.ctypes.data, x.size)
+    return out
+
+
 def ref_dequantize_rows(blocks, dtype, ne0, ne1) -> np.ndarray:
     b = np.ascontiguousarray(blocks, dtype=np.uint8)
     out = np.empty((ne1, ne0), np.float32)
-    rb = ne0 // 32 * BLOCK_BYTES[dtype]
+    rb = row_bytes(dtype, ne0)
     lib = _load_ref()
     for r in range(ne1):
         if lib.nref_dequantize_row(dtype, b.ctypes.data + r * rb, out[r], ne0) != 0:
@@ -473,6 +526,14 @@ class RefBackend:
         ff, ffp = _ff(freq_factors)
         if self._lib.nref_backend_rope(self._h, y, n, n_heads, head_dim, pos0, freq_base, int(neox), ffp):
             raise RuntimeError(self._lib.nref_last_error().decode())
+        return y
+
+    def matmul(self, blocks, dtype, ne0, ne1, x, n):
+        """CpuBackend::matmul (src/backend/cpu/cpu_backend.cpp:134) of a weight given as GGUF bytes [ne1, row]."""
+        b = np.ascontiguousarray(blocks, dtype=np.uint8)
+        y = np.empty((n, ne1), np.float32)
+        if self._lib.nref_backend_matmul(self._h, b.ctypes.data, dtype, ne0, ne1, _c(x), y, n):
+            raise ValueError(self._lib.nref_last_error().decode())
         return y
 
     def close(self):

@@ -293,10 +293,14 @@ void orc_quantize_q8_0(const float* x, uint8_t* blocks, int64_t n) {
 
 static int64_t orc_block_bytes(int dtype) { return dtype == 2 ? 18 : dtype == 6 ? 22 : dtype == 8 ? 34 : 0; }
 
+static int orc_dequantize_row_ext(int dtype, const uint8_t* p, float* dst, int64_t n);
+static int orc_matmul_q_ext(const uint8_t* w, int dtype, int64_t ne0, int64_t ne1, const float* x, float* y,
+                            int64_t n);
+
 int orc_dequantize_row(int dtype, const void* src, float* dst, int64_t n) {
   const uint8_t* p = (const uint8_t*)src;
   const int64_t bb = orc_block_bytes(dtype);
-  if (!bb) return -1;
+  if (!bb) return orc_dequantize_row_ext(dtype, p, dst, n);
   for (int64_t b = 0; b < n / 32; ++b) {
     const uint8_t* blk = p + b * bb;
     const float d = orc_fp16_to_fp32(orc_rd16(blk));
@@ -322,7 +326,7 @@ int orc_dequantize_row(int dtype, const void* src, float* dst, int64_t n) {
 
 int orc_matmul_q(const void* w, int dtype, int64_t ne0, int64_t ne1, const float* x, float* y, int64_t n) {
   const int64_t bb = orc_block_bytes(dtype), nb = ne0 / 32;
-  if (!bb) return -1;
+  if (!bb) return orc_matmul_q_ext((const uint8_t*)w, dtype, ne0, ne1, x, y, n);
   uint8_t* xa = (uint8_t*)malloc((size_t)(nb * 34));
   if (!xa) return -1;
   for (int64_t t = 0; t < n; ++t) {
@@ -356,6 +360,235 @@ int orc_matmul_q(const void* w, int dtype, int64_t ne0, int64_t ne1, const float
           sum += (dw * da) * (float)(s0 + s1);
         }
       }
+      y[t * ne1 + r] = sum;
+    }
+  }
+  free(xa);
+  return 0;
+}
+
+/* ---- Q5_1 (Q8_1 activations) and the k-quants Q4_K / Q5_K / Q6_K (Q8_K activations), src/quant.h:50-99 ---- */
+
+static int64_t orc_ext_block_bytes(int dtype) {
+  return dtype == 7 ? 24 : dtype == 12 ? 144 : dtype == 13 ? 176 : dtype == 14 ? 210 : 0;
+}
+
+/* The j-th 6-bit scale and minimum of a Q4_K / Q5_K super-block's 12 packed bytes (src/quant.cpp:54-63): j < 4
+ * in the low 6 bits of bytes j and j + 4; j >= 4 in the nibbles of byte j + 4 with their top two bits taken from
+ * bits 6-7 of bytes j - 4 (scale) and j (minimum). */
+static void orc_scale_min_k4(int j, const uint8_t* q, int* sc, int* m) {
+  if (j < 4) {
+    *sc = q[j] & 63;
+    *m = q[j + 4] & 63;
+  } else {
+    *sc = (q[j + 4] & 0x0F) | ((q[j - 4] >> 6) << 4);
+    *m = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+  }
+}
+
+/* The 256 integer values of a k-quant super-block in element order (src/quant.cpp:67-96). Q4_K: element 64c + l
+ * is the low nibble of qs[32c + l], element 64c + 32 + l its high nibble; Q5_K adds 16 where bit (2c) resp.
+ * (2c + 1) of qh[l] is set; Q6_K combines ql nibbles and qh bit pairs per 128-element half, minus 32. */
+static void orc_expand_k(int dtype, const uint8_t* blk, int8_t a[256]) {
+  if (dtype == 14) {
+    for (int h = 0; h < 2; ++h)
+      for (int l = 0; l < 32; ++l) {
+        const uint8_t* ql = blk + 64 * h;
+        const int qh = blk[128 + 32 * h + l];
+        a[128 * h + l] = (int8_t)(((ql[l] & 0xF) | ((qh & 3) << 4)) - 32);
+        a[128 * h + 32 + l] = (int8_t)(((ql[32 + l] & 0xF) | (((qh >> 2) & 3) << 4)) - 32);
+        a[128 * h + 64 + l] = (int8_t)(((ql[l] >> 4) | (((qh >> 4) & 3) << 4)) - 32);
+        a[128 * h + 96 + l] = (int8_t)(((ql[32 + l] >> 4) | (((qh >> 6) & 3) << 4)) - 32);
+      }
+    return;
+  }
+  const uint8_t* qs = blk + (dtype == 13 ? 48 : 16);
+  const uint8_t* qh = blk + 16;
+  for (int c = 0; c < 4; ++c)
+    for (int l = 0; l < 32; ++l) {
+      int lo = qs[32 * c + l] & 0xF, hi = qs[32 * c + l] >> 4;
+      if (dtype == 13) {
+        lo += (qh[l] >> (2 * c)) & 1 ? 16 : 0;
+        hi += (qh[l] >> (2 * c + 1)) & 1 ? 16 : 0;
+      }
+      a[64 * c + l] = (int8_t)lo;
+      a[64 * c + 32 + l] = (int8_t)hi;
+    }
+}
+
+/* Dequantization (src/quant.cpp:98-115, :206-242): Q5_1 x = q * d + m; Q4_K / Q5_K x = (d * sc) * q - dmin * m per
+ * 32-element sub-block; Q6_K x = (d * scale) * q per 16-element sub-block. Each product and sum rounded on its own. */
+static int orc_dequantize_row_ext(int dtype, const uint8_t* p, float* dst, int64_t n) {
+  const int64_t bb = orc_ext_block_bytes(dtype);
+  if (!bb) return -1;
+  if (dtype == 7) {
+    for (int64_t b = 0; b < n / 32; ++b) {
+      const uint8_t* blk = p + b * bb;
+      const float d = orc_fp16_to_fp32(orc_rd16(blk)), m = orc_fp16_to_fp32(orc_rd16(blk + 2));
+      const uint32_t qh = (uint32_t)blk[4] | ((uint32_t)blk[5] << 8) | ((uint32_t)blk[6] << 16) | ((uint32_t)blk[7] << 24);
+      for (int j = 0; j < 16; ++j) {
+        const int x0 = (blk[8 + j] & 0x0F) | (((qh >> j) << 4) & 0x10);
+        const int x1 = (blk[8 + j] >> 4) | ((qh >> (j + 12)) & 0x10);
+        dst[b * 32 + j] = (float)x0 * d + m;
+        dst[b * 32 + j + 16] = (float)x1 * d + m;
+      }
+    }
+    return 0;
+  }
+  for (int64_t b = 0; b < n / 256; ++b) {
+    const uint8_t* blk = p + b * bb;
+    int8_t a[256];
+    orc_expand_k(dtype, blk, a);
+    float* o = dst + b * 256;
+    if (dtype == 14) {
+      const float d = orc_fp16_to_fp32(orc_rd16(blk + 208));
+      for (int k = 0; k < 16; ++k) {
+        const float dk = d * (float)(int8_t)blk[192 + k];
+        for (int l = 0; l < 16; ++l) o[16 * k + l] = dk * (float)a[16 * k + l];
+      }
+    } else {
+      const float d = orc_fp16_to_fp32(orc_rd16(blk)), dmin = orc_fp16_to_fp32(orc_rd16(blk + 2));
+      for (int k = 0; k < 8; ++k) {
+        int sc, m;
+        orc_scale_min_k4(k, blk + 4, &sc, &m);
+        const float d1 = d * (float)sc, m1 = dmin * (float)m;
+        for (int l = 0; l < 32; ++l) o[32 * k + l] = d1 * (float)a[32 * k + l] - m1;
+      }
+    }
+  }
+  return 0;
+}
+
+/* Activations to Q8_1 blocks (36 bytes: fp16 d, fp16 s, 32 int8), src/quant.cpp:260-273: d and q as Q8_0, and
+ * s = fp16(sum(q) * d) from the scale before its fp16 rounding. */
+void orc_quantize_q8_1(const float* x, uint8_t* blocks, int64_t n) {
+  for (int64_t b = 0; b < n / 32; ++b) {
+    const float* xb = x + b * 32;
+    uint8_t* o = blocks + b * 36;
+    float amax = 0.f;
+    int has_nan = 0;
+    for (int j = 0; j < 32; ++j) {
+      amax = fmaxf(amax, fabsf(xb[j]));
+      has_nan |= isnan(xb[j]);
+    }
+    const float d = has_nan ? NAN : amax / 127.f;
+    const float id = d != 0.f ? 1.0f / d : 0.0f;
+    int sum = 0;
+    for (int j = 0; j < 32; ++j) {
+      const float r = roundf(xb[j] * id);
+      const int q = r != r ? 0 : (int)fminf(127.f, fmaxf(-127.f, r));
+      o[4 + j] = (uint8_t)(int8_t)q;
+      sum += q;
+    }
+    const uint16_t hd = orc_fp32_to_fp16(d), hs = orc_fp32_to_fp16((float)sum * d);
+    o[0] = (uint8_t)(hd & 0xFF);
+    o[1] = (uint8_t)(hd >> 8);
+    o[2] = (uint8_t)(hs & 0xFF);
+    o[3] = (uint8_t)(hs >> 8);
+  }
+}
+
+/* Activations to Q8_K blocks (292 bytes: float d, 256 int8, 16 int16 sums of 16), src/quant.cpp:276-307: the
+ * element of largest magnitude (the first on ties) gives iscale = -127 / max, q = round-half-even(iscale * x)
+ * after clamping to [-127, 127] (NaN -> 0), d = 1 / iscale; an all-zero block stays zero; a NaN makes d NaN. */
+void orc_quantize_q8_K(const float* x, uint8_t* blocks, int64_t n) {
+  for (int64_t b = 0; b < n / 256; ++b) {
+    const float* xb = x + b * 256;
+    uint8_t* o = blocks + b * 292;
+    memset(o, 0, 292);
+    float max = 0.f, amax = 0.f, d = 0.f;
+    int has_nan = 0;
+    for (int j = 0; j < 256; ++j) {
+      const float ax = fabsf(xb[j]);
+      if (ax > amax) {
+        amax = ax;
+        max = xb[j];
+      }
+      has_nan |= isnan(xb[j]);
+    }
+    int8_t* q = (int8_t*)(o + 4);
+    if (amax != 0.f) {
+      const float iscale = -127.f / max;
+      for (int j = 0; j < 256; ++j) {
+        const float v = iscale * xb[j];
+        q[j] = (int8_t)(v != v ? 0 : (int)nearbyintf(fminf(127.f, fmaxf(-127.f, v))));
+      }
+      for (int g = 0; g < 16; ++g) {
+        int sum = 0;
+        for (int i = 0; i < 16; ++i) sum += q[16 * g + i];
+        const int16_t s16 = (int16_t)sum;
+        memcpy(o + 260 + 2 * g, &s16, 2);
+      }
+      d = 1.f / iscale;
+    }
+    if (has_nan) d = NAN;
+    memcpy(o, &d, 4);
+  }
+}
+
+/* y[t, r] for Q5_1 (per block (d_w * d_a) * sumi + m_w * s_a, then added to the row sum, src/quant.cpp:371-392)
+ * and the k-quants (src/quant.cpp:117-146 and :399-418): per super-block eight int32 lanes (element e feeds lane
+ * e % 8, each product scaled by its sub-block's scale), sums[l] += (d_w * d_a) * lane[l]; Q4_K / Q5_K also subtract
+ * (dmin_w * d_a) * sum_k(bsum_k * m_k) from the running total; the eight lane sums are added to the total last. */
+static int orc_matmul_q_ext(const uint8_t* w, int dtype, int64_t ne0, int64_t ne1, const float* x, float* y,
+                            int64_t n) {
+  const int64_t bb = orc_ext_block_bytes(dtype);
+  if (!bb) return -1;
+  const int kq = dtype != 7;
+  const int64_t be = kq ? 256 : 32, ab = kq ? 292 : 36, nb = ne0 / be;
+  uint8_t* xa = (uint8_t*)malloc((size_t)(nb * ab));
+  if (!xa) return -1;
+  for (int64_t t = 0; t < n; ++t) {
+    if (kq) orc_quantize_q8_K(x + t * ne0, xa, ne0);
+    else orc_quantize_q8_1(x + t * ne0, xa, ne0);
+    for (int64_t r = 0; r < ne1; ++r) {
+      const uint8_t* wr = w + r * nb * bb;
+      float sum = 0.f, sums[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      for (int64_t b = 0; b < nb; ++b) {
+        const uint8_t* bw = wr + b * bb;
+        const uint8_t* ba = xa + b * ab;
+        if (!kq) {
+          const int8_t* aq = (const int8_t*)(ba + 4);
+          const uint32_t qh = (uint32_t)bw[4] | ((uint32_t)bw[5] << 8) | ((uint32_t)bw[6] << 16) | ((uint32_t)bw[7] << 24);
+          int s0 = 0, s1 = 0;
+          for (int j = 0; j < 16; ++j) {
+            s0 += ((bw[8 + j] & 0x0F) | (((qh >> j) << 4) & 0x10)) * aq[j];
+            s1 += ((bw[8 + j] >> 4) | ((qh >> (j + 12)) & 0x10)) * aq[j + 16];
+          }
+          const float dw = orc_fp16_to_fp32(orc_rd16(bw)), mw = orc_fp16_to_fp32(orc_rd16(bw + 2));
+          const float da = orc_fp16_to_fp32(orc_rd16(ba)), sa = orc_fp16_to_fp32(orc_rd16(ba + 2));
+          sum += (dw * da) * (float)(s0 + s1) + mw * sa;
+          continue;
+        }
+        float da;
+        memcpy(&da, ba, 4);
+        const int8_t* aq = (const int8_t*)(ba + 4);
+        int8_t a[256];
+        orc_expand_k(dtype, bw, a);
+        int lane[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        if (dtype == 14) {
+          for (int e = 0; e < 256; ++e) lane[e & 7] += (int8_t)bw[192 + e / 16] * (aq[e] * a[e]);
+          const float d = orc_fp16_to_fp32(orc_rd16(bw + 208)) * da;
+          for (int l = 0; l < 8; ++l) sums[l] += d * (float)lane[l];
+        } else {
+          int sumi = 0;
+          for (int k = 0; k < 8; ++k) {
+            int sc, m;
+            int16_t b0, b1;
+            orc_scale_min_k4(k, bw + 4, &sc, &m);
+            memcpy(&b0, ba + 260 + 4 * k, 2);
+            memcpy(&b1, ba + 262 + 4 * k, 2);
+            sumi += (b0 + b1) * m;
+            for (int e = 0; e < 32; ++e) lane[e & 7] += sc * (aq[32 * k + e] * a[32 * k + e]);
+          }
+          const float d = orc_fp16_to_fp32(orc_rd16(bw)) * da;
+          for (int l = 0; l < 8; ++l) sums[l] += d * (float)lane[l];
+          const float dmin = orc_fp16_to_fp32(orc_rd16(bw + 2)) * da;
+          sum -= dmin * (float)sumi;
+        }
+      }
+      if (kq)
+        for (int l = 0; l < 8; ++l) sum += sums[l];
       y[t * ne1 + r] = sum;
     }
   }

@@ -80,17 +80,22 @@ void orc_add(float* x, const float* y, int64_t count);
 /* gate[i] = g / (1 + e^-g) * up[i] in float (src/backend/cpu/ref_ops.cpp:217-222). */
 void orc_silu_mul(float* gate, const float* up, int64_t count);
 
-/* Quantized weights (src/quant.h). dtype codes are nibble's DType ids (ggml's): 2 = Q4_0, 6 = Q5_0, 8 = Q8_0.
- * Weights are the GGUF block bytes, row after row (ne0 % 32 == 0). */
+/* Quantized weights (src/quant.h). dtype codes are nibble's DType ids (ggml's): 2 = Q4_0, 6 = Q5_0, 7 = Q5_1,
+ * 8 = Q8_0, 12 = Q4_K, 13 = Q5_K, 14 = Q6_K. Weights are the GGUF block bytes, row after row (ne0 a multiple of
+ * the block: 32, or 256 for the k-quants). */
 /* Activations to Q8_0 blocks (34 bytes: fp16 d, 32 int8), src/quant.cpp:37-51, :250-257: per block d = max|x| /
  * 127 (NaN if the block holds a NaN), q = roundf(x * (1/d)) clamped to [-127, 127]. n % 32 == 0. */
 void orc_quantize_q8_0(const float* x, uint8_t* blocks, int64_t n);
-/* One row of n elements of a Q4_0 / Q5_0 / Q8_0 tensor to float (src/quant.cpp:158-205). Returns -1 for another
- * dtype. */
+/* As orc_quantize_q8_0 into Q8_1 blocks (36 bytes: fp16 d, fp16 s = fp16(sum(q) * d), 32 int8), src/quant.cpp:260. */
+void orc_quantize_q8_1(const float* x, uint8_t* blocks, int64_t n);
+/* Activations to Q8_K blocks (292 bytes: float d, 256 int8, 16 int16 sums), src/quant.cpp:276. n % 256 == 0. */
+void orc_quantize_q8_K(const float* x, uint8_t* blocks, int64_t n);
+/* One row of n elements of a quantized tensor to float (src/quant.cpp:158-246). Returns -1 for another dtype. */
 int orc_dequantize_row(int dtype, const void* src, float* dst, int64_t n);
 /* y[t, r] = dot(weight row r, Q8_0-quantized x row t): per block the integer dot and the reference's float term
  * (Q4_0: sumi * d_w * d_a; Q8_0: sumi * (d_w * d_a); Q5_0: (d_w * d_a) * sumi, src/quant.cpp:310-366), added to
- * the row's sum in block order. Returns -1 for an unsupported dtype. */
+ * the row's sum in block order; Q5_1 against Q8_1 activations and the k-quants against Q8_K ones in the order of
+ * src/quant.cpp:117-146, :371-418. Returns -1 for an unsupported dtype. */
 int orc_matmul_q(const void* w, int dtype, int64_t ne0, int64_t ne1, const float* x, float* y, int64_t n);
 
 #ifdef __cplusplus

@@ -179,14 +179,38 @@ int nref_dequantize_row(int dtype, const void* src, float* dst, int64_t n) {
   }
 }
 
-// nibble::cpu::matmul_rows with a quantized weight: x quantized row by row to Q8_0 (quantize_rows_q8_0), then the
-// scalar block dots (Q8_0-activation weight types only).
+// nibble::quantize_row_q8_1 (src/quant.cpp:260) into 36-byte blocks and nibble::quantize_row_q8_K (:276) into
+// 292-byte blocks.
+void nref_quantize_q8_1(const float* x, void* blocks, int64_t n) {
+  nibble::quantize_row_q8_1(x, static_cast<nibble::BlockQ8_1*>(blocks), n);
+}
+void nref_quantize_q8_K(const float* x, void* blocks, int64_t n) {
+  nibble::quantize_row_q8_K(x, static_cast<nibble::BlockQ8_K*>(blocks), n);
+}
+
+// nibble::cpu::matmul_rows with a quantized weight: x quantized row by row to the weight type's activation blocks
+// (Q8_0 by quantize_rows_q8_0; Q8_1 and Q8_K by quantize_row_q8_1 / quantize_row_q8_K, as CpuBackend::matmul_multi
+// does at src/backend/cpu/cpu_backend.cpp:165-207), then the scalar block dots.
 int nref_matmul_q(const void* w, int dtype, int64_t ne0, int64_t ne1, const float* x, float* y, int64_t n) {
   try {
-    std::vector<nibble::BlockQ8_0> xq(static_cast<size_t>(n * (ne0 / 32)));
-    nibble::cpu::quantize_rows_q8_0(x, xq.data(), n, ne0);
+    const auto act = nibble::act_type(static_cast<nibble::DType>(dtype));
+    std::vector<nibble::BlockQ8_0> xq;
+    std::vector<nibble::BlockQ8_1> xq1;
+    std::vector<nibble::BlockQ8_K> xqk;
     nibble::QuantActs acts;
-    acts.q8_0 = xq.data();
+    if (act == nibble::ActType::Q8_0) {
+      xq.resize(static_cast<size_t>(n * (ne0 / 32)));
+      nibble::cpu::quantize_rows_q8_0(x, xq.data(), n, ne0);
+      acts.q8_0 = xq.data();
+    } else if (act == nibble::ActType::Q8_1) {
+      xq1.resize(static_cast<size_t>(n * (ne0 / 32)));
+      for (int64_t t = 0; t < n; ++t) nibble::quantize_row_q8_1(x + t * ne0, xq1.data() + t * (ne0 / 32), ne0);
+      acts.q8_1 = xq1.data();
+    } else {
+      xqk.resize(static_cast<size_t>(n * (ne0 / 256)));
+      for (int64_t t = 0; t < n; ++t) nibble::quantize_row_q8_K(x + t * ne0, xqk.data() + t * (ne0 / 256), ne0);
+      acts.q8_K = xqk.data();
+    }
     nibble::cpu::matmul_rows(tensor_of(w, dtype, ne0, ne1), x, y, n, 0, ne1, &acts);
     return 0;
   } catch (const std::exception& e) {

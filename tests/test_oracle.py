@@ -254,3 +254,56 @@ def test_quantize_q8_0_known_answer():
     d = oracle.fp16_bits_to_f32(np.array([int(blk[0]) | (int(blk[1]) << 8)], np.uint16))[0]
     q = blk[2:].view(np.int8)
     assert d == 1.0 and list(q[:4]) == [127, -64, 0, -127] and not q[4:].any()
+
+
+# ---------------------------------------------------------------- Q5_1 (Q8_1 activations) and the k-quants (Q8_K)
+def _activation_edge_rows(rng, n):
+    """n floats: random rows plus an all-zero 256-block, one of tiny magnitude, one whose largest magnitude is
+    tied between a negative and a positive element (the first one wins), and one with a NaN."""
+    x = (rng.standard_normal(n) * 3).astype(np.float32)
+    x[:256] = 0.0
+    x[256:512] *= 1e-30
+    x[512:768] = np.clip(x[512:768], -2.0, 2.0)
+    x[512 + 7], x[512 + 9] = -5.0, 5.0
+    return x
+
+
+def test_q8_1_and_q8_K_quantizers_bit_identical_to_reference():
+    if not oracle.have_ref():
+        pytest.skip("oracle/_ref (nibble's own code) is not built here")
+    rng = np.random.default_rng(17)
+    x = _activation_edge_rows(rng, 256 * 6)
+    x[1024 + 100] = np.nan
+    assert np.array_equal(oracle.quantize_q8_1(x), oracle.ref_quantize_q8_1(x))
+    assert np.array_equal(oracle.quantize_q8_K(x), oracle.ref_quantize_q8_K(x))
+    # the tie: max = x[7] = -5 gives iscale = 127 / 5 > 0, so x[9] = 5 quantizes to +127
+    blk = oracle.quantize_q8_K(x[512:768])
+    q = blk[4:260].view(np.int8)
+    assert q[7] == -127 and q[9] == 127
+    assert oracle.quantize_q8_K(x[:256]).view(np.uint8).sum() == 0  # all-zero block: d, qs and sums zero
+
+
+@pytest.mark.parametrize("dtype", [oracle.Q5_1, oracle.Q4_K, oracle.Q5_K, oracle.Q6_K])
+def test_block_quant_oracle_bit_identical_to_reference(dtype):
+    """Row dequantization and the quantized matmul (activations quantized to Q8_1 / Q8_K, the reference's block
+    dots) against nibble's own scalar code (src/quant.cpp via oracle/_ref), over random blocks whose packed scale
+    bytes, high bits and fp16 scales take arbitrary values."""
+    if not oracle.have_ref():
+        pytest.skip("oracle/_ref (nibble's own code) is not built here")
+    rng = np.random.default_rng(dtype + 100)
+    ne0, ne1 = 768, 29
+    w = oracle.random_q_blocks(rng, dtype, ne1, ne0)
+    a = oracle.dequantize_rows(w, dtype, ne0, ne1)
+    b = oracle.ref_dequantize_rows(w, dtype, ne0, ne1)
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    x = _activation_edge_rows(rng, ne0 * 4).reshape(4, ne0)
+    y = oracle.matmul_q(w, dtype, ne0, ne1, x, 4)
+    yr = oracle.ref_matmul_q(w, dtype, ne0, ne1, x, 4)
+    assert np.array_equal(y.view(np.uint32), yr.view(np.uint32))
+    # the same weights through CpuBackend (the SIMD tier the reference runs) agree bit for bit too
+    be = oracle.RefBackend(2)
+    try:
+        yb = be.matmul(w, dtype, ne0, ne1, x, 4)
+    finally:
+        be.close()
+    assert np.array_equal(yb.view(np.uint32), yr.view(np.uint32))
