@@ -44,9 +44,21 @@ typedef enum {
   NBL_E_DEVICE = 5       /* a kernel found an out-of-range device-side index (see nbl_ctx_check) */
 } nbl_status;
 
-/* Element types. The quantized weight types are GGUF's block formats byte for byte (src/quant.h:30-60):
- * Q4_0 (18-byte blocks of 32), Q5_0 (22-byte blocks), Q8_0 (34-byte blocks). */
-typedef enum { NBL_F32 = 0, NBL_F16 = 1, NBL_BF16 = 2, NBL_Q4_0 = 3, NBL_Q5_0 = 4, NBL_Q8_0 = 5 } nbl_dtype;
+/* Element types. The quantized weight types are GGUF's block formats byte for byte (src/quant.h:30-99):
+ * Q4_0 (18-byte blocks of 32), Q5_0 (22-byte blocks), Q8_0 (34-byte blocks), Q5_1 (24-byte blocks of 32), and the
+ * k-quants Q4_K (144-byte blocks of 256), Q5_K (176-byte blocks) and Q6_K (210-byte blocks). */
+typedef enum {
+  NBL_F32 = 0,
+  NBL_F16 = 1,
+  NBL_BF16 = 2,
+  NBL_Q4_0 = 3,
+  NBL_Q5_0 = 4,
+  NBL_Q8_0 = 5,
+  NBL_Q5_1 = 6,
+  NBL_Q4_K = 7,
+  NBL_Q5_K = 8,
+  NBL_Q6_K = 9
+} nbl_dtype;
 
 typedef struct nbl_ctx nbl_ctx; /* device, stream, scratch, RoPE tables, allocation registry */
 typedef struct nbl_kv nbl_kv;   /* one paged K/V pool */
@@ -129,9 +141,9 @@ NBL_API int nbl_attention(nbl_ctx* ctx, const float* q, const float* k, const fl
                   int64_t n_heads, int64_t n_kv_heads, int64_t head_dim);
 
 /* ---- weights and the model's other ops (backend.h:54-70), fp32 device activations ---- */
-/* Uploads a host weight tensor of ne1 rows x ne0 elements, dtype NBL_F32, NBL_F16, NBL_Q4_0, NBL_Q5_0 or NBL_Q8_0
- * (quantized: the GGUF block bytes row after row, ne0 % 32 == 0; they are repacked into an internal aligned
- * layout), to device memory owned by the context: the device form of a weight Tensor view (src/tensor.h:57-70;
+/* Uploads a host weight tensor of ne1 rows x ne0 elements, dtype NBL_F32, NBL_F16 or a quantized type (the GGUF
+ * block bytes row after row, ne0 a multiple of the block: 32, or 256 for the k-quants; Q4_0 / Q5_0 / Q8_0 are
+ * repacked into an internal aligned layout, Q5_1 and the k-quants stay as they are), to device memory owned by the context: the device form of a weight Tensor view (src/tensor.h:57-70;
  * nibble's are views of the mmap'd GGUF). An F16 matrix gets an fp32 copy on its first matmul with more than 8 rows (the SGEMM path; decode-only use
  * never holds it). Freed by nbl_weight_destroy or with the context. Returns after the upload has completed (the
  * host buffer may be released). */

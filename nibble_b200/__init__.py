@@ -14,9 +14,10 @@ import ctypes as C
 from dataclasses import dataclass
 
 from . import _abi
-from ._abi import BF16, F16, F32, Q4_0, Q5_0, Q8_0, NibbleError, check
+from ._abi import BF16, F16, F32, Q4_0, Q4_K, Q5_0, Q5_1, Q5_K, Q6_K, Q8_0, NibbleError, check
 
-__all__ = ["Context", "KVPool", "Weight", "NibbleError", "RopeSpec", "F32", "F16", "BF16", "Q4_0", "Q5_0", "Q8_0",
+__all__ = ["Context", "KVPool", "Weight", "NibbleError", "RopeSpec", "F32", "F16", "BF16", "Q4_0", "Q5_0", "Q8_0", "Q5_1",
+           "Q4_K", "Q5_K", "Q6_K",
            "abi_version"]
 
 
@@ -102,14 +103,15 @@ class Weight:
 
     def __init__(self, ctx: "Context", host, dtype: int | None = None, ne0: int | None = None):
         """host: a C-contiguous numpy float32 / float16 array, 1-D (a vector) or 2-D [ne1, ne0]; or, with dtype
-        Q4_0 / Q5_0 / Q8_0 and ne0 given, the GGUF block bytes as uint8 [ne1, row bytes]."""
+        a quantized type (Q4_0 / Q5_0 / Q8_0 / Q5_1 / Q4_K / Q5_K / Q6_K) and ne0 given, the GGUF block bytes as
+        uint8 [ne1, row bytes]."""
         import numpy as np
         a = np.ascontiguousarray(host)
         if dtype is None:
             dtype = {np.dtype(np.float32): F32, np.dtype(np.float16): F16}.get(a.dtype)
             if dtype is None:
                 raise ValueError(f"weights must be float32 or float16, got {a.dtype}")
-        if dtype in (Q4_0, Q5_0, Q8_0):
+        if dtype in (Q4_0, Q5_0, Q8_0, Q5_1, Q4_K, Q5_K, Q6_K):
             if ne0 is None or a.ndim != 2:
                 raise ValueError("quantized weights take uint8 blocks [ne1, row bytes] and ne0")
             ne1 = a.shape[0]

@@ -13,7 +13,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libnibble_cuda.so")
 
 NBL_OK, NBL_E_INVALID, NBL_E_CUDA, NBL_E_NOMEM, NBL_E_UNSUPPORTED, NBL_E_DEVICE = range(6)
-F32, F16, BF16, Q4_0, Q5_0, Q8_0 = 0, 1, 2, 3, 4, 5
+F32, F16, BF16, Q4_0, Q5_0, Q8_0, Q5_1, Q4_K, Q5_K, Q6_K = 0, 1, 2, 3, 4, 5, 6, 7, 8, 9
 STATUS_NAMES = {0: "NBL_OK", 1: "NBL_E_INVALID", 2: "NBL_E_CUDA", 3: "NBL_E_NOMEM", 4: "NBL_E_UNSUPPORTED",
                 5: "NBL_E_DEVICE"}
 

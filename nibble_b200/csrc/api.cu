@@ -291,6 +291,14 @@ void quant_matmul(nbl_ctx* ctx, const nbl_weight* const* cws, float* const* ys, 
   nbl::launch_qgemm(ctx->stream, ws, ys, count, x, n, ctx->qgemm_act, ctx->num_sms, ctx->d_err);
 }
 
+// A matmul of n activation rows with a Q5_1 or k-quant weight: the rows quantized to Q8_1 / Q8_K blocks in the
+// context's scratch (grown to fit), then the block dots.
+void qblock_matmul(nbl_ctx* ctx, const nbl_weight* w, float* y, const float* x, int64_t n) {
+  grow_scratch(ctx, ctx->qblock_act, ctx->qblock_act_bytes, nbl::qblock_act_bytes(w->w.dtype, n, w->w.ne0),
+               "block-quant activations");
+  nbl::launch_qblock_matmul(ctx->stream, w->w, y, x, n, ctx->qblock_act, ctx->num_sms);
+}
+
 void require_weight(const nbl_ctx* ctx, const nbl_weight* w, const char* what) {
   require(w != nullptr && w->ctx == ctx, std::string(what) + ": weight is NULL or belongs to another context");
 }
@@ -358,6 +366,7 @@ int nbl_ctx_destroy(nbl_ctx* ctx) {
     if (ctx->qgemm_act) cudaFree(ctx->qgemm_act);
     if (ctx->fgemm_act) cudaFree(ctx->fgemm_act);
     if (ctx->qgemv_act) cudaFree(ctx->qgemv_act);
+    if (ctx->qblock_act) cudaFree(ctx->qblock_act);
     for (auto& a : ctx->allocs) cudaFree(a.first);
     for (auto& t : ctx->rope_tables) cudaFree(t.dev);
     if (ctx->scratch) cudaFree(ctx->scratch);
@@ -786,10 +795,14 @@ int nbl_weight_create(nbl_ctx* ctx, const void* host, int32_t dtype, int64_t ne0
   return guarded([&] {
     require(ctx && host && out, "weight_create: ctx, host or out is NULL");
     *out = nullptr;
-    require(dtype == NBL_F32 || dtype == NBL_F16 || nbl::is_quant(dtype),
-            "weight_create: dtype must be NBL_F32, NBL_F16, NBL_Q4_0, NBL_Q5_0 or NBL_Q8_0");
+    require(dtype == NBL_F32 || dtype == NBL_F16 || nbl::is_quant(dtype) || nbl::is_qblock(dtype),
+            "weight_create: dtype must be NBL_F32, NBL_F16 or a quantized type (Q4_0, Q5_0, Q8_0, Q5_1, Q4_K, Q5_K, "
+            "Q6_K)");
     require(ne0 > 0 && ne1 > 0, "weight_create: bad shape " + std::to_string(ne0) + " x " + std::to_string(ne1));
     require(!nbl::is_quant(dtype) || ne0 % 32 == 0, "weight_create: a quantized row must be whole 32-element blocks");
+    require(!nbl::is_qblock(dtype) || ne0 % nbl::qblock_elems(dtype) == 0,
+            "weight_create: a quantized row must be whole " + std::to_string(nbl::qblock_elems(dtype)) +
+                "-element blocks");
     const size_t elem = dtype == NBL_F32 ? 4 : 2;
     require(static_cast<uint64_t>(ne0) <= (uint64_t(1) << 40) / static_cast<uint64_t>(ne1),
             "weight_create: tensor too large");
@@ -828,6 +841,12 @@ int nbl_weight_create(nbl_ctx* ctx, const void* host, int32_t dtype, int64_t ne0
         w->w.q.d = reinterpret_cast<const uint16_t*>(base);
         w->w.q.qs = base + off_qs;
         w->w.q.qh = dtype == NBL_Q5_0 ? reinterpret_cast<const uint32_t*>(base + off_qh) : nullptr;
+      } else if (nbl::is_qblock(dtype)) {
+        // GGUF blocks as they are, row after row
+        const size_t bytes = static_cast<size_t>(ne1) * static_cast<size_t>(ne0 / nbl::qblock_elems(dtype)) *
+                             static_cast<size_t>(nbl::qblock_bytes(dtype));
+        w->w.dev = device_alloc(bytes, "weight");
+        nbl::check_cuda(cudaMemcpyAsync(w->w.dev, host, bytes, cudaMemcpyHostToDevice, ctx->stream), "weight upload");
       } else {
         w->w.dev = device_alloc(count * elem, "weight");
         nbl::check_cuda(cudaMemcpyAsync(w->w.dev, host, count * elem, cudaMemcpyHostToDevice, ctx->stream),
@@ -881,6 +900,8 @@ int nbl_embed(nbl_ctx* ctx, const nbl_weight* table, const int32_t* ids, int64_t
                                     ctx->stream),
                     "embed ids");
     if (nbl::is_quant(table->w.dtype)) nbl::launch_embed_q(ctx->stream, table->w, ctx->ids, n, out);
+    else if (nbl::is_qblock(table->w.dtype))
+      nbl::launch_embed_qblock(ctx->stream, table->w, ctx->ids, n, out, ctx->num_sms);
     else nbl::launch_embed(ctx->stream, table->w, ctx->ids, n, out, ctx->num_sms);
     nbl::check_cuda(cudaGetLastError(), "embed launch");
   });
@@ -895,6 +916,9 @@ int nbl_matmul(nbl_ctx* ctx, const nbl_weight* w, const float* x, float* y, int6
     use_device(ctx);
     if (nbl::is_quant(w->w.dtype)) {
       quant_matmul(ctx, &w, &y, 1, x, n);
+      nbl::check_cuda(cudaGetLastError(), "matmul launch");
+    } else if (nbl::is_qblock(w->w.dtype)) {
+      qblock_matmul(ctx, w, y, x, n);
       nbl::check_cuda(cudaGetLastError(), "matmul launch");
     } else if (n <= nbl::kGemvMaxRows) {
       nbl::launch_gemv(ctx->stream, w->w, x, y, n, ctx->num_sms);
@@ -921,7 +945,7 @@ int nbl_matmul_multi(nbl_ctx* ctx, const nbl_weight* const* ws, int32_t count, c
     use_device(ctx);
     bool any_quant = false, all_quant_same = true;
     for (int32_t i = 0; i < count; ++i) {
-      any_quant = any_quant || nbl::is_quant(ws[i]->w.dtype);
+      any_quant = any_quant || nbl::is_quant(ws[i]->w.dtype) || nbl::is_qblock(ws[i]->w.dtype);
       all_quant_same = all_quant_same && ws[i]->w.dtype == ws[0]->w.dtype && nbl::is_quant(ws[i]->w.dtype);
     }
     if (any_quant) {
@@ -933,6 +957,8 @@ int nbl_matmul_multi(nbl_ctx* ctx, const nbl_weight* const* ws, int32_t count, c
         for (int32_t i = 0; i < count; ++i) {
           if (nbl::is_quant(ws[i]->w.dtype)) {
             quant_matmul(ctx, ws + i, ys + i, 1, x, n);
+          } else if (nbl::is_qblock(ws[i]->w.dtype)) {
+            qblock_matmul(ctx, ws[i], ys[i], x, n);
           } else if (n <= nbl::kGemvMaxRows) {
             nbl::launch_gemv(ctx->stream, ws[i]->w, x, ys[i], n, ctx->num_sms);
           } else {

@@ -47,7 +47,11 @@ const nbl_weight* CudaBackend::device_weight(const Tensor& t) {
     case DType::Q4_0: dt = NBL_Q4_0; break;
     case DType::Q5_0: dt = NBL_Q5_0; break;
     case DType::Q8_0: dt = NBL_Q8_0; break;
-    default: throw Error("cuda backend: unsupported weight dtype (F32/F16/Q4_0/Q5_0/Q8_0 run on the GPU)");
+    case DType::Q5_1: dt = NBL_Q5_1; break;
+    case DType::Q4_K: dt = NBL_Q4_K; break;
+    case DType::Q5_K: dt = NBL_Q5_K; break;
+    case DType::Q6_K: dt = NBL_Q6_K; break;
+    default: throw Error("cuda backend: unsupported weight dtype");
   }
   nbl_weight* w = nullptr;
   check(nbl_weight_create(ctx_, t.data, dt, t.ne[0], t.rows(), &w));

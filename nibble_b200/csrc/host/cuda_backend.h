@@ -10,11 +10,10 @@
 // address (nbl_weight_create), so the first forward pass after construction allocates the model's device weights
 // and later ones allocate nothing.
 //
-// Coverage: every Backend op runs on the GPU for F32, F16, Q4_0, Q5_0 and Q8_0 weights -- embed, matmul
-// (weight-streaming GEMV for up to 8 rows, SGEMM above; the quantized types bit-identical to the CPU's block dots),
-// rmsnorm, add, add_bias, rope, copy, attention, silu_mul -- so nibble's Transformer (src/model/transformer.cpp) runs
-// on it unchanged. supports() is false for Q5_1 and the k-quants, so such a model refuses to load on it instead of
-// running anything on the CPU.
+// Coverage: every Backend op runs on the GPU for every weight type the reference supports (F32, F16, Q4_0, Q5_0,
+// Q8_0, Q5_1, Q4_K, Q5_K, Q6_K) -- embed, matmul (float: weight-streaming GEMV for up to 8 rows, tensor-core GEMM
+// above; quantized: bit-identical to the CPU's block dots), rmsnorm, add, add_bias, rope, copy, attention, silu_mul --
+// so nibble's Transformer (src/model/transformer.cpp) runs on it unchanged.
 //
 // The paged fp16/bf16 fast path (fused append, split-K decode, tcgen05 prefill) is reached through handle()
 // and the nbl_* functions, with check() turning their statuses into nibble::Error.
@@ -42,7 +41,8 @@ class CudaBackend final : public Backend {
   CudaBackend& operator=(const CudaBackend&) = delete;
 
   bool supports(DType t) const override {
-    return t == DType::F32 || t == DType::F16 || t == DType::Q4_0 || t == DType::Q5_0 || t == DType::Q8_0;
+    return t == DType::F32 || t == DType::F16 || t == DType::Q4_0 || t == DType::Q5_0 || t == DType::Q8_0 ||
+           t == DType::Q5_1 || t == DType::Q4_K || t == DType::Q5_K || t == DType::Q6_K;
   }
   void reserve(const ReserveParams& rp) override;
   float* alloc(int64_t n_floats) override;

@@ -92,6 +92,18 @@ size_t qgemm_act_bytes(int64_t n, int64_t ne0);
 void launch_qgemm(cudaStream_t st, const Weight* const* ws, float* const* ys, int count, const float* x, int64_t n,
                   void* act, int num_sms, int* err);
 
+// quant_blocks.cu: Q5_1 (Q8_1 activations) and the k-quants Q4_K / Q5_K / Q6_K (Q8_K activations), weights kept
+// in their GGUF block layout. launch_qblock_matmul quantizes the n rows of x into `act` (qblock_act_bytes) and
+// runs the block dots.
+bool is_qblock(int32_t dtype);
+int64_t qblock_elems(int32_t dtype);  // elements per block: 32 or 256
+int64_t qblock_bytes(int32_t dtype);  // GGUF bytes per block
+size_t qblock_act_bytes(int32_t dtype, int64_t n, int64_t ne0);
+void launch_qblock_matmul(cudaStream_t st, const Weight& w, float* y, const float* x, int64_t n, void* act,
+                          int num_sms);
+void launch_embed_qblock(cudaStream_t st, const Weight& table, const int32_t* ids, int64_t n, float* out,
+                         int num_sms);
+
 void launch_rmsnorm(cudaStream_t st, const float* x, const float* w, float* y, int64_t n, int64_t d, float eps);
 void launch_add(cudaStream_t st, float* x, const float* y, int64_t count, int num_sms);
 void launch_silu_mul(cudaStream_t st, float* gate, const float* up, int64_t count, int num_sms);

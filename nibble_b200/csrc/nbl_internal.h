@@ -66,6 +66,8 @@ struct nbl_ctx {
   size_t fgemm_act_bytes = 0;
   void* qgemv_act = nullptr;  // activations quantized for the quantized GEMV (up to 8 rows)
   size_t qgemv_act_bytes = 0;
+  void* qblock_act = nullptr;  // activations quantized to Q8_1 / Q8_K for Q5_1 and k-quant weights
+  size_t qblock_act_bytes = 0;
 };
 
 struct nbl_kv {

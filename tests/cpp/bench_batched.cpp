@@ -2,7 +2,7 @@
 // model decoding together, against the reference's serving model of one Session per Model, whose throughput for N
 // users is one sequence's tg rate (nibble's Transformer decodes one token of one sequence per forward pass).
 //
-//   nbl_batched_bench [--shape tinyllama|qwen05] [--type F16|Q4_0|Q8_0|Q5_0|F32] [-p 128] [-n 64]
+//   nbl_batched_bench [--shape tinyllama|qwen05] [--type F16|F32|Q4_0|Q5_0|Q8_0|Q5_1|Q4_K|Q5_K|Q6_K] [-p 128] [-n 64]
 //                     [--seqs 1,8,32,64] [--out file.jsonl]
 //
 // For each N: N sequences are opened and each is prefilled with a P-token prompt (token i % n_vocab, shifted per
@@ -39,6 +39,10 @@ DType type_of(const std::string& name) {
   if (name == "Q4_0") return DType::Q4_0;
   if (name == "Q5_0") return DType::Q5_0;
   if (name == "Q8_0") return DType::Q8_0;
+  if (name == "Q5_1") return DType::Q5_1;
+  if (name == "Q4_K") return DType::Q4_K;
+  if (name == "Q5_K") return DType::Q5_K;
+  if (name == "Q6_K") return DType::Q6_K;
   throw Error("unknown --type '" + name + "'");
 }
 

@@ -5,7 +5,7 @@
 // min / max tokens per second -- on a random in-memory model of a named shape (no model file exists here, so the
 // loader and tokenizer are not involved; the prompt is token i % n_vocab as in the reference).
 //
-//   nbl_model_bench [--backend cuda|cpu] [--shape tinyllama|qwen05] [--type F16|F32|Q4_0|Q5_0|Q8_0] [-p 512]
+//   nbl_model_bench [--backend cuda|cpu] [--shape tinyllama|qwen05] [--type F16|F32|Q4_0|Q5_0|Q8_0|Q5_1|Q4_K|Q5_K|Q6_K] [-p 512]
 //                   [-n 128] [-r 5] [-t threads] [--out file.jsonl]
 //
 // Prints the reference's table and, with --out, appends its JSON line per test with a "backend" field added.
@@ -65,7 +65,11 @@ DType type_of(const std::string& name) {
   if (name == "Q4_0") return DType::Q4_0;
   if (name == "Q5_0") return DType::Q5_0;
   if (name == "Q8_0") return DType::Q8_0;
-  throw Error("unknown --type '" + name + "' (F32, F16, Q4_0, Q5_0, Q8_0)");
+  if (name == "Q5_1") return DType::Q5_1;
+  if (name == "Q4_K") return DType::Q4_K;
+  if (name == "Q5_K") return DType::Q5_K;
+  if (name == "Q6_K") return DType::Q6_K;
+  throw Error("unknown --type '" + name + "' (F32, F16, Q4_0, Q5_0, Q8_0, Q5_1, Q4_K, Q5_K, Q6_K)");
 }
 
 }  // namespace

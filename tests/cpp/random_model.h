@@ -1,7 +1,8 @@
 // A random decoder-only model held in memory: nibble's LlamaConfig and Weights (Tensor views into host vectors),
 // shaped like a qwen2 or llama GGUF model, for tests and measurements that run nibble's own Transformer without a
 // model file. Values: projections N(0, 1/in) (or quantized blocks of that spread), norms N(1, 0.1), biases
-// N(0, 0.5); F32, F16, Q4_0, Q5_0 or Q8_0 projection, embedding and output weights.
+// N(0, 0.5); F32, F16 or quantized (Q4_0, Q5_0, Q8_0, Q5_1, Q4_K, Q5_K, Q6_K) projection, embedding and output
+// weights.
 #pragma once
 #include <cmath>
 #include <cstdint>
@@ -20,7 +21,7 @@ namespace model = nibble::model;
 
 struct Shape {
   bool qwen;    // qwen2 (Q/K/V biases, NeoX rope, theta 1e6) or llama (interleaved rope, freq factors, theta 5e5)
-  DType wtype;  // projection, embedding and output weights: F32, F16, Q4_0, Q5_0 or Q8_0
+  DType wtype;  // projection, embedding and output weights: F32, F16 or a quantized type
   int64_t n_layers, n_embd, n_ff, n_heads, n_kv_heads, n_vocab;
 };
 
@@ -57,21 +58,38 @@ struct Rng {
   }
 };
 
-// Quantized blocks (GGUF layout, 32 elements each): uniformly random value bits and an fp16 scale that gives the
-// row about the same spread as a float matrix of N(0, 1/in).
+// Quantized blocks (GGUF layout; 32 elements each, 256 for the k-quants): uniformly random value bits (and packed
+// sub-block scales) with fp16 scales that give the row about the same spread as a float matrix of N(0, 1/in);
+// Q5_1's minimum and Q4_K / Q5_K's dmin put the block's mean near zero.
 inline Tensor quant_matrix(Model& m, Rng& rng, int64_t in, int64_t out, DType t) {
-  const int64_t bb = t == DType::Q4_0 ? 18 : t == DType::Q5_0 ? 22 : 34;
-  const float rms = t == DType::Q4_0 ? 4.6f : t == DType::Q5_0 ? 9.2f : 73.9f;  // of the block's integer values
+  const bool kq = t == DType::Q4_K || t == DType::Q5_K || t == DType::Q6_K;
+  const int64_t bb = t == DType::Q4_0 ? 18 : t == DType::Q5_0 ? 22 : t == DType::Q5_1 ? 24 : t == DType::Q8_0 ? 34
+                     : t == DType::Q4_K ? 144 : t == DType::Q5_K ? 176 : 210;
+  // rms of the block's integer values (k-quants: of sub-block scale x value)
+  const float rms = t == DType::Q4_0 ? 4.6f : t == DType::Q5_0 ? 9.2f : t == DType::Q5_1 ? 9.2f : t == DType::Q8_0 ? 73.9f
+                    : t == DType::Q4_K ? 160.f : t == DType::Q5_K ? 330.f : 1370.f;
   const float sd = 1.f / std::sqrt(static_cast<float>(in)) / rms;
-  const int64_t nb = in / 32 * out;
+  const int64_t nb = in / (kq ? 256 : 32) * out;
   std::vector<uint16_t> raw(static_cast<size_t>((nb * bb + 1) / 2));
   auto* bytes = reinterpret_cast<uint8_t*>(raw.data());
+  auto put = [](uint8_t* p, float v) {
+    const uint16_t h = nibble::fp32_to_fp16(v);
+    p[0] = static_cast<uint8_t>(h & 0xFF);
+    p[1] = static_cast<uint8_t>(h >> 8);
+  };
   for (int64_t b = 0; b < nb; ++b) {
     uint8_t* blk = bytes + b * bb;
-    const uint16_t d = nibble::fp32_to_fp16(sd * (0.5f + static_cast<float>(rng.next() & 0xFFFF) / 65536.f));
-    blk[0] = static_cast<uint8_t>(d & 0xFF);
-    blk[1] = static_cast<uint8_t>(d >> 8);
-    for (int64_t i = 2; i < bb; ++i) blk[i] = static_cast<uint8_t>(rng.next());
+    const float d = sd * (0.5f + static_cast<float>(rng.next() & 0xFFFF) / 65536.f);
+    const int64_t first = t == DType::Q6_K ? 0 : t == DType::Q5_1 || t == DType::Q4_K || t == DType::Q5_K ? 4 : 2;
+    for (int64_t i = first; i < bb; ++i) blk[i] = static_cast<uint8_t>(rng.next());
+    if (t == DType::Q6_K) {
+      put(blk + 208, d);
+    } else {
+      put(blk, d);
+      if (t == DType::Q5_1) put(blk + 2, -15.5f * d);
+      if (t == DType::Q4_K) put(blk + 2, 7.5f * d);
+      if (t == DType::Q5_K) put(blk + 2, 15.5f * d);
+    }
   }
   m.f16.push_back(std::move(raw));
   return view(t, 2, in, out, m.f16.back().data());

@@ -147,10 +147,11 @@ static void contracts(CudaBackend& be) {
     threw = true;
   }
   CHECK(threw);
-  // float and Q8_0-activation quantized weights run on the GPU; the others are refused at load time
+  // every weight type the reference supports runs on the GPU (src/tensor.h:21-31)
   CHECK(be.supports(nibble::DType::F32) && be.supports(nibble::DType::F16));
   CHECK(be.supports(nibble::DType::Q4_0) && be.supports(nibble::DType::Q5_0) && be.supports(nibble::DType::Q8_0));
-  CHECK(!be.supports(nibble::DType::Q5_1) && !be.supports(nibble::DType::Q4_K) && !be.supports(nibble::DType::Q6_K));
+  CHECK(be.supports(nibble::DType::Q5_1) && be.supports(nibble::DType::Q4_K) && be.supports(nibble::DType::Q5_K) &&
+        be.supports(nibble::DType::Q6_K));
   threw = false;
   try {
     be.attention(nullptr, nullptr, nullptr, nullptr, 1, 0, 6, 4, 16);
