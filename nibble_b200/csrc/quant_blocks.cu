@@ -19,9 +19,15 @@
 // Q5_1 gives each lane one 32-element block (dp4a on the 5-bit values) and adds the block terms to the row's sum
 // one block at a time, broadcast from the lane that holds it.
 //
-// Layouts: a weight stays in its GGUF block layout on the device (ne1 rows of ne0 / block-elements blocks). The
-// quantized activations of n rows are int8 values [n][ne0], the block scales as fp32 [n][blocks], and Q8_1's block
-// sums s as fp32 [n][blocks] or Q8_K's 16 sums per block as int32 [n][blocks][16].
+// Decode (n <= 8 activation rows) splits the two parts between the warps of a CTA: the integer dots of a CTA's
+// (weight row, super-block) items run on all its warps at once into shared memory, then one warp per weight row runs
+// the float chains over a chunk of super-blocks in order. More rows run one warp per (weight row, 4 activation rows).
+//
+// Layouts: a weight stays in its GGUF block layout on the device (ne1 rows of ne0 / block-elements blocks). Q8_1
+// activations of n rows are int8 values [n][ne0], scales fp32 [n][blocks] and sums s fp32 [n][blocks]. Q8_K
+// activations are stored lane-major, int8 [n][blocks][32 lanes][8] (lane i's bytes are elements i + 32 j), with the
+// scales fp32 [n][blocks] and the eight 32-element sub-block sums (bsums[2k] + bsums[2k + 1], the pair the dots use)
+// int32 [n][blocks][8].
 #include <algorithm>
 
 #include "model_ops.h"
@@ -81,7 +87,7 @@ __global__ void quantize_q8_1_kernel(const float* __restrict__ x, int64_t blocks
 }
 
 // Q8_K: lane i quantizes elements i + 32 j (j = 0..7) of 256-element block `blk`.
-__global__ void quantize_q8_K_kernel(const float* __restrict__ x, int64_t blocks, int8_t* __restrict__ qs,
+__global__ void quantize_q8_K_kernel(const float* __restrict__ x, int64_t blocks, uint2* __restrict__ qs,
                                      float* __restrict__ d, int* __restrict__ bsums) {
   const int lane = threadIdx.x & 31;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
@@ -127,13 +133,19 @@ __global__ void quantize_q8_K_kernel(const float* __restrict__ x, int64_t blocks
       dout = __fdiv_rn(1.f, iscale);
     }
     if (nan) dout = __int_as_float(0x7fc00000);
+    uint32_t lo = 0, hi = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      lo |= (static_cast<uint32_t>(q[j]) & 0xFFu) << (8 * j);
+      hi |= (static_cast<uint32_t>(q[j + 4]) & 0xFFu) << (8 * j);
+    }
+    qs[blk * 32 + lane] = make_uint2(lo, hi);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      qs[blk * 256 + lane + 32 * j] = static_cast<int8_t>(q[j]);
-      int g = q[j];  // group 2j (lanes 0-15) or 2j + 1 (lanes 16-31)
+      int g = q[j];  // sub-block j: element lane + 32 j of every lane
 #pragma unroll
-      for (int o = 8; o > 0; o >>= 1) g += __shfl_xor_sync(kFull, g, o);
-      if ((lane & 15) == 0) bsums[blk * 16 + 2 * j + (lane >> 4)] = g;
+      for (int o = 16; o > 0; o >>= 1) g += __shfl_xor_sync(kFull, g, o);
+      if (lane == j) bsums[blk * 8 + j] = g;
     }
     if (lane == 0) d[blk] = dout;
   }
@@ -158,10 +170,10 @@ struct KTraits<NBL_Q6_K> {
   static constexpr bool kMin = false;
 };
 
-// The values of elements lane + 32 j (j = 0..7) of a super-block, their sub-block scales (sub-block j for Q4_K /
-// Q5_K, 16-element sub-block 2 j + lane / 16 for Q6_K) and minimums.
+// The values of elements lane + 32 j (j = 0..7) of a super-block and their sub-block scales (sub-block j for Q4_K /
+// Q5_K, 16-element sub-block 2 j + lane / 16 for Q6_K).
 template <int DT>
-__device__ __forceinline__ void decode_k(const uint8_t* blk, int lane, int (&wq)[8], int (&sc)[8], int (&mn)[8]) {
+__device__ __forceinline__ void decode_k(const uint8_t* blk, int lane, int (&wq)[8], int (&sc)[8]) {
   if constexpr (DT == NBL_Q6_K) {
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
@@ -173,10 +185,7 @@ __device__ __forceinline__ void decode_k(const uint8_t* blk, int lane, int (&wq)
       wq[4 * h + 3] = ((ql1 >> 4) | (((qh >> 6) & 3) << 4)) - 32;
     }
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      sc[j] = static_cast<int8_t>(blk[192 + 2 * j + (lane >> 4)]);
-      mn[j] = 0;
-    }
+    for (int j = 0; j < 8; ++j) sc[j] = static_cast<int8_t>(blk[192 + 2 * j + (lane >> 4)]);
   } else {
     constexpr int kQs = DT == NBL_Q5_K ? 48 : 16;
     const int qh = DT == NBL_Q5_K ? blk[16 + lane] : 0;
@@ -187,20 +196,46 @@ __device__ __forceinline__ void decode_k(const uint8_t* blk, int lane, int (&wq)
       wq[2 * c + 1] = (byte >> 4) + (((qh >> (2 * c + 1)) & 1) << 4);
     }
 #pragma unroll
-    for (int j = 0; j < 8; ++j) scale_min_k4(j, blk + 4, sc[j], mn[j]);
+    for (int j = 0; j < 8; ++j) {
+      int m;
+      scale_min_k4(j, blk + 4, sc[j], m);
+    }
   }
+}
+
+// This lane's integer share of accumulator lane (lane % 8): sum_j sc[j] * (a * w) over its elements lane + 32 j,
+// then the lanes holding the same accumulator lane (lane, lane ^ 8, lane ^ 16, lane ^ 24) added together.
+__device__ __forceinline__ int kdot(const uint2 av, const int (&wq)[8], const int (&sc)[8]) {
+  int p = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int a = static_cast<int8_t>(((j < 4 ? av.x : av.y) >> (8 * (j & 3))) & 0xFFu);
+    p += sc[j] * (a * wq[j]);
+  }
+  p += __shfl_xor_sync(kFull, p, 8);
+  return p + __shfl_xor_sync(kFull, p, 16);
+}
+
+// The Q4_K / Q5_K min-term integer of one super-block: sum_k (bsums[2k] + bsums[2k + 1]) * m[k], lane k % 8 taking
+// term k and three shuffles adding them (every lane ends with the sum). `sums` points at the block's 8 pair sums.
+__device__ __forceinline__ int kmin_sum(const uint8_t* blk, const int* sums, int lane) {
+  int sck, mk;
+  scale_min_k4(lane & 7, blk + 4, sck, mk);
+  int v = sums[lane & 7] * mk;
+  v += __shfl_xor_sync(kFull, v, 1);
+  v += __shfl_xor_sync(kFull, v, 2);
+  return v + __shfl_xor_sync(kFull, v, 4);
 }
 
 // One warp per (weight row, up to kRowsPerWarp activation rows); CTAs of kWarps weight rows.
 template <int DT>
 __global__ void __launch_bounds__(kWarps * 32) kquant_matmul_kernel(
-    const uint8_t* __restrict__ w, int64_t ne1, int nb, const int8_t* __restrict__ aqs, const float* __restrict__ ad,
+    const uint8_t* __restrict__ w, int64_t ne1, int nb, const uint2* __restrict__ aqs, const float* __restrict__ ad,
     const int* __restrict__ asum, float* __restrict__ y, int64_t n) {
   using Tr = KTraits<DT>;
   const int lane = threadIdx.x & 31;
   const int64_t r = static_cast<int64_t>(blockIdx.x) * kWarps + (threadIdx.x >> 5);
   if (r >= ne1) return;  // the whole warp leaves together
-  const int64_t ne0 = static_cast<int64_t>(nb) * 256;
   const uint8_t* wrow = w + r * nb * Tr::kBytes;
   for (int64_t t0 = static_cast<int64_t>(blockIdx.y) * kRowsPerWarp; t0 < n;
        t0 += static_cast<int64_t>(gridDim.y) * kRowsPerWarp) {
@@ -210,27 +245,19 @@ __global__ void __launch_bounds__(kWarps * 32) kquant_matmul_kernel(
     for (int tt = 0; tt < kRowsPerWarp; ++tt) sums[tt] = tot[tt] = 0.f;
     for (int b = 0; b < nb; ++b) {
       const uint8_t* blk = wrow + static_cast<int64_t>(b) * Tr::kBytes;
-      int wq[8], sc[8], mn[8];
-      decode_k<DT>(blk, lane, wq, sc, mn);
+      int wq[8], sc[8];
+      decode_k<DT>(blk, lane, wq, sc);
       const float dw = f16_at(blk + (DT == NBL_Q6_K ? 208 : 0));
       const float dminw = Tr::kMin ? f16_at(blk + 2) : 0.f;
 #pragma unroll
       for (int tt = 0; tt < kRowsPerWarp; ++tt) {
         if (tt < nt) {
           const int64_t t = t0 + tt;
-          const int8_t* aq = aqs + t * ne0 + static_cast<int64_t>(b) * 256;
-          int p = 0;
-#pragma unroll
-          for (int j = 0; j < 8; ++j) p += sc[j] * (static_cast<int>(aq[lane + 32 * j]) * wq[j]);
-          p += __shfl_xor_sync(kFull, p, 8);
-          p += __shfl_xor_sync(kFull, p, 16);  // accumulator lane (lane % 8) of this super-block
+          const int p = kdot(aqs[(t * nb + b) * 32 + lane], wq, sc);  // accumulator lane (lane % 8)
           const float da = ad[t * nb + b];
           sums[tt] = __fadd_rn(sums[tt], __fmul_rn(__fmul_rn(dw, da), static_cast<float>(p)));
           if constexpr (Tr::kMin) {
-            const int* bs = asum + (t * nb + b) * 16;
-            int sumi = 0;
-#pragma unroll
-            for (int k = 0; k < 8; ++k) sumi += (bs[2 * k] + bs[2 * k + 1]) * mn[k];
+            const int sumi = kmin_sum(blk, asum + (t * nb + b) * 8, lane);
             tot[tt] = __fsub_rn(tot[tt], __fmul_rn(__fmul_rn(dminw, da), static_cast<float>(sumi)));
           }
         }
@@ -243,6 +270,74 @@ __global__ void __launch_bounds__(kWarps * 32) kquant_matmul_kernel(
 #pragma unroll
         for (int l = 0; l < 8; ++l) res = __fadd_rn(res, __shfl_sync(kFull, sums[tt], l));
         if (lane == 0) y[(t0 + tt) * ne1 + r] = res;
+      }
+    }
+  }
+}
+
+// Decode: CTAs of kWarps warps over `rows_per_cta` weight rows and all n <= kGemvMaxRows activation rows. Per chunk
+// of up to kChunk super-blocks, phase 1 spreads the (row, super-block) items over the warps and leaves each item's
+// eight accumulator-lane dots and min-term integer in shared memory; phase 2 has warp r carry row r's float chains
+// (lanes 0-7 the accumulator lanes, lane 8 the min-term total; one per activation row) through the chunk in order.
+constexpr int kChunk = 16;
+template <int DT>
+__global__ void __launch_bounds__(kWarps * 32) kquant_gemv_kernel(
+    const uint8_t* __restrict__ w, int64_t ne1, int nb, const uint2* __restrict__ aqs, const float* __restrict__ ad,
+    const int* __restrict__ asum, float* __restrict__ y, int n, int rows_per_cta) {
+  using Tr = KTraits<DT>;
+  extern __shared__ int part[];  // [n][rows_per_cta][kChunk][9]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rows_per_cta;
+  const int rows = ne1 - r0 < rows_per_cta ? static_cast<int>(ne1 - r0) : rows_per_cta;
+  float st[kGemvMaxRows];
+#pragma unroll
+  for (int t = 0; t < kGemvMaxRows; ++t) st[t] = 0.f;
+  for (int b0 = 0; b0 < nb; b0 += kChunk) {
+    const int cb = nb - b0 < kChunk ? nb - b0 : kChunk;
+    for (int it = warp; it < rows * cb; it += kWarps) {
+      const int r = it / cb, bb = it - r * cb;
+      const int64_t b = b0 + bb;
+      const uint8_t* blk = w + ((r0 + r) * nb + b) * Tr::kBytes;
+      int wq[8], sc[8];
+      decode_k<DT>(blk, lane, wq, sc);
+      for (int t = 0; t < n; ++t) {
+        const int p = kdot(aqs[(static_cast<int64_t>(t) * nb + b) * 32 + lane], wq, sc);
+        int* slot = part + ((t * rows_per_cta + r) * kChunk + bb) * 9;
+        if (lane < 8) slot[lane] = p;
+        if constexpr (Tr::kMin) {
+          const int sumi = kmin_sum(blk, asum + (static_cast<int64_t>(t) * nb + b) * 8, lane);
+          if (lane == 8) slot[8] = sumi;
+        }
+      }
+    }
+    __syncthreads();
+    if (warp < rows && lane < (Tr::kMin ? 9 : 8)) {
+      const uint8_t* wrow = w + (r0 + warp) * nb * Tr::kBytes;
+#pragma unroll
+      for (int t = 0; t < kGemvMaxRows; ++t) {
+        if (t < n) {
+          for (int bb = 0; bb < cb; ++bb) {
+            const uint8_t* blk = wrow + static_cast<int64_t>(b0 + bb) * Tr::kBytes;
+            const float da = ad[static_cast<int64_t>(t) * nb + b0 + bb];
+            const float v = static_cast<float>(part[((t * rows_per_cta + warp) * kChunk + bb) * 9 + lane]);
+            if (lane < 8)
+              st[t] = __fadd_rn(st[t], __fmul_rn(__fmul_rn(f16_at(blk + (DT == NBL_Q6_K ? 208 : 0)), da), v));
+            else
+              st[t] = __fsub_rn(st[t], __fmul_rn(__fmul_rn(f16_at(blk + 2), da), v));
+          }
+        }
+      }
+    }
+    __syncthreads();
+  }
+  if (warp < rows) {
+#pragma unroll
+    for (int t = 0; t < kGemvMaxRows; ++t) {
+      if (t < n) {
+        float res = Tr::kMin ? __shfl_sync(kFull, st[t], 8) : 0.f;
+#pragma unroll
+        for (int l = 0; l < 8; ++l) res = __fadd_rn(res, __shfl_sync(kFull, st[t], l));
+        if (lane == 0) y[static_cast<int64_t>(t) * ne1 + r0 + warp] = res;
       }
     }
   }
@@ -364,42 +459,56 @@ int64_t qblock_bytes(int32_t dtype) {
 size_t qblock_act_bytes(int32_t dtype, int64_t n, int64_t ne0) {
   const int64_t nb = ne0 / qblock_elems(dtype);
   return align256(static_cast<size_t>(n * ne0)) + align256(static_cast<size_t>(n * nb) * sizeof(float)) +
-         static_cast<size_t>(n * nb) * (dtype == NBL_Q5_1 ? sizeof(float) : 16 * sizeof(int));
+         static_cast<size_t>(n * nb) * (dtype == NBL_Q5_1 ? sizeof(float) : 8 * sizeof(int));
 }
 
 void launch_qblock_matmul(cudaStream_t st, const Weight& w, float* y, const float* x, int64_t n, void* act,
                           int num_sms) {
   const int64_t nb = w.ne0 / qblock_elems(w.dtype), blocks = n * nb;
   auto* base = static_cast<uint8_t*>(act);
-  auto* qs = reinterpret_cast<int8_t*>(base);
   auto* d = reinterpret_cast<float*>(base + align256(static_cast<size_t>(n * w.ne0)));
   void* extra = reinterpret_cast<uint8_t*>(d) + align256(static_cast<size_t>(blocks) * sizeof(float));
   const unsigned qgrid =
       static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>((blocks + 7) / 8, int64_t(num_sms) * 16)));
-  if (w.dtype == NBL_Q5_1)
-    quantize_q8_1_kernel<<<qgrid, 256, 0, st>>>(x, blocks, qs, d, static_cast<float*>(extra));
-  else
-    quantize_q8_K_kernel<<<qgrid, 256, 0, st>>>(x, blocks, qs, d, static_cast<int*>(extra));
-  const dim3 grid(static_cast<unsigned>((w.ne1 + kWarps - 1) / kWarps),
-                  static_cast<unsigned>(std::min<int64_t>((n + kRowsPerWarp - 1) / kRowsPerWarp, 65535)));
   const auto* wb = static_cast<const uint8_t*>(w.dev);
   const int inb = static_cast<int>(nb);
+  if (w.dtype == NBL_Q5_1) {
+    auto* qs = reinterpret_cast<int8_t*>(base);
+    quantize_q8_1_kernel<<<qgrid, 256, 0, st>>>(x, blocks, qs, d, static_cast<float*>(extra));
+    const dim3 grid(static_cast<unsigned>((w.ne1 + kWarps - 1) / kWarps),
+                    static_cast<unsigned>(std::min<int64_t>((n + kRowsPerWarp - 1) / kRowsPerWarp, 65535)));
+    q5_1_matmul_kernel<<<grid, kWarps * 32, 0, st>>>(wb, w.ne1, inb, qs, d, static_cast<const float*>(extra), y, n);
+    return;
+  }
+  auto* qs = reinterpret_cast<uint2*>(base);
+  const auto* sums = static_cast<const int*>(extra);
+  quantize_q8_K_kernel<<<qgrid, 256, 0, st>>>(x, blocks, qs, d, static_cast<int*>(extra));
+  if (n <= kGemvMaxRows) {
+    // weight rows per CTA: the most of 8, 4, 2 that still gives every SM four CTAs, else 1
+    int per = 8;
+    while (per > 1 && (w.ne1 + per - 1) / per < 4LL * num_sms) per >>= 1;
+    const unsigned grid = static_cast<unsigned>((w.ne1 + per - 1) / per);
+    const size_t smem = static_cast<size_t>(n) * per * kChunk * 9 * sizeof(int);
+    const int in = static_cast<int>(n);
+    switch (w.dtype) {
+      case NBL_Q4_K:
+        kquant_gemv_kernel<NBL_Q4_K><<<grid, kWarps * 32, smem, st>>>(wb, w.ne1, inb, qs, d, sums, y, in, per);
+        break;
+      case NBL_Q5_K:
+        kquant_gemv_kernel<NBL_Q5_K><<<grid, kWarps * 32, smem, st>>>(wb, w.ne1, inb, qs, d, sums, y, in, per);
+        break;
+      default:
+        kquant_gemv_kernel<NBL_Q6_K><<<grid, kWarps * 32, smem, st>>>(wb, w.ne1, inb, qs, d, sums, y, in, per);
+        break;
+    }
+    return;
+  }
+  const dim3 grid(static_cast<unsigned>((w.ne1 + kWarps - 1) / kWarps),
+                  static_cast<unsigned>(std::min<int64_t>((n + kRowsPerWarp - 1) / kRowsPerWarp, 65535)));
   switch (w.dtype) {
-    case NBL_Q5_1:
-      q5_1_matmul_kernel<<<grid, kWarps * 32, 0, st>>>(wb, w.ne1, inb, qs, d, static_cast<const float*>(extra), y, n);
-      break;
-    case NBL_Q4_K:
-      kquant_matmul_kernel<NBL_Q4_K>
-          <<<grid, kWarps * 32, 0, st>>>(wb, w.ne1, inb, qs, d, static_cast<const int*>(extra), y, n);
-      break;
-    case NBL_Q5_K:
-      kquant_matmul_kernel<NBL_Q5_K>
-          <<<grid, kWarps * 32, 0, st>>>(wb, w.ne1, inb, qs, d, static_cast<const int*>(extra), y, n);
-      break;
-    default:
-      kquant_matmul_kernel<NBL_Q6_K>
-          <<<grid, kWarps * 32, 0, st>>>(wb, w.ne1, inb, qs, d, static_cast<const int*>(extra), y, n);
-      break;
+    case NBL_Q4_K: kquant_matmul_kernel<NBL_Q4_K><<<grid, kWarps * 32, 0, st>>>(wb, w.ne1, inb, qs, d, sums, y, n); break;
+    case NBL_Q5_K: kquant_matmul_kernel<NBL_Q5_K><<<grid, kWarps * 32, 0, st>>>(wb, w.ne1, inb, qs, d, sums, y, n); break;
+    default: kquant_matmul_kernel<NBL_Q6_K><<<grid, kWarps * 32, 0, st>>>(wb, w.ne1, inb, qs, d, sums, y, n); break;
   }
 }
 
