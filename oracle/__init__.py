@@ -38,15 +38,16 @@ MODEL_CHECK = os.path.join(HERE, "_ref", "nbl_model_check")
 MODEL_BENCH = os.path.join(HERE, "_ref", "nbl_model_bench")
 BATCHED_CHECK = os.path.join(HERE, "_ref", "nbl_batched_check")
 BATCHED_BENCH = os.path.join(HERE, "_ref", "nbl_batched_bench")
+GOLDEN_CHECK = os.path.join(HERE, "_ref", "nbl_golden_check")
 
 
 def build(with_ref: bool | None = None) -> None:
     """Compiles liboracle.so, and oracle/_ref when the reference tree is present (or with_ref is True): nibble's own
-    code, and -- once nibble_b200/libnibble_cuda.so exists -- the Transformer drop-in check and bench binaries and the
-    multi-sequence decoder's check and bench."""
+    code, the golden-vector check of the quantized arithmetic, and -- once nibble_b200/libnibble_cuda.so exists -- the
+    Transformer drop-in check and bench binaries and the multi-sequence decoder's check and bench."""
     targets = ["oracle"]
     if with_ref or (with_ref is None and os.path.isdir(os.path.join(REF_TREE, "src"))):
-        targets.append("ref")
+        targets += ["ref", "golden-check"]
         if os.path.exists(os.path.join(os.path.dirname(HERE), "nibble_b200", "libnibble_cuda.so")):
             targets += ["model-check", "model-bench", "batched-check", "batched-bench"]
     subprocess.run(["make", "-s", "-C", HERE, f"REF={REF_TREE}", "-j8", *targets], check=True)

@@ -324,6 +324,38 @@ int orc_dequantize_row(int dtype, const void* src, float* dst, int64_t n) {
   return 0;
 }
 
+/* One weight row of nb Q4_0 / Q5_0 / Q8_0 blocks against nb Q8_0 activation blocks (src/quant.cpp:310-366). */
+static float orc_dot_q8_0_family(int dtype, const uint8_t* wr, const uint8_t* xa, int64_t nb, int64_t bb) {
+  float sum = 0.f;
+  for (int64_t b = 0; b < nb; ++b) {
+    const uint8_t* bw = wr + b * bb;
+    const uint8_t* ba = xa + b * 34;
+    const int8_t* aq = (const int8_t*)(ba + 2);
+    const float dw = orc_fp16_to_fp32(orc_rd16(bw)), da = orc_fp16_to_fp32(orc_rd16(ba));
+    if (dtype == 8) {
+      int s = 0;
+      for (int j = 0; j < 32; ++j) s += (int8_t)bw[2 + j] * aq[j];
+      sum += (float)s * (dw * da);
+    } else if (dtype == 2) {
+      int s0 = 0, s1 = 0;
+      for (int j = 0; j < 16; ++j) {
+        s0 += ((bw[2 + j] & 0x0F) - 8) * aq[j];
+        s1 += ((bw[2 + j] >> 4) - 8) * aq[j + 16];
+      }
+      sum += (float)(s0 + s1) * dw * da;
+    } else {
+      const uint32_t qh = (uint32_t)bw[2] | ((uint32_t)bw[3] << 8) | ((uint32_t)bw[4] << 16) | ((uint32_t)bw[5] << 24);
+      int s0 = 0, s1 = 0;
+      for (int j = 0; j < 16; ++j) {
+        s0 += (((bw[6 + j] & 0x0F) | (((qh >> j) << 4) & 0x10)) - 16) * aq[j];
+        s1 += (((bw[6 + j] >> 4) | ((qh >> (j + 12)) & 0x10)) - 16) * aq[j + 16];
+      }
+      sum += (dw * da) * (float)(s0 + s1);
+    }
+  }
+  return sum;
+}
+
 int orc_matmul_q(const void* w, int dtype, int64_t ne0, int64_t ne1, const float* x, float* y, int64_t n) {
   const int64_t bb = orc_block_bytes(dtype), nb = ne0 / 32;
   if (!bb) return orc_matmul_q_ext((const uint8_t*)w, dtype, ne0, ne1, x, y, n);
@@ -331,37 +363,7 @@ int orc_matmul_q(const void* w, int dtype, int64_t ne0, int64_t ne1, const float
   if (!xa) return -1;
   for (int64_t t = 0; t < n; ++t) {
     orc_quantize_q8_0(x + t * ne0, xa, ne0);
-    for (int64_t r = 0; r < ne1; ++r) {
-      const uint8_t* wr = (const uint8_t*)w + r * nb * bb;
-      float sum = 0.f;
-      for (int64_t b = 0; b < nb; ++b) {
-        const uint8_t* bw = wr + b * bb;
-        const uint8_t* ba = xa + b * 34;
-        const int8_t* aq = (const int8_t*)(ba + 2);
-        const float dw = orc_fp16_to_fp32(orc_rd16(bw)), da = orc_fp16_to_fp32(orc_rd16(ba));
-        if (dtype == 8) {
-          int s = 0;
-          for (int j = 0; j < 32; ++j) s += (int8_t)bw[2 + j] * aq[j];
-          sum += (float)s * (dw * da);
-        } else if (dtype == 2) {
-          int s0 = 0, s1 = 0;
-          for (int j = 0; j < 16; ++j) {
-            s0 += ((bw[2 + j] & 0x0F) - 8) * aq[j];
-            s1 += ((bw[2 + j] >> 4) - 8) * aq[j + 16];
-          }
-          sum += (float)(s0 + s1) * dw * da;
-        } else {
-          const uint32_t qh = (uint32_t)bw[2] | ((uint32_t)bw[3] << 8) | ((uint32_t)bw[4] << 16) | ((uint32_t)bw[5] << 24);
-          int s0 = 0, s1 = 0;
-          for (int j = 0; j < 16; ++j) {
-            s0 += (((bw[6 + j] & 0x0F) | (((qh >> j) << 4) & 0x10)) - 16) * aq[j];
-            s1 += (((bw[6 + j] >> 4) | ((qh >> (j + 12)) & 0x10)) - 16) * aq[j + 16];
-          }
-          sum += (dw * da) * (float)(s0 + s1);
-        }
-      }
-      y[t * ne1 + r] = sum;
-    }
+    for (int64_t r = 0; r < ne1; ++r) y[t * ne1 + r] = orc_dot_q8_0_family(dtype, (const uint8_t*)w + r * nb * bb, xa, nb, bb);
   }
   free(xa);
   return 0;
@@ -530,6 +532,60 @@ void orc_quantize_q8_K(const float* x, uint8_t* blocks, int64_t n) {
  * and the k-quants (src/quant.cpp:117-146 and :399-418): per super-block eight int32 lanes (element e feeds lane
  * e % 8, each product scaled by its sub-block's scale), sums[l] += (d_w * d_a) * lane[l]; Q4_K / Q5_K also subtract
  * (dmin_w * d_a) * sum_k(bsum_k * m_k) from the running total; the eight lane sums are added to the total last. */
+/* One weight row of nb Q5_1 blocks against Q8_1 ones, or of nb k-quant super-blocks against Q8_K ones. */
+static float orc_dot_ext(int dtype, const uint8_t* wr, const uint8_t* xa, int64_t nb) {
+  const int64_t bb = orc_ext_block_bytes(dtype);
+  const int kq = dtype != 7;
+  const int64_t ab = kq ? 292 : 36;
+  float sum = 0.f, sums[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  for (int64_t b = 0; b < nb; ++b) {
+    const uint8_t* bw = wr + b * bb;
+    const uint8_t* ba = xa + b * ab;
+    if (!kq) {
+      const int8_t* aq = (const int8_t*)(ba + 4);
+      const uint32_t qh = (uint32_t)bw[4] | ((uint32_t)bw[5] << 8) | ((uint32_t)bw[6] << 16) | ((uint32_t)bw[7] << 24);
+      int s0 = 0, s1 = 0;
+      for (int j = 0; j < 16; ++j) {
+        s0 += ((bw[8 + j] & 0x0F) | (((qh >> j) << 4) & 0x10)) * aq[j];
+        s1 += ((bw[8 + j] >> 4) | ((qh >> (j + 12)) & 0x10)) * aq[j + 16];
+      }
+      const float dw = orc_fp16_to_fp32(orc_rd16(bw)), mw = orc_fp16_to_fp32(orc_rd16(bw + 2));
+      const float da = orc_fp16_to_fp32(orc_rd16(ba)), sa = orc_fp16_to_fp32(orc_rd16(ba + 2));
+      sum += (dw * da) * (float)(s0 + s1) + mw * sa;
+      continue;
+    }
+    float da;
+    memcpy(&da, ba, 4);
+    const int8_t* aq = (const int8_t*)(ba + 4);
+    int8_t a[256];
+    orc_expand_k(dtype, bw, a);
+    int lane[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (dtype == 14) {
+      for (int e = 0; e < 256; ++e) lane[e & 7] += (int8_t)bw[192 + e / 16] * (aq[e] * a[e]);
+      const float d = orc_fp16_to_fp32(orc_rd16(bw + 208)) * da;
+      for (int l = 0; l < 8; ++l) sums[l] += d * (float)lane[l];
+    } else {
+      int sumi = 0;
+      for (int k = 0; k < 8; ++k) {
+        int sc, m;
+        int16_t b0, b1;
+        orc_scale_min_k4(k, bw + 4, &sc, &m);
+        memcpy(&b0, ba + 260 + 4 * k, 2);
+        memcpy(&b1, ba + 262 + 4 * k, 2);
+        sumi += (b0 + b1) * m;
+        for (int e = 0; e < 32; ++e) lane[e & 7] += sc * (aq[32 * k + e] * a[32 * k + e]);
+      }
+      const float d = orc_fp16_to_fp32(orc_rd16(bw)) * da;
+      for (int l = 0; l < 8; ++l) sums[l] += d * (float)lane[l];
+      const float dmin = orc_fp16_to_fp32(orc_rd16(bw + 2)) * da;
+      sum -= dmin * (float)sumi;
+    }
+  }
+  if (kq)
+    for (int l = 0; l < 8; ++l) sum += sums[l];
+  return sum;
+}
+
 static int orc_matmul_q_ext(const uint8_t* w, int dtype, int64_t ne0, int64_t ne1, const float* x, float* y,
                             int64_t n) {
   const int64_t bb = orc_ext_block_bytes(dtype);
@@ -541,57 +597,15 @@ static int orc_matmul_q_ext(const uint8_t* w, int dtype, int64_t ne0, int64_t ne
   for (int64_t t = 0; t < n; ++t) {
     if (kq) orc_quantize_q8_K(x + t * ne0, xa, ne0);
     else orc_quantize_q8_1(x + t * ne0, xa, ne0);
-    for (int64_t r = 0; r < ne1; ++r) {
-      const uint8_t* wr = w + r * nb * bb;
-      float sum = 0.f, sums[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      for (int64_t b = 0; b < nb; ++b) {
-        const uint8_t* bw = wr + b * bb;
-        const uint8_t* ba = xa + b * ab;
-        if (!kq) {
-          const int8_t* aq = (const int8_t*)(ba + 4);
-          const uint32_t qh = (uint32_t)bw[4] | ((uint32_t)bw[5] << 8) | ((uint32_t)bw[6] << 16) | ((uint32_t)bw[7] << 24);
-          int s0 = 0, s1 = 0;
-          for (int j = 0; j < 16; ++j) {
-            s0 += ((bw[8 + j] & 0x0F) | (((qh >> j) << 4) & 0x10)) * aq[j];
-            s1 += ((bw[8 + j] >> 4) | ((qh >> (j + 12)) & 0x10)) * aq[j + 16];
-          }
-          const float dw = orc_fp16_to_fp32(orc_rd16(bw)), mw = orc_fp16_to_fp32(orc_rd16(bw + 2));
-          const float da = orc_fp16_to_fp32(orc_rd16(ba)), sa = orc_fp16_to_fp32(orc_rd16(ba + 2));
-          sum += (dw * da) * (float)(s0 + s1) + mw * sa;
-          continue;
-        }
-        float da;
-        memcpy(&da, ba, 4);
-        const int8_t* aq = (const int8_t*)(ba + 4);
-        int8_t a[256];
-        orc_expand_k(dtype, bw, a);
-        int lane[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-        if (dtype == 14) {
-          for (int e = 0; e < 256; ++e) lane[e & 7] += (int8_t)bw[192 + e / 16] * (aq[e] * a[e]);
-          const float d = orc_fp16_to_fp32(orc_rd16(bw + 208)) * da;
-          for (int l = 0; l < 8; ++l) sums[l] += d * (float)lane[l];
-        } else {
-          int sumi = 0;
-          for (int k = 0; k < 8; ++k) {
-            int sc, m;
-            int16_t b0, b1;
-            orc_scale_min_k4(k, bw + 4, &sc, &m);
-            memcpy(&b0, ba + 260 + 4 * k, 2);
-            memcpy(&b1, ba + 262 + 4 * k, 2);
-            sumi += (b0 + b1) * m;
-            for (int e = 0; e < 32; ++e) lane[e & 7] += sc * (aq[32 * k + e] * a[32 * k + e]);
-          }
-          const float d = orc_fp16_to_fp32(orc_rd16(bw)) * da;
-          for (int l = 0; l < 8; ++l) sums[l] += d * (float)lane[l];
-          const float dmin = orc_fp16_to_fp32(orc_rd16(bw + 2)) * da;
-          sum -= dmin * (float)sumi;
-        }
-      }
-      if (kq)
-        for (int l = 0; l < 8; ++l) sum += sums[l];
-      y[t * ne1 + r] = sum;
-    }
+    for (int64_t r = 0; r < ne1; ++r) y[t * ne1 + r] = orc_dot_ext(dtype, w + r * nb * bb, xa, nb);
   }
   free(xa);
   return 0;
+}
+
+float orc_vec_dot(int dtype, const void* w, const void* act, int64_t n_blocks) {
+  const int64_t bb = orc_block_bytes(dtype);
+  if (bb) return orc_dot_q8_0_family(dtype, (const uint8_t*)w, (const uint8_t*)act, n_blocks, bb);
+  if (orc_ext_block_bytes(dtype)) return orc_dot_ext(dtype, (const uint8_t*)w, (const uint8_t*)act, n_blocks);
+  return NAN;
 }

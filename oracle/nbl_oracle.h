@@ -97,6 +97,10 @@ int orc_dequantize_row(int dtype, const void* src, float* dst, int64_t n);
  * the row's sum in block order; Q5_1 against Q8_1 activations and the k-quants against Q8_K ones in the order of
  * src/quant.cpp:117-146, :371-418. Returns -1 for an unsupported dtype. */
 int orc_matmul_q(const void* w, int dtype, int64_t ne0, int64_t ne1, const float* x, float* y, int64_t n);
+/* The block dot of one weight row (n_blocks blocks of dtype) with activation blocks already in the companion format
+ * (Q8_0 for Q4_0/Q5_0/Q8_0, Q8_1 for Q5_1, Q8_K for the k-quants): nibble's dot_*_q8_* (src/quant.cpp:117-146,
+ * :310-418). NaN for another dtype. */
+float orc_vec_dot(int dtype, const void* w, const void* act, int64_t n_blocks);
 
 #ifdef __cplusplus
 }

@@ -307,3 +307,15 @@ def test_block_quant_oracle_bit_identical_to_reference(dtype):
     finally:
         be.close()
     assert np.array_equal(yb.view(np.uint32), yr.view(np.uint32))
+
+
+def test_quant_oracle_matches_reference_golden_vectors():
+    """The oracle's Q8_0 / Q8_1 / Q8_K quantizers, every block dot and every dequantization against the golden
+    vectors nibble ships (llama.cpp's outputs on inputs regenerated by nibble's own generators and checked by hash):
+    oracle/golden_quant.cpp, built from the reference tree where it is present."""
+    import subprocess
+    if not os.path.exists(oracle.GOLDEN_CHECK):
+        pytest.skip("oracle/_ref/nbl_golden_check is built only where the reference tree is present")
+    r = subprocess.run([oracle.GOLDEN_CHECK], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "golden checks passed" in r.stdout
