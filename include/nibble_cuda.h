@@ -150,8 +150,8 @@ NBL_API int nbl_attention(nbl_ctx* ctx, const float* q, const float* k, const fl
 NBL_API int nbl_weight_create(nbl_ctx* ctx, const void* host, int32_t dtype, int64_t ne0, int64_t ne1,
                               nbl_weight** out);
 NBL_API int nbl_weight_destroy(nbl_weight* w);
-/* The uploaded tensor: device address of its elements (F32/F16: in its own dtype; quantized: the internal
- * layout), dtype and shape. Any out pointer may be NULL. An F32 vector's address is what nbl_add_bias takes. */
+/* The uploaded tensor: device address of its elements (F32/F16: in its own dtype; Q4_0/Q5_0/Q8_0: the internal
+ * layout; Q5_1 and the k-quants: the GGUF blocks as uploaded), dtype and shape. Any out pointer may be NULL. An F32 vector's address is what nbl_add_bias takes. */
 NBL_API int nbl_weight_data(const nbl_weight* w, const void** dev, int32_t* dtype, int64_t* ne0, int64_t* ne1);
 /* Backend::embed (backend.h:54-55; cpu::embed ref_ops.cpp:80-98): out[t, :] = row ids[t] of table, widened to
  * fp32 (bit-identical). ids is HOST memory (a std::span in the reference); an id outside [0, ne1) is
