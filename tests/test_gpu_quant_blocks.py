@@ -65,11 +65,12 @@ def test_block_quant_matmul_bit_exact(nbl_ctx, name, n):
 
 @pytest.mark.parametrize("name", sorted(TYPES))
 def test_block_quant_matmul_many_rows(nbl_ctx, name):
-    """A prefill-sized call (300 activation rows) and a wide output (20,000 weight rows)."""
+    """A prefill-sized call (300 activation rows) and decode-sized ones whose weight row counts give the decode
+    kernel 8 (20,000 rows), 4 (4,000) and 2 (2,048) weight rows per CTA."""
     import torch
     odt, cdt = TYPES[name]
     rng = np.random.default_rng(200 + cdt)
-    for ne1, ne0, n in [(96, 512, 300), (20000, 256, 2)]:
+    for ne1, ne0, n in [(96, 512, 300), (20000, 256, 2), (4000, 512, 8), (2048, 256, 1)]:
         w = oracle.random_q_blocks(rng, odt, ne1, ne0)
         x = _acts(rng, n, ne0)
         wt = nbl_ctx.weight(w, cdt, ne0)
