@@ -88,6 +88,8 @@ def _load_oracle():
     lib.orc_dequantize_row.restype = C.c_int
     lib.orc_matmul_q.argtypes = [C.c_void_p, C.c_int, _i64, _i64, _f32p, _f32p, _i64]
     lib.orc_matmul_q.restype = C.c_int
+    lib.orc_vec_dot.argtypes = [C.c_int, C.c_void_p, C.c_void_p, _i64]
+    lib.orc_vec_dot.restype = C.c_float
     _lib = lib
     return lib
 
@@ -334,6 +336,14 @@ def matmul_q(blocks, dtype, ne0, ne1, x, n) -> np.ndarray:
     if _load_oracle().orc_matmul_q(b.ctypes.data, dtype, ne0, ne1, _c(x), y, n) != 0:
         raise ValueError("dtype")
     return y
+
+
+def vec_dot(dtype, w_row, act_blocks, n_blocks) -> np.float32:
+    """One weight row's block dot with activation blocks already quantized (Q8_0 / Q8_1 / Q8_K bytes): nibble's
+    dot_*_q8_* (src/quant.cpp:117-146, :310-418)."""
+    w = np.ascontiguousarray(w_row, dtype=np.uint8)
+    a = np.ascontiguousarray(act_blocks, dtype=np.uint8)
+    return np.float32(_load_oracle().orc_vec_dot(dtype, w.ctypes.data, a.ctypes.data, n_blocks))
 
 
 def random_q_blocks(rng, dtype, ne1, ne0, scale=0.02) -> np.ndarray:
