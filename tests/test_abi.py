@@ -74,3 +74,21 @@ def test_python_wrapper_raises_nibble_error():
     import nibble_b200 as nb
     with pytest.raises(nb.NibbleError):
         nb.Context(0, use_torch_stream=False)
+
+
+def test_dtype_codes_match_header():
+    """The Python binding's element-type codes are the header's nbl_dtype values, and the quantized ones map to
+    nibble's DType ids the oracle uses (src/tensor.h:21-31) in the same order the CudaBackend maps them."""
+    from nibble_b200 import _abi
+    import oracle
+    with open(HEADER) as f:
+        text = f.read()
+    enum = dict((k, int(v)) for k, v in re.findall(r"\bNBL_(F32|F16|BF16|Q\d_[0-9K])\s*=\s*(\d+)", text))
+    assert set(enum) == {"F32", "F16", "BF16", "Q4_0", "Q5_0", "Q8_0", "Q5_1", "Q4_K", "Q5_K", "Q6_K"}
+    for name, code in enum.items():
+        assert getattr(_abi, name) == code, name
+    with open(os.path.join(ROOT, "nibble_b200", "csrc", "host", "cuda_backend.cpp")) as f:
+        mapped = dict(re.findall(r"case DType::(\w+): dt = NBL_(\w+);", f.read()))
+    assert mapped == {n: n for n in ("F32", "F16", "Q4_0", "Q5_0", "Q8_0", "Q5_1", "Q4_K", "Q5_K", "Q6_K")}
+    for name in ("Q4_0", "Q5_0", "Q5_1", "Q8_0", "Q4_K", "Q5_K", "Q6_K"):
+        assert getattr(oracle, name) in oracle.BLOCK_BYTES
