@@ -319,3 +319,34 @@ def test_quant_oracle_matches_reference_golden_vectors():
     r = subprocess.run([oracle.GOLDEN_CHECK], capture_output=True, text=True, timeout=120)
     assert r.returncode == 0, r.stdout + r.stderr
     assert "golden checks passed" in r.stdout
+
+
+def test_activation_quantizers_on_hostile_rows_bit_identical_to_reference():
+    """Rows a corrupt or overflowing model can produce -- +-Inf, NaN, a subnormal largest magnitude (an infinite
+    inverse scale), values near the float maximum -- quantize to the same bytes as nibble's own Q8_0 / Q8_1 / Q8_K
+    quantizers (src/quant.cpp:37-51, :250-307 define every one of these cases)."""
+    if not oracle.have_ref():
+        pytest.skip("oracle/_ref (nibble's own code) is not built here")
+    rng = np.random.default_rng(23)
+    rows = []
+    for fill in ("inf", "ninf", "nan", "subnormal", "huge", "mixed"):
+        x = (rng.standard_normal(256) * 3).astype(np.float32)
+        if fill == "inf":
+            x[17] = np.inf
+        elif fill == "ninf":
+            x[200] = -np.inf
+        elif fill == "nan":
+            x[5] = np.nan
+        elif fill == "subnormal":
+            x = (rng.standard_normal(256) * 1e-42).astype(np.float32)
+        elif fill == "huge":
+            x = (np.clip(rng.standard_normal(256), -3.0, 3.0) * 1e38).astype(np.float32)
+        else:
+            x[::7] = 0.0
+            x[3], x[4] = np.inf, np.nan
+        rows.append(x)
+    x = np.concatenate(rows)
+    with np.errstate(all="ignore"):
+        assert np.array_equal(oracle.quantize_q8_0(x), oracle.ref_quantize_q8_0(x))
+        assert np.array_equal(oracle.quantize_q8_1(x), oracle.ref_quantize_q8_1(x))
+        assert np.array_equal(oracle.quantize_q8_K(x), oracle.ref_quantize_q8_K(x))
