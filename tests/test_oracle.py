@@ -350,3 +350,99 @@ def test_activation_quantizers_on_hostile_rows_bit_identical_to_reference():
         assert np.array_equal(oracle.quantize_q8_0(x), oracle.ref_quantize_q8_0(x))
         assert np.array_equal(oracle.quantize_q8_1(x), oracle.ref_quantize_q8_1(x))
         assert np.array_equal(oracle.quantize_q8_K(x), oracle.ref_quantize_q8_K(x))
+
+
+# ---------------------------------------------------------------- known answers for Q5_1 / Q8_1 / Q8_K / k-quants
+# Hand-built blocks whose values follow from the formats (src/quant.h:50-99); the cases restate the reference's own
+# known-answer tests (tests/test_quant.cpp:286-327, :466-496, :612-655) with the expected values derived here.
+def _f16(v):
+    return int(oracle.f32_to_fp16_bits(np.array([v], np.float32))[0])
+
+
+def _put16(blk, off, v):
+    h = _f16(v)
+    blk[off], blk[off + 1] = h & 0xFF, h >> 8
+
+
+def test_q5_1_known_answer():
+    blk = np.zeros(24, np.uint8)
+    _put16(blk, 0, 0.5)    # d
+    _put16(blk, 2, -1.0)   # m
+    blk[4 + 2] = 0x01      # qh bit 16: element 16's fifth bit
+    blk[8] = 0x10          # qs[0]: element 0 = 0, element 16 = 1
+    y = oracle.dequantize_rows(blk, oracle.Q5_1, 32, 1)[0]
+    assert y[0] == -1.0            # 0 * 0.5 - 1
+    assert y[16] == 7.5            # (1 + 16) * 0.5 - 1
+    assert y[17] == -1.0
+
+
+def test_q8_1_known_answer():
+    blk = oracle.quantize_q8_1(np.full(32, 127.0, np.float32))
+    h = blk[:4].view(np.uint16)
+    assert h[0] == _f16(1.0)        # d = 127 / 127
+    assert h[1] == _f16(4064.0)     # s = 32 * 127 * d
+    assert np.all(blk[4:].view(np.int8) == 127)
+    assert not oracle.quantize_q8_1(np.zeros(32, np.float32)).any()
+
+
+def test_q8_K_known_answer():
+    x = np.zeros(256, np.float32)
+    x[:4] = [-127.0, 2.5, 3.5, -2.5]
+    blk = oracle.quantize_q8_K(x)
+    q = blk[4:260].view(np.int8)
+    assert blk[:4].view(np.float32)[0] == 1.0          # iscale = -127 / -127, d = 1 / iscale
+    assert list(q[:4]) == [-127, 2, 4, -2]             # half to even, not half away from zero
+    sums = blk[260:292].view(np.int16)
+    assert sums[0] == -123 and not sums[1:].any()
+    x = np.zeros(256, np.float32)
+    x[0] = 127.0
+    blk = oracle.quantize_q8_K(x)
+    assert blk[:4].view(np.float32)[0] == -1.0 and blk[4:260].view(np.int8)[0] == -127  # the sign flips into d
+
+
+def _k_scales():
+    """Packed 6-bit scales / minimums with sub-block 0 = (2, 3), 1 = (1, 1), 4 = (17, 18): sub-blocks 4-7 keep their
+    low four bits in the nibbles of bytes 8-11 and their top two bits in bits 6-7 of bytes 0-3 (scale) / 4-7 (min)."""
+    s = np.zeros(12, np.uint8)
+    s[0] = 2 | (17 >> 4) << 6
+    s[4] = 3 | (18 >> 4) << 6
+    s[1], s[5] = 1, 1
+    s[8] = (17 & 15) | (18 & 15) << 4
+    return s
+
+
+@pytest.mark.parametrize("dtype", [oracle.Q4_K, oracle.Q5_K])
+def test_q4_K_q5_K_known_answer(dtype):
+    blk = np.zeros(oracle.BLOCK_BYTES[dtype], np.uint8)
+    _put16(blk, 0, 1.0)    # d
+    _put16(blk, 2, 0.5)    # dmin
+    blk[4:16] = _k_scales()
+    qs = 48 if dtype == oracle.Q5_K else 16
+    blk[qs + 0] = 0x5A     # element 0 = 10 (sub-block 0), element 32 = 5 (sub-block 1)
+    blk[qs + 64] = 0x03    # element 128 = 3 (sub-block 4)
+    if dtype == oracle.Q5_K:
+        blk[16] = 0x01     # element 0's fifth bit
+    y = oracle.dequantize_rows(blk, dtype, 256, 1)[0]
+    assert y[0] == (2 * 26 - 0.5 * 3 if dtype == oracle.Q5_K else 2 * 10 - 0.5 * 3)
+    assert y[32] == 1 * 5 - 0.5 * 1
+    assert y[128] == 17 * 3 - 0.5 * 18
+
+
+def test_q6_K_known_answer():
+    blk = np.zeros(210, np.uint8)
+    _put16(blk, 208, 0.5)
+    blk[192] = 2                      # scale of elements 0-15
+    blk[192 + 4] = np.uint8(0xFF)     # scale -1 for elements 64-79
+    blk[0] = 0x21                     # element 0 low bits 1, element 64 low bits 2
+    blk[128] = 0x03                   # element 0 high bits 3
+    y = oracle.dequantize_rows(blk, oracle.Q6_K, 256, 1)[0]
+    assert y[0] == 0.5 * 2 * ((1 | 3 << 4) - 32)
+    assert y[64] == 0.5 * -1 * (2 - 32)
+
+
+@pytest.mark.parametrize("dtype", [oracle.Q4_K, oracle.Q5_K, oracle.Q6_K])
+def test_k_dot_against_zero_activations_is_zero(dtype):
+    rng = np.random.default_rng(dtype)
+    w = oracle.random_q_blocks(rng, dtype, 1, 256)
+    act = oracle.quantize_q8_K(np.zeros(256, np.float32))
+    assert oracle.vec_dot(dtype, w[0], act, 1) == 0.0
