@@ -58,17 +58,16 @@ def peaks():
         return 6650.0, 1590.0, 1400.0, "fallback"
 
 
-def profile_traffic(name):
-    """Per-launch DRAM bytes (read + write) recorded from an ncu capture in profiles/<name>.md, or None."""
-    path = os.path.join(ROOT, "profiles", name + ".md")
-    try:
-        with open(path) as f:
-            for line in f:
-                if line.startswith("traffic_bytes_per_launch:"):
-                    return float(line.split(":", 1)[1].strip())
-    except OSError:
-        pass
-    return None
+# Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of the dominant kernels at this bench's full
+# sizes, from one ncu capture each on a smaller case of the same kernel, scaled by the units processed (traffic grows
+# in proportion):
+#   decode_kernel, config 2: `ncu --set full --clock-control none -k regex:decode_kernel -s 3 -c 1 python bench.py
+#     --seqs 8 --steps 1 --warmup 3 --no-prefill --no-extra --no-e2e --cpu-seconds 0` -> 1.0838 GB for 128 rows,
+#     x 8 for the 1024-row launch;
+#   prefill_kernel, config 3: `ncu --set full --clock-control none -k regex:prefill_kernel -s 3 -c 1 python bench.py
+#     --workload prefill --prefill-seqs 1 --steps 1 --warmup 3` -> 371.3 MB for 22 items, x 8 for 176 items.
+TRAFFIC_DECODE_CFG2 = 8670288000
+TRAFFIC_PREFILL_CFG3 = 2970780000
 
 
 class ClockSampler:
@@ -240,7 +239,7 @@ def decode_batched(args, world, rank, local):
     hbm, _, _, src = peaks()
     decode_bytes = kv_bytes + qo_bytes
     achieved = decode_bytes / (kern_ms * 1e-3) / 1e9
-    traffic = profile_traffic("decode_kernel_cfg2")
+    traffic = TRAFFIC_DECODE_CFG2 * rows / (SEQ2 * LAYERS2)
     res = {
         "metric": "decode attn HBM GB/s", "value": world * step_bytes / (ms * 1e-3) / 1e9, "unit": "GB/s",
         "ms_per_step": ms, "dtype": "fp16 KV, fp32 accumulate",
@@ -335,7 +334,7 @@ def prefill(args, world, rank, local, steps=None, warmup=None):
                    "sequences_per_gpu": seqs, "tokens": T3, "layers": LAYERS3, "flops_per_step_per_gpu": flops},
         "roofline": {"kernel": "prefill_kernel", "bound": "tensor", "achieved": ach, "peak": bf16, "unit": "TFLOP/s",
                      "frac": ach / bf16, "peak_source": f"{src} bf16_tflops (burst)", "frac_of_sustained": ach / bf16_sus,
-                     "frac_of_nominal_2250": ach / 2250.0, "traffic": profile_traffic("prefill_kernel_cfg3")},
+                     "frac_of_nominal_2250": ach / 2250.0, "traffic": TRAFFIC_PREFILL_CFG3 * items / (SEQ3 * LAYERS3)},
     }
     kv.close()
     ctx.close()

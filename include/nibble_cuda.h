@@ -233,14 +233,15 @@ NBL_API int nbl_decode_step_host(nbl_ctx* ctx, nbl_kv* kv, const float* q_in_h, 
                                  float* out_h, int32_t n_chunks);
 
 /* Same arguments and results as nbl_attn_decode, but the call allocates no device memory: the split partials
- * live in a fixed 8 MiB array inside the library (held on every GPU that loads it, until the process exits)
- * instead of context scratch. For callers that may not allocate once running -- e.g. an engine that owns all
- * device memory through its own pool, or a decode loop that cannot take cudaMalloc's device-wide sync.
+ * live in a fixed 8 MiB array inside the library (held on every GPU the library has created a context on, until
+ * the process exits) instead of context scratch. For callers that may not allocate once running -- e.g. an
+ * engine that owns all device memory through its own pool, or a decode loop that cannot take cudaMalloc's
+ * device-wide sync. nbl_ctx_create sets the array up (loads it, resolves its device address) and loads the
+ * decode kernels, so every call of this entry point, the first included, allocates nothing.
  * An explicit n_splits whose partials (n_splits * n_rows * n_heads * 65 floats) exceed the array is rejected
  * with NBL_E_INVALID; with n_splits = 0 the split count is reduced until they fit. All calls on a device share
  * the array (each call writes every partial it reads, so nothing needs clearing); calls whose kernels overlap
- * on the GPU race on it and must be serialised. The first call on a device resolves the array's address and
- * should come before any stream capture. No counterpart in the reference (nibble's CPU backend sizes its
+ * on the GPU race on it and must be serialised. No counterpart in the reference (nibble's CPU backend sizes its
  * scratch once in reserve()). */
 NBL_API int nbl_attn_decode_static(nbl_ctx* ctx, const nbl_kv* kv, const float* q, const int32_t* page_table,
                                    int32_t pt_stride, const int32_t* seq_lens, int32_t max_seq_len, int32_t n_rows,

@@ -341,6 +341,8 @@ int nbl_ctx_create(int device, nbl_ctx** out) {
       ctx->stream = ctx->own_stream;
       ctx->d_err = static_cast<int*>(device_alloc(sizeof(int), "error word"));
       nbl::check_cuda(cudaMemset(ctx->d_err, 0, sizeof(int)), "error word init");
+      // nbl_attn_decode_static's fixed partials array and kernels, placed now while allocating is allowed
+      nbl::prepare_static_decode(device);
     } catch (...) {
       if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
       delete ctx;

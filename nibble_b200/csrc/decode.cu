@@ -362,6 +362,25 @@ void launch_g(cudaStream_t st, const CUtensorMap& tmap, const DecodeArgs& a, int
 
 }  // namespace
 
+void preload_decode() {
+  // Setting the shared-memory attribute needs each kernel's function handle, which loads the module (CUDA loads
+  // modules lazily on first use); the merge kernel is loaded the same way.
+  auto set = [](const void* fn) {
+    check_cuda(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes),
+               "decode smem attribute");
+  };
+  set(reinterpret_cast<const void*>(decode_kernel<1>));
+  set(reinterpret_cast<const void*>(decode_kernel<2>));
+  set(reinterpret_cast<const void*>(decode_kernel<3>));
+  set(reinterpret_cast<const void*>(decode_kernel<4>));
+  set(reinterpret_cast<const void*>(decode_kernel<5>));
+  set(reinterpret_cast<const void*>(decode_kernel<6>));
+  set(reinterpret_cast<const void*>(decode_kernel<7>));
+  set(reinterpret_cast<const void*>(decode_kernel<8>));
+  cudaFuncAttributes attr;
+  check_cuda(cudaFuncGetAttributes(&attr, lse_merge_kernel), "lse_merge attributes");
+}
+
 DecodePlan plan_decode(int n_rows, int n_kv_heads, int group, int n_heads, int max_seq_len, int page_size,
                        int num_sms, int requested_splits) {
   (void)group;

@@ -5,21 +5,23 @@
 // all of a GPU's memory for its own pool at start-up and treats any later cudaMalloc as a failure, or a
 // latency-critical decode loop that cannot afford cudaMalloc's implicit device-wide synchronisation. The
 // ordinary entry point grows the context's scratch on demand (or needs nbl_reserve beforehand); this one uses
-// a static array whose size is fixed when the library is loaded.
+// a static array of fixed size.
 //
 // Limits and sharing:
-//   * the array holds kStaticScratchBytes (8 MiB) on every GPU that loads the library, until the process
-//     exits; a request whose split partials need more is rejected (NBL_E_INVALID) when the caller asked for an
-//     explicit split count, and served with fewer splits (down to one split, which needs no scratch) when the
-//     split count is left to the library;
+//   * the array holds kStaticScratchBytes (8 MiB) on every GPU the library has created a context on, until the
+//     process exits; a request whose split partials need more is rejected (NBL_E_INVALID) when the caller asked
+//     for an explicit split count, and served with fewer splits (down to one split, which needs no scratch) when
+//     the split count is left to the library;
 //   * every call on a device shares the one array and it keeps the last call's contents; the decode kernel
 //     writes every partial it later merges, so nothing has to start at zero. Two calls whose kernels overlap on
 //     the GPU (different streams, or different contexts on the same device) race on the array: serialise them;
-//   * the first call on a device looks up the array's device address (cudaGetSymbolAddress, with that device
-//     current) and caches it; that first call should come before any stream capture.
+//   * set-up happens in nbl_ctx_create, once per device, with that device current: the module holding the array
+//     is loaded (which is when CUDA places the array in device memory), its address is resolved with
+//     cudaGetSymbolAddress and cached, and the decode kernels are loaded too. So the entry point's own calls,
+//     the first one included, allocate nothing.
 // No reference counterpart: nibble's CPU backend sizes its scratch once in reserve() (cpu_backend.cpp:24-67).
-#include <atomic>
 #include <mutex>
+#include <new>
 #include <string>
 
 #include "nbl_internal.h"
@@ -31,25 +33,35 @@ constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_decode_scratch[kStaticScratchBytes];
 
-// Per-device device address of g_decode_scratch (host code must not use the symbol itself as a pointer).
+// Per-device device address of g_decode_scratch. In host code the symbol itself is only a host-side stand-in,
+// never a device address, so kernels are given these resolved addresses.
 std::mutex g_addr_mu;
 void* g_addr[kMaxDevices] = {};
 
-void* static_scratch(int device) {
+void* resolved_scratch(int device) {
   if (device < 0 || device >= kMaxDevices) nbl::fail(NBL_E_UNSUPPORTED, "attn_decode_static: device id >= 64");
   std::lock_guard<std::mutex> lock(g_addr_mu);
-  if (!g_addr[device]) {
-    void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_decode_scratch);  // the context's device is current
-    if (e != cudaSuccess || !p)
-      nbl::fail(NBL_E_CUDA, std::string("attn_decode_static: cannot resolve the static scratch array: ") +
-                                cudaGetErrorString(e));
-    g_addr[device] = p;
-  }
+  if (!g_addr[device])
+    nbl::fail(NBL_E_CUDA, "attn_decode_static: the static partials array was not set up on device " +
+                              std::to_string(device) + " (nbl_ctx_create does it)");
   return g_addr[device];
 }
 
 }  // namespace
+
+void nbl::prepare_static_decode(int device) {
+  if (device < 0 || device >= kMaxDevices) return;  // such a device can only be refused by the entry point
+  std::lock_guard<std::mutex> lock(g_addr_mu);
+  if (g_addr[device]) return;
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_decode_scratch);  // the caller made `device` current
+  if (e != cudaSuccess || !p) {
+    cudaGetLastError();  // leave no stale error for a later launch check to report
+    nbl::fail(NBL_E_CUDA, std::string("cannot set up the static decode partials array: ") + cudaGetErrorString(e));
+  }
+  nbl::preload_decode();
+  g_addr[device] = p;
+}
 
 extern "C" NBL_API int nbl_attn_decode_static(nbl_ctx* ctx, const nbl_kv* kv, const float* q,
                                               const int32_t* page_table, int32_t pt_stride, const int32_t* seq_lens,
@@ -79,18 +91,21 @@ extern "C" NBL_API int nbl_attn_decode_static(nbl_ctx* ctx, const nbl_kv* kv, co
                                      std::to_string(plan.scratch_bytes) + " bytes of split partials; the static "
                                      "array holds " + std::to_string(kStaticScratchBytes) +
                                      " (ask for fewer splits, or pass 0)");
-      // Library-chosen split count: the largest count whose partials fit (one split needs none).
+      // Library-chosen split count: the largest count whose partials fit (one split needs none). With 148 SMs the
+      // planner's own choice needs at most 7.9 MB, so this only guards parts with more SMs.
       const size_t per_split = size_t(n_rows) * n_heads * (64 + 1) * sizeof(float);
       const int fit = static_cast<int>(kStaticScratchBytes / per_split);
       plan = nbl::plan_decode(n_rows, kv->cfg.n_kv_heads, group, n_heads, max_seq_len, kv->cfg.page_size,
                               ctx->num_sms, fit >= 2 ? fit : 1);
     }
-    void* scratch = plan.n_splits > 1 ? static_scratch(ctx->device) : nullptr;
+    void* scratch = plan.n_splits > 1 ? resolved_scratch(ctx->device) : nullptr;
     nbl::launch_decode(ctx->stream, kv, q, page_table, pt_stride, seq_lens, n_rows, n_heads, out, lse, plan, scratch,
                        ctx->d_err);
     return NBL_OK;
   } catch (const nbl::Failure& e) {
     return nbl::record_error(e.status, e.what());
+  } catch (const std::bad_alloc&) {
+    return nbl::record_error(NBL_E_NOMEM, "host allocation failed");
   } catch (const std::exception& e) {
     return nbl::record_error(NBL_E_INVALID, e.what());
   }

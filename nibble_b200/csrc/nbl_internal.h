@@ -118,6 +118,13 @@ DecodePlan plan_decode(int n_rows, int n_kv_heads, int group, int n_heads, int m
 void launch_decode(cudaStream_t st, const nbl_kv* kv, const float* q, const int32_t* page_table, int32_t pt_stride,
                    const int32_t* seq_lens, int n_rows, int n_heads, float* out, float* lse, const DecodePlan& plan,
                    void* scratch, int* err);
+// Loads the decode and merge kernels on the current device and sets their shared-memory attribute, so a later
+// launch needs no module load (which allocates device memory).
+void preload_decode();
+// decode_static.cu: places the allocation-free decode's static partials array on the current device (device id
+// `device`), resolves its address and preloads the decode kernels. Called by nbl_ctx_create, while allocation is
+// still allowed, so nbl_attn_decode_static itself allocates nothing.
+void prepare_static_decode(int device);
 void launch_lse_merge(cudaStream_t st, const float* part_o, const float* part_lse, int n_parts, int64_t rows,
                       int head_dim, float* out, float* lse,
                       int64_t o_stride = -1, int64_t lse_stride = -1);

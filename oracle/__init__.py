@@ -23,7 +23,9 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libnibble_ref.so")
-REF_TREE = os.environ.get("NIBBLE_REFERENCE_TREE", "/root/reference")
+# The nibble source tree the _ref targets compile from: NIBBLE_REFERENCE_TREE, else a checkout named "reference"
+# beside this repository. Without one, only liboracle.so is built (the prebuilt _ref files are used as they are).
+REF_TREE = os.environ.get("NIBBLE_REFERENCE_TREE") or os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
 
 _f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
 _u16p = np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS")

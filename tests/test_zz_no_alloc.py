@@ -84,3 +84,42 @@ def test_static_decode_refuses_partials_larger_than_its_array(setup):
     assert e.value.status == nb._abi.NBL_E_INVALID and "static" in str(e.value)
     _static_decode(ctx, kv, q, big_table, big_lens, 300, out, lse, 0)  # the library-chosen count fits
     ctx.check()
+
+
+def test_static_decode_allocates_no_device_memory():
+    """Free device memory (cudaMemGetInfo) is the same before the entry point's first call on a fresh context and
+    after two calls: one with the library's own split count, one with an explicit count whose partials fill most
+    of the array. The context, pool and every tensor exist before the first reading."""
+    import torch
+    import nibble_b200 as nb
+    ctx = nb.Context(0)
+    H, KV = 8, 1
+    rows = 544  # the largest library-chosen partials on 148 SMs: 7 splits x 544 rows x 8 heads x 65 floats
+    lens = [8192] * rows
+    table, n_pages = make_page_tables(lens, 16, shuffle_seed=9)
+    kv = ctx.kv_pool(n_pages, KV)
+    g = torch.Generator(device="cuda").manual_seed(7)
+    pool = kv.tensor().view(torch.float16)
+    pool.copy_(torch.randn(pool.shape, generator=g, device="cuda").half())
+    d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()  # noqa: E731
+    t_table, t_lens = d(table), d(np.array(lens, np.int32))
+    q = torch.randn((rows, H, D), device="cuda", generator=g)
+    outs = [torch.full((rows, H, D), float("nan"), device="cuda") for _ in range(2)]
+    lses = [torch.full((rows, H), float("nan"), device="cuda") for _ in range(2)]
+    ref, ref_lse = torch.empty_like(q), torch.empty((rows, H), device="cuda")
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info()[0]
+    _static_decode(ctx, kv, q, t_table, t_lens, 8192, outs[0], lses[0], 0)
+    _static_decode(ctx, kv, q, t_table, t_lens, 8192, outs[1], lses[1], 7)  # 7.9 MB of the 8 MiB array
+    ctx.check()
+    torch.cuda.synchronize()
+    free1 = torch.cuda.mem_get_info()[0]
+    assert free1 == free0, f"free device memory changed by {free0 - free1} bytes"
+    ctx.attn_decode(kv, q, t_table, t_lens, 8192, ref, ref_lse)  # the ordinary entry point, after the reading
+    ctx.check()
+    torch.cuda.synchronize()
+    for out, lse in zip(outs, lses):
+        assert max_rel_err_per_head(out.cpu().numpy(), ref.cpu().numpy()) <= 1e-4
+        np.testing.assert_allclose(lse.cpu().numpy(), ref_lse.cpu().numpy(), rtol=0, atol=2e-5)
+    kv.close()
+    ctx.close()
