@@ -271,6 +271,16 @@ NBL_API int nbl_lse_merge(nbl_ctx* ctx, const float* part_o, const float* part_l
 NBL_API int nbl_lse_merge_packed(nbl_ctx* ctx, const float* packed, int32_t n_parts, int64_t rows, int32_t head_dim,
                                  float* out, float* lse);
 
+/* ---- diagnostics ---- */
+/* Runs the library's bounded device wait (the routine every TMA / tensor-core completion wait uses) in a one-thread
+ * kernel against an mbarrier that nothing arrives on, with a limit of limit_ns (0 < limit_ns <= 1e9): the wait gives
+ * up, the kernel returns, and the next nbl_ctx_check reports NBL_E_DEVICE ("a bounded wait ... gave up") and clears
+ * the flag, after which the context runs normally. Shows that a lost completion ends a launch with an error instead
+ * of a hang, without faulting anything. Until that check, later waits of the context give up at once (the timeout
+ * bit is sticky). No reference counterpart; the reference reports failures as nibble::Error
+ * (include/nibble/error.h:8-13). */
+NBL_API int nbl_selftest_bounded_wait(nbl_ctx* ctx, int64_t limit_ns);
+
 #ifdef __cplusplus
 }
 #endif

@@ -59,20 +59,22 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s: legitimate waits here last microseconds
 
-// Waits for the phase with the given parity to complete. Gives up after kWaitLimitNs of wall-clock time, or at
-// once when another wait of this context has already timed out (kErrTimeout is sticky until nbl_ctx_check),
-// so one lost completion ends the whole launch in seconds. Returns false on giving up.
+// Waits for the phase with the given parity to complete. Gives up after limit_ns (kWaitLimitNs unless a caller
+// passes another) of wall-clock time, or at once when another wait of this context has already timed out
+// (kErrTimeout is sticky until nbl_ctx_check), so one lost completion ends the whole launch in seconds. Returns
+// false on giving up.
 //
 // The polling loop with its timer sits in a separate non-inlined function: inlined, its reconvergence code made
 // every wait cost ~108 cycles even when the phase had already completed (measured on B200), against ~16 for
 // the bare try_wait and ~48 for this split form.
-static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, int* err) {
+static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, int* err,
+                                                   uint64_t limit_ns = kWaitLimitNs) {
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 63u) == 0) {
       if (err && (*reinterpret_cast<volatile int*>(err) & kErrTimeout)) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (globaltimer_ns() - t0 > limit_ns) {
         flag_error(err, kErrTimeout);
         return false;
       }
