@@ -102,10 +102,25 @@ NBL_API int nbl_ctx_set_stream(nbl_ctx* ctx, void* stream);
 /* Returns the context to its own stream. */
 NBL_API int nbl_ctx_use_own_stream(nbl_ctx* ctx);
 NBL_API void* nbl_ctx_stream(nbl_ctx* ctx);
+/* Waits for the context's queued work (with the paged route on, recorded query-row ops are launched first). */
 NBL_API int nbl_ctx_sync(nbl_ctx* ctx);
-/* Synchronises, then returns NBL_E_DEVICE (and clears the flag) if any kernel since the last check skipped
- * an out-of-range page id, position or length. */
+/* Synchronises (as nbl_ctx_sync), then returns NBL_E_DEVICE (and clears the flag) if any kernel since the last check
+ * skipped an out-of-range page id, position or length, or gave up a bounded wait. */
 NBL_API int nbl_ctx_check(nbl_ctx* ctx);
+
+/* Serves the drop-in Backend ops below from fp16 pages (on != 0) or keeps the reference's flat fp32 K/V blocks
+ * (on == 0, the default of a new context; nibble_b200/csrc/host/cuda_backend.h's CudaBackend turns it on).
+ * With it on, the first nbl_attention on a pair of K/V blocks from nbl_alloc with head_dim 64 binds them: from
+ * then on their rows are fp16 pages inside the K block's own memory (no allocation), a matmul output aimed at
+ * their rows is staged, nbl_add_bias / nbl_rope on those rows and on the query rows are recorded, and
+ * nbl_attention runs them as one fused bias + RoPE + fp16 append launch followed by the split-K decode kernel
+ * (n <= 8 rows, fp32 accuracy) or the tcgen05 prefill kernel (n > 8 rows, fp16 operands). Every other access to
+ * such a block (nbl_read, nbl_copy, ...) first turns it back into flat fp32 rows (values rounded to fp16), so each
+ * op keeps its Backend meaning; a recorded query op is applied before anything else reads the rows. Call it
+ * before nbl_reserve and before allocating the K/V blocks (the reserve sizes the staging; K/V-shaped blocks then
+ * get room for whole 16-position pages). Turning it off returns every bound block to flat fp32 rows. Replaces
+ * the flat fp32 cache of src/model/transformer.cpp:74-90 behind the unchanged Backend calls (:171-202). */
+NBL_API int nbl_ctx_set_paged_kv(nbl_ctx* ctx, int32_t on);
 
 /* ---- Backend memory ops ---- */
 /* Backend::reserve (backend.h:42-45; CpuBackend::reserve cpu_backend.cpp:24-67): sizes the split-K scratch and

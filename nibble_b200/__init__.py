@@ -160,6 +160,11 @@ class Context:
         """Runs later kernels on this cudaStream_t (0 / None = CUDA's default stream)."""
         check(_abi.lib.nbl_ctx_set_stream(self.handle, stream))
 
+    def set_paged_kv(self, on: bool = True):
+        """Backend-level K/V blocks as fp16 pages with the fused append and the paged kernels (nbl_ctx_set_paged_kv);
+        call before reserve() and before allocating the blocks."""
+        check(_abi.lib.nbl_ctx_set_paged_kv(self.handle, 1 if on else 0))
+
     def sync(self):
         check(_abi.lib.nbl_ctx_sync(self.handle))
 

@@ -50,6 +50,7 @@ SIGNATURES = {
     "nbl_ctx_stream": [_P],
     "nbl_ctx_sync": [_P],
     "nbl_ctx_check": [_P],
+    "nbl_ctx_set_paged_kv": [_P, _I32],
     "nbl_reserve": [_P, _I64, _I64, _I64, _I64],
     "nbl_alloc": [_P, _I64, C.POINTER(_P)],
     "nbl_free": [_P, _P],

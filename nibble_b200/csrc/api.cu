@@ -45,7 +45,9 @@ void require(bool ok, const std::string& msg) {
 // Makes the context's device current for the calling thread.
 void use_device(nbl_ctx* ctx) { nbl::check_cuda(cudaSetDevice(ctx->device), "cudaSetDevice"); }
 
-void* device_alloc(size_t bytes, const char* what) {
+}  // namespace
+
+void* nbl::device_alloc(size_t bytes, const char* what) {
   void* p = nullptr;
   const cudaError_t e = cudaMalloc(&p, bytes);
   if (e != cudaSuccess) {
@@ -57,7 +59,7 @@ void* device_alloc(size_t bytes, const char* what) {
 }
 
 // Grows the context's split-K scratch to at least `bytes` (device allocation; not during stream capture).
-void ensure_scratch(nbl_ctx* ctx, size_t bytes) {
+void nbl::ensure_scratch(nbl_ctx* ctx, size_t bytes) {
   if (ctx->scratch_bytes >= bytes) return;
   void* p = device_alloc(bytes, "attention scratch");
   if (ctx->scratch) {
@@ -70,7 +72,7 @@ void ensure_scratch(nbl_ctx* ctx, size_t bytes) {
 
 // Returns the device cos/sin table for (base, head_dim, factors) covering positions [0, n_pos), building it
 // on the host in double with the reference's expression (src/backend/cpu/ref_ops.cpp:173-176) if needed.
-const nbl::RopeTable& rope_table(nbl_ctx* ctx, const nbl_rope_params& rp, int64_t head_dim, int64_t n_pos) {
+const nbl::RopeTable& nbl::rope_table(nbl_ctx* ctx, const nbl_rope_params& rp, int64_t head_dim, int64_t n_pos) {
   const int64_t half = head_dim / 2;
   // the cache hit is the per-call path (every layer of every token): compare in place, allocate nothing
   auto same_factors = [&](const nbl::RopeTable& t) {
@@ -112,6 +114,8 @@ const nbl::RopeTable& rope_table(nbl_ctx* ctx, const nbl_rope_params& rp, int64_
   return ctx->rope_tables.back();
 }
 
+namespace {
+
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
@@ -138,6 +142,10 @@ void nbl::encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, voi
 }
 
 int nbl::record_error(int status, const std::string& msg) { return set_error(status, msg); }
+
+using nbl::device_alloc;
+using nbl::ensure_scratch;
+using nbl::rope_table;
 
 namespace {
 
@@ -356,6 +364,7 @@ int nbl_ctx_destroy(nbl_ctx* ctx) {
   if (!ctx) return NBL_OK;
   return guarded([&] {
     use_device(ctx);
+    nbl::route_destroy(ctx, false);
     cudaStreamSynchronize(ctx->stream);
     for (nbl_kv* kv : ctx->kvs) {
       cudaFree(kv->pool);
@@ -403,6 +412,7 @@ int nbl_ctx_sync(nbl_ctx* ctx) {
   return guarded([&] {
     require(ctx != nullptr, "nbl_ctx_sync: ctx is NULL");
     use_device(ctx);
+    nbl::route_flush_queries(ctx);
     nbl::check_cuda(cudaStreamSynchronize(ctx->stream), "stream synchronize");
   });
 }
@@ -411,6 +421,7 @@ int nbl_ctx_check(nbl_ctx* ctx) {
   return guarded([&] {
     require(ctx != nullptr, "nbl_ctx_check: ctx is NULL");
     use_device(ctx);
+    nbl::route_flush_queries(ctx);
     int host = 0;
     nbl::check_cuda(cudaMemcpyAsync(&host, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream), "error word");
     nbl::check_cuda(cudaStreamSynchronize(ctx->stream), "error word");
@@ -424,6 +435,14 @@ int nbl_ctx_check(nbl_ctx* ctx) {
       if (host & nbl::kErrSmemAlign) what += " shared memory was not 1024-byte aligned;";
       nbl::fail(NBL_E_DEVICE, "device-side check failed (flags " + std::to_string(host) + "):" + what);
     }
+  });
+}
+
+int nbl_ctx_set_paged_kv(nbl_ctx* ctx, int32_t on) {
+  return guarded([&] {
+    require(ctx != nullptr, "nbl_ctx_set_paged_kv: ctx is NULL");
+    use_device(ctx);
+    nbl::route_enable(ctx, on != 0);
   });
 }
 
@@ -443,6 +462,7 @@ int nbl_reserve(nbl_ctx* ctx, int64_t n_ctx, int64_t n_heads, int64_t max_rows, 
     if (plan.scratch_bytes) ensure_scratch(ctx, plan.scratch_bytes);
     if (max_rows > 0) ensure_ids(ctx, max_rows);
     if (max_rows > nbl::kGemvMaxRows) cublas_handle(ctx);
+    nbl::route_reserve(ctx, n_ctx, n_heads, max_rows, max_width);
   });
 }
 
@@ -454,7 +474,7 @@ int nbl_alloc(nbl_ctx* ctx, int64_t n_floats, float** out) {
     if (static_cast<uint64_t>(n_floats) > (UINT64_MAX - 255) / sizeof(float))
       nbl::fail(NBL_E_INVALID, "alloc: size of " + std::to_string(n_floats) + " floats overflows");
     use_device(ctx);
-    size_t bytes = static_cast<size_t>(n_floats) * sizeof(float);
+    size_t bytes = static_cast<size_t>(nbl::route_alloc_floats(ctx, n_floats)) * sizeof(float);
     bytes = std::max<size_t>((bytes + 255) & ~size_t(255), 256);
     void* p = device_alloc(bytes, "alloc");
     const cudaError_t e = cudaMemsetAsync(p, 0, bytes, ctx->stream);
@@ -463,7 +483,7 @@ int nbl_alloc(nbl_ctx* ctx, int64_t n_floats, float** out) {
       nbl::check_cuda(e, "alloc zero-fill");
     }
     try {
-      ctx->allocs.emplace(p, bytes);
+      ctx->allocs.emplace(p, nbl_ctx::Alloc{bytes, n_floats});
     } catch (...) {
       cudaFree(p);
       throw;
@@ -479,6 +499,7 @@ int nbl_free(nbl_ctx* ctx, float* p) {
     auto it = ctx->allocs.find(p);
     if (it == ctx->allocs.end()) return;  // not ours: ignored, like CpuBackend::free (cpu_backend.cpp:96-102)
     use_device(ctx);
+    nbl::route_free(ctx, p);
     nbl::check_cuda(cudaStreamSynchronize(ctx->stream), "free sync");
     cudaFree(p);
     ctx->allocs.erase(it);
@@ -489,6 +510,7 @@ int nbl_read(nbl_ctx* ctx, float* host_dst, const float* src, int64_t n) {
   return guarded([&] {
     require(ctx && host_dst && src && n >= 0, "read: dst/src NULL or n < 0");
     use_device(ctx);
+    nbl::route_touch(ctx, src, n, nbl::Access::kRead);
     nbl::check_cuda(cudaMemcpyAsync(host_dst, src, static_cast<size_t>(n) * sizeof(float), cudaMemcpyDeviceToHost,
                                     ctx->stream),
                     "read");
@@ -500,6 +522,7 @@ int nbl_write(nbl_ctx* ctx, float* dst, const float* host_src, int64_t n) {
   return guarded([&] {
     require(ctx && dst && host_src && n >= 0, "write: dst/src NULL or n < 0");
     use_device(ctx);
+    nbl::route_touch(ctx, dst, n, nbl::Access::kWrite);
     nbl::check_cuda(cudaMemcpyAsync(dst, host_src, static_cast<size_t>(n) * sizeof(float), cudaMemcpyHostToDevice,
                                     ctx->stream),
                     "write");
@@ -511,6 +534,7 @@ int nbl_add_bias(nbl_ctx* ctx, float* x, const float* bias, int64_t width, int64
   return guarded([&] {
     require(ctx && x && bias && width > 0 && n > 0, "add_bias: x/bias NULL or width/n not positive");
     use_device(ctx);
+    if (nbl::route_add_bias(ctx, x, bias, width, n)) return;
     nbl::launch_add_bias(ctx->stream, x, bias, width, n);
   });
 }
@@ -524,6 +548,7 @@ int nbl_rope(nbl_ctx* ctx, float* x, int64_t n, int64_t n_heads, int64_t head_di
                 std::to_string(head_dim) + " (must be even) pos0=" + std::to_string(pos0));
     use_device(ctx);
     const auto& tab = rope_table(ctx, *rope, head_dim, pos0 + n);
+    if (nbl::route_rope(ctx, x, n, n_heads, head_dim, pos0, *rope)) return;
     nbl::launch_rope_f32(ctx->stream, x, n, n_heads, head_dim, pos0, rope->neox != 0, tab.dev, ctx->d_err);
   });
 }
@@ -538,6 +563,11 @@ int nbl_attention(nbl_ctx* ctx, const float* q, const float* k, const float* v, 
                 std::to_string(n_heads) + " n_kv_heads=" + std::to_string(n_kv_heads) + " head_dim=" +
                 std::to_string(head_dim) + " (n_heads must be a multiple of n_kv_heads; head_dim <= 256)");
     use_device(ctx);
+    if (nbl::route_attention(ctx, q, k, v, out, n, pos0, n_heads, n_kv_heads, head_dim)) return;
+    nbl::route_touch(ctx, q, n * n_heads * head_dim, nbl::Access::kRead);
+    nbl::route_touch(ctx, k, (pos0 + n) * n_kv_heads * head_dim, nbl::Access::kRead);
+    nbl::route_touch(ctx, v, (pos0 + n) * n_kv_heads * head_dim, nbl::Access::kRead);
+    nbl::route_touch(ctx, out, n * n_heads * head_dim, nbl::Access::kWrite);
     const float scale = 1.0f / std::sqrt(static_cast<float>(head_dim));
     nbl::launch_attention_f32(ctx->stream, q, k, v, out, n, pos0, n_heads, n_kv_heads, head_dim, scale, ctx->num_sms);
   });
@@ -612,6 +642,7 @@ int nbl_rope_kv_append(nbl_ctx* ctx, nbl_kv* kv, const void* q_in, const void* k
   return guarded([&] {
     require(ctx && kv && q_in && k_in && v_in && q_out && tok_row && tok_pos && page_table && rope,
             "rope_kv_append: NULL argument");
+    nbl::route_flush_queries(ctx);
     require(kv->ctx == ctx, "rope_kv_append: pool belongs to another context");
     require(is_dtype(in_dtype) && is_dtype(q_out_dtype), "rope_kv_append: bad dtype");
     require(n_tok >= 0 && n_tok <= INT32_MAX && pt_stride > 0, "rope_kv_append: n_tok or pt_stride out of range");
@@ -631,6 +662,7 @@ int nbl_attn_decode(nbl_ctx* ctx, const nbl_kv* kv, const float* q, const int32_
                     float* lse, int32_t n_splits) {
   return guarded([&] {
     require(ctx && kv && q && page_table && seq_lens && out, "attn_decode: NULL argument");
+    nbl::route_flush_queries(ctx);
     require(kv->ctx == ctx, "attn_decode: pool belongs to another context");
     require(kv->cfg.dtype == NBL_F16, "attn_decode: the decode kernel reads an NBL_F16 pool");
     require(n_rows >= 0 && pt_stride > 0 && max_seq_len >= 0 && n_splits >= 0, "attn_decode: negative size");
@@ -655,6 +687,7 @@ int nbl_decode_step_host(nbl_ctx* ctx, nbl_kv* kv, const float* q_in_h, const fl
   return guarded([&] {
     require(ctx && kv && q_in_h && k_in_h && v_in_h && page_table && seq_lens && rope && out_h,
             "decode_step_host: NULL argument");
+    nbl::route_flush_queries(ctx);
     require(kv->ctx == ctx, "decode_step_host: pool belongs to another context");
     require(kv->cfg.dtype == NBL_F16, "decode_step_host: the decode kernel reads an NBL_F16 pool");
     require(n_rows >= 0 && pt_stride > 0 && max_seq_len >= 1 && n_chunks >= 0,
@@ -753,6 +786,7 @@ int nbl_attn_prefill(nbl_ctx* ctx, const nbl_kv* kv, const void* q, int32_t q_dt
                      int32_t out_dtype) {
   return guarded([&] {
     require(ctx && kv && q && q_start && q_len && kv_pos0 && page_table && out, "attn_prefill: NULL argument");
+    nbl::route_flush_queries(ctx);
     require(kv->ctx == ctx, "attn_prefill: pool belongs to another context");
     require(q_dtype == kv->cfg.dtype, "attn_prefill: q must have the pool's dtype");
     require(out_dtype == NBL_F32 || out_dtype == kv->cfg.dtype, "attn_prefill: out must be F32 or the pool dtype");
@@ -771,6 +805,7 @@ int nbl_lse_merge(nbl_ctx* ctx, const float* part_o, const float* part_lse, int3
                   int32_t head_dim, float* out, float* lse) {
   return guarded([&] {
     require(ctx && part_o && part_lse && out, "lse_merge: NULL argument");
+    nbl::route_flush_queries(ctx);
     require(n_parts > 0 && rows >= 0 && head_dim > 0 && head_dim <= 256, "lse_merge: bad size");
     if (rows == 0) return;
     use_device(ctx);
@@ -782,6 +817,7 @@ int nbl_lse_merge_packed(nbl_ctx* ctx, const float* packed, int32_t n_parts, int
                          float* out, float* lse) {
   return guarded([&] {
     require(ctx && packed && out, "lse_merge_packed: NULL argument");
+    nbl::route_flush_queries(ctx);
     require(n_parts > 0 && rows >= 0 && head_dim > 0 && head_dim <= 256, "lse_merge_packed: bad size");
     if (rows == 0) return;
     use_device(ctx);
@@ -897,6 +933,7 @@ int nbl_embed(nbl_ctx* ctx, const nbl_weight* table, const int32_t* ids, int64_t
                                      std::to_string(table->w.ne1) + ")");
     if (n == 0) return;
     use_device(ctx);
+    nbl::route_touch(ctx, out, n * table->w.ne0, nbl::Access::kWrite);
     ensure_ids(ctx, n);
     nbl::check_cuda(cudaMemcpyAsync(ctx->ids, ids, static_cast<size_t>(n) * sizeof(int32_t), cudaMemcpyHostToDevice,
                                     ctx->stream),
@@ -916,6 +953,8 @@ int nbl_matmul(nbl_ctx* ctx, const nbl_weight* w, const float* x, float* y, int6
     require(n >= 0 && n <= INT32_MAX && w->w.ne0 <= INT32_MAX && w->w.ne1 <= INT32_MAX, "matmul: bad size");
     if (n == 0) return;
     use_device(ctx);
+    nbl::route_touch(ctx, x, n * w->w.ne0, nbl::Access::kRead);
+    y = nbl::route_output(ctx, y, n, w->w.ne1);
     if (nbl::is_quant(w->w.dtype)) {
       quant_matmul(ctx, &w, &y, 1, x, n);
       nbl::check_cuda(cudaGetLastError(), "matmul launch");
@@ -945,6 +984,10 @@ int nbl_matmul_multi(nbl_ctx* ctx, const nbl_weight* const* ws, int32_t count, c
     }
     if (n == 0) return;
     use_device(ctx);
+    nbl::route_touch(ctx, x, n * ws[0]->w.ne0, nbl::Access::kRead);
+    std::vector<float*> outs(static_cast<size_t>(count));
+    for (int32_t i = 0; i < count; ++i) outs[i] = nbl::route_output(ctx, ys[i], n, ws[i]->w.ne1);
+    ys = outs.data();
     bool any_quant = false, all_quant_same = true;
     for (int32_t i = 0; i < count; ++i) {
       any_quant = any_quant || nbl::is_quant(ws[i]->w.dtype) || nbl::is_qblock(ws[i]->w.dtype);
@@ -995,6 +1038,8 @@ int nbl_rmsnorm(nbl_ctx* ctx, const float* x, const nbl_weight* weight, float* y
     require(n >= 0 && n <= INT32_MAX, "rmsnorm: bad n");
     if (n == 0) return;
     use_device(ctx);
+    nbl::route_touch(ctx, x, n * weight->w.ne0, nbl::Access::kRead);
+    nbl::route_touch(ctx, y, n * weight->w.ne0, nbl::Access::kWrite);
     nbl::launch_rmsnorm(ctx->stream, x, static_cast<const float*>(weight->w.dev), y, n, weight->w.ne0, eps);
     nbl::check_cuda(cudaGetLastError(), "rmsnorm launch");
   });
@@ -1005,6 +1050,8 @@ int nbl_add(nbl_ctx* ctx, float* x, const float* y, int64_t count) {
     require(ctx && x && y && count >= 0, "add: NULL argument or count < 0");
     if (count == 0) return;
     use_device(ctx);
+    nbl::route_touch(ctx, x, count, nbl::Access::kReadWrite);
+    nbl::route_touch(ctx, y, count, nbl::Access::kRead);
     nbl::launch_add(ctx->stream, x, y, count, ctx->num_sms);
     nbl::check_cuda(cudaGetLastError(), "add launch");
   });
@@ -1015,6 +1062,8 @@ int nbl_copy(nbl_ctx* ctx, float* dst, const float* src, int64_t count) {
     require(ctx && dst && src && count >= 0, "copy: NULL argument or count < 0");
     if (count == 0 || dst == src) return;
     use_device(ctx);
+    nbl::route_touch(ctx, src, count, nbl::Access::kRead);
+    nbl::route_touch(ctx, dst, count, nbl::Access::kWrite);
     nbl::check_cuda(cudaMemcpyAsync(dst, src, static_cast<size_t>(count) * sizeof(float), cudaMemcpyDeviceToDevice,
                                     ctx->stream),
                     "copy");
@@ -1026,6 +1075,8 @@ int nbl_silu_mul(nbl_ctx* ctx, float* gate, const float* up, int64_t count) {
     require(ctx && gate && up && count >= 0, "silu_mul: NULL argument or count < 0");
     if (count == 0) return;
     use_device(ctx);
+    nbl::route_touch(ctx, gate, count, nbl::Access::kReadWrite);
+    nbl::route_touch(ctx, up, count, nbl::Access::kRead);
     nbl::launch_silu_mul(ctx->stream, gate, up, count, ctx->num_sms);
     nbl::check_cuda(cudaGetLastError(), "silu_mul launch");
   });

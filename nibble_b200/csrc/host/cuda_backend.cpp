@@ -14,7 +14,16 @@ void check(int status) {
   throw Error("cuda backend: " + msg);
 }
 
-CudaBackend::CudaBackend(int device) { check(nbl_ctx_create(device, &ctx_)); }
+CudaBackend::CudaBackend(int device, bool paged_kv) {
+  check(nbl_ctx_create(device, &ctx_));
+  if (paged_kv) {
+    const int st = nbl_ctx_set_paged_kv(ctx_, 1);
+    if (st != NBL_OK) {
+      nbl_ctx_destroy(ctx_);
+      check(st);
+    }
+  }
+}
 
 CudaBackend::~CudaBackend() { nbl_ctx_destroy(ctx_); }  // releases the uploaded weights too
 

@@ -15,8 +15,13 @@
 // above; quantized: bit-identical to the CPU's block dots), rmsnorm, add, add_bias, rope, copy, attention, silu_mul --
 // so nibble's Transformer (src/model/transformer.cpp) runs on it unchanged.
 //
-// The paged fp16/bf16 fast path (fused append, split-K decode, tcgen05 prefill) is reached through handle()
-// and the nbl_* functions, with check() turning their statuses into nibble::Error.
+// Attention (the default, paged_kv = true): the Transformer's per-layer K/V blocks become fp16 pages the first time
+// attention() sees them (head_dim 64), and the calls it makes per layer -- matmul_multi into the cache rows, add_bias,
+// rope(q), rope(kc), attention (transformer.cpp:171-202) -- run as the matmul, ONE fused bias + RoPE + fp16 append
+// launch and the split-K decode kernel (up to 8 query rows) or the tcgen05 prefill kernel (longer chunks); see
+// nbl_ctx_set_paged_kv. Other head sizes keep the flat fp32 cache and the fp32 CUDA-core attention kernels.
+// The same kernels over many sequences' pages are reached through handle() and the nbl_* functions (BatchedDecoder),
+// with check() turning their statuses into nibble::Error.
 #include <unordered_map>
 
 #include "../../../include/nibble_cuda.h"
@@ -35,7 +40,10 @@ void check(int status);
 
 class CudaBackend final : public Backend {
  public:
-  explicit CudaBackend(int device = 0);
+  // paged_kv: K/V blocks handed to attention() with head_dim 64 are kept as fp16 pages and served by the
+  // split-K decode / tcgen05 prefill kernels with the bias + RoPE + append fused (nbl_ctx_set_paged_kv); false keeps
+  // the reference's flat fp32 cache and the fp32 CUDA-core attention.
+  explicit CudaBackend(int device = 0, bool paged_kv = true);
   ~CudaBackend() override;
   CudaBackend(const CudaBackend&) = delete;
   CudaBackend& operator=(const CudaBackend&) = delete;

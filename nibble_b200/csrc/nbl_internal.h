@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <map>
 #include <stdexcept>
 #include <string>
 #include <unordered_map>
@@ -43,7 +44,12 @@ struct nbl_ctx {
   cudaStream_t own_stream = nullptr;
   cudaStream_t stream = nullptr;
   int* d_err = nullptr;                        // device error word (nbl_ctx_check)
-  std::unordered_map<void*, size_t> allocs;    // Backend::alloc registry
+  struct Alloc {
+    size_t bytes;    // allocated (rounded up, padded for whole K/V pages when the paged route is on)
+    int64_t floats;  // requested
+  };
+  std::map<void*, Alloc> allocs;               // Backend::alloc registry
+  void* route = nullptr;                       // nbl::Route when the paged K/V route is on (backend_route.cu)
   void* scratch = nullptr;                     // split-K partials
   size_t scratch_bytes = 0;
   int64_t reserved_ctx = 0, reserved_heads = 0;
@@ -84,6 +90,13 @@ namespace nbl {
 // Stores msg as the calling thread's nbl_last_error() message and returns status (for entry points defined
 // outside api.cu).
 int record_error(int status, const std::string& msg);
+
+// cudaMalloc that fails with NBL_E_NOMEM and a message naming `what`.
+void* device_alloc(size_t bytes, const char* what);
+// Grows the context's split-K scratch to at least `bytes` (waits for queued work before freeing the old buffer).
+void ensure_scratch(nbl_ctx* ctx, size_t bytes);
+// The device cos/sin table for (base, head_dim, factors) covering positions [0, n_pos), built on first use.
+const RopeTable& rope_table(nbl_ctx* ctx, const nbl_rope_params& rp, int64_t head_dim, int64_t n_pos);
 
 // Encodes a tiled TMA descriptor (driver entry point resolved once through the runtime; no libcuda link).
 // dims/strides in elements/bytes as cuTensorMapEncodeTiled takes them; 128-byte swizzle unless told otherwise, zero
@@ -128,6 +141,32 @@ void prepare_static_decode(int device);
 void launch_lse_merge(cudaStream_t st, const float* part_o, const float* part_lse, int n_parts, int64_t rows,
                       int head_dim, float* out, float* lse,
                       int64_t o_stride = -1, int64_t lse_stride = -1);
+// backend_route.cu: the drop-in Backend ops served from fp16 pages (nbl_ctx_set_paged_kv). Every hook is a no-op
+// returning "not handled" while the route is off.
+enum class Access { kRead, kWrite, kReadWrite };  // kWrite: the op overwrites the whole range without reading it
+void route_enable(nbl_ctx* ctx, bool on);
+// Ends the route; restore_blocks: paged blocks go back to flat fp32 rows first (not needed when the context is
+// being destroyed).
+void route_destroy(nbl_ctx* ctx, bool restore_blocks);
+// Size to allocate for a Backend::alloc of n_floats (candidate K/V blocks get room for whole 16-position pages).
+int64_t route_alloc_floats(nbl_ctx* ctx, int64_t n_floats);
+void route_reserve(nbl_ctx* ctx, int64_t n_ctx, int64_t n_heads, int64_t max_rows, int64_t max_width);
+// Before an op accesses [p, p + n_floats): recorded ops on it are applied (or dropped when it is overwritten whole),
+// paged K/V blocks it overlaps are turned back into flat fp32 rows.
+void route_touch(nbl_ctx* ctx, const void* p, int64_t n_floats, Access access);
+// Where a matmul writes its n x width output meant for y (staging for rows of a paged K/V block; else y).
+float* route_output(nbl_ctx* ctx, float* y, int64_t n, int64_t width);
+// true: recorded or applied; false: the caller launches the ordinary kernel.
+bool route_add_bias(nbl_ctx* ctx, float* x, const float* bias, int64_t width, int64_t n);
+bool route_rope(nbl_ctx* ctx, float* x, int64_t n, int64_t heads, int64_t head_dim, int64_t pos0,
+                const nbl_rope_params& rp);
+bool route_attention(nbl_ctx* ctx, const float* q, const float* k, const float* v, float* out, int64_t n,
+                     int64_t pos0, int64_t n_heads, int64_t n_kv_heads, int64_t head_dim);
+// Before Backend::free of p (the surviving block of a paged pair is turned back into flat rows).
+void route_free(nbl_ctx* ctx, void* p);
+// Applies recorded query ops (before entry points outside the Backend set read arbitrary device memory).
+void route_flush_queries(nbl_ctx* ctx);
+
 // prefill.cu
 void launch_prefill(cudaStream_t st, const nbl_kv* kv, const void* q, int64_t n_q_rows, const int32_t* q_start,
                     const int32_t* q_len, const int32_t* kv_pos0, const int32_t* page_table, int32_t pt_stride,

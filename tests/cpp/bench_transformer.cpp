@@ -6,7 +6,9 @@
 // loader and tokenizer are not involved; the prompt is token i % n_vocab as in the reference).
 //
 //   nbl_model_bench [--backend cuda|cpu] [--shape tinyllama|qwen05] [--type F16|F32|Q4_0|Q5_0|Q8_0|Q5_1|Q4_K|Q5_K|Q6_K] [-p 512]
-//                   [-n 128] [-r 5] [-t threads] [--out file.jsonl]
+//                   [-n 128] [-r 5] [-t threads] [--kv paged|flat] [--out file.jsonl]
+// --kv (CUDA only): paged (default) keeps the K/V cache as fp16 pages served by the fused append, the split-K decode
+// and the tcgen05 prefill kernels; flat keeps the reference's fp32 cache and the fp32 CUDA-core attention.
 //
 // Prints the reference's table and, with --out, appends its JSON line per test with a "backend" field added.
 // Built by oracle/Makefile (target model-bench) where the reference tree is present.
@@ -75,7 +77,7 @@ DType type_of(const std::string& name) {
 }  // namespace
 
 int main(int argc, char** argv) {
-  std::string backend = "cuda", shape_name = "tinyllama", type_name = "F16", out_path;
+  std::string backend = "cuda", shape_name = "tinyllama", type_name = "F16", out_path, kv_mode = "paged";
   long p = 512, n = 128, r = 5;
   int threads = 0;
   for (int i = 1; i + 1 < argc; i += 2) {
@@ -88,6 +90,7 @@ int main(int argc, char** argv) {
     else if (a == "-r") r = std::stol(v);
     else if (a == "-t") threads = std::stoi(v);
     else if (a == "--out") out_path = v;
+    else if (a == "--kv") kv_mode = v;
     else {
       std::fprintf(stderr, "unknown argument %s\n", a.c_str());
       return 2;
@@ -102,8 +105,9 @@ int main(int argc, char** argv) {
     std::unique_ptr<Backend> be;
     std::string kernels;
     if (backend == "cuda") {
-      be = std::make_unique<cuda::CudaBackend>(0);
-      kernels = "cuda-sm100a";
+      if (kv_mode != "paged" && kv_mode != "flat") throw Error("unknown --kv '" + kv_mode + "' (paged or flat)");
+      be = std::make_unique<cuda::CudaBackend>(0, kv_mode == "paged");
+      kernels = "cuda-sm100a-kv-" + kv_mode;
       threads = 1;
     } else {
       pool = std::make_unique<ThreadPool>(threads);
