@@ -19,8 +19,13 @@ Workloads (the benchmark configurations 1-5, synthetic seeded inputs of their sh
   model_qgemm     the weight matmuls of a 512-token prefill of the Q4_0 model on the tcgen05 kind::i8 path.
                   Metric: tokens/s of the matmul part.
   model_fgemm     the same for the F16 model on the tcgen05 kind::f16 path (activations split into two fp16 terms).
-With N > 1 (torchrun, one rank per GPU, NCCL) every rank runs its own shard of the same per-GPU work ("weak"
-scaling: the sequences shard with no collective); value = all ranks' work / max-over-ranks device time.
+With N > 1 (torchrun, one rank per GPU, NCCL) the benchmark configurations' fixed total work is split over the ranks
+("strong" scaling): config 2's 64 sequences and config 3's 176 (sequence, layer) items evenly by sequence with no
+collective, config 5's sequences by LPT on KV length, config 4's one KV sequence in contiguous chunks with one NCCL
+all-gather of the (O, lse) partials and the LSE merge. --scaling weak gives every rank the whole configuration
+instead (a labelled extra). value = all ranks' work / max-over-ranks device time. Every run checks sampled rows of
+its own results (config 2), and the merged long-context result (config 4) on rank 0, against a float64 attention
+computed on the GPU from the same fp16 cache; a mismatch fails the run.
 
 --impl reference times nibble's own CPU attention (CpuBackend::attention with its AVX2/AVX-VNNI tier on a
 ThreadPool of all host threads, compiled from the reference sources into oracle/_ref) on a bounded sample of the
@@ -160,12 +165,62 @@ def fill_normal_(t, seed):
         flat[i:i + n].copy_(torch.randn(n, generator=g, device=t.device, dtype=torch.float32).to(flat.dtype))
 
 
+def gather_row_kv(kv, table_row, length, n_kv):
+    """K, V [length, n_kv, 64] of one row of a paged fp16 pool, as device tensors (pages gathered in order)."""
+    import torch
+    pool = kv.tensor().view(torch.float16).view(-1, 2, n_kv, 16, D)
+    npg = (length + 15) // 16
+    idx = torch.as_tensor(np.asarray(table_row[:npg], np.int64), device=pool.device)
+    pages = pool.index_select(0, idx)  # [npg, 2, KV, 16, D]
+    k = pages[:, 0].permute(0, 2, 1, 3).reshape(npg * 16, n_kv, D)[:length]
+    v = pages[:, 1].permute(0, 2, 1, 3).reshape(npg * 16, n_kv, D)[:length]
+    return k, v
+
+
+def attention_f64(q, k, v):
+    """Single-query causal attention in float64 on the GPU: q [H, D], k/v [L, KVH, D] -> [H, D] (the parity check
+    of the bench runs; the tests hold the kernels against the C oracle)."""
+    import torch
+    H, kvh = q.shape[0], k.shape[1]
+    g = H // kvh
+    kk = k.double().repeat_interleave(g, dim=1)  # [L, H, D]
+    vv = v.double().repeat_interleave(g, dim=1)
+    s = torch.einsum("hd,lhd->hl", q.double(), kk) / math.sqrt(q.shape[1])
+    p = torch.softmax(s, dim=1)
+    return torch.einsum("hl,lhd->hd", p, vv)
+
+
+def rel_err_per_head(got, ref):
+    """max over heads of max|got - ref| / max|ref| (the decode tolerance metric), got/ref [H, D]."""
+    import torch
+    g, r = got.double(), ref.double()
+    return float(((g - r).abs().amax(1) / r.abs().amax(1).clamp_min(1e-30)).max())
+
+
+def fail_together(bad, world, what):
+    """Every rank learns whether any rank's parity check failed, and all exit non-zero together."""
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        t = torch.tensor([1.0 if bad else 0.0], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        bad = t.item() > 0
+    if bad:
+        raise SystemExit(f"parity check failed: {what}")
+
+
 # ---------------------------------------------------------------- config 2: batched decode
 def decode_batched(args, world, rank, local):
     import torch
     import nibble_b200 as nb
     from nibble_b200.workloads import make_page_tables
-    seqs = args.seqs or SEQ2
+    total_seqs = args.seqs or SEQ2
+    if args.scaling == "weak":
+        seqs = total_seqs
+    else:
+        if total_seqs % world:
+            raise SystemExit(f"config 2: {total_seqs} sequences do not split evenly over {world} GPUs")
+        seqs = total_seqs // world
     rows = seqs * LAYERS2
     length = CTX2 + 1
     ctx = nb.Context(local)
@@ -221,6 +276,14 @@ def decode_batched(args, world, rank, local):
     ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
     kern_ms = statistics.mean(a.elapsed_time(b) for a, b in kev)
     ctx.check()
+    # parity of sampled rows of this rank's results: the last step's roped queries and outputs against a float64
+    # attention over the same fp16 pages (4097 keys, the appended token included)
+    worst = 0.0
+    for r in sorted({0, rows // 3, rows // 2, rows - 1}):
+        k, v = gather_row_kv(kv, table[r], length, KV2)
+        worst = max(worst, rel_err_per_head(out[r], attention_f64(q[r], k, v)))
+    fail_together(worst > 1e-4, world, f"config 2 rows: relative error {worst:.3e} > 1e-4")
+    worst = max_over_ranks(worst, world)
     e2e_ms = None
     if not args.no_e2e:
         # e2e through the C ABI: pinned host inputs -> nbl_write, kernels, nbl_read of the outputs, every step
@@ -242,11 +305,15 @@ def decode_batched(args, world, rank, local):
     traffic = TRAFFIC_DECODE_CFG2 * rows / (SEQ2 * LAYERS2)
     res = {
         "metric": "decode attn HBM GB/s", "value": world * step_bytes / (ms * 1e-3) / 1e9, "unit": "GB/s",
-        "ms_per_step": ms, "dtype": "fp16 KV, fp32 accumulate",
+        "ms_per_step": ms, "dtype": "fp16 KV, fp32 accumulate", "scaling": args.scaling,
+        "parity": {"check": "4 sampled rows per GPU vs float64 attention on the same fp16 pages",
+                   "max_rel_err_per_head": worst, "tolerance": 1e-4},
         "config": {"workload": "config 2: Llama-3.2-1B batched decode", "heads": f"{H2}q/{KV2}kv", "head_dim": D,
-                   "sequences_per_gpu": seqs, "layers": LAYERS2, "kv_tokens": length, "page_size": 16,
+                   "sequences_total": seqs * world, "sequences_per_gpu": seqs, "layers": LAYERS2, "kv_tokens": length,
+                   "page_size": 16,
                    "kv_bytes_per_step_per_gpu": kv_bytes, "algorithmic_bytes_per_step_per_gpu": step_bytes,
-                   "l2": "inputs (8.6 GB/GPU) larger than L2; no flush needed", "parallelism": f"sequence-sharded x{world}"},
+                   "l2": f"inputs ({kv_bytes / 1e9:.2f} GB/GPU) larger than L2; no flush needed",
+                   "parallelism": f"sequence-sharded x{world}"},
         "e2e": None if e2e_ms is None else {
             "value": world * step_bytes / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": e2e_ms,
             "h2d_bytes_per_step": int(q_in_h.numel() * 4 + k_in_h.numel() * 4 + v_in_h.numel() * 4),
@@ -279,7 +346,13 @@ def prefill(args, world, rank, local, steps=None, warmup=None):
     steps = steps or args.steps
     warmup = warmup or args.warmup
     seqs = args.prefill_seqs or SEQ3
-    items = seqs * LAYERS3
+    total_items = seqs * LAYERS3  # (sequence, layer) units
+    if args.scaling == "weak":
+        items = total_items
+    else:
+        if total_items % world:
+            raise SystemExit(f"config 3: {total_items} items do not split evenly over {world} GPUs")
+        items = total_items // world
     ctx = nb.Context(local)
     table, n_pages = make_page_tables([T3] * items, 16, shuffle_seed=200 + rank)
     kv = ctx.kv_pool(n_pages, KV3, dtype=nb.BF16)
@@ -329,9 +402,10 @@ def prefill(args, world, rank, local, steps=None, warmup=None):
     ach = flops / (kern_ms * 1e-3) / 1e12
     res = {
         "metric": "prefill attn TFLOP/s", "value": world * flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s",
-        "ms_per_step": ms, "kernel_ms": kern_ms, "dtype": "bf16 operands, fp32 accumulate",
+        "ms_per_step": ms, "kernel_ms": kern_ms, "dtype": "bf16 operands, fp32 accumulate", "scaling": args.scaling,
         "config": {"workload": "config 3: TinyLlama-1.1B causal prefill", "heads": f"{H3}q/{KV3}kv", "head_dim": D,
-                   "sequences_per_gpu": seqs, "tokens": T3, "layers": LAYERS3, "flops_per_step_per_gpu": flops},
+                   "items_total": items * world, "items_per_gpu": items, "tokens": T3, "layers": LAYERS3,
+                   "flops_per_step_per_gpu": flops},
         "roofline": {"kernel": "prefill_kernel", "bound": "tensor", "achieved": ach, "peak": bf16, "unit": "TFLOP/s",
                      "frac": ach / bf16, "peak_source": f"{src} bf16_tflops (burst)", "frac_of_sustained": ach / bf16_sus,
                      "frac_of_nominal_2250": ach / 2250.0, "traffic": TRAFFIC_PREFILL_CFG3 * items / (SEQ3 * LAYERS3)},
@@ -418,15 +492,57 @@ def decode_long(args, world, rank, local, steps, warmup):
     torch.cuda.synchronize()
     ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
     ctx.check()
-    if world > 1 and rank == 0:  # the merged result equals rank 0's own merge of the same gathered partials
-        assert torch.isfinite(merged).all()
+    # the exchange on its own: the all-gather and the merge, each timed with events on this stream
+    ag_ms = merge_ms = 0.0
+    if world > 1:
+        import torch.distributed as dist
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
+               torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        barrier(world)
+        for x0, x1, x2 in ev:
+            x0.record(main)
+            dist.all_gather_into_tensor(recv, send)
+            x1.record(main)
+            ctx.lse_merge_packed(recv, world, rows * H4, D, merged)
+            x2.record(main)
+        torch.cuda.synchronize()
+        ag_ms = max_over_ranks(statistics.mean(a.elapsed_time(b) for a, b, _ in ev), world)
+        merge_ms = max_over_ranks(statistics.mean(b.elapsed_time(c) for _, b, c in ev), world)
+    kern_max_ms = max_over_ranks(kern_ms, world)
     del graph  # released before the process group is destroyed
+    # parity: layer 0's merged result on rank 0 against a float64 attention over the whole 131073-token cache, whose
+    # chunks the ranks send to rank 0 (an all-gather of each rank's layer-0 K/V, outside the timed region)
+    k0, v0 = gather_row_kv(kv, table[0], my_len, KV4)
+    chunk = max(b_ - a_ for a_, b_ in kv_split(length, world))
+    mine = torch.zeros((2, chunk, KV4, D), dtype=torch.float16, device="cuda")
+    mine[0, :my_len], mine[1, :my_len] = k0, v0
+    if world > 1:
+        import torch.distributed as dist
+        every = torch.empty((world,) + tuple(mine.shape), dtype=torch.float16, device="cuda")
+        dist.all_gather_into_tensor(every, mine)
+    else:
+        every = mine[None]
+    err = 0.0
+    if rank == 0:
+        spans = kv_split(length, world)
+        kf = torch.cat([every[r, 0, :b_ - a_] for r, (a_, b_) in enumerate(spans)])
+        vf = torch.cat([every[r, 1, :b_ - a_] for r, (a_, b_) in enumerate(spans)])
+        got = (merged if world > 1 else out.view(rows * H4, D))[:H4]
+        err = rel_err_per_head(got, attention_f64(q[0], kf, vf))
+    fail_together(err > 1e-4, world, f"config 4 merged layer 0: relative error {err:.3e} > 1e-4")
+    del every, mine
     total_kv = rows * length * KV4 * D * 2 * 2
     my_kv = rows * my_len * KV4 * D * 2 * 2
     hbm, _, _, src = peaks()
     ach = (my_kv + 2 * rows * H4 * D * 4) / (kern_ms * 1e-3) / 1e9
+    parts = {"decode": kern_max_ms, "all_gather": ag_ms, "merge": merge_ms}
     res = {"metric": "decode attn HBM GB/s", "value": total_kv / (ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ms,
            "scaling": "strong",
+           "step_ms_breakdown": {**parts, "graph_step": ms, "decode_share": kern_max_ms / ms,
+                                 "limiter": "decode (HBM)" if kern_max_ms >= 0.5 * ms else
+                                            max(("all_gather", ag_ms), ("merge", merge_ms), key=lambda t: t[1])[0]},
+           "parity": {"check": "layer 0 merged over all ranks' chunks vs float64 attention on rank 0",
+                      "max_rel_err_per_head": err, "tolerance": 1e-4},
            "config": {"workload": "config 4: long-context decode, KV split over ranks", "kv_tokens": length,
                       "layers": LAYERS4, "heads": f"{H4}q/{KV4}kv", "kv_tokens_this_rank": my_len,
                       "exchange": "one NCCL all-gather of packed (O, lse) for all layers + LSE merge, the step "
@@ -783,6 +899,9 @@ def main():
     ap.add_argument("--seqs", type=int, default=0, help="config-2 sequences per GPU (default 64; smaller for profiling)")
     ap.add_argument("--prefill-seqs", type=int, default=0, help="config-3 sequences per GPU (default 8)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample length (0 skips it)")
+    ap.add_argument("--scaling", choices=["strong", "weak"], default="strong",
+                    help="strong: the configuration's total work split over the GPUs (default); weak: every GPU runs "
+                         "all of it")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -819,7 +938,7 @@ def main():
             res["model_decode_gemv_q4_0"] = model_gemv(args, world, rank, local, legs, 3, wtype="Q4_0")
             res["model_prefill_qgemm_q4_0"] = model_qgemm(args, world, rank, local, legs, 3)
             res["model_prefill_fgemm_f16"] = model_qgemm(args, world, rank, local, legs, 3, wtype="F16")
-    res.setdefault("scaling", "weak")
+    res.setdefault("scaling", args.scaling)
     res.update({"n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
                 "vs_baseline": None, "data": "synthetic (seeded N(0,1))"})
     res["gpu_launches"] = res.pop("gpu_launches_per_step", 2) * args.steps

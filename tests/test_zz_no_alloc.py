@@ -123,3 +123,33 @@ def test_static_decode_allocates_no_device_memory():
         np.testing.assert_allclose(lse.cpu().numpy(), ref_lse.cpu().numpy(), rtol=0, atol=2e-5)
     kv.close()
     ctx.close()
+
+
+def test_static_decode_uses_fewer_splits_when_the_library_plan_does_not_fit():
+    """2100 rows of 8 query heads over one KV head: the library's own plan wants two splits (8.7 MB of partials, more
+    than the 8 MiB array) to fill the last wave of CTAs; the static entry point runs the largest split count that
+    fits (one) and its results match the ordinary entry point's two-split results, on two calls in a row."""
+    import torch
+    import nibble_b200 as nb
+    ctx = nb.Context(0)
+    H, KV, rows, L = 8, 1, 2100, 1024
+    table, n_pages = make_page_tables([L] * rows, 16, shuffle_seed=11)
+    kv = ctx.kv_pool(n_pages, KV)
+    g = torch.Generator(device="cuda").manual_seed(12)
+    pool = kv.tensor().view(torch.float16)
+    pool.copy_(torch.randn(pool.shape, generator=g, device="cuda").half())
+    d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()  # noqa: E731
+    t_table, t_lens = d(table), d(np.full(rows, L, np.int32))
+    ref, ref_lse = torch.empty((rows, H, D), device="cuda"), torch.empty((rows, H), device="cuda")
+    for seed in (13, 14):
+        q = torch.randn((rows, H, D), device="cuda", generator=torch.Generator(device="cuda").manual_seed(seed))
+        out = torch.full((rows, H, D), float("nan"), device="cuda")
+        lse = torch.full((rows, H), float("nan"), device="cuda")
+        _static_decode(ctx, kv, q, t_table, t_lens, L, out, lse, 0)
+        ctx.attn_decode(kv, q, t_table, t_lens, L, ref, ref_lse)
+        ctx.check()
+        torch.cuda.synchronize()
+        assert max_rel_err_per_head(out.cpu().numpy(), ref.cpu().numpy()) <= 1e-4
+        np.testing.assert_allclose(lse.cpu().numpy(), ref_lse.cpu().numpy(), rtol=0, atol=2e-5)
+    kv.close()
+    ctx.close()
