@@ -984,6 +984,7 @@ int nbl_matmul_multi(nbl_ctx* ctx, const nbl_weight* const* ws, int32_t count, c
     }
     if (n == 0) return;
     use_device(ctx);
+    if (nbl::route_matmul_multi(ctx, ws, count, x, ys, n)) return;
     nbl::route_touch(ctx, x, n * ws[0]->w.ne0, nbl::Access::kRead);
     std::vector<float*> outs(static_cast<size_t>(count));
     for (int32_t i = 0; i < count; ++i) outs[i] = nbl::route_output(ctx, ys[i], n, ws[i]->w.ne1);

@@ -11,7 +11,9 @@
 //     add_bias / rope on those rows, and add_bias / rope on the query rows, are recorded rather than launched;
 //   * fusion: attention() then runs ONE bias + RoPE + fp16 append launch (rope_kv_append) writing the new rows
 //     into their pages and the roped queries, followed by the split-K decode kernel (n <= 8 rows) or the tcgen05
-//     prefill kernel (n > 8 rows, queries narrowed to fp16 by the same launch).
+//     prefill kernel (n > 8 rows, queries narrowed to fp16 by the same launch). For up to 8 rows with float
+//     weights the Q/K/V matmul_multi itself is recorded too, and attention() runs it as the projection GEMV with the
+//     bias + RoPE + page write in its epilogue (launch_gemv_qkv): projection, append and rotation in one launch.
 //
 // Anything else that touches a paged pair (a read, a copy into its rows, an op on the staged rows) first turns
 // it back into flat fp32 rows -- pages widened in place, staged rows written out with their deferred ops applied
@@ -28,6 +30,7 @@
 #include <string>
 #include <vector>
 
+#include "model_ops.h"
 #include "nbl_internal.h"
 
 namespace nbl {
@@ -194,6 +197,17 @@ struct Binding {
   }
 };
 
+// A recorded Q/K/V projection: matmul_multi({wq, wk, wv}, x, {q, K rows, V rows}, n) whose K/V outputs are the
+// staged rows of `b`; not yet launched.
+struct Projection {
+  bool on = false;
+  const Weight* w[3] = {nullptr, nullptr, nullptr};
+  const float* x = nullptr;
+  int64_t n = 0;
+  float* q = nullptr;
+  Binding* b = nullptr;
+};
+
 struct Route {
   float* stage = nullptr;  // [2 (K, V)][stage_rows][stage_width] fp32
   int64_t stage_rows = 0, stage_width = 0;
@@ -207,6 +221,7 @@ struct Route {
   cudaStream_t meta_stream = nullptr;
   std::vector<std::unique_ptr<Binding>> binds;
   Deferred pq;  // recorded bias / rope on a buffer that is not K/V (the query rows)
+  Projection proj;
 };
 
 namespace {
@@ -214,6 +229,22 @@ namespace {
 Route* route_of(nbl_ctx* ctx) { return ctx ? static_cast<Route*>(ctx->route) : nullptr; }
 
 void launch_check(const char* what) { check_cuda(cudaGetLastError(), what); }
+
+// A recorded projection, launched as the plain GEMV into its outputs (the query rows and the K/V staging).
+void flush_projection(nbl_ctx* ctx, Route& r) {
+  if (!r.proj.on) return;
+  Projection& p = r.proj;
+  float* ys[3] = {p.q, p.b->sk.p, p.b->sv.p};
+  launch_gemv_multi(ctx->stream, p.w, ys, 3, p.x, p.n, ctx->num_sms);
+  launch_check("projection launch");
+  p = Projection{};
+}
+
+bool range_overlaps(const void* p, int64_t floats, const void* q, int64_t q_floats) {
+  const auto a = reinterpret_cast<uintptr_t>(p), b = a + static_cast<uintptr_t>(floats) * sizeof(float);
+  const auto c = reinterpret_cast<uintptr_t>(q), d = c + static_cast<uintptr_t>(q_floats) * sizeof(float);
+  return a < d && c < b;
+}
 
 int grid_for(int64_t work, int num_sms) {
   return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((work + 255) / 256, int64_t(num_sms) * 8)));
@@ -224,8 +255,13 @@ void set_page_smem(const void* fn, int bytes) {
     check_cuda(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes), "page smem attribute");
 }
 
-// Runs the recorded bias / rotation of d on its rows (the same kernels nbl_add_bias / nbl_rope launch).
+// Runs the recorded bias / rotation of d on its rows (the same kernels nbl_add_bias / nbl_rope launch), after the
+// recorded projection that writes those rows.
 void apply(nbl_ctx* ctx, Deferred& d) {
+  Route& r = *route_of(ctx);
+  if ((d.bias || d.rope.on) && r.proj.on &&
+      (d.p == r.proj.q || d.p == r.proj.b->sk.p || d.p == r.proj.b->sv.p))
+    flush_projection(ctx, r);
   if (d.bias) {
     launch_add_bias(ctx->stream, d.p, d.bias, d.width, d.n);
     launch_check("add_bias launch");
@@ -255,6 +291,7 @@ void convert_rows_to_pages(nbl_ctx* ctx, Binding& b, const float* src_k, const f
 // Staged rows of one side: deferred ops applied, then narrowed into their pages.
 void flush_staged(nbl_ctx* ctx, Binding& b, Staged& s, bool is_v) {
   if (!s.on) return;
+  if (route_of(ctx)->proj.on && route_of(ctx)->proj.b == &b) flush_projection(ctx, *route_of(ctx));
   apply(ctx, s);
   convert_rows_to_pages(ctx, b, is_v ? nullptr : s.p, is_v ? s.p : nullptr, s.row0, s.row0, s.n);
   s = Staged{};
@@ -263,6 +300,7 @@ void flush_staged(nbl_ctx* ctx, Binding& b, Staged& s, bool is_v) {
 // Pages -> flat fp32 rows (K in place, V into v's block when write_v), then staged rows written over their rows.
 void demote(nbl_ctx* ctx, Binding& b, bool write_k = true, bool write_v = true) {
   if (!b.paged) return;
+  if (route_of(ctx)->proj.on && route_of(ctx)->proj.b == &b) flush_projection(ctx, *route_of(ctx));
   apply(ctx, b.sk);
   apply(ctx, b.sv);
   const int smem = b.kvh * 4096;
@@ -400,6 +438,7 @@ void route_destroy(nbl_ctx* ctx, bool restore_blocks) {
   if (!r) return;
   if (restore_blocks) {
     // every block back to flat fp32 rows and every recorded op applied, so the blocks stay valid without the route
+    flush_projection(ctx, *r);
     if (r->pq.on) apply(ctx, r->pq);
     while (!r->binds.empty()) unbind(ctx, *r, r->binds.back().get(), true, true);
     check_cuda(cudaStreamSynchronize(ctx->stream), "leaving the paged route");
@@ -457,6 +496,13 @@ void route_touch(nbl_ctx* ctx, const void* p, int64_t n_floats, Access access) {
   Route* r = route_of(ctx);
   if (!r || !p || n_floats <= 0) return;
   const auto a = reinterpret_cast<uintptr_t>(p), b = a + static_cast<uintptr_t>(n_floats) * sizeof(float);
+  if (r->proj.on) {
+    const Projection& pj = r->proj;
+    const bool same_q = p == pj.q && n_floats == pj.n * pj.w[0]->ne1;
+    const bool hits_q = range_overlaps(p, n_floats, pj.q, pj.n * pj.w[0]->ne1) && !(access == Access::kRecord && same_q);
+    const bool writes_x = access != Access::kRead && range_overlaps(p, n_floats, pj.x, pj.n * pj.w[0]->ne0);
+    if (hits_q || writes_x) flush_projection(ctx, *r);
+  }
   if (overlaps(r->pq, a, b)) {
     const auto q0 = reinterpret_cast<uintptr_t>(r->pq.p);
     const auto q1 = q0 + static_cast<uintptr_t>(r->pq.n * r->pq.width) * sizeof(float);
@@ -495,6 +541,41 @@ float* route_output(nbl_ctx* ctx, float* y, int64_t n, int64_t width) {
   return y;
 }
 
+bool route_matmul_multi(nbl_ctx* ctx, const nbl_weight* const* ws, int32_t count, const float* x,
+                        float* const* ys, int64_t n) {
+  Route* r = route_of(ctx);
+  if (!r || count != 3 || n < 1 || n > kDecodeRows) return false;
+  bool kv_is_v = true, vv_is_v = false;
+  Binding* b = binding_at(*r, ys[1], &kv_is_v);
+  if (!b || !b->paged || kv_is_v || binding_at(*r, ys[2], &vv_is_v) != b || !vv_is_v || binding_at(*r, ys[0]))
+    return false;
+  const Weight* w[3] = {&ws[0]->w, &ws[1]->w, &ws[2]->w};
+  if (w[0]->ne1 % kHd || w[1]->ne1 != b->kvw || !gemv_qkv_ok(w, x, n, w[0]->ne1 / kHd, b->kvh)) return false;
+  const int64_t off_k = ys[1] - b->k, off_v = ys[2] - b->v;
+  if (off_k != off_v || off_k % b->kvw || off_k / b->kvw + n > b->n_ctx || n > r->stage_rows) return false;
+  if (range_overlaps(x, n * w[0]->ne0, ys[0], n * w[0]->ne1)) return false;
+  // the same bookkeeping a plain matmul_multi does: earlier recorded work on these buffers runs or is dropped
+  route_touch(ctx, x, n * w[0]->ne0, Access::kRead);
+  route_touch(ctx, ys[0], n * w[0]->ne1, Access::kWrite);
+  flush_projection(ctx, *r);
+  for (bool is_v : {false, true}) {
+    Staged& st = is_v ? b->sv : b->sk;
+    if (st.on) flush_staged(ctx, *b, st, is_v);
+    st.on = true;
+    st.row0 = off_k / b->kvw;
+    st.n = n;
+    st.width = b->kvw;
+    st.p = r->stage + (is_v ? r->stage_rows * r->stage_width : 0);
+  }
+  r->proj.on = true;
+  for (int i = 0; i < 3; ++i) r->proj.w[i] = w[i];
+  r->proj.x = x;
+  r->proj.n = n;
+  r->proj.q = ys[0];
+  r->proj.b = b;
+  return true;
+}
+
 // Exactly the staged rows of one side, or null.
 static Staged* staged_exact(Binding& b, bool is_v, const float* x, int64_t n, int64_t width) {
   Staged& s = is_v ? b.sv : b.sk;
@@ -520,7 +601,7 @@ bool route_add_bias(nbl_ctx* ctx, float* x, const float* bias, int64_t width, in
     r->pq.bias = bias;
     return true;
   }
-  route_touch(ctx, x, n * width, Access::kReadWrite);
+  route_touch(ctx, x, n * width, Access::kRecord);
   if (r->pq.on) return false;
   r->pq = Deferred{};
   r->pq.on = true;
@@ -559,7 +640,7 @@ bool route_rope(nbl_ctx* ctx, float* x, int64_t n, int64_t heads, int64_t head_d
     r->pq.rope = std::move(rr);
     return true;
   }
-  route_touch(ctx, x, n * heads * head_dim, Access::kReadWrite);
+  route_touch(ctx, x, n * heads * head_dim, Access::kRecord);
   if (r->pq.on) return false;
   r->pq = Deferred{};
   r->pq.on = true;
@@ -603,7 +684,37 @@ bool route_attention(nbl_ctx* ctx, const float* q, const float* k, const float* 
   const int32_t* lens = r->meta + 2 * r->meta_rows;
   const int32_t* item = r->meta + 3 * r->meta_rows;
   float* qw = const_cast<float*>(q);  // the deferred rope(q) of the reference writes q in place
-  if (fused) {
+  const bool fused_proj = fused && decode && r->proj.on && r->proj.b == b && r->proj.q == q && r->proj.n == n &&
+                          r->proj.w[0]->ne1 == H * kHd;
+  if (fused_proj) {
+    // the recorded Q/K/V projection with bias + RoPE + fp16 page write in its epilogue: one launch
+    const nbl_rope_params rp = sk.rope.params();
+    const auto& tab = rope_table(ctx, rp, kHd, b->n_pages * kPage);
+    QkvEpilogue e;
+    e.bq = pq.bias;
+    e.bk = sk.bias;
+    e.bv = sv.bias;
+    e.q_out = qw;
+    e.pool = b->kv.pool;
+    e.n_pages = b->n_pages;
+    e.page_table = r->ident;
+    e.pt_stride = static_cast<int32_t>(r->ident_pages);
+    e.tab = tab.dev;
+    e.tab_pos = tab.n_pos;
+    e.pos0 = static_cast<int32_t>(pos0);
+    e.n_heads = static_cast<int32_t>(H);
+    e.n_kv_heads = b->kvh;
+    e.neox = rp.neox;
+    e.err = ctx->d_err;
+    if (!launch_gemv_qkv(ctx->stream, r->proj.w, r->proj.x, n, e, ctx->num_sms))
+      fail(NBL_E_CUDA, "attention: the recorded projection no longer qualifies for the fused launch");
+    launch_check("fused projection launch");
+    r->proj = Projection{};
+    sk = Staged{};
+    sv = Staged{};
+    pq = Deferred{};
+  } else if (fused) {
+    flush_projection(ctx, *r);
     const nbl_rope_params rp = sk.rope.params();
     const auto& tab = rope_table(ctx, rp, kHd, b->n_pages * kPage);
     launch_rope_kv_append(ctx->stream, &b->kv, q, sk.p, sv.p, NBL_F32, pq.bias, sk.bias, sv.bias,
@@ -641,6 +752,7 @@ bool route_attention(nbl_ctx* ctx, const float* q, const float* k, const float* 
 void route_free(nbl_ctx* ctx, void* p) {
   Route* r = route_of(ctx);
   if (!r || !p) return;
+  flush_projection(ctx, *r);  // its inputs or outputs may be in the block
   auto it = ctx->allocs.find(p);
   const int64_t floats = it == ctx->allocs.end() ? 0 : it->second.floats;
   const auto a = reinterpret_cast<uintptr_t>(p), e = a + static_cast<uintptr_t>(floats) * sizeof(float);
@@ -654,6 +766,10 @@ void route_free(nbl_ctx* ctx, void* p) {
 
 void route_flush_queries(nbl_ctx* ctx) {
   Route* r = route_of(ctx);
+  if (r && r->proj.on) {
+    check_cuda(cudaSetDevice(ctx->device), "cudaSetDevice");
+    flush_projection(ctx, *r);
+  }
   if (r && r->pq.on) {
     check_cuda(cudaSetDevice(ctx->device), "cudaSetDevice");
     apply(ctx, r->pq);

@@ -75,13 +75,83 @@ __device__ __forceinline__ void gemv_row(const GemvBatch& b, int64_t r, int64_t 
   wr += local * ne0;
 }
 
+// Fused Q/K/V epilogue: virtual row vr = 2u + h is member h of pair u. Pairs are numbered Q heads' first, then K's,
+// then V's, 32 per head: a Q or K pair is the RoPE pair i of its head (NeoX: elements i and i + 32; else 2i and
+// 2i + 1), a V pair is elements 2i and 2i + 1. Returns the weight-row number in the batch (Q rows, then K, then V).
+__device__ __forceinline__ int64_t qkv_row(int64_t vr, const QkvEpilogue& e, int& region, int& head, int& pair) {
+  const int64_t u = vr >> 1;
+  const int half = static_cast<int>(vr & 1);
+  const int64_t qu = int64_t(e.n_heads) * 32, ku = int64_t(e.n_kv_heads) * 32;
+  int64_t base, rel;
+  if (u < qu) {
+    region = 0;
+    rel = u;
+    base = 0;
+  } else if (u < qu + ku) {
+    region = 1;
+    rel = u - qu;
+    base = int64_t(e.n_heads) * 64;
+  } else {
+    region = 2;
+    rel = u - qu - ku;
+    base = (int64_t(e.n_heads) + e.n_kv_heads) * 64;
+  }
+  head = static_cast<int>(rel >> 5);
+  pair = static_cast<int>(rel & 31);
+  const int within = region != 2 && e.neox ? pair + 32 * half : 2 * pair + half;
+  return base + int64_t(head) * 64 + within;
+}
+
+// The epilogue of pair (ia, ib) of one head for activation row t: bias, rotation (Q, K), and the stores.
+__device__ __forceinline__ void qkv_store(const QkvEpilogue& e, int region, int head, int pair, int t, float a,
+                                          float b) {
+  const int ia = region != 2 && e.neox ? pair : 2 * pair;
+  const int ib = region != 2 && e.neox ? pair + 32 : 2 * pair + 1;
+  const float* bias = region == 0 ? e.bq : (region == 1 ? e.bk : e.bv);
+  const int64_t boff = int64_t(head) * 64;
+  if (bias) {
+    a = __fadd_rn(a, bias[boff + ia]);
+    b = __fadd_rn(b, bias[boff + ib]);
+  }
+  const int64_t pos = int64_t(e.pos0) + t;
+  if (region != 2) {
+    if (pos >= e.tab_pos) {
+      flag_error(e.err, kErrLength);
+      return;
+    }
+    rope_rotate(a, b, e.tab[pos * 32 + pair], a, b);
+  }
+  if (region == 0) {
+    float* q = e.q_out + int64_t(t) * e.n_heads * 64 + boff;
+    q[ia] = a;
+    q[ib] = b;
+    return;
+  }
+  if (pos >= int64_t(e.pt_stride) * 16) {
+    flag_error(e.err, kErrLength);
+    return;
+  }
+  const int32_t page = e.page_table[pos >> 4];
+  if (page < 0 || page >= e.n_pages) {
+    flag_error(e.err, kErrPageId);
+    return;
+  }
+  __half* slot = static_cast<__half*>(e.pool) +
+                 ((int64_t(page) * 2 + (region == 2 ? 1 : 0)) * e.n_kv_heads + head) * 1024 + (pos & 15) * 64;
+  slot[ia] = __float2half_rn(a);
+  slot[ib] = __float2half_rn(b);
+}
+
 // XREG (one activation row whose width fits one group, n_chunks <= 32 * kUnroll): each lane holds its slice of x --
 // the kVec elements of each of its chunks, at most 64 floats -- in registers, so only the weights pass through L1
 // (with x read through L1 as well, a 16-byte weight chunk costs 48 bytes of L1 traffic, and L1, not DRAM, limits
 // the large matrices).
-template <typename T, int NT, bool XREG>
+//
+// EPI: the fused Q/K/V projection (launch_gemv_qkv). A warp takes pairs of rows instead of rows (qkv_row) and, when
+// a pair's second row is done, lanes 0..NT-1 run the epilogue of one activation row each.
+template <typename T, int NT, bool XREG, bool EPI = false>
 __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvBatch b, const float* __restrict__ x,
-                                                            int64_t ne0) {
+                                                            int64_t ne0, const QkvEpilogue e) {
   static_assert(!XREG || NT == 1, "x in registers holds one activation row");
   constexpr int kVec = 16 / sizeof(T);  // weight elements per 16-byte load
   constexpr int kGroup = 32 * kUnroll;  // chunks per (row, group) item
@@ -96,14 +166,20 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvBatch b, c
   const int64_t n_warps = int64_t(gridDim.x) * (kGemvThreads / 32);
   const int64_t n_chunks = ne0 / kVec;
   const int64_t groups = (n_chunks + kGroup - 1) / kGroup;
-  int64_t r = int64_t(blockIdx.x) * (kGemvThreads / 32) + (threadIdx.x >> 5);
+  const int64_t warp_id = int64_t(blockIdx.x) * (kGemvThreads / 32) + (threadIdx.x >> 5);
+  // r: the warp's current (virtual) row. Plain: rows warp_id, warp_id + n_warps, ...; EPI: pairs warp_id,
+  // warp_id + n_warps, ..., each as its two virtual rows 2u, 2u + 1.
+  int64_t r = EPI ? 2 * warp_id : warp_id;
+  auto next_row = [&](int64_t v) -> int64_t { return EPI ? ((v & 1) ? v - 1 + 2 * n_warps : v + 1) : v + n_warps; };
+  int region = 0, head = 0, pair = 0;
+  auto phys = [&](int64_t v) -> int64_t { return EPI ? qkv_row(v, e, region, head, pair) : v; };
   int64_t g = 0;
   const T* wr = nullptr;
   float* ybase = nullptr;
   int64_t local = 0, rows_j = 0;
   uint4 raw[kUnroll];
   if (r < total) {
-    gemv_row<T>(b, r, ne0, wr, ybase, local, rows_j);
+    gemv_row<T>(b, phys(r), ne0, wr, ybase, local, rows_j);
     gemv_load<kUnroll>(raw, wr, 0, lane, n_chunks);  // independent of the previous kernel: before the wait
   }
   asm volatile("griddepcontrol.wait;" ::: "memory");  // x (the previous kernel's output) is visible after this
@@ -120,9 +196,11 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvBatch b, c
     }
   }
   float acc[NT];
+  float first = 0.f;  // EPI: lane t's sum of activation row t for the pair's first member
 #pragma unroll
   for (int t = 0; t < NT; ++t) acc[t] = 0.f;
   while (r < total) {
+    const int64_t r_cur = r;
     uint4 cur[kUnroll];
 #pragma unroll
     for (int u = 0; u < kUnroll; ++u) cur[u] = raw[u];
@@ -133,11 +211,12 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvBatch b, c
     const bool row_done = g + 1 == groups;
     int64_t r2 = r, g2 = g + 1;
     if (row_done) {
-      r2 = r + n_warps;
+      r2 = next_row(r);
       g2 = 0;
     }
+    int region_cur = region, head_cur = head, pair_cur = pair;
     if (r2 < total) {
-      if (row_done) gemv_row<T>(b, r2, ne0, wr, ybase, local, rows_j);
+      if (row_done) gemv_row<T>(b, phys(r2), ne0, wr, ybase, local, rows_j);
       gemv_load<kUnroll>(raw, wr, g2 * kGroup, lane, n_chunks);
     }
 #pragma unroll
@@ -177,13 +256,33 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvBatch b, c
       }
     }
     if (row_done) {
+      if constexpr (!EPI) {
 #pragma unroll
-      for (int t = 0; t < NT; ++t) {
-        float s = acc[t];
+        for (int t = 0; t < NT; ++t) {
+          float s = acc[t];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        if (lane == 0) y_cur[t * rows_cur + local_cur] = s;
-        acc[t] = 0.f;
+          for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+          if (lane == 0) y_cur[t * rows_cur + local_cur] = s;
+          acc[t] = 0.f;
+        }
+      } else {
+        (void)y_cur;
+        (void)local_cur;
+        (void)rows_cur;
+        float s_t = 0.f;  // lane t keeps activation row t's sum
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+          float s = acc[t];
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+          if (lane == t) s_t = s;
+          acc[t] = 0.f;
+        }
+        if ((r_cur & 1) == 0) {
+          first = s_t;  // the pair's first member; lanes >= NT hold nothing
+        } else if (lane < NT) {
+          qkv_store(e, region_cur, head_cur, pair_cur, lane, first, s_t);
+        }
       }
     }
     r = r2;
@@ -291,18 +390,19 @@ int elementwise_grid(int64_t count, int num_sms) {
 
 // Launched with programmatic stream serialization: the kernel may start while the previous one in the stream is
 // still running, and orders itself behind it with griddepcontrol.wait before reading x.
-template <typename T, int NT, bool XREG = false>
-void gemv_t(cudaStream_t st, const GemvBatch& b, const float* x, int64_t ne0, int num_sms) {
+template <typename T, int NT, bool XREG = false, bool EPI = false>
+void gemv_t(cudaStream_t st, const GemvBatch& b, const float* x, int64_t ne0, int num_sms,
+            const QkvEpilogue& e = QkvEpilogue{}) {
   // resident CTAs per SM for this instantiation (its register count decides: 3 or 4)
   static const int per_sm = [] {
     int n = 0;
-    check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_kernel<T, NT, XREG>, kGemvThreads, 0),
+    check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_kernel<T, NT, XREG, EPI>, kGemvThreads, 0),
                "gemv occupancy");
     return std::max(1, std::min(n, kGemvCtasPerSm));
   }();
   const int64_t warps_per_cta = kGemvThreads / 32;
-  const int64_t grid = std::min<int64_t>((b.row_end[b.count - 1] + warps_per_cta - 1) / warps_per_cta,
-                                         int64_t(num_sms) * per_sm);
+  const int64_t items = EPI ? b.row_end[b.count - 1] / 2 : b.row_end[b.count - 1];  // pairs for EPI
+  const int64_t grid = std::min<int64_t>((items + warps_per_cta - 1) / warps_per_cta, int64_t(num_sms) * per_sm);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(grid));
   cfg.blockDim = dim3(kGemvThreads);
@@ -312,22 +412,23 @@ void gemv_t(cudaStream_t st, const GemvBatch& b, const float* x, int64_t ne0, in
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  check_cuda(cudaLaunchKernelEx(&cfg, gemv_kernel<T, NT, XREG>, b, x, ne0), "gemv launch");
+  check_cuda(cudaLaunchKernelEx(&cfg, gemv_kernel<T, NT, XREG, EPI>, b, x, ne0, e), "gemv launch");
 }
 
-template <typename T>
-void gemv_dispatch(cudaStream_t st, const GemvBatch& b, const float* x, int64_t ne0, int64_t n, int sms) {
+template <typename T, bool EPI = false>
+void gemv_dispatch(cudaStream_t st, const GemvBatch& b, const float* x, int64_t ne0, int64_t n, int sms,
+                   const QkvEpilogue& e = QkvEpilogue{}) {
   constexpr int64_t kVec = 16 / sizeof(T);
-  if (n == 1 && ne0 / kVec <= 32 * kUnroll) return gemv_t<T, 1, true>(st, b, x, ne0, sms);
+  if (n == 1 && ne0 / kVec <= 32 * kUnroll) return gemv_t<T, 1, true, EPI>(st, b, x, ne0, sms, e);
   switch (n) {
-    case 1: return gemv_t<T, 1>(st, b, x, ne0, sms);
-    case 2: return gemv_t<T, 2>(st, b, x, ne0, sms);
-    case 3: return gemv_t<T, 3>(st, b, x, ne0, sms);
-    case 4: return gemv_t<T, 4>(st, b, x, ne0, sms);
-    case 5: return gemv_t<T, 5>(st, b, x, ne0, sms);
-    case 6: return gemv_t<T, 6>(st, b, x, ne0, sms);
-    case 7: return gemv_t<T, 7>(st, b, x, ne0, sms);
-    default: return gemv_t<T, 8>(st, b, x, ne0, sms);
+    case 1: return gemv_t<T, 1, false, EPI>(st, b, x, ne0, sms, e);
+    case 2: return gemv_t<T, 2, false, EPI>(st, b, x, ne0, sms, e);
+    case 3: return gemv_t<T, 3, false, EPI>(st, b, x, ne0, sms, e);
+    case 4: return gemv_t<T, 4, false, EPI>(st, b, x, ne0, sms, e);
+    case 5: return gemv_t<T, 5, false, EPI>(st, b, x, ne0, sms, e);
+    case 6: return gemv_t<T, 6, false, EPI>(st, b, x, ne0, sms, e);
+    case 7: return gemv_t<T, 7, false, EPI>(st, b, x, ne0, sms, e);
+    default: return gemv_t<T, 8, false, EPI>(st, b, x, ne0, sms, e);
   }
 }
 
@@ -383,6 +484,32 @@ void launch_gemv_multi(cudaStream_t st, const Weight* const* ws, float* const* y
     if (w0.dtype == NBL_F32) gemv_dispatch<float>(st, b, x + t0 * w0.ne0, w0.ne0, nt, num_sms);
     else gemv_dispatch<__half>(st, b, x + t0 * w0.ne0, w0.ne0, nt, num_sms);
   }
+}
+
+bool gemv_qkv_ok(const Weight* const* ws, const float* x, int64_t n, int64_t n_heads, int64_t n_kv_heads) {
+  const Weight &wq = *ws[0], &wk = *ws[1], &wv = *ws[2];
+  return n >= 1 && n <= kGemvMaxRows && wq.dtype == wk.dtype && wq.dtype == wv.dtype &&
+         (wq.dtype == NBL_F32 || wq.dtype == NBL_F16) && wq.ne0 == wk.ne0 && wq.ne0 == wv.ne0 &&
+         wq.ne1 == n_heads * 64 && wk.ne1 == n_kv_heads * 64 && wv.ne1 == wk.ne1 && n_heads > 0 && n_kv_heads > 0 &&
+         gemv_vector_ok(wq, x) && gemv_vector_ok(wk, x) && gemv_vector_ok(wv, x);
+}
+
+bool launch_gemv_qkv(cudaStream_t st, const Weight* const* ws, const float* x, int64_t n, const QkvEpilogue& e,
+                     int num_sms) {
+  const Weight& wq = *ws[0];
+  if (!gemv_qkv_ok(ws, x, n, e.n_heads, e.n_kv_heads)) return false;
+  GemvBatch b{};
+  b.count = 3;
+  int64_t rows = 0;
+  for (int i = 0; i < 3; ++i) {
+    b.w[i] = ws[i]->dev;
+    b.y[i] = nullptr;  // the epilogue stores instead
+    rows += ws[i]->ne1;
+    b.row_end[i] = rows;
+  }
+  if (wq.dtype == NBL_F32) gemv_dispatch<float, true>(st, b, x, wq.ne0, n, num_sms, e);
+  else gemv_dispatch<__half, true>(st, b, x, wq.ne0, n, num_sms, e);
+  return true;
 }
 
 void launch_gemv(cudaStream_t st, const Weight& w, const float* x, float* y, int64_t n, int num_sms) {

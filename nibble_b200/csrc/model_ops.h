@@ -57,6 +57,32 @@ struct QBatch {
   int count;
 };
 void launch_gemv(cudaStream_t st, const Weight& w, const float* x, float* y, int64_t n, int num_sms);
+// The epilogue of the fused Q/K/V projection (launch_gemv_qkv): what the reference does to the projections' outputs
+// before attention (src/model/transformer.cpp:171-198), applied to the dot products before they are stored.
+struct QkvEpilogue {
+  const float* bq = nullptr;  // biases (fp32, device) or null
+  const float* bk = nullptr;
+  const float* bv = nullptr;
+  float* q_out = nullptr;     // [n][n_heads * 64] fp32: rope(x . Wq^T + bq)
+  void* pool = nullptr;       // fp16 pages [n_pages][2][n_kv_heads][16][64]
+  int64_t n_pages = 0;
+  const int32_t* page_table = nullptr;  // the sequence's page ids (one row)
+  int32_t pt_stride = 0;
+  const float2* tab = nullptr;          // RoPE (cos, sin) [tab_pos][32]
+  int64_t tab_pos = 0;
+  int32_t pos0 = 0;                     // position of activation row 0 (row t is at pos0 + t)
+  int32_t n_heads = 0, n_kv_heads = 0;
+  int32_t neox = 0;
+  int* err = nullptr;
+};
+// y = x . W^T for the Q, K and V weights (ws[0..2], F32 or F16, head_dim 64) of n <= kGemvMaxRows activation rows, with
+// the epilogue fused: each warp computes both members of a RoPE pair (NeoX (i, i+32) or interleaved (2i, 2i+1)) of
+// one head, adds the bias, rotates Q and K at the row's position, writes q to e.q_out and K / V narrowed to fp16 (RNE)
+// into their page slots. The same arithmetic as the GEMV followed by nbl_rope_kv_append, bit for bit. False when the
+// weights do not qualify (caller runs the unfused path).
+bool gemv_qkv_ok(const Weight* const* ws, const float* x, int64_t n, int64_t n_heads, int64_t n_kv_heads);
+bool launch_gemv_qkv(cudaStream_t st, const Weight* const* ws, const float* x, int64_t n, const QkvEpilogue& e,
+                     int num_sms);
 // All weights share ne0; n rows of x. Weights of mixed dtype, or unaligned ones, run one scalar launch each.
 void launch_gemv_multi(cudaStream_t st, const Weight* const* ws, float* const* ys, int count, const float* x,
                        int64_t n, int num_sms);

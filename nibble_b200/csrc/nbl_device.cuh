@@ -18,6 +18,14 @@ __device__ __forceinline__ void flag_error(int* err, int bit) {
   if (err) atomicOr(err, bit);
 }
 
+// One RoPE rotation of the pair (a, b) by the angle whose (cos, sin) is cs: a' = a*c - b*s, b' = a*s + b*c, each
+// product and sum separately rounded (no contraction), which is what nibble's cpu::rope computes in float
+// (src/backend/cpu/ref_ops.cpp:166-185); every kernel that rotates uses this one function.
+__device__ __forceinline__ void rope_rotate(float a, float b, float2 cs, float& ra, float& rb) {
+  ra = __fsub_rn(__fmul_rn(a, cs.x), __fmul_rn(b, cs.y));
+  rb = __fadd_rn(__fmul_rn(a, cs.y), __fmul_rn(b, cs.x));
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

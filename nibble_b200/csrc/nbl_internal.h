@@ -143,7 +143,9 @@ void launch_lse_merge(cudaStream_t st, const float* part_o, const float* part_ls
                       int64_t o_stride = -1, int64_t lse_stride = -1);
 // backend_route.cu: the drop-in Backend ops served from fp16 pages (nbl_ctx_set_paged_kv). Every hook is a no-op
 // returning "not handled" while the route is off.
-enum class Access { kRead, kWrite, kReadWrite };  // kWrite: the op overwrites the whole range without reading it
+// kWrite: the op overwrites the whole range without reading it; kRecord: an elementwise op about to be recorded on
+// the range (a recorded projection writing exactly that range may stay recorded: the op will run after it).
+enum class Access { kRead, kWrite, kReadWrite, kRecord };
 void route_enable(nbl_ctx* ctx, bool on);
 // Ends the route; restore_blocks: paged blocks go back to flat fp32 rows first (not needed when the context is
 // being destroyed).
@@ -156,6 +158,10 @@ void route_reserve(nbl_ctx* ctx, int64_t n_ctx, int64_t n_heads, int64_t max_row
 void route_touch(nbl_ctx* ctx, const void* p, int64_t n_floats, Access access);
 // Where a matmul writes its n x width output meant for y (staging for rows of a paged K/V block; else y).
 float* route_output(nbl_ctx* ctx, float* y, int64_t n, int64_t width);
+// Backend::matmul_multi of {wq, wk, wv} into {q, K rows, V rows} of a paged pair for up to 8 rows with float weights:
+// recorded (true) so attention() can run it with the bias + RoPE + append in its epilogue; false: run it normally.
+bool route_matmul_multi(nbl_ctx* ctx, const nbl_weight* const* ws, int32_t count, const float* x, float* const* ys,
+                        int64_t n);
 // true: recorded or applied; false: the caller launches the ordinary kernel.
 bool route_add_bias(nbl_ctx* ctx, float* x, const float* bias, int64_t width, int64_t n);
 bool route_rope(nbl_ctx* ctx, float* x, int64_t n, int64_t heads, int64_t head_dim, int64_t pos0,

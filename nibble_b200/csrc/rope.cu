@@ -12,10 +12,7 @@
 namespace nbl {
 namespace {
 
-__device__ __forceinline__ void rotate(float a, float b, float2 cs, float& ra, float& rb) {
-  ra = __fsub_rn(__fmul_rn(a, cs.x), __fmul_rn(b, cs.y));
-  rb = __fadd_rn(__fmul_rn(a, cs.y), __fmul_rn(b, cs.x));
-}
+__device__ __forceinline__ void rotate(float a, float b, float2 cs, float& ra, float& rb) { rope_rotate(a, b, cs, ra, rb); }
 
 // Pair i of a head_dim-wide head: element offsets of its two members (NeoX: i, i+half; else 2i, 2i+1).
 __device__ __forceinline__ void pair_index(int i, int half, bool neox, int& ia, int& ib) {

@@ -96,6 +96,10 @@ int main(int argc, char** argv) {
       return 2;
     }
   }
+  if (r < 1 || p < 1 || n < 1) {
+    std::fprintf(stderr, "-p, -n and -r must be at least 1\n");
+    return 2;
+  }
   try {
     const nbl_test::Shape shape = shape_of(shape_name, type_of(type_name));
     nbl_test::Model m;

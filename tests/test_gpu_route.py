@@ -37,7 +37,7 @@ E = 128
 class Layer:
     """One attention layer's weights and buffers in one context, driven like run_chunk."""
 
-    def __init__(self, ctx, H, KV, bias, spec, w, n_ctx, max_rows):
+    def __init__(self, ctx, H, KV, bias, spec, w, n_ctx, max_rows, wdtype=np.float32):
         import torch
         self.ctx, self.H, self.KV, self.spec = ctx, H, KV, spec
         self.kvw = KV * D
@@ -47,7 +47,7 @@ class Layer:
         self.h = ctx.alloc(max_rows * E)
         self.q = ctx.alloc(max_rows * H * D)
         self.out = ctx.alloc(max_rows * H * D)
-        self.wq, self.wk, self.wv = (ctx.weight(a) for a in w[:3])
+        self.wq, self.wk, self.wv = (ctx.weight(a.astype(wdtype)) for a in w[:3])
         self.b = [ctx.weight(a) for a in w[3:]] if bias else None
         self.bdev = None
         if bias:
@@ -80,7 +80,7 @@ class Layer:
         return a
 
 
-def run_case(H, KV, bias, spec, seed, read_between):
+def run_case(H, KV, bias, spec, seed, read_between, wdtype=np.float32):
     import nibble_b200 as nb
     rng = np.random.default_rng(seed)
     w = [(rng.standard_normal((H * D, E)) / np.sqrt(E)).astype(np.float32),
@@ -92,8 +92,8 @@ def run_case(H, KV, bias, spec, seed, read_between):
     xs = [rng.standard_normal((n, E)).astype(np.float32) for n in CHUNKS]
     cp, cf = nb.Context(0), nb.Context(0)
     cp.set_paged_kv(True)
-    lp = Layer(cp, H, KV, bias, spec, w, N_CTX, 160)
-    lf = Layer(cf, H, KV, bias, spec, w, N_CTX, 160)
+    lp = Layer(cp, H, KV, bias, spec, w, N_CTX, 160, wdtype)
+    lf = Layer(cf, H, KV, bias, spec, w, N_CTX, 160, wdtype)
     outs, queries = [], []
     pos0 = 0
     for x in xs:
@@ -144,13 +144,16 @@ CASES = {
 }
 
 
+@pytest.mark.parametrize("wdtype", [np.float32, np.float16], ids=["F32", "F16"])
 @pytest.mark.parametrize("name", list(CASES))
-def test_transformer_layer_sequence_on_pages(name):
+def test_transformer_layer_sequence_on_pages(name, wdtype):
+    """Chunks of up to 8 rows run the recorded Q/K/V projection with bias + RoPE + page write in its epilogue (one
+    launch); longer chunks the projection, then one append launch. Both must reproduce the flat context's rows."""
     import nibble_b200 as nb
     H, KV, bias, sp = CASES[name]
     spec = nb.RopeSpec(**sp)
-    plain = run_case(H, KV, bias, spec, seed=len(name), read_between=False)
-    checked = run_case(H, KV, bias, spec, seed=len(name), read_between=True)
+    plain = run_case(H, KV, bias, spec, seed=len(name), read_between=False, wdtype=wdtype)
+    checked = run_case(H, KV, bias, spec, seed=len(name), read_between=True, wdtype=wdtype)
     for a, b in zip(plain, checked):  # converting the cache back and forth changes no bit
         assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
 
