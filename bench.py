@@ -21,8 +21,9 @@ Workloads (the benchmark configurations 1-5, synthetic seeded inputs of their sh
   model_fgemm     the same for the F16 model on the tcgen05 kind::f16 path (activations split into two fp16 terms).
 With N > 1 (torchrun, one rank per GPU, NCCL) the benchmark configurations' fixed total work is split over the ranks
 ("strong" scaling): config 2's 64 sequences and config 3's 176 (sequence, layer) items evenly by sequence with no
-collective, config 5's sequences by LPT on KV length, config 4's one KV sequence in contiguous chunks with one NCCL
-all-gather of the (O, lse) partials and the LSE merge. --scaling weak gives every rank the whole configuration
+collective, config 5's sequences by LPT on KV length, config 4's one KV sequence in contiguous chunks whose (O, lse)
+partials every rank stores straight into the other ranks' memory over NVLink before the LSE merge
+(nbl_lse_exchange_peers; --exchange nccl uses one NCCL all-gather instead). --scaling weak gives every rank the whole configuration
 instead (a labelled extra). value = all ranks' work / max-over-ranks device time. Every run checks sampled rows of
 its own results (config 2), and the merged long-context result (config 4) on rank 0, against a float64 attention
 computed on the GPU from the same fp16 cache; a mismatch fails the run.
@@ -446,15 +447,23 @@ def decode_long(args, world, rank, local, steps, warmup):
     t_table, lens = d(table), d(np.full(rows, my_len, np.int32))
     main = torch.cuda.current_stream()
 
+    px = ndist.PeerExchange(ctx, rows * H4, D) if world > 1 and args.exchange == "peer" else None
+
     def decode():
         ctx.attn_decode(kv, q, t_table, lens, max(1, my_len), out, lse)
+
+    def exchange():
+        if px is not None:  # partials stored straight into the peers' memory, merged once every flag is up
+            px.exchange(send, merged)
+        else:
+            import torch.distributed as dist
+            dist.all_gather_into_tensor(recv, send)
+            ctx.lse_merge_packed(recv, world, rows * H4, D, merged)
 
     def step():
         decode()
         if world > 1:
-            import torch.distributed as dist
-            dist.all_gather_into_tensor(recv, send)
-            ctx.lse_merge_packed(recv, world, rows * H4, D, merged)
+            exchange()
 
     for _ in range(warmup):
         step()
@@ -492,22 +501,17 @@ def decode_long(args, world, rank, local, steps, warmup):
     torch.cuda.synchronize()
     ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
     ctx.check()
-    # the exchange on its own: the all-gather and the merge, each timed with events on this stream
-    ag_ms = merge_ms = 0.0
+    # the exchange on its own (peer stores + flags + merge, or the NCCL all-gather + merge), timed with events
+    ex_ms = 0.0
     if world > 1:
-        import torch.distributed as dist
-        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
-               torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
         barrier(world)
-        for x0, x1, x2 in ev:
+        for x0, x1 in ev:
             x0.record(main)
-            dist.all_gather_into_tensor(recv, send)
+            exchange()
             x1.record(main)
-            ctx.lse_merge_packed(recv, world, rows * H4, D, merged)
-            x2.record(main)
         torch.cuda.synchronize()
-        ag_ms = max_over_ranks(statistics.mean(a.elapsed_time(b) for a, b, _ in ev), world)
-        merge_ms = max_over_ranks(statistics.mean(b.elapsed_time(c) for _, b, c in ev), world)
+        ex_ms = max_over_ranks(statistics.mean(a.elapsed_time(b) for a, b in ev), world)
     kern_max_ms = max_over_ranks(kern_ms, world)
     del graph  # released before the process group is destroyed
     # parity: layer 0's merged result on rank 0 against a float64 attention over the whole 131073-token cache, whose
@@ -531,22 +535,27 @@ def decode_long(args, world, rank, local, steps, warmup):
         err = rel_err_per_head(got, attention_f64(q[0], kf, vf))
     fail_together(err > 1e-4, world, f"config 4 merged layer 0: relative error {err:.3e} > 1e-4")
     del every, mine
+    if px is not None:
+        px.close()
     total_kv = rows * length * KV4 * D * 2 * 2
     my_kv = rows * my_len * KV4 * D * 2 * 2
     hbm, _, _, src = peaks()
     ach = (my_kv + 2 * rows * H4 * D * 4) / (kern_ms * 1e-3) / 1e9
-    parts = {"decode": kern_max_ms, "all_gather": ag_ms, "merge": merge_ms}
+    parts = {"decode": kern_max_ms, "exchange": ex_ms}
     res = {"metric": "decode attn HBM GB/s", "value": total_kv / (ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ms,
            "scaling": "strong",
            "step_ms_breakdown": {**parts, "graph_step": ms, "decode_share": kern_max_ms / ms,
-                                 "limiter": "decode (HBM)" if kern_max_ms >= 0.5 * ms else
-                                            max(("all_gather", ag_ms), ("merge", merge_ms), key=lambda t: t[1])[0]},
+                                 "exchange_kind": ("peer stores over NVLink + flags + merge (nbl_lse_exchange_peers)"
+                                                   if px is not None else "NCCL all-gather + nbl_lse_merge_packed"),
+                                 "limiter": "decode (HBM)" if kern_max_ms >= 0.5 * ms else "exchange"},
            "parity": {"check": "layer 0 merged over all ranks' chunks vs float64 attention on rank 0",
                       "max_rel_err_per_head": err, "tolerance": 1e-4},
            "config": {"workload": "config 4: long-context decode, KV split over ranks", "kv_tokens": length,
                       "layers": LAYERS4, "heads": f"{H4}q/{KV4}kv", "kv_tokens_this_rank": my_len,
-                      "exchange": "one NCCL all-gather of packed (O, lse) for all layers + LSE merge, the step "
-                                  "replayed as one CUDA graph" if world > 1 else "none (one GPU; CUDA graph)"},
+                      "exchange": ("packed (O, lse) of all layers stored into every peer's memory, flags, LSE merge"
+                                   if px is not None else "one NCCL all-gather of packed (O, lse) for all layers + "
+                                   "LSE merge") + ", the step replayed as one CUDA graph" if world > 1 else
+                                  "none (one GPU; CUDA graph)"},
            "roofline": {"kernel": "decode_kernel (+ lse_merge)", "bound": "hbm", "achieved": ach, "peak": hbm,
                         "unit": "GB/s", "frac": ach / hbm, "peak_source": src, "kernel_ms": kern_ms}}
     kv.close()
@@ -899,6 +908,8 @@ def main():
     ap.add_argument("--seqs", type=int, default=0, help="config-2 sequences per GPU (default 64; smaller for profiling)")
     ap.add_argument("--prefill-seqs", type=int, default=0, help="config-3 sequences per GPU (default 8)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample length (0 skips it)")
+    ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
+                    help="config 4 at N > 1: partials stored into the peers' memory (default) or an NCCL all-gather")
     ap.add_argument("--scaling", choices=["strong", "weak"], default="strong",
                     help="strong: the configuration's total work split over the GPUs (default); weak: every GPU runs "
                          "all of it")

@@ -286,6 +286,21 @@ NBL_API int nbl_lse_merge(nbl_ctx* ctx, const float* part_o, const float* part_l
 NBL_API int nbl_lse_merge_packed(nbl_ctx* ctx, const float* packed, int32_t n_parts, int64_t rows, int32_t head_dim,
                                  float* out, float* lse);
 
+/* The long-context exchange without a collective library: every rank's (O, lse) partials cross NVLink as plain stores
+ * into the other ranks' memory, and each rank merges once all have arrived (nbl_lse_merge_packed's arithmetic).
+ * send: this rank's packed partials [rows * head_dim outputs | rows lse] (device). recv_bufs[p] / flag_bufs[p]: rank
+ * p's receive buffer ([2][world][rows * (head_dim + 1)] floats) and flag words ([world] uint32, zero before the first
+ * call), as device addresses valid in this process (peer memory mapped by the caller, e.g. a symmetric-memory
+ * allocation); sync: two uint32 of this rank's device memory, zero before the first call. Two launches on the
+ * context's stream: the push (stores, then per-rank release flags at system scope) and the merge (waits on its own
+ * flags with acquire loads, bounded by the library's 2 s wait limit: a rank that never arrives ends the merge with
+ * NBL_E_DEVICE at nbl_ctx_check and no output). Every rank must make the same sequence of calls. world <= 8. No
+ * reference counterpart (the reference never splits a softmax across devices); replaces the all-gather +
+ * nbl_lse_merge_packed pair for GPUs that reach each other's memory (NVLink / NVSwitch). */
+NBL_API int nbl_lse_exchange_peers(nbl_ctx* ctx, const float* send, int64_t rows, int32_t head_dim, int32_t world,
+                                   int32_t rank, void* const* recv_bufs, void* const* flag_bufs, uint32_t* sync,
+                                   float* out, float* lse);
+
 /* ---- diagnostics ---- */
 /* Runs the library's bounded device wait (the routine every TMA / tensor-core completion wait uses) in a one-thread
  * kernel against an mbarrier that nothing arrives on, with a limit of limit_ns (0 < limit_ns <= 1e9): the wait gives

@@ -20,7 +20,7 @@ CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libnibble_cuda.so")
 STAMP = LIB + ".stamp"
 SOURCES = ["api.cu", "rope.cu", "attn_f32.cu", "decode.cu", "decode_static.cu", "prefill.cu", "model_ops.cu", "quant_ops.cu", "quant_gemm.cu", "quant_blocks.cu", "f32_gemm.cu", "selftest.cu", "backend_route.cu"]
-HEADERS = ["nbl_device.cuh", "nbl_internal.h", "nbl_errors.h", "model_ops.h", "quant_common.cuh"]
+HEADERS = ["qkv_epilogue.cuh", "nbl_device.cuh", "nbl_internal.h", "nbl_errors.h", "model_ops.h", "quant_common.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
          "--expt-relaxed-constexpr", "-I" + os.path.join(ROOT, "include")]

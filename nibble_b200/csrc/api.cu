@@ -147,6 +147,22 @@ using nbl::device_alloc;
 using nbl::ensure_scratch;
 using nbl::rope_table;
 
+void* nbl::qgemv_scratch(nbl_ctx* ctx, int64_t ne0) {
+  const size_t need = nbl::gemv_q_act_bytes(ne0);
+  if (ctx->qgemv_act_bytes < need) {
+    nbl::route_flush_projection(ctx);  // a recorded projection reads the old buffer
+    if (ctx->qgemv_act) {
+      nbl::check_cuda(cudaStreamSynchronize(ctx->stream), "quant gemv scratch");
+      cudaFree(ctx->qgemv_act);
+      ctx->qgemv_act = nullptr;
+      ctx->qgemv_act_bytes = 0;
+    }
+    ctx->qgemv_act = device_alloc(need, "quant gemv activations");
+    ctx->qgemv_act_bytes = need;
+  }
+  return ctx->qgemv_act;
+}
+
 namespace {
 
 bool is_dtype(int32_t d) { return d == NBL_F32 || d == NBL_F16 || d == NBL_BF16; }
@@ -279,18 +295,7 @@ void quant_matmul(nbl_ctx* ctx, const nbl_weight* const* cws, float* const* ys, 
   const nbl::Weight* ws[nbl::kMaxMulti];
   for (int i = 0; i < count; ++i) ws[i] = &cws[i]->w;
   if (n <= nbl::kGemvMaxRows) {
-    const size_t need = nbl::gemv_q_act_bytes(ws[0]->ne0);
-    if (ctx->qgemv_act_bytes < need) {
-      if (ctx->qgemv_act) {
-        nbl::check_cuda(cudaStreamSynchronize(ctx->stream), "quant gemv scratch");
-        cudaFree(ctx->qgemv_act);
-        ctx->qgemv_act = nullptr;
-        ctx->qgemv_act_bytes = 0;
-      }
-      ctx->qgemv_act = device_alloc(need, "quant gemv activations");
-      ctx->qgemv_act_bytes = need;
-    }
-    nbl::launch_gemv_q(ctx->stream, ws, ys, count, x, n, ctx->qgemv_act, ctx->num_sms);
+    nbl::launch_gemv_q(ctx->stream, ws, ys, count, x, n, nbl::qgemv_scratch(ctx, ws[0]->ne0), ctx->num_sms);
     return;
   }
   for (int i = 0; i < count; ++i) nbl::prepare_qgemm(ctx->stream, const_cast<nbl_weight*>(cws[i])->w, ctx->num_sms);
@@ -824,6 +829,29 @@ int nbl_lse_merge_packed(nbl_ctx* ctx, const float* packed, int32_t n_parts, int
     const int64_t part = rows * (int64_t(head_dim) + 1);  // [rows * head_dim outputs | rows lse] per part
     nbl::launch_lse_merge(ctx->stream, packed, packed + rows * head_dim, n_parts, rows, head_dim, out, lse, part,
                           part);
+  });
+}
+
+int nbl_lse_exchange_peers(nbl_ctx* ctx, const float* send, int64_t rows, int32_t head_dim, int32_t world,
+                           int32_t rank, void* const* recv_bufs, void* const* flag_bufs, uint32_t* sync, float* out,
+                           float* lse) {
+  return guarded([&] {
+    require(ctx && send && recv_bufs && flag_bufs && sync && out, "lse_exchange_peers: NULL argument");
+    require(world >= 1 && world <= nbl::kMaxPeers && rank >= 0 && rank < world,
+            "lse_exchange_peers: world must be 1.." + std::to_string(nbl::kMaxPeers) + " and rank in [0, world)");
+    require(rows >= 0 && head_dim > 0 && head_dim <= 256, "lse_exchange_peers: bad size");
+    float* recv[nbl::kMaxPeers];
+    uint32_t* flags[nbl::kMaxPeers];
+    for (int p = 0; p < world; ++p) {
+      require(recv_bufs[p] && flag_bufs[p], "lse_exchange_peers: NULL peer buffer");
+      recv[p] = static_cast<float*>(recv_bufs[p]);
+      flags[p] = static_cast<uint32_t*>(flag_bufs[p]);
+    }
+    if (rows == 0) return;
+    use_device(ctx);
+    nbl::route_flush_queries(ctx);
+    nbl::launch_lse_exchange_peers(ctx->stream, send, rows, head_dim, world, rank, recv, flags, sync, out, lse,
+                                   ctx->d_err, ctx->num_sms);
   });
 }
 

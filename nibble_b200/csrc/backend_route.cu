@@ -11,8 +11,8 @@
 //     add_bias / rope on those rows, and add_bias / rope on the query rows, are recorded rather than launched;
 //   * fusion: attention() then runs ONE bias + RoPE + fp16 append launch (rope_kv_append) writing the new rows
 //     into their pages and the roped queries, followed by the split-K decode kernel (n <= 8 rows) or the tcgen05
-//     prefill kernel (n > 8 rows, queries narrowed to fp16 by the same launch). For up to 8 rows with float
-//     weights the Q/K/V matmul_multi itself is recorded too, and attention() runs it as the projection GEMV with the
+//     prefill kernel (n > 8 rows, queries narrowed to fp16 by the same launch). For up to 8 rows with float or
+//     Q4_0 / Q5_0 / Q8_0 weights the Q/K/V matmul_multi itself is recorded too, and attention() runs it as the projection GEMV with the
 //     bias + RoPE + page write in its epilogue (launch_gemv_qkv): projection, append and rotation in one launch.
 //
 // Anything else that touches a paged pair (a read, a copy into its rows, an op on the staged rows) first turns
@@ -206,6 +206,7 @@ struct Projection {
   int64_t n = 0;
   float* q = nullptr;
   Binding* b = nullptr;
+  void* act = nullptr;  // quantized weights: the activation scratch of the quantized GEMV
 };
 
 struct Route {
@@ -235,7 +236,8 @@ void flush_projection(nbl_ctx* ctx, Route& r) {
   if (!r.proj.on) return;
   Projection& p = r.proj;
   float* ys[3] = {p.q, p.b->sk.p, p.b->sv.p};
-  launch_gemv_multi(ctx->stream, p.w, ys, 3, p.x, p.n, ctx->num_sms);
+  if (is_quant(p.w[0]->dtype)) launch_gemv_q(ctx->stream, p.w, ys, 3, p.x, p.n, p.act, ctx->num_sms);
+  else launch_gemv_multi(ctx->stream, p.w, ys, 3, p.x, p.n, ctx->num_sms);
   launch_check("projection launch");
   p = Projection{};
 }
@@ -550,7 +552,9 @@ bool route_matmul_multi(nbl_ctx* ctx, const nbl_weight* const* ws, int32_t count
   if (!b || !b->paged || kv_is_v || binding_at(*r, ys[2], &vv_is_v) != b || !vv_is_v || binding_at(*r, ys[0]))
     return false;
   const Weight* w[3] = {&ws[0]->w, &ws[1]->w, &ws[2]->w};
-  if (w[0]->ne1 % kHd || w[1]->ne1 != b->kvw || !gemv_qkv_ok(w, x, n, w[0]->ne1 / kHd, b->kvh)) return false;
+  if (w[0]->ne1 % kHd || w[1]->ne1 != b->kvw) return false;
+  const bool quant = gemv_q_qkv_ok(w, n, w[0]->ne1 / kHd, b->kvh);
+  if (!quant && !gemv_qkv_ok(w, x, n, w[0]->ne1 / kHd, b->kvh)) return false;
   const int64_t off_k = ys[1] - b->k, off_v = ys[2] - b->v;
   if (off_k != off_v || off_k % b->kvw || off_k / b->kvw + n > b->n_ctx || n > r->stage_rows) return false;
   if (range_overlaps(x, n * w[0]->ne0, ys[0], n * w[0]->ne1)) return false;
@@ -558,6 +562,7 @@ bool route_matmul_multi(nbl_ctx* ctx, const nbl_weight* const* ws, int32_t count
   route_touch(ctx, x, n * w[0]->ne0, Access::kRead);
   route_touch(ctx, ys[0], n * w[0]->ne1, Access::kWrite);
   flush_projection(ctx, *r);
+  void* act = quant ? qgemv_scratch(ctx, w[0]->ne0) : nullptr;  // sized as the plain quantized GEMV would
   for (bool is_v : {false, true}) {
     Staged& st = is_v ? b->sv : b->sk;
     if (st.on) flush_staged(ctx, *b, st, is_v);
@@ -573,6 +578,7 @@ bool route_matmul_multi(nbl_ctx* ctx, const nbl_weight* const* ws, int32_t count
   r->proj.n = n;
   r->proj.q = ys[0];
   r->proj.b = b;
+  r->proj.act = act;
   return true;
 }
 
@@ -706,7 +712,10 @@ bool route_attention(nbl_ctx* ctx, const float* q, const float* k, const float* 
     e.n_kv_heads = b->kvh;
     e.neox = rp.neox;
     e.err = ctx->d_err;
-    if (!launch_gemv_qkv(ctx->stream, r->proj.w, r->proj.x, n, e, ctx->num_sms))
+    const bool launched = is_quant(r->proj.w[0]->dtype)
+                              ? launch_gemv_q_qkv(ctx->stream, r->proj.w, r->proj.x, n, r->proj.act, e, ctx->num_sms)
+                              : launch_gemv_qkv(ctx->stream, r->proj.w, r->proj.x, n, e, ctx->num_sms);
+    if (!launched)
       fail(NBL_E_CUDA, "attention: the recorded projection no longer qualifies for the fused launch");
     launch_check("fused projection launch");
     r->proj = Projection{};
@@ -762,6 +771,11 @@ void route_free(nbl_ctx* ctx, void* p) {
     if (b->k == p || b->v == p) hit = b.get();
   // the surviving block of the pair keeps its rows as flat fp32 (the freed one's are not written)
   if (hit) unbind(ctx, *r, hit, hit->k != p, hit->v != p);
+}
+
+void route_flush_projection(nbl_ctx* ctx) {
+  Route* r = route_of(ctx);
+  if (r && r->proj.on) flush_projection(ctx, *r);
 }
 
 void route_flush_queries(nbl_ctx* ctx) {

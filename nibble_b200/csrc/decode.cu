@@ -326,9 +326,89 @@ __global__ void __launch_bounds__(kWarps * 32, kCtasPerSm)
 
 // One CTA per group of rows; a thread per head dimension. part_o [n_parts, rows, D], part_lse [n_parts, rows].
 // Part p's outputs start at part_o + p * o_stride ([rows, head_dim]) and its lse at part_lse + p * lse_stride.
+__device__ __forceinline__ void lse_merge_rows(const float* __restrict__ part_o, int64_t o_stride,
+                                               const float* __restrict__ part_lse, int64_t lse_stride, int n_parts,
+                                               int64_t rows, int head_dim, float* __restrict__ out,
+                                               float* __restrict__ lse);
 __global__ void lse_merge_kernel(const float* __restrict__ part_o, int64_t o_stride, const float* __restrict__ part_lse,
                                  int64_t lse_stride, int n_parts, int64_t rows, int head_dim, float* __restrict__ out,
                                  float* __restrict__ lse) {
+  lse_merge_rows(part_o, o_stride, part_lse, lse_stride, n_parts, rows, head_dim, out, lse);
+}
+
+// ---- the long-context exchange over peer memory (nbl_lse_exchange_peers)
+// Every rank's receive buffer holds [2 (epoch parity)][world][part] floats, a part being one rank's packed
+// [rows * D outputs | rows lse]; every rank's flag words hold [world] epochs. Rank r's push writes its part into
+// slot r of the epoch's half of every rank's buffer, then -- once every CTA's stores are fenced -- stores the epoch
+// into word r of every rank's flags (release, system scope). A rank merges after it has seen the epoch (acquire)
+// in all words. Two halves suffice: a rank pushes epoch e + 1 only after its own merge of e, which needed every
+// rank's push of e, so no rank can overwrite a half another rank may still be reading.
+struct PeerBufs {
+  float* recv[kMaxPeers];
+  uint32_t* flags[kMaxPeers];
+};
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// sync[0] = this rank's last pushed epoch, sync[1] = CTAs done with the current push (back to 0 after it).
+__global__ void peer_push_kernel(const float* __restrict__ send, int64_t part, PeerBufs px, int world, int rank,
+                                 uint32_t* sync) {
+  const uint32_t e = sync[0] + 1u;  // read by every CTA before the last one (which waits for all) updates it
+  const int64_t off = (int64_t(e & 1u) * world + rank) * part;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < part; i += int64_t(gridDim.x) * blockDim.x) {
+    const float v = send[i];
+    for (int p = 0; p < world; ++p) px.recv[p][off + i] = v;
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const uint32_t prev = atomicAdd(&sync[1], 1u);
+    if (prev == gridDim.x - 1) {  // the last CTA: every part store of this rank is fenced
+      __threadfence_system();
+      sync[0] = e;
+      sync[1] = 0u;
+      for (int p = 0; p < world; ++p) st_release_sys(px.flags[p] + rank, e);
+    }
+  }
+}
+
+// Waits (bounded by kWaitLimitNs of %globaltimer; on timeout flags kErrTimeout and writes nothing) until every
+// rank's epoch has arrived in this rank's flags, then merges the world parts of that epoch.
+__global__ void peer_merge_kernel(const float* __restrict__ recv, const uint32_t* flags, const uint32_t* sync,
+                                  int world, int64_t part, int64_t rows, int head_dim, float* __restrict__ out,
+                                  float* __restrict__ lse, int* err) {
+  __shared__ int ok;
+  const uint32_t e = sync[0];
+  if (threadIdx.x == 0 && threadIdx.y == 0) {
+    ok = 1;
+    const uint64_t t0 = globaltimer_ns();
+    for (int q = 0; q < world && ok; ++q) {
+      while (static_cast<int32_t>(ld_acquire_sys(flags + q) - e) < 0) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs || (*reinterpret_cast<volatile int*>(err) & kErrTimeout)) {
+          flag_error(err, kErrTimeout);
+          ok = 0;
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (!ok) return;
+  const float* base = recv + int64_t(e & 1u) * world * part;
+  lse_merge_rows(base, part, base + rows * head_dim, part, world, rows, head_dim, out, lse);
+}
+
+__device__ __forceinline__ void lse_merge_rows(const float* __restrict__ part_o, int64_t o_stride,
+                                               const float* __restrict__ part_lse, int64_t lse_stride, int n_parts,
+                                               int64_t rows, int head_dim, float* __restrict__ out,
+                                               float* __restrict__ lse) {
   const int d = threadIdx.x;
   for (int64_t r = blockIdx.x * int64_t(blockDim.y) + threadIdx.y; r < rows; r += int64_t(gridDim.x) * blockDim.y) {
     float mx = -INFINITY;
@@ -476,6 +556,26 @@ void launch_decode(cudaStream_t st, const nbl_kv* kv, const float* q, const int3
   check_cuda(cudaGetLastError(), "decode launch");
   if (plan.n_splits > 1)
     launch_lse_merge(st, a.part_o, a.part_lse, plan.n_splits, int64_t(n_rows) * n_heads, kD, out, lse);
+}
+
+void launch_lse_exchange_peers(cudaStream_t st, const float* send, int64_t rows, int head_dim, int world, int rank,
+                               float* const* recv, uint32_t* const* flags, uint32_t* sync, float* out, float* lse,
+                               int* err, int num_sms) {
+  PeerBufs px{};
+  for (int p = 0; p < world; ++p) {
+    px.recv[p] = recv[p];
+    px.flags[p] = flags[p];
+  }
+  const int64_t part = rows * (int64_t(head_dim) + 1);
+  const int push_grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((part + 255) / 256, num_sms)));
+  peer_push_kernel<<<push_grid, 256, 0, st>>>(send, part, px, world, rank, sync);
+  check_cuda(cudaGetLastError(), "peer push launch");
+  const int tx = head_dim <= 32 ? 32 : (head_dim <= 64 ? 64 : (head_dim <= 128 ? 128 : 256));
+  const int ty = std::max(1, 256 / tx);
+  const int64_t blocks = std::min<int64_t>((rows + ty - 1) / ty, int64_t(num_sms) * 4);
+  peer_merge_kernel<<<static_cast<unsigned>(std::max<int64_t>(blocks, 1)), dim3(tx, ty), 0, st>>>(
+      recv[rank], flags[rank], sync, world, part, rows, head_dim, out, lse, err);
+  check_cuda(cudaGetLastError(), "peer merge launch");
 }
 
 void launch_lse_merge(cudaStream_t st, const float* part_o, const float* part_lse, int n_parts, int64_t rows,

@@ -109,6 +109,13 @@ size_t gemv_q_act_bytes(int64_t ne0);
 void launch_gemv_q(cudaStream_t st, const Weight* const* ws, float* const* ys, int count, const float* x, int64_t n,
                    void* act, int num_sms);
 void launch_embed_q(cudaStream_t st, const Weight& table, const int32_t* ids, int64_t n, float* out);
+// The fused Q/K/V projection (see launch_gemv_qkv) for Q4_0 / Q5_0 / Q8_0 weights: x quantized into act, then the
+// quantized GEMV with the bias + RoPE + fp16 page write in its epilogue; block dots bit-identical to launch_gemv_q.
+// The context's scratch for the quantized GEMV's activations (grown to gemv_q_act_bytes(ne0) on first need).
+void* qgemv_scratch(nbl_ctx* ctx, int64_t ne0);
+bool gemv_q_qkv_ok(const Weight* const* ws, int64_t n, int64_t n_heads, int64_t n_kv_heads);
+bool launch_gemv_q_qkv(cudaStream_t st, const Weight* const* ws, const float* x, int64_t n, void* act,
+                       const QkvEpilogue& e, int num_sms);
 // quant_gemm.cu: the same matmul for more than kGemvMaxRows activation rows, on the tensor cores. prepare_qgemm
 // makes a weight's operands (once); launch_qgemm quantizes x into `act` (qgemm_act_bytes) and runs weights of one
 // quantized type sharing ne0 (count <= kMaxMulti, each prepared).

@@ -170,8 +170,16 @@ bool route_attention(nbl_ctx* ctx, const float* q, const float* k, const float* 
                      int64_t pos0, int64_t n_heads, int64_t n_kv_heads, int64_t head_dim);
 // Before Backend::free of p (the surviving block of a paged pair is turned back into flat rows).
 void route_free(nbl_ctx* ctx, void* p);
+// Launches a recorded Q/K/V projection (before the scratch it reads is replaced).
+void route_flush_projection(nbl_ctx* ctx);
 // Applies recorded query ops (before entry points outside the Backend set read arbitrary device memory).
 void route_flush_queries(nbl_ctx* ctx);
+
+// decode.cu: the long-context exchange over peer memory (nbl_lse_exchange_peers); at most kMaxPeers ranks.
+constexpr int kMaxPeers = 8;
+void launch_lse_exchange_peers(cudaStream_t st, const float* send, int64_t rows, int head_dim, int world, int rank,
+                               float* const* recv, uint32_t* const* flags, uint32_t* sync, float* out, float* lse,
+                               int* err, int num_sms);
 
 // prefill.cu
 void launch_prefill(cudaStream_t st, const nbl_kv* kv, const void* q, int64_t n_q_rows, const int32_t* q_start,

@@ -20,6 +20,7 @@
 
 #include "model_ops.h"
 #include "nbl_device.cuh"
+#include "qkv_epilogue.cuh"
 #include "quant_common.cuh"
 
 namespace nbl {
@@ -95,9 +96,12 @@ __global__ void quantize_rows_kernel(const float* __restrict__ x, int8_t* __rest
 // each round of 32 block terms is added to the row's sum in block order. The warp's first row is prefetched into
 // L2 before the kernel waits for the quantizer. REG (NT == 1, at most kQRegBlocks blocks per lane): each lane
 // keeps its activation blocks in registers across rows.
-template <int T, int NT, bool REG>
+// EPI: the fused Q/K/V projection (launch_gemv_q_qkv): a warp takes the two rows of a RoPE pair (qkv_row) one after
+// the other and, once both sums are done, lanes 0..NT-1 run the epilogue of one activation row each.
+template <int T, int NT, bool REG, bool EPI = false>
 __global__ void __launch_bounds__(kQThreads) gemv_q_kernel(const QBatch b, const int8_t* __restrict__ aq,
-                                                           const float* __restrict__ ad, int64_t ne0) {
+                                                           const float* __restrict__ ad, int64_t ne0,
+                                                           const QkvEpilogue e) {
   constexpr int kQs = QTraits<T>::kQsBytes;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t nb = ne0 / 32;
@@ -125,11 +129,13 @@ __global__ void __launch_bounds__(kQThreads) gemv_q_kernel(const QBatch b, const
       }
     lr = r - begin;
   };
-  if (r0 < total) {
+  const int64_t n_items = EPI ? total / 2 : total;  // rows, or RoPE pairs of rows
+  int region = 0, head = 0, pair = 0;
+  if (r0 < n_items) {
     QWeightView w;
     float* y;
     int64_t lr, rows_j;
-    locate(r0, w, y, lr, rows_j);
+    locate(EPI ? qkv_row(2 * r0, e, region, head, pair) : r0, w, y, lr, rows_j);
     for (int64_t blk = lane; blk < nb; blk += 32)
       asm volatile("prefetch.global.L2 [%0];" ::"l"(w.qs + (lr * nb + blk) * kQs));
   }
@@ -150,7 +156,11 @@ __global__ void __launch_bounds__(kQThreads) gemv_q_kernel(const QBatch b, const
       }
     }
   }
-  for (int64_t r = r0; r < total; r += n_warps) {
+  for (int64_t item = r0; item < n_items; item += n_warps) {
+  float first[EPI ? NT : 1];
+#pragma unroll 1
+  for (int member = 0; member < (EPI ? 2 : 1); ++member) {
+    const int64_t r = EPI ? qkv_row(2 * item + member, e, region, head, pair) : item;
     QWeightView w;
     float* y;
     int64_t lr, rows_j;
@@ -189,9 +199,19 @@ __global__ void __launch_bounds__(kQThreads) gemv_q_kernel(const QBatch b, const
 #pragma unroll
         for (int t = 0; t < NT; ++t) sum[t] = __fadd_rn(sum[t], __shfl_sync(0xffffffffu, term[t], j));
     }
-    if (lane == 0)
+    if constexpr (!EPI) {
+      if (lane == 0)
 #pragma unroll
-      for (int t = 0; t < NT; ++t) y[t * rows_j + lr] = sum[t];
+        for (int t = 0; t < NT; ++t) y[t * rows_j + lr] = sum[t];
+    } else if (member == 0) {
+#pragma unroll
+      for (int t = 0; t < NT; ++t) first[t] = sum[t];  // every lane holds every row's sum
+    } else {
+#pragma unroll
+      for (int t = 0; t < NT; ++t)
+        if (lane == t) qkv_store(e, region, head, pair, t, first[t], sum[t]);
+    }
+  }
   }
 }
 
@@ -231,11 +251,12 @@ cudaLaunchAttribute pdl_attr() {
 }
 
 // Both launches use programmatic stream serialization (each kernel waits for its predecessor before reading).
-template <int T, int NT, bool REG>
-void gemv_q_t(cudaStream_t st, const QBatch& b, const int8_t* aq, const float* ad, int64_t ne0, int num_sms) {
-  const int64_t total = b.row_end[b.count - 1];
+template <int T, int NT, bool REG, bool EPI = false>
+void gemv_q_t(cudaStream_t st, const QBatch& b, const int8_t* aq, const float* ad, int64_t ne0, int num_sms,
+              const QkvEpilogue& e = QkvEpilogue{}) {
+  const int64_t total = EPI ? b.row_end[b.count - 1] / 2 : b.row_end[b.count - 1];
   int per_sm = 0;
-  check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_q_kernel<T, NT, REG>, kQThreads, 0),
+  check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_q_kernel<T, NT, REG, EPI>, kQThreads, 0),
              "quant gemv occupancy");
   const int64_t grid = std::min<int64_t>((total + kQThreads / 32 - 1) / (kQThreads / 32),
                                          int64_t(num_sms) * std::max(1, std::min(per_sm, 8)));
@@ -246,23 +267,36 @@ void gemv_q_t(cudaStream_t st, const QBatch& b, const int8_t* aq, const float* a
   cudaLaunchAttribute attr[1] = {pdl_attr()};
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  check_cuda(cudaLaunchKernelEx(&cfg, gemv_q_kernel<T, NT, REG>, b, aq, ad, ne0), "quant gemv launch");
+  check_cuda(cudaLaunchKernelEx(&cfg, gemv_q_kernel<T, NT, REG, EPI>, b, aq, ad, ne0, e), "quant gemv launch");
 }
 
-template <int T>
+template <int T, bool EPI = false>
 void gemv_q_dispatch(cudaStream_t st, const QBatch& b, const int8_t* aq, const float* ad, int64_t ne0, int64_t n,
-                     int sms) {
-  if (n == 1 && ne0 / 32 <= 32 * kQRegBlocks) return gemv_q_t<T, 1, true>(st, b, aq, ad, ne0, sms);
+                     int sms, const QkvEpilogue& e = QkvEpilogue{}) {
+  if (n == 1 && ne0 / 32 <= 32 * kQRegBlocks) return gemv_q_t<T, 1, true, EPI>(st, b, aq, ad, ne0, sms, e);
   switch (n) {
-    case 1: return gemv_q_t<T, 1, false>(st, b, aq, ad, ne0, sms);
-    case 2: return gemv_q_t<T, 2, false>(st, b, aq, ad, ne0, sms);
-    case 3: return gemv_q_t<T, 3, false>(st, b, aq, ad, ne0, sms);
-    case 4: return gemv_q_t<T, 4, false>(st, b, aq, ad, ne0, sms);
-    case 5: return gemv_q_t<T, 5, false>(st, b, aq, ad, ne0, sms);
-    case 6: return gemv_q_t<T, 6, false>(st, b, aq, ad, ne0, sms);
-    case 7: return gemv_q_t<T, 7, false>(st, b, aq, ad, ne0, sms);
-    default: return gemv_q_t<T, 8, false>(st, b, aq, ad, ne0, sms);
+    case 1: return gemv_q_t<T, 1, false, EPI>(st, b, aq, ad, ne0, sms, e);
+    case 2: return gemv_q_t<T, 2, false, EPI>(st, b, aq, ad, ne0, sms, e);
+    case 3: return gemv_q_t<T, 3, false, EPI>(st, b, aq, ad, ne0, sms, e);
+    case 4: return gemv_q_t<T, 4, false, EPI>(st, b, aq, ad, ne0, sms, e);
+    case 5: return gemv_q_t<T, 5, false, EPI>(st, b, aq, ad, ne0, sms, e);
+    case 6: return gemv_q_t<T, 6, false, EPI>(st, b, aq, ad, ne0, sms, e);
+    case 7: return gemv_q_t<T, 7, false, EPI>(st, b, aq, ad, ne0, sms, e);
+    default: return gemv_q_t<T, 8, false, EPI>(st, b, aq, ad, ne0, sms, e);
   }
+}
+
+// The activation rows quantized to Q8_0 blocks into act (int8 values, then the block scales): one launch.
+void quantize_act(cudaStream_t st, const float* x, int64_t nt, int64_t ne0, int8_t* aq, float* ad) {
+  const int64_t nb = ne0 / 32;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>((nt * nb + 7) / 8));
+  cfg.blockDim = dim3(256);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1] = {pdl_attr()};
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  check_cuda(cudaLaunchKernelEx(&cfg, quantize_rows_kernel, x, aq, ad, nt * nb), "quantize activations launch");
 }
 
 }  // namespace
@@ -285,19 +319,10 @@ void launch_gemv_q(cudaStream_t st, const Weight* const* ws, float* const* ys, i
   const int64_t ne0 = w0.ne0, nb = ne0 / 32;
   int8_t* aq = static_cast<int8_t*>(act);
   float* ad = reinterpret_cast<float*>(aq + kGemvMaxRows * ne0);
+  (void)nb;
   for (int64_t t0 = 0; t0 < n; t0 += kGemvMaxRows) {
     const int64_t nt = std::min<int64_t>(kGemvMaxRows, n - t0);
-    {
-      cudaLaunchConfig_t cfg = {};
-      cfg.gridDim = dim3(static_cast<unsigned>((nt * nb + 7) / 8));
-      cfg.blockDim = dim3(256);
-      cfg.stream = st;
-      cudaLaunchAttribute attr[1] = {pdl_attr()};
-      cfg.attrs = attr;
-      cfg.numAttrs = 1;
-      check_cuda(cudaLaunchKernelEx(&cfg, quantize_rows_kernel, x + t0 * ne0, aq, ad, nt * nb),
-                 "quantize activations launch");
-    }
+    quantize_act(st, x + t0 * ne0, nt, ne0, aq, ad);
     QBatch b{};
     b.count = count;
     int64_t rows = 0;
@@ -313,6 +338,37 @@ void launch_gemv_q(cudaStream_t st, const Weight* const* ws, float* const* ys, i
       default: gemv_q_dispatch<NBL_Q8_0>(st, b, aq, ad, ne0, nt, num_sms); break;
     }
   }
+}
+
+bool gemv_q_qkv_ok(const Weight* const* ws, int64_t n, int64_t n_heads, int64_t n_kv_heads) {
+  const Weight &wq = *ws[0], &wk = *ws[1], &wv = *ws[2];
+  return n >= 1 && n <= kGemvMaxRows && is_quant(wq.dtype) && wk.dtype == wq.dtype && wv.dtype == wq.dtype &&
+         wq.ne0 == wk.ne0 && wq.ne0 == wv.ne0 && n_heads > 0 && n_kv_heads > 0 && wq.ne1 == n_heads * 64 &&
+         wk.ne1 == n_kv_heads * 64 && wv.ne1 == wk.ne1;
+}
+
+bool launch_gemv_q_qkv(cudaStream_t st, const Weight* const* ws, const float* x, int64_t n, void* act,
+                       const QkvEpilogue& e, int num_sms) {
+  if (!gemv_q_qkv_ok(ws, n, e.n_heads, e.n_kv_heads)) return false;
+  const int64_t ne0 = ws[0]->ne0;
+  int8_t* aq = static_cast<int8_t*>(act);
+  float* ad = reinterpret_cast<float*>(aq + kGemvMaxRows * ne0);
+  quantize_act(st, x, n, ne0, aq, ad);
+  QBatch b{};
+  b.count = 3;
+  int64_t rows = 0;
+  for (int i = 0; i < 3; ++i) {
+    b.w[i] = ws[i]->q;
+    b.y[i] = nullptr;  // the epilogue stores instead
+    rows += ws[i]->ne1;
+    b.row_end[i] = rows;
+  }
+  switch (ws[0]->dtype) {
+    case NBL_Q4_0: gemv_q_dispatch<NBL_Q4_0, true>(st, b, aq, ad, ne0, n, num_sms, e); break;
+    case NBL_Q5_0: gemv_q_dispatch<NBL_Q5_0, true>(st, b, aq, ad, ne0, n, num_sms, e); break;
+    default: gemv_q_dispatch<NBL_Q8_0, true>(st, b, aq, ad, ne0, n, num_sms, e); break;
+  }
+  return true;
 }
 
 void launch_embed_q(cudaStream_t st, const Weight& table, const int32_t* ids, int64_t n, float* out) {

@@ -48,3 +48,53 @@ def all_gather_partials(packed, group=None):
     else:
         dist.all_gather(list(out.unbind(0)), packed, group=group)
     return out
+
+
+class PeerExchange:
+    """The same exchange without a collective library (nbl_lse_exchange_peers): each rank stores its packed partials
+    straight into every other rank's receive buffer over NVLink and raises one flag word per peer; each rank merges
+    as soon as all flags show the step. The buffers are symmetric-memory allocations from torch.distributed (the
+    same size on every rank, each rank's mapped into every other's address space), used here only for that mapping.
+    All ranks must construct it together and call exchange() the same number of times."""
+
+    def __init__(self, ctx, rows: int, head_dim: int, group=None):
+        import ctypes as C
+        import torch
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm
+        self.ctx, self.rows, self.head_dim = ctx, rows, head_dim
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > 8:
+            raise ValueError("the peer exchange takes at most 8 ranks")
+        group = group if group is not None else dist.group.WORLD
+        dev = torch.device("cuda", torch.cuda.current_device())
+        part = rows * (head_dim + 1)
+        self.recv = symm.empty(2 * self.world * part, dtype=torch.float32, device=dev)
+        self.flags = symm.empty(max(self.world, 4), dtype=torch.int32, device=dev)
+        self.flags.zero_()
+        self.sync = torch.zeros(2, dtype=torch.int32, device=dev)
+        torch.cuda.synchronize()
+        hr = symm.rendezvous(self.recv, group)
+        hf = symm.rendezvous(self.flags, group)
+
+        def peers(h, t):  # every rank's address of this tensor, mapped in this process
+            off = t.data_ptr() - int(h.buffer_ptrs[self.rank])
+            if len(h.buffer_ptrs) != self.world or off < 0 or off + t.numel() * t.element_size() > int(h.buffer_size):
+                raise RuntimeError("symmetric-memory buffer does not cover the tensor on every rank")
+            return (C.c_void_p * self.world)(*[int(p) + off for p in h.buffer_ptrs])
+
+        self._recv_ptrs, self._flag_ptrs = peers(hr, self.recv), peers(hf, self.flags)
+        self._handles = (hr, hf)
+        dist.barrier(group)
+
+    def exchange(self, send, out, lse=None):
+        """send: this rank's packed partials [rows * head_dim + rows] fp32; out [rows, head_dim] (+ lse [rows])."""
+        from . import _abi, _ptr
+        _abi.check(_abi.lib.nbl_lse_exchange_peers(
+            self.ctx.handle, _ptr(send), self.rows, self.head_dim, self.world, self.rank, self._recv_ptrs,
+            self._flag_ptrs, _ptr(self.sync), _ptr(out), _ptr(lse)))
+
+    def close(self):
+        self._handles = None
+        self.recv = self.flags = self.sync = None

@@ -1,6 +1,8 @@
 """The config-4 exchange on real GPUs: two ranks (one process per GPU, NCCL) split one long KV sequence into
 contiguous chunks, each attends its chunk with nbl_attn_decode (lse out), one NCCL all-gather moves the packed
-(O, lse) partials, and nbl_lse_merge gives both ranks the full-context result. Checked against the CPU oracle on
+(O, lse) partials, and nbl_lse_merge gives both ranks the full-context result; the exchange over peer memory
+(nbl_lse_exchange_peers: stores into the other rank's symmetric-memory buffer, flags, merge) must give the same
+bits on five steps in a row. Checked against the CPU oracle on
 the whole sequence (max relative error per head <= 1e-4), and the two ranks' merged outputs must be identical.
 
 Needs two GPUs (skipped otherwise). NVLS is off (NCCL_NVLS_ENABLE=0) and the process group has a short timeout,
@@ -75,6 +77,16 @@ def _worker(rank, world, port, outdir):
         ctx.lse_merge_packed(g, 2, ROWS * H, D, merged_packed)
         ctx.check()
         assert torch.equal(merged, merged_packed)
+        # the exchange over peer memory (stores into the other rank's buffer + flags, nbl_lse_exchange_peers) gives
+        # the same bits, call after call (the buffers alternate halves by step; flags count the steps)
+        px = ndist.PeerExchange(ctx, ROWS * H, D)
+        send = ndist.pack_partials(out, lse)
+        for step in range(5):
+            merged_peer = torch.full_like(merged, float("nan"))
+            px.exchange(send, merged_peer)
+            ctx.check()
+            assert torch.equal(merged, merged_peer), f"peer exchange differs at step {step}"
+        px.close()
         np.save(os.path.join(outdir, f"merged{rank}.npy"), merged.cpu().numpy())
         dist.barrier()
         kv.close()

@@ -47,7 +47,12 @@ class Layer:
         self.h = ctx.alloc(max_rows * E)
         self.q = ctx.alloc(max_rows * H * D)
         self.out = ctx.alloc(max_rows * H * D)
-        self.wq, self.wk, self.wv = (ctx.weight(a.astype(wdtype)) for a in w[:3])
+        if isinstance(wdtype, str):  # GGUF blocks of a quantized type, made by run_case
+            import nibble_b200 as nb
+            code = getattr(nb._abi, wdtype)
+            self.wq, self.wk, self.wv = (ctx.weight(a, code, E) for a in w[:3])
+        else:
+            self.wq, self.wk, self.wv = (ctx.weight(a.astype(wdtype)) for a in w[:3])
         self.b = [ctx.weight(a) for a in w[3:]] if bias else None
         self.bdev = None
         if bias:
@@ -90,6 +95,9 @@ def run_case(H, KV, bias, spec, seed, read_between, wdtype=np.float32):
          (rng.standard_normal(KV * D) * 0.5).astype(np.float32),
          (rng.standard_normal(KV * D) * 0.5).astype(np.float32)]
     xs = [rng.standard_normal((n, E)).astype(np.float32) for n in CHUNKS]
+    if isinstance(wdtype, str):
+        w[:3] = [oracle.random_q_blocks(rng, getattr(oracle, wdtype), rows, E, scale=0.01)
+                 for rows in (H * D, KV * D, KV * D)]
     cp, cf = nb.Context(0), nb.Context(0)
     cp.set_paged_kv(True)
     lp = Layer(cp, H, KV, bias, spec, w, N_CTX, 160, wdtype)
@@ -144,11 +152,12 @@ CASES = {
 }
 
 
-@pytest.mark.parametrize("wdtype", [np.float32, np.float16], ids=["F32", "F16"])
+@pytest.mark.parametrize("wdtype", [np.float32, np.float16, "Q4_0", "Q8_0"], ids=["F32", "F16", "Q4_0", "Q8_0"])
 @pytest.mark.parametrize("name", list(CASES))
 def test_transformer_layer_sequence_on_pages(name, wdtype):
     """Chunks of up to 8 rows run the recorded Q/K/V projection with bias + RoPE + page write in its epilogue (one
-    launch); longer chunks the projection, then one append launch. Both must reproduce the flat context's rows."""
+    launch: the float GEMV, or the quantized GEMV after its activation quantizer); longer chunks the projection,
+    then one append launch. Both must reproduce the flat context's rows."""
     import nibble_b200 as nb
     H, KV, bias, sp = CASES[name]
     spec = nb.RopeSpec(**sp)
