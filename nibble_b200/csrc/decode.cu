@@ -358,13 +358,23 @@ __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
 }
 
 // sync[0] = this rank's last pushed epoch, sync[1] = CTAs done with the current push (back to 0 after it).
+// VEC: part % 4 == 0 and 16-byte-aligned buffers, so every store over NVLink is 16 bytes.
+template <bool VEC>
 __global__ void peer_push_kernel(const float* __restrict__ send, int64_t part, PeerBufs px, int world, int rank,
                                  uint32_t* sync) {
   const uint32_t e = sync[0] + 1u;  // read by every CTA before the last one (which waits for all) updates it
   const int64_t off = (int64_t(e & 1u) * world + rank) * part;
-  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < part; i += int64_t(gridDim.x) * blockDim.x) {
-    const float v = send[i];
-    for (int p = 0; p < world; ++p) px.recv[p][off + i] = v;
+  if constexpr (VEC) {
+    const int64_t n4 = part / 4;
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n4; i += int64_t(gridDim.x) * blockDim.x) {
+      const float4 v = reinterpret_cast<const float4*>(send)[i];
+      for (int p = 0; p < world; ++p) reinterpret_cast<float4*>(px.recv[p] + off)[i] = v;
+    }
+  } else {
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < part; i += int64_t(gridDim.x) * blockDim.x) {
+      const float v = send[i];
+      for (int p = 0; p < world; ++p) px.recv[p][off + i] = v;
+    }
   }
   __threadfence_system();
   __syncthreads();
@@ -389,14 +399,16 @@ __global__ void peer_merge_kernel(const float* __restrict__ recv, const uint32_t
   if (threadIdx.x == 0 && threadIdx.y == 0) {
     ok = 1;
     const uint64_t t0 = globaltimer_ns();
+    // relaxed polls; one acquire load per flag once it shows the epoch orders the data reads after it
     for (int q = 0; q < world && ok; ++q) {
-      while (static_cast<int32_t>(ld_acquire_sys(flags + q) - e) < 0) {
+      while (static_cast<int32_t>(*reinterpret_cast<const volatile uint32_t*>(flags + q) - e) < 0) {
         if (globaltimer_ns() - t0 > kWaitLimitNs || (*reinterpret_cast<volatile int*>(err) & kErrTimeout)) {
           flag_error(err, kErrTimeout);
           ok = 0;
           break;
         }
       }
+      if (ok) (void)ld_acquire_sys(flags + q);
     }
   }
   __syncthreads();
@@ -567,8 +579,12 @@ void launch_lse_exchange_peers(cudaStream_t st, const float* send, int64_t rows,
     px.flags[p] = flags[p];
   }
   const int64_t part = rows * (int64_t(head_dim) + 1);
-  const int push_grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((part + 255) / 256, num_sms)));
-  peer_push_kernel<<<push_grid, 256, 0, st>>>(send, part, px, world, rank, sync);
+  bool vec = part % 4 == 0 && (reinterpret_cast<uintptr_t>(send) & 15u) == 0;
+  for (int p = 0; p < world; ++p) vec = vec && (reinterpret_cast<uintptr_t>(recv[p]) & 15u) == 0;
+  const int64_t items = vec ? part / 4 : part;
+  const int push_grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((items + 255) / 256, num_sms)));
+  if (vec) peer_push_kernel<true><<<push_grid, 256, 0, st>>>(send, part, px, world, rank, sync);
+  else peer_push_kernel<false><<<push_grid, 256, 0, st>>>(send, part, px, world, rank, sync);
   check_cuda(cudaGetLastError(), "peer push launch");
   const int tx = head_dim <= 32 ? 32 : (head_dim <= 64 ? 64 : (head_dim <= 128 ? 128 : 256));
   const int ty = std::max(1, 256 / tx);
