@@ -22,8 +22,8 @@ Workloads (the benchmark configurations 1-5, synthetic seeded inputs of their sh
 With N > 1 (torchrun, one rank per GPU, NCCL) the benchmark configurations' fixed total work is split over the ranks
 ("strong" scaling): config 2's 64 sequences and config 3's 176 (sequence, layer) items evenly by sequence with no
 collective, config 5's sequences by LPT on KV length, config 4's one KV sequence in contiguous chunks whose (O, lse)
-partials every rank stores straight into the other ranks' memory over NVLink before the LSE merge
-(nbl_lse_exchange_peers; --exchange nccl uses one NCCL all-gather instead). --scaling weak gives every rank the whole configuration
+partials one NCCL all-gather moves before the LSE merge (--exchange peer: every rank stores its partials straight
+into the other ranks' memory over NVLink instead, nbl_lse_exchange_peers). --scaling weak gives every rank the whole configuration
 instead (a labelled extra). value = all ranks' work / max-over-ranks device time. Every run checks sampled rows of
 its own results (config 2), and the merged long-context result (config 4) on rank 0, against a float64 attention
 computed on the GPU from the same fp16 cache; a mismatch fails the run.
@@ -908,8 +908,9 @@ def main():
     ap.add_argument("--seqs", type=int, default=0, help="config-2 sequences per GPU (default 64; smaller for profiling)")
     ap.add_argument("--prefill-seqs", type=int, default=0, help="config-3 sequences per GPU (default 8)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample length (0 skips it)")
-    ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
-                    help="config 4 at N > 1: partials stored into the peers' memory (default) or an NCCL all-gather")
+    ap.add_argument("--exchange", choices=["peer", "nccl"], default="nccl",
+                    help="config 4 at N > 1: an NCCL all-gather (default; measured faster at 8 GPUs) or the partials "
+                         "stored straight into the peers' memory")
     ap.add_argument("--scaling", choices=["strong", "weak"], default="strong",
                     help="strong: the configuration's total work split over the GPUs (default); weak: every GPU runs "
                          "all of it")
