@@ -47,12 +47,6 @@ constexpr int kPage = 16;
 constexpr int kQBytes = kBM * kD * 2;     // one Q tile: 16 KB
 constexpr int kBoxBytes = kPage * kD * 2; // 2 KB
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: p may reach 2^8 before the reference max moves
-#ifndef NBL_PREFILL_WARP_ARRIVE
-#define NBL_PREFILL_WARP_ARRIVE 1
-#endif
-// The softmax warps signal P written / O read with one arrival per warp (after __syncwarp) instead of one per thread:
-// 4 shared-memory atomics per head and tile instead of 128.
-constexpr bool kArrivePerWarp = NBL_PREFILL_WARP_ARRIVE != 0;
 
 template <int NH, int BN>
 struct Cfg {
@@ -273,9 +267,9 @@ __global__ void __launch_bounds__(Cfg<NH, BN>::kThreads, Cfg<NH, BN>::kCtasPerSm
     }
     for (int g = 0; g < NH; ++g) {
       mbar_init(&bars[C::kBarSFull + g], 1);
-      mbar_init(&bars[C::kBarPFull + g], kArrivePerWarp ? 4 : 128);
+      mbar_init(&bars[C::kBarPFull + g], 128);
       mbar_init(&bars[C::kBarODone + g], 1);
-      mbar_init(&bars[C::kBarODrained + g], kArrivePerWarp ? 4 : 128);
+      mbar_init(&bars[C::kBarODrained + g], 128);
     }
     fence_barrier_init();
   }
@@ -489,12 +483,7 @@ __global__ void __launch_bounds__(Cfg<NH, BN>::kThreads, Cfg<NH, BN>::kCtasPerSm
         }
         tc_wait_st();
         tc_fence_before();
-        if (kArrivePerWarp) {
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&bars[C::kBarPFull + g]);
-        } else {
-          mbar_arrive(&bars[C::kBarPFull + g]);
-        }
+        mbar_arrive(&bars[C::kBarPFull + g]);
       }
       if (!ok) break;
       // ---- epilogue: O_g out of TMEM (then the next work's first PV may overwrite it), normalise, store
@@ -506,12 +495,7 @@ __global__ void __launch_bounds__(Cfg<NH, BN>::kThreads, Cfg<NH, BN>::kCtasPerSm
       tmem_ld32_wait(tO, *reinterpret_cast<uint32_t(*)[32]>(&o[0]));
       tmem_ld32_wait(tO + 32, *reinterpret_cast<uint32_t(*)[32]>(&o[32]));
       tc_fence_before();
-      if (kArrivePerWarp) {
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars[C::kBarODrained + g]);
-      } else {
-        mbar_arrive(&bars[C::kBarODrained + g]);
-      }
+      mbar_arrive(&bars[C::kBarODrained + g]);
       if (wk.m0 + r < wk.qlen) {
         const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
         const int64_t orow = (int64_t(wk.qs) + wk.m0 + r) * a.n_heads + wk.head0 + g;
