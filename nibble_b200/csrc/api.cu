@@ -70,6 +70,20 @@ void nbl::ensure_scratch(nbl_ctx* ctx, size_t bytes) {
   ctx->scratch_bytes = bytes;
 }
 
+unsigned* nbl::split_counts(nbl_ctx* ctx, int64_t units) {
+  if (ctx->split_counts_n >= units) return ctx->split_counts;
+  const int64_t n = std::max<int64_t>(units, 4096);
+  auto* p = static_cast<unsigned*>(device_alloc(size_t(n) * sizeof(unsigned), "split-K counters"));
+  nbl::check_cuda(cudaMemset(p, 0, size_t(n) * sizeof(unsigned)), "split-K counters");
+  if (ctx->split_counts) {
+    nbl::check_cuda(cudaStreamSynchronize(ctx->stream), "split-K counters sync");
+    cudaFree(ctx->split_counts);
+  }
+  ctx->split_counts = p;
+  ctx->split_counts_n = n;
+  return p;
+}
+
 // Returns the device cos/sin table for (base, head_dim, factors) covering positions [0, n_pos), building it
 // on the host in double with the reference's expression (src/backend/cpu/ref_ops.cpp:173-176) if needed.
 const nbl::RopeTable& nbl::rope_table(nbl_ctx* ctx, const nbl_rope_params& rp, int64_t head_dim, int64_t n_pos) {
@@ -386,6 +400,7 @@ int nbl_ctx_destroy(nbl_ctx* ctx) {
     for (auto& a : ctx->allocs) cudaFree(a.first);
     for (auto& t : ctx->rope_tables) cudaFree(t.dev);
     if (ctx->scratch) cudaFree(ctx->scratch);
+    if (ctx->split_counts) cudaFree(ctx->split_counts);
     if (ctx->io) cudaFree(ctx->io);
     for (cudaEvent_t e : ctx->events) cudaEventDestroy(e);
     if (ctx->up_stream) cudaStreamDestroy(ctx->up_stream);
@@ -679,9 +694,13 @@ int nbl_attn_decode(nbl_ctx* ctx, const nbl_kv* kv, const float* q, const int32_
     use_device(ctx);
     const auto plan = nbl::plan_decode(n_rows, kv->cfg.n_kv_heads, n_heads / kv->cfg.n_kv_heads, n_heads,
                                        max_seq_len, kv->cfg.page_size, ctx->num_sms, n_splits);
-    if (plan.scratch_bytes) ensure_scratch(ctx, plan.scratch_bytes);
+    unsigned* counts = nullptr;
+    if (plan.scratch_bytes) {
+      ensure_scratch(ctx, plan.scratch_bytes);
+      counts = nbl::split_counts(ctx, int64_t(n_rows) * kv->cfg.n_kv_heads);
+    }
     nbl::launch_decode(ctx->stream, kv, q, page_table, pt_stride, seq_lens, n_rows, n_heads, out, lse, plan,
-                       ctx->scratch, ctx->d_err);
+                       ctx->scratch, ctx->d_err, counts);
   });
 }
 
@@ -747,7 +766,11 @@ int nbl_decode_step_host(nbl_ctx* ctx, nbl_kv* kv, const float* q_in_h, const fl
                                   kv->cfg.page_size, ctx->num_sms, 0);
       scratch = std::max(scratch, plans[c].scratch_bytes);
     }
-    if (scratch) ensure_scratch(ctx, scratch);
+    unsigned* counts = nullptr;
+    if (scratch) {
+      ensure_scratch(ctx, scratch);
+      counts = nbl::split_counts(ctx, (n_rows + chunks - 1) / chunks * int64_t(kvh) + kvh);
+    }
     // Chunks touch disjoint rows and pages, so without split partials (which share the context scratch) odd
     // chunks run on a second compute stream: one chunk's last wave overlaps the next chunk's first.
     const bool two = scratch == 0 && chunks > 1;
@@ -775,7 +798,8 @@ int nbl_decode_step_host(nbl_ctx* ctx, nbl_kv* kv, const float* q_in_h, const fl
                                  n_heads, rope->neox != 0, tab.dev, tab.n_pos, ctx->d_err, static_cast<int32_t>(r0),
                                  seq_lens);
       nbl::launch_decode(cs, kv, q + r0 * q_row, page_table + r0 * pt_stride, pt_stride, seq_lens + r0,
-                         static_cast<int>(nr), n_heads, out + r0 * q_row, nullptr, plans[c], ctx->scratch, ctx->d_err);
+                         static_cast<int>(nr), n_heads, out + r0 * q_row, nullptr, plans[c], ctx->scratch, ctx->d_err,
+                         counts);
       nbl::check_cuda(cudaEventRecord(ev_out[c], cs), "cudaEventRecord");
       nbl::check_cuda(cudaStreamWaitEvent(ctx->down_stream, ev_out[c], 0), "cudaStreamWaitEvent");
       nbl::check_cuda(cudaMemcpyAsync(out_h + r0 * q_row, out + r0 * q_row, nr * q_row * sizeof(float),

@@ -747,9 +747,13 @@ bool route_attention(nbl_ctx* ctx, const float* q, const float* k, const float* 
   if (decode) {
     const auto plan = plan_decode(static_cast<int>(n), b->kvh, static_cast<int>(G), static_cast<int>(H),
                                   static_cast<int>(pos0 + n), kPage, ctx->num_sms, 0);
-    if (plan.scratch_bytes) ensure_scratch(ctx, plan.scratch_bytes);
+    unsigned* counts = nullptr;
+    if (plan.scratch_bytes) {
+      ensure_scratch(ctx, plan.scratch_bytes);
+      counts = split_counts(ctx, n * b->kvh);
+    }
     launch_decode(ctx->stream, &b->kv, q, r->ident, static_cast<int32_t>(r->ident_pages), lens, static_cast<int>(n),
-                  static_cast<int>(H), out, nullptr, plan, ctx->scratch, ctx->d_err);
+                  static_cast<int>(H), out, nullptr, plan, ctx->scratch, ctx->d_err, counts);
   } else {
     launch_prefill(ctx->stream, &b->kv, r->q16, n, item, item + 1, item + 2, r->ident,
                    static_cast<int32_t>(r->ident_pages), 1, static_cast<int>(H), static_cast<int>(n), out, NBL_F32,

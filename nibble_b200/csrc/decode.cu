@@ -9,7 +9,12 @@
 // contiguous range of pages. Inside the CTA the 4 warps take the split's 2-page chunks round-robin; each warp
 // owns a private 3-stage ring in shared memory filled by TMA (one 16x64 box per page for K and for V, 128-byte
 // swizzle) and keeps its own online-softmax state, so the main loop has no CTA-wide barrier. The warps' states
-// are merged through shared memory at the end; splits are merged by lse_merge_kernel.
+// are merged through shared memory at the end; splits are merged by the last split of each (row, KV head) to
+// finish (an arrival counter per pair), or by lse_merge_kernel when the caller has no counters.
+//
+// Page ids are read ahead: the first three chunks' ids by six lanes at once, before q is loaded, so a CTA's first
+// K/V loads issue after one page-table latency; in the loop, the ids of the chunk a stage takes next are read at
+// the top of the iteration and used at its end.
 //
 // Arithmetic. Scores S^T[token][head] = K * Q^T and O^T[dim][head] = V^T * P^T run on the tensor cores
 // (mma.sync m16n8k16, fp16 operands, fp32 accumulation). K and V are fp16 in the pool, so they are exact
@@ -47,6 +52,7 @@ struct DecodeArgs {
   float* lse;
   float* part_o;    // [n_splits, n_rows, n_heads, 64] when n_splits > 1
   float* part_lse;  // [n_splits, n_rows, n_heads]
+  unsigned* counts; // [n_rows * n_kv_heads] arrival counters, all 0 between launches; NULL: lse_merge_kernel merges
   int* err;
   int64_t n_pages;
   int32_t pt_stride;
@@ -93,6 +99,47 @@ __global__ void __launch_bounds__(kWarps * 32, kCtasPerSm)
   }
   __syncwarp();
 
+  const uint64_t policy = policy_evict_first();
+  static_assert(kChunkPages == 2, "a chunk's page ids travel as two lanes' values");
+  // Page id of page j of this warp's chunk i, read by one lane; -1 past the split (never loaded).
+  auto chunk_pid = [&](int i, int j) -> int32_t {
+    const int pg = p_begin + (warp + kWarps * i) * kChunkPages + j;
+    return i < my_n && pg < p_end ? pt_row[pg] : -1;
+  };
+  // loaded: bit 2 * stage + j set when page j of the chunk in ring stage `stage` was loaded (identical in every
+  // lane; tokens of pages not loaded are masked).
+  uint32_t loaded = 0;
+  // Loads chunk i of this warp into ring stage `stage` given its page ids (all lanes call it; lane 0 issues).
+  // Pages whose id is out of range are not loaded and flag the error word.
+  auto issue = [&](int i, int stage, int32_t pid0, int32_t pid1) {
+    const int pg0 = p_begin + (warp + kWarps * i) * kChunkPages;
+    const int npg = min(kChunkPages, p_end - pg0);
+    const bool ok0 = pid0 >= 0 && pid0 < a.n_pages;
+    const bool ok1 = npg > 1 && pid1 >= 0 && pid1 < a.n_pages;
+    loaded = (loaded & ~(3u << (2 * stage))) | ((ok0 ? 1u : 0u) << (2 * stage)) | ((ok1 ? 2u : 0u) << (2 * stage));
+    if (lane != 0) return;
+    if (!ok0 || (npg > 1 && !ok1)) flag_error(a.err, kErrPageId);
+    uint8_t* st = ring + stage * kStageBytes;
+    mbar_arrive_expect_tx(&bars[stage], (int(ok0) + int(ok1)) * 2u * kBoxBytes);
+    if (ok0) {
+      tma_load_2d_hint(st, &tmap, 0, ((pid0 * 2 + 0) * a.n_kv_heads + kvh) * kPage, &bars[stage], policy);
+      tma_load_2d_hint(st + kChunkPages * kBoxBytes, &tmap, 0, ((pid0 * 2 + 1) * a.n_kv_heads + kvh) * kPage,
+                       &bars[stage], policy);
+    }
+    if (ok1) {
+      tma_load_2d_hint(st + kBoxBytes, &tmap, 0, ((pid1 * 2 + 0) * a.n_kv_heads + kvh) * kPage, &bars[stage], policy);
+      tma_load_2d_hint(st + (kChunkPages + 1) * kBoxBytes, &tmap, 0, ((pid1 * 2 + 1) * a.n_kv_heads + kvh) * kPage,
+                       &bars[stage], policy);
+    }
+  };
+  // The first kStages chunks: lane 2c + j reads page j of chunk c, so all their loads issue after one page-table
+  // latency, before q is read (q's load latency overlaps theirs).
+  {
+    const int32_t pf = lane < 2 * kStages ? chunk_pid(lane >> 1, lane & 1) : -1;
+    for (int i = 0; i < min(kStages, my_n); ++i)
+      issue(i, i, __shfl_sync(0xffffffffu, pf, 2 * i), __shfl_sync(0xffffffffu, pf, 2 * i + 1));
+  }
+
   // ---- Q^T as the B operand of S^T = K Q^T: lane holds head n = lane/4, dims 16ks + 2(lane%4) + {0,1} (+8)
   uint32_t qh[4][2], ql[4][2];
   {
@@ -111,32 +158,6 @@ __global__ void __launch_bounds__(kWarps * 32, kCtasPerSm)
       }
   }
 
-  const uint64_t policy = policy_evict_first();
-  // Lane 0 loads chunk i of this warp into ring stage `stage`; pages whose id is out of range are not loaded
-  // (their tokens are masked below) and flag the error word.
-  auto issue = [&](int i, int stage) {
-    const int pg0 = p_begin + (warp + kWarps * i) * kChunkPages;
-    const int npg = min(kChunkPages, p_end - pg0);
-    uint8_t* st = ring + stage * kStageBytes;
-    int32_t pid[kChunkPages];
-    uint32_t bytes = 0;
-    for (int j = 0; j < npg; ++j) {
-      pid[j] = pt_row[pg0 + j];
-      if (pid[j] >= 0 && pid[j] < a.n_pages) bytes += 2 * kBoxBytes;
-      else flag_error(a.err, kErrPageId);
-    }
-    mbar_arrive_expect_tx(&bars[stage], bytes);
-    for (int j = 0; j < npg; ++j) {
-      if (pid[j] < 0 || pid[j] >= a.n_pages) continue;
-      const int32_t yk = ((pid[j] * 2 + 0) * a.n_kv_heads + kvh) * kPage;
-      const int32_t yv = ((pid[j] * 2 + 1) * a.n_kv_heads + kvh) * kPage;
-      tma_load_2d_hint(st + j * kBoxBytes, &tmap, 0, yk, &bars[stage], policy);
-      tma_load_2d_hint(st + (kChunkPages + j) * kBoxBytes, &tmap, 0, yv, &bars[stage], policy);
-    }
-  };
-  if (lane == 0)
-    for (int i = 0; i < min(kStages, my_n); ++i) issue(i, i);
-
   float o[4][4];
 #pragma unroll
   for (int mt = 0; mt < 4; ++mt)
@@ -153,11 +174,12 @@ __global__ void __launch_bounds__(kWarps * 32, kCtasPerSm)
     const int pg0 = p_begin + (warp + kWarps * i) * kChunkPages;
     const int npg = min(kChunkPages, p_end - pg0);
     const int tok0 = pg0 * kPage;
+    // page ids of the chunk this stage takes next, read now and used at the end of the iteration
+    const int32_t nxt = lane < kChunkPages ? chunk_pid(i + kStages, lane) : -1;
     // valid-token mask: inside the sequence, on a loaded page
     uint32_t vmask = 0;
     for (int j = 0; j < npg; ++j) {
-      const int32_t pid = pt_row[pg0 + j];
-      if (pid < 0 || pid >= a.n_pages) continue;
+      if (!((loaded >> (2 * stage + j)) & 1u)) continue;
       const int nv = min(kPage, len - (tok0 + j * kPage));
       if (nv > 0) vmask |= (nv >= 32 ? 0xffffffffu : ((1u << nv) - 1u)) << (j * kPage);
     }
@@ -259,9 +281,10 @@ __global__ void __launch_bounds__(kWarps * 32, kCtasPerSm)
       }
     }
     __syncwarp();
-    if (lane == 0 && i + kStages < my_n) {
-      fence_proxy_async_smem();  // order this warp's generic smem accesses before the next async write
-      issue(i + kStages, stage);
+    if (i + kStages < my_n) {
+      const int32_t p0 = __shfl_sync(0xffffffffu, nxt, 0), p1 = __shfl_sync(0xffffffffu, nxt, 1);
+      if (lane == 0) fence_proxy_async_smem();  // order this warp's generic smem accesses before the next async write
+      issue(i + kStages, stage, p0, p1);
     }
   }
   // After a timed-out wait, drain the loads still in flight (chunks done .. done+kStages-1; bounded) before the
@@ -321,6 +344,35 @@ __global__ void __launch_bounds__(kWarps * 32, kCtasPerSm)
       a.part_o[prow * kD + d] = val;
       if (d == 0) a.part_lse[prow] = lse_nat;
     }
+  }
+  if (a.n_splits == 1 || a.counts == nullptr) return;
+  // The last split of this (row, KV head) to finish merges all splits' partials (as lse_merge_kernel does), so no
+  // second launch waits for the whole grid. The arrival counter wraps back to 0 on the last arrival (atomicInc),
+  // ready for the next launch; every CTA reaches this point, whatever happened in its main loop.
+  __shared__ int last;
+  __threadfence();  // this CTA's partials are visible device-wide before its arrival is counted
+  __syncthreads();
+  if (threadIdx.x == 0) last = atomicInc(&a.counts[rest], static_cast<unsigned>(a.n_splits - 1)) ==
+                               static_cast<unsigned>(a.n_splits - 1);
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  for (int idx = threadIdx.x; idx < G * kD; idx += kWarps * 32) {
+    const int g = idx / kD, d = idx % kD;
+    const int64_t r = int64_t(row) * a.n_heads + kvh * G + g;
+    const int64_t lse_stride = int64_t(a.n_rows) * a.n_heads;
+    float mx = -INFINITY;
+    for (int p = 0; p < a.n_splits; ++p) mx = fmaxf(mx, __ldcg(a.part_lse + p * lse_stride + r));
+    float W = 0.f, O = 0.f;
+    if (mx != -INFINITY) {
+      for (int p = 0; p < a.n_splits; ++p) {
+        const float w = expf(__ldcg(a.part_lse + p * lse_stride + r) - mx);
+        W += w;
+        if (w > 0.f) O += w * __ldcg(a.part_o + (p * lse_stride + r) * kD + d);
+      }
+    }
+    a.out[r * kD + d] = W > 0.f ? O / W : 0.f;
+    if (d == 0 && a.lse) a.lse[r] = W > 0.f ? mx + logf(W) : -INFINITY;
   }
 }
 
@@ -530,7 +582,7 @@ DecodePlan plan_decode(int n_rows, int n_kv_heads, int group, int n_heads, int m
 
 void launch_decode(cudaStream_t st, const nbl_kv* kv, const float* q, const int32_t* page_table, int32_t pt_stride,
                    const int32_t* seq_lens, int n_rows, int n_heads, float* out, float* lse, const DecodePlan& plan,
-                   void* scratch, int* err) {
+                   void* scratch, int* err, unsigned* counts) {
   const auto& c = kv->cfg;
   const int group = n_heads / c.n_kv_heads;
   DecodeArgs a{};
@@ -551,6 +603,7 @@ void launch_decode(cudaStream_t st, const nbl_kv* kv, const float* q, const int3
   if (plan.n_splits > 1) {
     a.part_o = static_cast<float*>(scratch);
     a.part_lse = a.part_o + size_t(plan.n_splits) * n_rows * n_heads * kD;
+    a.counts = counts;
   }
   const int64_t grid = int64_t(n_rows) * c.n_kv_heads * plan.n_splits;
   if (grid > 0x7fffffff) fail(NBL_E_INVALID, "decode: rows * kv_heads * splits exceeds the grid limit");
@@ -566,7 +619,7 @@ void launch_decode(cudaStream_t st, const nbl_kv* kv, const float* q, const int3
     default: fail(NBL_E_UNSUPPORTED, "decode: n_heads / n_kv_heads must be 1..8");
   }
   check_cuda(cudaGetLastError(), "decode launch");
-  if (plan.n_splits > 1)
+  if (plan.n_splits > 1 && counts == nullptr)
     launch_lse_merge(st, a.part_o, a.part_lse, plan.n_splits, int64_t(n_rows) * n_heads, kD, out, lse);
 }
 

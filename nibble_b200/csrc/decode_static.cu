@@ -13,8 +13,11 @@
 //     for an explicit split count, and served with fewer splits (down to one split, which needs no scratch) when
 //     the split count is left to the library;
 //   * every call on a device shares the one array and it keeps the last call's contents; the decode kernel
-//     writes every partial it later merges, so nothing has to start at zero. Two calls whose kernels overlap on
-//     the GPU (different streams, or different contexts on the same device) race on the array: serialise them;
+//     writes every partial it later merges, so nothing has to start at zero. The splits' arrival counters (one
+//     per (row, KV head), kStaticCounts of them) live in a second static array, zeroed at set-up and left at
+//     zero by every launch; calls with more (row, KV head) pairs merge with a second kernel instead. Two calls
+//     whose kernels overlap on the GPU (different streams, or different contexts on the same device) race on
+//     the arrays: serialise them;
 //   * set-up happens in nbl_ctx_create, once per device, with that device current: the module holding the array
 //     is loaded (which is when CUDA places the array in device memory), its address is resolved with
 //     cudaGetSymbolAddress and cached, and the decode kernels are loaded too. So the entry point's own calls,
@@ -32,11 +35,16 @@ constexpr size_t kStaticScratchBytes = size_t(8) << 20;
 constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_decode_scratch[kStaticScratchBytes];
+// 8 MiB of partials hold at most 8 MiB / (2 splits x 65 floats x 4 bytes) = 16131 (row, head) pairs, so with
+// splits every (row, KV head) pair of a call that fits has a counter.
+constexpr int kStaticCounts = 16384;
+static __device__ unsigned g_decode_counts[kStaticCounts];
 
 // Per-device device address of g_decode_scratch. In host code the symbol itself is only a host-side stand-in,
 // never a device address, so kernels are given these resolved addresses.
 std::mutex g_addr_mu;
 void* g_addr[kMaxDevices] = {};
+unsigned* g_counts_addr[kMaxDevices] = {};
 
 void* resolved_scratch(int device) {
   if (device < 0 || device >= kMaxDevices) nbl::fail(NBL_E_UNSUPPORTED, "attn_decode_static: device id >= 64");
@@ -54,13 +62,17 @@ void nbl::prepare_static_decode(int device) {
   std::lock_guard<std::mutex> lock(g_addr_mu);
   if (g_addr[device]) return;
   void* p = nullptr;
-  const cudaError_t e = cudaGetSymbolAddress(&p, g_decode_scratch);  // the caller made `device` current
-  if (e != cudaSuccess || !p) {
+  void* pc = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_decode_scratch);  // the caller made `device` current
+  if (e == cudaSuccess) e = cudaGetSymbolAddress(&pc, g_decode_counts);
+  if (e == cudaSuccess) e = cudaMemset(pc, 0, sizeof(g_decode_counts));
+  if (e != cudaSuccess || !p || !pc) {
     cudaGetLastError();  // leave no stale error for a later launch check to report
     nbl::fail(NBL_E_CUDA, std::string("cannot set up the static decode partials array: ") + cudaGetErrorString(e));
   }
   nbl::preload_decode();
   g_addr[device] = p;
+  g_counts_addr[device] = static_cast<unsigned*>(pc);
 }
 
 extern "C" NBL_API int nbl_attn_decode_static(nbl_ctx* ctx, const nbl_kv* kv, const float* q,
@@ -100,8 +112,11 @@ extern "C" NBL_API int nbl_attn_decode_static(nbl_ctx* ctx, const nbl_kv* kv, co
                               ctx->num_sms, fit >= 2 ? fit : 1);
     }
     void* scratch = plan.n_splits > 1 ? resolved_scratch(ctx->device) : nullptr;
+    unsigned* counts = plan.n_splits > 1 && int64_t(n_rows) * kv->cfg.n_kv_heads <= kStaticCounts
+                           ? g_counts_addr[ctx->device]
+                           : nullptr;
     nbl::launch_decode(ctx->stream, kv, q, page_table, pt_stride, seq_lens, n_rows, n_heads, out, lse, plan, scratch,
-                       ctx->d_err);
+                       ctx->d_err, counts);
     return NBL_OK;
   } catch (const nbl::Failure& e) {
     return nbl::record_error(e.status, e.what());

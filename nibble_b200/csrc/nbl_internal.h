@@ -52,6 +52,8 @@ struct nbl_ctx {
   void* route = nullptr;                       // nbl::Route when the paged K/V route is on (backend_route.cu)
   void* scratch = nullptr;                     // split-K partials
   size_t scratch_bytes = 0;
+  unsigned* split_counts = nullptr;            // split-K arrival counters, one per (row, KV head); 0 between launches
+  int64_t split_counts_n = 0;
   int64_t reserved_ctx = 0, reserved_heads = 0;
   std::vector<nbl::RopeTable> rope_tables;
   std::vector<nbl_kv*> kvs;
@@ -95,6 +97,9 @@ int record_error(int status, const std::string& msg);
 void* device_alloc(size_t bytes, const char* what);
 // Grows the context's split-K scratch to at least `bytes` (waits for queued work before freeing the old buffer).
 void ensure_scratch(nbl_ctx* ctx, size_t bytes);
+// The context's split-K arrival counters for `units` (row, KV head) pairs: zeroed when allocated, and every
+// decode launch leaves the counters it used at 0 again. Grows like ensure_scratch.
+unsigned* split_counts(nbl_ctx* ctx, int64_t units);
 // The device cos/sin table for (base, head_dim, factors) covering positions [0, n_pos), built on first use.
 const RopeTable& rope_table(nbl_ctx* ctx, const nbl_rope_params& rp, int64_t head_dim, int64_t n_pos);
 
@@ -130,7 +135,7 @@ DecodePlan plan_decode(int n_rows, int n_kv_heads, int group, int n_heads, int m
                        int num_sms, int requested_splits);
 void launch_decode(cudaStream_t st, const nbl_kv* kv, const float* q, const int32_t* page_table, int32_t pt_stride,
                    const int32_t* seq_lens, int n_rows, int n_heads, float* out, float* lse, const DecodePlan& plan,
-                   void* scratch, int* err);
+                   void* scratch, int* err, unsigned* counts = nullptr);
 // Loads the decode and merge kernels on the current device and sets their shared-memory attribute, so a later
 // launch needs no module load (which allocates device memory).
 void preload_decode();
