@@ -535,41 +535,33 @@ DecodePlan plan_decode(int n_rows, int n_kv_heads, int group, int n_heads, int m
   int ns = 1;
   if (requested_splits > 0) {
     ns = requested_splits;
-  } else if (units < 2 * slots) {
-    // Enough splits for >= 2 waves, at least 8 pages (4 chunks, one per warp) each; prefer a count whose CTA
-    // total fills the last wave (>= 92% of slots busy on average).
+  } else if (units * 5 < slots * 4) {
+    // Fewer units than ~0.8 of a wave of CTAs. Measured on config-2 and config-4 slices: splitting a row costs
+    // 10-15 % (each CTA's start and end, the merge), while CTAs that all run in one wave keep HBM busy; so the
+    // largest split count whose CTAs still fit one wave, with at least 8 pages per split (16 rows x 8 KV heads
+    // at 16k-64k tokens: 2 splits, 8-15 % faster than 4 or 9).
     const int ns_max = std::max(1, max_pages / 8);
-    const int ns_min = static_cast<int>(std::min<int64_t>(ns_max, (2 * slots + units - 1) / units));
-    int best = ns_min;
-    double best_eff = 0.0;
-    for (int c = ns_min; c <= std::min(ns_max, ns_min * 4); ++c) {
-      const int64_t ctas = units * c;
-      const double eff = double(ctas) / double(((ctas + slots - 1) / slots) * slots);
-      if (eff > best_eff + 1e-9) {
-        best_eff = eff;
-        best = c;
+    ns = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(ns_max, slots / units)));
+    if ((max_pages + ns - 1) / ns > 3072) {
+      // Very long rows (131k tokens on 128 units: 2 splits leave 4097 pages per CTA): at least two waves,
+      // preferring a count whose CTA total fills the last wave (>= 92 % of slots busy on average).
+      const int ns_min = static_cast<int>(std::min<int64_t>(ns_max, (2 * slots + units - 1) / units));
+      int best = ns_min;
+      double best_eff = 0.0;
+      for (int c = ns_min; c <= std::min(ns_max, ns_min * 4); ++c) {
+        const int64_t ctas = units * c;
+        const double eff = double(ctas) / double(((ctas + slots - 1) / slots) * slots);
+        if (eff > best_eff + 1e-9) {
+          best_eff = eff;
+          best = c;
+        }
+        if (eff >= 0.92) break;
       }
-      if (eff >= 0.92) break;
+      ns = best;
     }
-    ns = best;
-  } else {
-    // Enough rows for two waves: split only to fill the last wave (1024 units on 296 slots leave it 46 % busy,
-    // 86 % over the launch; two splits make it 98.8 %). At most 4 splits of at least 8 pages.
-    auto eff = [&](int c) {
-      const int64_t ctas = units * c;
-      return double(ctas) / double(((ctas + slots - 1) / slots) * slots);
-    };
-    const int ns_max = std::max(1, std::min(4, max_pages / 8));
-    int best = 1;
-    for (int c = 1; c <= ns_max; ++c) {
-      if (eff(c) > eff(best) + 1e-9) best = c;
-      if (eff(c) >= 0.92) {
-        best = c;
-        break;
-      }
-    }
-    ns = best;
   }
+  // Otherwise one split: at 256-2048 units of 4097-token rows one split measured faster than 2, 3 or 4 at every
+  // size, although a part-empty last wave is left.
   ns = std::min(ns, max_pages);
   int pps = (max_pages + ns - 1) / ns;
   pps = (pps + kChunkPages - 1) / kChunkPages * kChunkPages;  // splits start on a chunk boundary

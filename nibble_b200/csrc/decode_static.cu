@@ -103,9 +103,9 @@ extern "C" NBL_API int nbl_attn_decode_static(nbl_ctx* ctx, const nbl_kv* kv, co
                                      std::to_string(plan.scratch_bytes) + " bytes of split partials; the static "
                                      "array holds " + std::to_string(kStaticScratchBytes) +
                                      " (ask for fewer splits, or pass 0)");
-      // Library-chosen split count: the largest count whose partials fit (one split needs none). The planner asks
-      // for more than the array holds when many rows leave the last wave of CTAs part-empty (e.g. 2100 rows of 8
-      // heads: two splits, 8.7 MB).
+      // Library-chosen split count: the largest count whose partials fit (one split needs none). On 148 SMs the
+      // planner's own counts always fit (it splits only fewer than ~240 (row, KV head) pairs, into at most ~3300
+      // CTAs: <= 6.9 MB of partials); a part with more SMs could ask for more.
       const size_t per_split = size_t(n_rows) * n_heads * (64 + 1) * sizeof(float);
       const int fit = static_cast<int>(kStaticScratchBytes / per_split);
       plan = nbl::plan_decode(n_rows, kv->cfg.n_kv_heads, group, n_heads, max_seq_len, kv->cfg.page_size,

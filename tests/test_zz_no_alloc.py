@@ -88,13 +88,15 @@ def test_static_decode_refuses_partials_larger_than_its_array(setup):
 
 def test_static_decode_allocates_no_device_memory():
     """Free device memory (cudaMemGetInfo) is the same before the entry point's first call on a fresh context and
-    after two calls: one with the library's own split count, one with an explicit count whose partials fill most
-    of the array. The context, pool and every tensor exist before the first reading."""
+    after two calls: one on the first 8 rows with the library's own split count (37 splits: the rows are split to
+    fill one wave of CTAs, merged through the static counters), one on all rows with an explicit count whose
+    partials fill most of the array. The context, pool and every tensor exist before the first reading."""
     import torch
     import nibble_b200 as nb
     ctx = nb.Context(0)
     H, KV = 8, 1
-    rows = 544  # the largest library-chosen partials on 148 SMs: 7 splits x 544 rows x 8 heads x 65 floats
+    rows = 544  # 7 splits x 544 rows x 8 heads x 65 floats = 7.9 MB of the 8 MiB array
+    few = 8  # library plan: 8 units on 148 SMs x 2 CTAs -> 37 splits
     lens = [8192] * rows
     table, n_pages = make_page_tables(lens, 16, shuffle_seed=9)
     kv = ctx.kv_pool(n_pages, KV)
@@ -109,7 +111,7 @@ def test_static_decode_allocates_no_device_memory():
     ref, ref_lse = torch.empty_like(q), torch.empty((rows, H), device="cuda")
     torch.cuda.synchronize()
     free0 = torch.cuda.mem_get_info()[0]
-    _static_decode(ctx, kv, q, t_table, t_lens, 8192, outs[0], lses[0], 0)
+    _static_decode(ctx, kv, q[:few], t_table[:few], t_lens[:few], 8192, outs[0][:few], lses[0][:few], 0)
     _static_decode(ctx, kv, q, t_table, t_lens, 8192, outs[1], lses[1], 7)  # 7.9 MB of the 8 MiB array
     ctx.check()
     torch.cuda.synchronize()
@@ -118,17 +120,46 @@ def test_static_decode_allocates_no_device_memory():
     ctx.attn_decode(kv, q, t_table, t_lens, 8192, ref, ref_lse)  # the ordinary entry point, after the reading
     ctx.check()
     torch.cuda.synchronize()
-    for out, lse in zip(outs, lses):
+    for out, lse, n in zip(outs, lses, (few, rows)):
+        assert max_rel_err_per_head(out[:n].cpu().numpy(), ref[:n].cpu().numpy()) <= 1e-4
+        np.testing.assert_allclose(lse[:n].cpu().numpy(), ref_lse[:n].cpu().numpy(), rtol=0, atol=2e-5)
+    kv.close()
+    ctx.close()
+
+
+def test_static_decode_long_rows_with_the_library_split_count():
+    """Sixteen 65,537-token rows of 8 query heads over one KV head: the library splits every row 18 ways (16 units
+    fill one wave of CTAs), and the last split of each row merges all 18 through the static arrival counters. Two
+    calls in a row (the counters must be back at zero after each launch) match the ordinary entry point."""
+    import torch
+    import nibble_b200 as nb
+    ctx = nb.Context(0)
+    H, KV, rows, L = 8, 1, 16, 65537
+    table, n_pages = make_page_tables([L] * rows, 16, shuffle_seed=15)
+    kv = ctx.kv_pool(n_pages, KV)
+    g = torch.Generator(device="cuda").manual_seed(16)
+    pool = kv.tensor().view(torch.float16)
+    pool.copy_(torch.randn(pool.shape, generator=g, device="cuda").half())
+    d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()  # noqa: E731
+    t_table, t_lens = d(table), d(np.full(rows, L, np.int32))
+    ref, ref_lse = torch.empty((rows, H, D), device="cuda"), torch.empty((rows, H), device="cuda")
+    for seed in (17, 18):
+        q = torch.randn((rows, H, D), device="cuda", generator=torch.Generator(device="cuda").manual_seed(seed))
+        out = torch.full((rows, H, D), float("nan"), device="cuda")
+        lse = torch.full((rows, H), float("nan"), device="cuda")
+        _static_decode(ctx, kv, q, t_table, t_lens, L, out, lse, 0)
+        ctx.attn_decode(kv, q, t_table, t_lens, L, ref, ref_lse)
+        ctx.check()
+        torch.cuda.synchronize()
         assert max_rel_err_per_head(out.cpu().numpy(), ref.cpu().numpy()) <= 1e-4
         np.testing.assert_allclose(lse.cpu().numpy(), ref_lse.cpu().numpy(), rtol=0, atol=2e-5)
     kv.close()
     ctx.close()
 
 
-def test_static_decode_uses_fewer_splits_when_the_library_plan_does_not_fit():
-    """2100 rows of 8 query heads over one KV head: the library's own plan wants two splits (8.7 MB of partials, more
-    than the 8 MiB array) to fill the last wave of CTAs; the static entry point runs the largest split count that
-    fits (one) and its results match the ordinary entry point's two-split results, on two calls in a row."""
+def test_static_decode_many_rows_with_the_library_split_count():
+    """2100 rows of 8 query heads over one KV head: the library runs one split per row (no partials), and the
+    static entry point's results match the ordinary entry point's, on two calls in a row."""
     import torch
     import nibble_b200 as nb
     ctx = nb.Context(0)
