@@ -68,11 +68,11 @@ def peaks():
 # sizes, from one ncu capture each on a smaller case of the same kernel, scaled by the units processed (traffic grows
 # in proportion):
 #   decode_kernel, config 2: `ncu --set full --clock-control none -k regex:decode_kernel -s 3 -c 1 python bench.py
-#     --seqs 8 --steps 1 --warmup 3 --no-prefill --no-extra --no-e2e --cpu-seconds 0` -> 1.0838 GB for 128 rows,
-#     x 8 for the 1024-row launch;
+#     --seqs 8 --steps 1 --warmup 3 --no-prefill --no-extra --no-e2e --cpu-seconds 0` -> 1.0834 GB for 128 rows
+#     (1.079154 GB read + 4.28 MB written), x 8 for the 1024-row launch;
 #   prefill_kernel, config 3: `ncu --set full --clock-control none -k regex:prefill_kernel -s 3 -c 1 python bench.py
 #     --workload prefill --prefill-seqs 1 --steps 1 --warmup 3` -> 371.3 MB for 22 items, x 8 for 176 items.
-TRAFFIC_DECODE_CFG2 = 8670288000
+TRAFFIC_DECODE_CFG2 = 8667488000
 TRAFFIC_PREFILL_CFG3 = 2970780000
 
 
