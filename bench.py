@@ -23,7 +23,8 @@ With N > 1 (torchrun, one rank per GPU, NCCL) the benchmark configurations' fixe
 ("strong" scaling): config 2's 64 sequences and config 3's 176 (sequence, layer) items evenly by sequence with no
 collective, config 5's sequences by LPT on KV length, config 4's one KV sequence in contiguous chunks whose (O, lse)
 partials one NCCL all-gather moves before the LSE merge (--exchange peer: every rank stores its partials straight
-into the other ranks' memory over NVLink instead, nbl_lse_exchange_peers). --scaling weak gives every rank the whole configuration
+into the other ranks' memory over NVLink instead, nbl_lse_exchange_peers; --exchange fused: the decode kernel stores
+them there itself, nbl_attn_decode_peers). --scaling weak gives every rank the whole configuration
 instead (a labelled extra). value = all ranks' work / max-over-ranks device time. Every run checks sampled rows of
 its own results (config 2), and the merged long-context result (config 4) on rank 0, against a float64 attention
 computed on the GPU from the same fp16 cache; a mismatch fails the run.
@@ -447,7 +448,8 @@ def decode_long(args, world, rank, local, steps, warmup):
     t_table, lens = d(table), d(np.full(rows, my_len, np.int32))
     main = torch.cuda.current_stream()
 
-    px = ndist.PeerExchange(ctx, rows * H4, D) if world > 1 and args.exchange == "peer" else None
+    px = ndist.PeerExchange(ctx, rows * H4, D) if world > 1 and args.exchange in ("peer", "fused") else None
+    fused = px is not None and args.exchange == "fused"
 
     def decode():
         ctx.attn_decode(kv, q, t_table, lens, max(1, my_len), out, lse)
@@ -461,6 +463,9 @@ def decode_long(args, world, rank, local, steps, warmup):
             ctx.lse_merge_packed(recv, world, rows * H4, D, merged)
 
     def step():
+        if fused:  # the decode kernel stores its finished rows into every rank's buffer; then the merge
+            px.decode_exchange(kv, q, t_table, lens, max(1, my_len), merged.view(rows, H4, D))
+            return
         decode()
         if world > 1:
             exchange()
@@ -501,9 +506,10 @@ def decode_long(args, world, rank, local, steps, warmup):
     torch.cuda.synchronize()
     ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
     ctx.check()
-    # the exchange on its own (peer stores + flags + merge, or the NCCL all-gather + merge), timed with events
+    # the exchange on its own (peer stores + flags + merge, or the NCCL all-gather + merge), timed with events; fused
+    # into the decode it has no launch of its own, so its part is the step minus the decode alone
     ex_ms = 0.0
-    if world > 1:
+    if world > 1 and not fused:
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
         barrier(world)
         for x0, x1 in ev:
@@ -513,6 +519,8 @@ def decode_long(args, world, rank, local, steps, warmup):
         torch.cuda.synchronize()
         ex_ms = max_over_ranks(statistics.mean(a.elapsed_time(b) for a, b in ev), world)
     kern_max_ms = max_over_ranks(kern_ms, world)
+    if fused:
+        ex_ms = max(0.0, ms - kern_max_ms)
     del graph  # released before the process group is destroyed
     # parity: layer 0's merged result on rank 0 against a float64 attention over the whole 131073-token cache, whose
     # chunks the ranks send to rank 0 (an all-gather of each rank's layer-0 K/V, outside the timed region)
@@ -545,7 +553,9 @@ def decode_long(args, world, rank, local, steps, warmup):
     res = {"metric": "decode attn HBM GB/s", "value": total_kv / (ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ms,
            "scaling": "strong",
            "step_ms_breakdown": {**parts, "graph_step": ms, "decode_share": kern_max_ms / ms,
-                                 "exchange_kind": ("peer stores over NVLink + flags + merge (nbl_lse_exchange_peers)"
+                                 "exchange_kind": ("decode kernel storing into the peers' memory + flags + merge "
+                                                   "(nbl_attn_decode_peers; exchange = step - decode)" if fused else
+                                                   "peer stores over NVLink + flags + merge (nbl_lse_exchange_peers)"
                                                    if px is not None else "NCCL all-gather + nbl_lse_merge_packed"),
                                  "limiter": "decode (HBM)" if kern_max_ms >= 0.5 * ms else "exchange"},
            "parity": {"check": "layer 0 merged over all ranks' chunks vs float64 attention on rank 0",
@@ -908,9 +918,9 @@ def main():
     ap.add_argument("--seqs", type=int, default=0, help="config-2 sequences per GPU (default 64; smaller for profiling)")
     ap.add_argument("--prefill-seqs", type=int, default=0, help="config-3 sequences per GPU (default 8)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample length (0 skips it)")
-    ap.add_argument("--exchange", choices=["peer", "nccl"], default="nccl",
-                    help="config 4 at N > 1: an NCCL all-gather (default; measured faster at 8 GPUs) or the partials "
-                         "stored straight into the peers' memory")
+    ap.add_argument("--exchange", choices=["peer", "nccl", "fused"], default="nccl",
+                    help="config 4 at N > 1: an NCCL all-gather (default; measured faster at 8 GPUs), the partials "
+                         "stored straight into the peers' memory by a push kernel, or by the decode kernel itself")
     ap.add_argument("--scaling", choices=["strong", "weak"], default="strong",
                     help="strong: the configuration's total work split over the GPUs (default); weak: every GPU runs "
                          "all of it")

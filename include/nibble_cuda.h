@@ -301,6 +301,20 @@ NBL_API int nbl_lse_exchange_peers(nbl_ctx* ctx, const float* send, int64_t rows
                                    int32_t rank, void* const* recv_bufs, void* const* flag_bufs, uint32_t* sync,
                                    float* out, float* lse);
 
+/* nbl_attn_decode with the exchange of nbl_lse_exchange_peers fused into it: the decode kernel stores each
+ * (row, head)'s final (O, lse) -- this rank's partial over its KV chunk -- straight into slot `rank` of every rank's
+ * receive buffer (over NVLink for the other ranks), and its last finalising CTA raises this rank's flag word on every
+ * rank (system-scope release); then the merge waits for all ranks' flags (bounded, as in nbl_lse_exchange_peers) and
+ * writes out [n_rows, n_heads, 64] and, if non-NULL, lse [n_rows, n_heads]. No send buffer and no separate push
+ * launch. recv_bufs / flag_bufs / sync as for nbl_lse_exchange_peers with rows = n_rows * n_heads and head_dim 64;
+ * the pool and its arguments as for nbl_attn_decode (the library chooses the split count). Every rank must make the
+ * same sequence of calls; world <= 8. No reference counterpart (the reference never splits a softmax across
+ * devices). */
+NBL_API int nbl_attn_decode_peers(nbl_ctx* ctx, const nbl_kv* kv, const float* q, const int32_t* page_table,
+                                  int32_t pt_stride, const int32_t* seq_lens, int32_t max_seq_len, int32_t n_rows,
+                                  int32_t n_heads, int32_t world, int32_t rank, void* const* recv_bufs,
+                                  void* const* flag_bufs, uint32_t* sync, float* out, float* lse);
+
 /* ---- diagnostics ---- */
 /* Runs the library's bounded device wait (the routine every TMA / tensor-core completion wait uses) in a one-thread
  * kernel against an mbarrier that nothing arrives on, with a limit of limit_ns (0 < limit_ns <= 1e9): the wait gives

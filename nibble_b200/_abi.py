@@ -83,6 +83,7 @@ SIGNATURES = {
     "nbl_silu_mul": [_P, _P, _P, _I64],
     "nbl_selftest_bounded_wait": [_P, _I64],
     "nbl_lse_exchange_peers": [_P, _P, _I64, _I32, _I32, _I32, _P, _P, _P, _P, _P],
+    "nbl_attn_decode_peers": [_P, _P, _P, _P, _I32, _P, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _P, _P],
 }
 _RESTYPES = {"nbl_last_error": C.c_size_t, "nbl_ctx_stream": _P}
 

@@ -81,7 +81,7 @@ def build(force: bool = False, verbose: bool = False, extra: list[str] | None = 
     if failed:
         raise RuntimeError(f"nvcc failed for {', '.join(failed)}")
     tmp = LIB + ".tmp"
-    subprocess.run([cc, *ARCH, "-shared", "-o", tmp, *objs, "-lcudart_static", "-lcublas", "-lrt", "-ldl", "-lpthread"],
+    subprocess.run([cc, *ARCH, "-shared", "-o", tmp, *objs, "-lcudart_static", "-lrt", "-ldl", "-lpthread"],
                    check=True)
     os.replace(tmp, LIB)
     with open(STAMP, "w") as f:

@@ -181,30 +181,6 @@ namespace {
 
 bool is_dtype(int32_t d) { return d == NBL_F32 || d == NBL_F16 || d == NBL_BF16; }
 
-constexpr size_t kCublasWorkspace = size_t(32) << 20;
-
-// The context's SGEMM handle with a fixed workspace (so a matmul allocates nothing), created once.
-cublasHandle_t cublas_handle(nbl_ctx* ctx) {
-  if (!ctx->cublas) {
-    cublasHandle_t h = nullptr;
-    if (cublasCreate(&h) != CUBLAS_STATUS_SUCCESS) nbl::fail(NBL_E_CUDA, "cublasCreate failed");
-    void* ws = nullptr;
-    try {
-      ws = device_alloc(kCublasWorkspace, "SGEMM workspace");
-      if (cublasSetWorkspace(h, ws, kCublasWorkspace) != CUBLAS_STATUS_SUCCESS ||
-          cublasSetMathMode(h, CUBLAS_DEFAULT_MATH) != CUBLAS_STATUS_SUCCESS)  // fp32 arithmetic, no TF32
-        nbl::fail(NBL_E_CUDA, "cublas workspace/math mode setup failed");
-    } catch (...) {
-      if (ws) cudaFree(ws);
-      cublasDestroy(h);
-      throw;
-    }
-    ctx->cublas = h;
-    ctx->cublas_ws = ws;
-  }
-  return static_cast<cublasHandle_t>(ctx->cublas);
-}
-
 // Grows the device token-id staging buffer to n ids.
 void ensure_ids(nbl_ctx* ctx, int64_t n) {
   if (ctx->ids_cap >= n) return;
@@ -221,22 +197,8 @@ void release_weight(nbl_weight* w) {
   nbl::release_qgemm(w->w.qg);
   if (w->w.tf_hi) cudaFree(w->w.tf_hi);
   if (w->w.tf_lo) cudaFree(w->w.tf_lo);
-  if (w->w.f32 && w->w.f32 != w->w.dev) cudaFree(w->w.f32);
   cudaFree(w->w.dev);
   delete w;
-}
-
-// The fp32 copy an F16 matrix needs for the SGEMM path, made on its first multi-row matmul (so decode-only use
-// never holds it). Allocates once per weight.
-const float* weight_f32(nbl_ctx* ctx, const nbl_weight* cw) {
-  auto* w = const_cast<nbl_weight*>(cw);
-  if (!w->w.f32) {
-    const int64_t count = w->w.ne0 * w->w.ne1;
-    w->w.f32 = static_cast<float*>(device_alloc(static_cast<size_t>(count) * sizeof(float), "weight fp32 copy"));
-    nbl::launch_widen_f16(ctx->stream, w->w.dev, w->w.f32, count, ctx->num_sms);
-    nbl::check_cuda(cudaGetLastError(), "widen launch");
-  }
-  return w->w.f32;
 }
 
 // Grows a context-owned scratch buffer to `need` bytes (waiting for queued work before freeing the old one).
@@ -273,12 +235,12 @@ void fgemm_operand(nbl_ctx* ctx, const nbl_weight* cw, const void** hi, const fl
 
 // Float-weight matmuls of n > kGemvMaxRows activation rows for weights sharing x: groups of up to kMaxMulti
 // weights of one float type whose rows TMA can tile run as one tensor-core GEMM launch; a row width TMA cannot
-// tile runs SGEMM.
+// tile runs the library's fp32 CUDA-core GEMM.
 void float_gemm(nbl_ctx* ctx, const nbl_weight* const* ws, float* const* ys, int count, const float* x, int64_t n) {
   for (int i0 = 0; i0 < count;) {
     const nbl::Weight& w0 = ws[i0]->w;
     if (!nbl::fgemm_supported(w0.dtype, w0.ne0)) {
-      nbl::gemm_f32(cublas_handle(ctx), ctx->stream, weight_f32(ctx, ws[i0]), x, ys[i0], w0.ne0, w0.ne1, n);
+      nbl::launch_gemm_fallback(ctx->stream, w0, x, ys[i0], n);
       ++i0;
       continue;
     }
@@ -390,8 +352,6 @@ int nbl_ctx_destroy(nbl_ctx* ctx) {
       delete kv;
     }
     for (nbl_weight* w : ctx->weights) release_weight(w);
-    if (ctx->cublas) cublasDestroy(static_cast<cublasHandle_t>(ctx->cublas));
-    if (ctx->cublas_ws) cudaFree(ctx->cublas_ws);
     if (ctx->ids) cudaFree(ctx->ids);
     if (ctx->qgemm_act) cudaFree(ctx->qgemm_act);
     if (ctx->fgemm_act) cudaFree(ctx->fgemm_act);
@@ -481,7 +441,6 @@ int nbl_reserve(nbl_ctx* ctx, int64_t n_ctx, int64_t n_heads, int64_t max_rows, 
                                        16, ctx->num_sms, 0);
     if (plan.scratch_bytes) ensure_scratch(ctx, plan.scratch_bytes);
     if (max_rows > 0) ensure_ids(ctx, max_rows);
-    if (max_rows > nbl::kGemvMaxRows) cublas_handle(ctx);
     nbl::route_reserve(ctx, n_ctx, n_heads, max_rows, max_width);
   });
 }
@@ -879,6 +838,46 @@ int nbl_lse_exchange_peers(nbl_ctx* ctx, const float* send, int64_t rows, int32_
   });
 }
 
+int nbl_attn_decode_peers(nbl_ctx* ctx, const nbl_kv* kv, const float* q, const int32_t* page_table,
+                          int32_t pt_stride, const int32_t* seq_lens, int32_t max_seq_len, int32_t n_rows,
+                          int32_t n_heads, int32_t world, int32_t rank, void* const* recv_bufs,
+                          void* const* flag_bufs, uint32_t* sync, float* out, float* lse) {
+  return guarded([&] {
+    require(ctx && kv && q && page_table && seq_lens && recv_bufs && flag_bufs && sync && out,
+            "attn_decode_peers: NULL argument");
+    require(kv->ctx == ctx, "attn_decode_peers: pool belongs to another context");
+    require(kv->cfg.dtype == NBL_F16 && kv->cfg.head_dim == 64 && kv->cfg.page_size == 16,
+            "attn_decode_peers: the decode kernel reads an NBL_F16 pool of head_dim 64, 16-token pages");
+    require(world >= 1 && world <= nbl::kMaxPeers && rank >= 0 && rank < world,
+            "attn_decode_peers: world must be 1.." + std::to_string(nbl::kMaxPeers) + " and rank in [0, world)");
+    require(n_rows >= 0 && pt_stride > 0 && max_seq_len >= 0, "attn_decode_peers: negative size");
+    require(n_heads > 0 && n_heads % kv->cfg.n_kv_heads == 0 && n_heads / kv->cfg.n_kv_heads <= 8,
+            "attn_decode_peers: n_heads must be a multiple of n_kv_heads with at most 8 query heads per KV head");
+    require(int64_t(max_seq_len) <= int64_t(pt_stride) * kv->cfg.page_size,
+            "attn_decode_peers: max_seq_len exceeds pt_stride * page_size");
+    float* recv[nbl::kMaxPeers];
+    uint32_t* flags[nbl::kMaxPeers];
+    for (int p = 0; p < world; ++p) {
+      require(recv_bufs[p] && flag_bufs[p], "attn_decode_peers: NULL peer buffer");
+      recv[p] = static_cast<float*>(recv_bufs[p]);
+      flags[p] = static_cast<uint32_t*>(flag_bufs[p]);
+    }
+    if (n_rows == 0) return;
+    use_device(ctx);
+    nbl::route_flush_queries(ctx);
+    const auto plan = nbl::plan_decode(n_rows, kv->cfg.n_kv_heads, n_heads / kv->cfg.n_kv_heads, n_heads,
+                                       max_seq_len, kv->cfg.page_size, ctx->num_sms, 0);
+    unsigned* counts = nullptr;
+    if (plan.scratch_bytes) {
+      ensure_scratch(ctx, plan.scratch_bytes);
+      counts = nbl::split_counts(ctx, int64_t(n_rows) * kv->cfg.n_kv_heads);
+    }
+    nbl::launch_decode_peers(ctx->stream, kv, q, page_table, pt_stride, seq_lens, n_rows, n_heads, plan,
+                             ctx->scratch, counts, world, rank, recv, flags, sync, out, lse, ctx->d_err,
+                             ctx->num_sms);
+  });
+}
+
 // ---- weights and the model's other ops ----
 
 int nbl_weight_create(nbl_ctx* ctx, const void* host, int32_t dtype, int64_t ne0, int64_t ne1, nbl_weight** out) {
@@ -942,7 +941,6 @@ int nbl_weight_create(nbl_ctx* ctx, const void* host, int32_t dtype, int64_t ne0
         nbl::check_cuda(cudaMemcpyAsync(w->w.dev, host, count * elem, cudaMemcpyHostToDevice, ctx->stream),
                         "weight upload");
       }
-      if (dtype == NBL_F32) w->w.f32 = static_cast<float*>(w->w.dev);  // F16: fp32 copy on first SGEMM use
       nbl::check_cuda(cudaStreamSynchronize(ctx->stream), "weight upload");
       ctx->weights.push_back(w);
     } catch (...) {

@@ -44,6 +44,28 @@ constexpr int kSmemBytes = 1024 /*alignment slack*/ + kRingBytes + kWarps * kPBy
 constexpr int kCtasPerSm = 2;
 constexpr float kLn2 = 0.6931471805599453f;
 
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// The cross-rank exchange fused into the decode (world > 0): a (row, KV head)'s final (O, lse) is stored straight
+// into slot `rank` of the current epoch's half of every rank's receive buffer ([2][world][part] floats, part =
+// rows * heads * 64 outputs followed by rows * heads lse, the layout nbl_lse_exchange_peers uses), over NVLink for
+// the other ranks; the grid's last finalising CTA then raises this rank's flag word on every rank. sync: [0] the
+// last epoch this rank pushed, [1] finalised (row, KV head) pairs of the current launch (0 between launches).
+struct PeerOut {
+  float* recv[kMaxPeers];
+  uint32_t* flags[kMaxPeers];
+  uint32_t* sync;
+  int world, rank;  // world 0: no exchange, results go to out / lse
+  int64_t part;
+};
+
 struct DecodeArgs {
   const float* q;
   const int32_t* page_table;
@@ -59,6 +81,7 @@ struct DecodeArgs {
   int n_rows, n_heads, n_kv_heads;
   int n_splits, pages_per_split;
   float scale_log2;  // log2(e) / sqrt(head_dim)
+  PeerOut px;
 };
 
 __device__ __forceinline__ float fmax3(float a, float b, float c) { return fmaxf(a, fmaxf(b, c)); }
@@ -318,6 +341,22 @@ __global__ void __launch_bounds__(kWarps * 32, kCtasPerSm)
       w_o[dim * 8 + head] = o[mt][c];
     }
   __syncthreads();
+  // A finished (row, head) output: to out / lse, or with the exchange fused in, into every rank's receive buffer.
+  // The epoch is read before this CTA is counted below, so before the last CTA advances it.
+  const uint32_t epoch = a.px.world > 0 ? a.px.sync[0] + 1u : 0u;
+  auto finish = [&](int64_t r, int d, float val, float lse_nat) {
+    if (a.px.world == 0) {
+      a.out[r * kD + d] = val;
+      if (d == 0 && a.lse) a.lse[r] = lse_nat;
+      return;
+    }
+    const int64_t slot = (int64_t(epoch & 1u) * a.px.world + a.px.rank) * a.px.part;
+    const int64_t n_out = int64_t(a.n_rows) * a.n_heads * kD;
+    for (int p = 0; p < a.px.world; ++p) {
+      a.px.recv[p][slot + r * kD + d] = val;
+      if (d == 0) a.px.recv[p][slot + n_out + r] = lse_nat;
+    }
+  };
   for (int idx = threadIdx.x; idx < G * kD; idx += kWarps * 32) {
     const int g = idx / kD, d = idx % kD;
     float mx = -INFINITY;
@@ -337,42 +376,56 @@ __global__ void __launch_bounds__(kWarps * 32, kCtasPerSm)
     const float val = L > 0.f ? O / L : 0.f;
     const float lse_nat = L > 0.f ? (mx + __log2f(L)) * kLn2 : -INFINITY;
     if (a.n_splits == 1) {
-      a.out[(int64_t(row) * a.n_heads + head) * kD + d] = val;
-      if (d == 0 && a.lse) a.lse[int64_t(row) * a.n_heads + head] = lse_nat;
+      finish(int64_t(row) * a.n_heads + head, d, val, lse_nat);
     } else {
       const int64_t prow = (int64_t(split) * a.n_rows + row) * a.n_heads + head;
       a.part_o[prow * kD + d] = val;
       if (d == 0) a.part_lse[prow] = lse_nat;
     }
   }
-  if (a.n_splits == 1 || a.counts == nullptr) return;
-  // The last split of this (row, KV head) to finish merges all splits' partials (as lse_merge_kernel does), so no
-  // second launch waits for the whole grid. The arrival counter wraps back to 0 on the last arrival (atomicInc),
-  // ready for the next launch; every CTA reaches this point, whatever happened in its main loop.
-  __shared__ int last;
-  __threadfence();  // this CTA's partials are visible device-wide before its arrival is counted
-  __syncthreads();
-  if (threadIdx.x == 0) last = atomicInc(&a.counts[rest], static_cast<unsigned>(a.n_splits - 1)) ==
-                               static_cast<unsigned>(a.n_splits - 1);
-  __syncthreads();
-  if (!last) return;
-  __threadfence();
-  for (int idx = threadIdx.x; idx < G * kD; idx += kWarps * 32) {
-    const int g = idx / kD, d = idx % kD;
-    const int64_t r = int64_t(row) * a.n_heads + kvh * G + g;
-    const int64_t lse_stride = int64_t(a.n_rows) * a.n_heads;
-    float mx = -INFINITY;
-    for (int p = 0; p < a.n_splits; ++p) mx = fmaxf(mx, __ldcg(a.part_lse + p * lse_stride + r));
-    float W = 0.f, O = 0.f;
-    if (mx != -INFINITY) {
-      for (int p = 0; p < a.n_splits; ++p) {
-        const float w = expf(__ldcg(a.part_lse + p * lse_stride + r) - mx);
-        W += w;
-        if (w > 0.f) O += w * __ldcg(a.part_o + (p * lse_stride + r) * kD + d);
+  if (a.n_splits > 1) {
+    if (a.counts == nullptr) return;  // lse_merge_kernel merges the splits
+    // The last split of this (row, KV head) to finish merges all splits' partials (as lse_merge_kernel does), so no
+    // second launch waits for the whole grid. The arrival counter wraps back to 0 on the last arrival (atomicInc),
+    // ready for the next launch; every CTA reaches this point, whatever happened in its main loop.
+    __shared__ int last;
+    __threadfence();  // this CTA's partials are visible device-wide before its arrival is counted
+    __syncthreads();
+    if (threadIdx.x == 0) last = atomicInc(&a.counts[rest], static_cast<unsigned>(a.n_splits - 1)) ==
+                                 static_cast<unsigned>(a.n_splits - 1);
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    for (int idx = threadIdx.x; idx < G * kD; idx += kWarps * 32) {
+      const int g = idx / kD, d = idx % kD;
+      const int64_t r = int64_t(row) * a.n_heads + kvh * G + g;
+      const int64_t lse_stride = int64_t(a.n_rows) * a.n_heads;
+      float mx = -INFINITY;
+      for (int p = 0; p < a.n_splits; ++p) mx = fmaxf(mx, __ldcg(a.part_lse + p * lse_stride + r));
+      float W = 0.f, O = 0.f;
+      if (mx != -INFINITY) {
+        for (int p = 0; p < a.n_splits; ++p) {
+          const float w = expf(__ldcg(a.part_lse + p * lse_stride + r) - mx);
+          W += w;
+          if (w > 0.f) O += w * __ldcg(a.part_o + (p * lse_stride + r) * kD + d);
+        }
       }
+      finish(r, d, W > 0.f ? O / W : 0.f, W > 0.f ? mx + logf(W) : -INFINITY);
     }
-    a.out[r * kD + d] = W > 0.f ? O / W : 0.f;
-    if (d == 0 && a.lse) a.lse[r] = W > 0.f ? mx + logf(W) : -INFINITY;
+  }
+  if (a.px.world == 0) return;
+  // This CTA finalised its (row, KV head): count it; the grid's last one publishes the epoch to every rank once
+  // every finalising CTA's peer stores are fenced at system scope.
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned units = static_cast<unsigned>(a.n_rows) * static_cast<unsigned>(a.n_kv_heads);
+    if (atomicAdd(&a.px.sync[1], 1u) == units - 1u) {
+      __threadfence_system();
+      a.px.sync[0] = epoch;
+      a.px.sync[1] = 0u;
+      for (int p = 0; p < a.px.world; ++p) st_release_sys(a.px.flags[p] + a.px.rank, epoch);
+    }
   }
 }
 
@@ -399,15 +452,6 @@ struct PeerBufs {
   float* recv[kMaxPeers];
   uint32_t* flags[kMaxPeers];
 };
-
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
 
 // sync[0] = this rank's last pushed epoch, sync[1] = CTAs done with the current push (back to 0 after it).
 // VEC: part % 4 == 0 and 16-byte-aligned buffers, so every store over NVLink is 16 bytes.
@@ -572,11 +616,12 @@ DecodePlan plan_decode(int n_rows, int n_kv_heads, int group, int n_heads, int m
   return p;
 }
 
-void launch_decode(cudaStream_t st, const nbl_kv* kv, const float* q, const int32_t* page_table, int32_t pt_stride,
-                   const int32_t* seq_lens, int n_rows, int n_heads, float* out, float* lse, const DecodePlan& plan,
-                   void* scratch, int* err, unsigned* counts) {
+namespace {
+
+DecodeArgs decode_args(const nbl_kv* kv, const float* q, const int32_t* page_table, int32_t pt_stride,
+                       const int32_t* seq_lens, int n_rows, int n_heads, float* out, float* lse, const DecodePlan& plan,
+                       void* scratch, int* err, unsigned* counts) {
   const auto& c = kv->cfg;
-  const int group = n_heads / c.n_kv_heads;
   DecodeArgs a{};
   a.q = q;
   a.page_table = page_table;
@@ -597,7 +642,12 @@ void launch_decode(cudaStream_t st, const nbl_kv* kv, const float* q, const int3
     a.part_lse = a.part_o + size_t(plan.n_splits) * n_rows * n_heads * kD;
     a.counts = counts;
   }
-  const int64_t grid = int64_t(n_rows) * c.n_kv_heads * plan.n_splits;
+  return a;
+}
+
+void launch_decode_kernel(cudaStream_t st, const nbl_kv* kv, const DecodeArgs& a) {
+  const int group = a.n_heads / a.n_kv_heads;
+  const int64_t grid = int64_t(a.n_rows) * a.n_kv_heads * a.n_splits;
   if (grid > 0x7fffffff) fail(NBL_E_INVALID, "decode: rows * kv_heads * splits exceeds the grid limit");
   switch (group) {
     case 1: launch_g<1>(st, kv->tmap, a, static_cast<int>(grid)); break;
@@ -611,8 +661,48 @@ void launch_decode(cudaStream_t st, const nbl_kv* kv, const float* q, const int3
     default: fail(NBL_E_UNSUPPORTED, "decode: n_heads / n_kv_heads must be 1..8");
   }
   check_cuda(cudaGetLastError(), "decode launch");
+}
+
+void launch_peer_merge(cudaStream_t st, const float* recv, const uint32_t* flags, const uint32_t* sync, int world,
+                       int64_t part, int64_t rows, int head_dim, float* out, float* lse, int* err, int num_sms) {
+  const int tx = head_dim <= 32 ? 32 : (head_dim <= 64 ? 64 : (head_dim <= 128 ? 128 : 256));
+  const int ty = std::max(1, 256 / tx);
+  const int64_t blocks = std::min<int64_t>((rows + ty - 1) / ty, int64_t(num_sms) * 4);
+  peer_merge_kernel<<<static_cast<unsigned>(std::max<int64_t>(blocks, 1)), dim3(tx, ty), 0, st>>>(
+      recv, flags, sync, world, part, rows, head_dim, out, lse, err);
+  check_cuda(cudaGetLastError(), "peer merge launch");
+}
+
+}  // namespace
+
+void launch_decode(cudaStream_t st, const nbl_kv* kv, const float* q, const int32_t* page_table, int32_t pt_stride,
+                   const int32_t* seq_lens, int n_rows, int n_heads, float* out, float* lse, const DecodePlan& plan,
+                   void* scratch, int* err, unsigned* counts) {
+  const DecodeArgs a = decode_args(kv, q, page_table, pt_stride, seq_lens, n_rows, n_heads, out, lse, plan, scratch,
+                                   err, counts);
+  launch_decode_kernel(st, kv, a);
   if (plan.n_splits > 1 && counts == nullptr)
     launch_lse_merge(st, a.part_o, a.part_lse, plan.n_splits, int64_t(n_rows) * n_heads, kD, out, lse);
+}
+
+void launch_decode_peers(cudaStream_t st, const nbl_kv* kv, const float* q, const int32_t* page_table,
+                         int32_t pt_stride, const int32_t* seq_lens, int n_rows, int n_heads, const DecodePlan& plan,
+                         void* scratch, unsigned* counts, int world, int rank, float* const* recv,
+                         uint32_t* const* flags, uint32_t* sync, float* out, float* lse, int* err, int num_sms) {
+  if (plan.n_splits > 1 && counts == nullptr) fail(NBL_E_INVALID, "decode_peers: split counters are required");
+  DecodeArgs a = decode_args(kv, q, page_table, pt_stride, seq_lens, n_rows, n_heads, nullptr, nullptr, plan, scratch,
+                             err, counts);
+  a.px.world = world;
+  a.px.rank = rank;
+  a.px.sync = sync;
+  a.px.part = int64_t(n_rows) * n_heads * (kD + 1);
+  for (int p = 0; p < world; ++p) {
+    a.px.recv[p] = recv[p];
+    a.px.flags[p] = flags[p];
+  }
+  launch_decode_kernel(st, kv, a);
+  launch_peer_merge(st, recv[rank], flags[rank], sync, world, a.px.part, int64_t(n_rows) * n_heads, kD, out, lse, err,
+                    num_sms);
 }
 
 void launch_lse_exchange_peers(cudaStream_t st, const float* send, int64_t rows, int head_dim, int world, int rank,
@@ -631,12 +721,7 @@ void launch_lse_exchange_peers(cudaStream_t st, const float* send, int64_t rows,
   if (vec) peer_push_kernel<true><<<push_grid, 256, 0, st>>>(send, part, px, world, rank, sync);
   else peer_push_kernel<false><<<push_grid, 256, 0, st>>>(send, part, px, world, rank, sync);
   check_cuda(cudaGetLastError(), "peer push launch");
-  const int tx = head_dim <= 32 ? 32 : (head_dim <= 64 ? 64 : (head_dim <= 128 ? 128 : 256));
-  const int ty = std::max(1, 256 / tx);
-  const int64_t blocks = std::min<int64_t>((rows + ty - 1) / ty, int64_t(num_sms) * 4);
-  peer_merge_kernel<<<static_cast<unsigned>(std::max<int64_t>(blocks, 1)), dim3(tx, ty), 0, st>>>(
-      recv[rank], flags[rank], sync, world, part, rows, head_dim, out, lse, err);
-  check_cuda(cudaGetLastError(), "peer merge launch");
+  launch_peer_merge(st, recv[rank], flags[rank], sync, world, part, rows, head_dim, out, lse, err, num_sms);
 }
 
 void launch_lse_merge(cudaStream_t st, const float* part_o, const float* part_lse, int n_parts, int64_t rows,

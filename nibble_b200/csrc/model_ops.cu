@@ -4,9 +4,8 @@
 //
 // Weights (F32 or F16, [ne1 rows][ne0]) live on the device as uploaded by nbl_weight_create. Decode-sized
 // matmuls (n <= kGemvMaxRows activation rows) stream the weight once with 16-byte loads and keep all n rows'
-// accumulators in registers: HBM-bound on the weight bytes. Larger n goes to cuBLAS SGEMM on an fp32 copy of
-// the weight (plain fp32 arithmetic, no TF32, so results stay within fp32 rounding of the CPU's).
-#include <cublas_v2.h>
+// accumulators in registers: HBM-bound on the weight bytes. Larger n goes to the tensor-core GEMM (f32_gemm.cu), or,
+// for a row width TMA cannot tile, to this file's fp32 CUDA-core GEMM (results within fp32 rounding of the CPU's).
 
 #include <algorithm>
 
@@ -246,11 +245,6 @@ __global__ void gemv_scalar_kernel(const T* __restrict__ w, const float* __restr
   if (lane == 0) y[t * ne1 + r] = s;
 }
 
-__global__ void widen_f16_kernel(const __half* __restrict__ src, float* __restrict__ dst, int64_t count) {
-  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < count; i += int64_t(gridDim.x) * blockDim.x)
-    dst[i] = __half2float(src[i]);
-}
-
 // ---------------------------------------------------------------- rmsnorm
 // One CTA per row: sum of squares in double, scale = 1 / sqrt(ss / d + eps) in double, y = x * scale * w rounded
 // once to float -- the reference's arithmetic (ref_ops.cpp:138-148); only the order of the double sum differs.
@@ -378,8 +372,60 @@ void launch_embed(cudaStream_t st, const Weight& table, const int32_t* ids, int6
     embed_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half*>(table.dev), ids, out, table.ne0);
 }
 
-void launch_widen_f16(cudaStream_t st, const void* src, float* dst, int64_t count, int num_sms) {
-  widen_f16_kernel<<<elementwise_grid(count, num_sms), 256, 0, st>>>(static_cast<const __half*>(src), dst, count);
+// y[n][ne1] = x[n][ne0] . W[ne1][ne0]^T in fp32 on the CUDA cores, for float weights whose row width the tensor-core
+// GEMM cannot tile with TMA (ne0 not a multiple of 8 for F16, of 4 for F32: no model nibble loads has such a width,
+// so this is a correctness path, not a fast one). 64 x 64 output tiles; each of 256 threads accumulates a 4 x 4 block
+// with fused multiply-adds over k in order, so every output is one fp32 sum of the reference's products (within
+// the fp32 summation bound of the reference's own loop, ref_ops.cpp:109-136). K is staged through shared memory
+// 16 columns at a time; any shape and any 4-byte-aligned pointers.
+constexpr int kSgTile = 64;
+
+template <typename T>
+__global__ void __launch_bounds__(256) sgemm_nt_kernel(const T* __restrict__ w, const float* __restrict__ x,
+                                                       float* __restrict__ y, int64_t ne0, int64_t ne1, int64_t n) {
+  constexpr int kK = 16;
+  __shared__ float xs[kK][kSgTile + 4];  // [k][activation row]
+  __shared__ float ws[kK][kSgTile + 4];  // [k][weight row]
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int64_t row0 = int64_t(blockIdx.y) * kSgTile, col0 = int64_t(blockIdx.x) * kSgTile;
+  float acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+  for (int64_t k0 = 0; k0 < ne0; k0 += kK) {
+    for (int i = threadIdx.x; i < kSgTile * kK; i += 256) {
+      const int r = i / kK, k = i % kK;
+      const int64_t gk = k0 + k;
+      xs[k][r] = row0 + r < n && gk < ne0 ? x[(row0 + r) * ne0 + gk] : 0.f;
+      ws[k][r] = col0 + r < ne1 && gk < ne0 ? static_cast<float>(w[(col0 + r) * ne0 + gk]) : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < kK; ++k) {
+      float a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        a[i] = xs[k][ty * 4 + i];
+        b[i] = ws[k][tx * 4 + i];
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t r = row0 + ty * 4 + i;
+    if (r >= n) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int64_t c = col0 + tx * 4 + j;
+      if (c < ne1) y[r * ne1 + c] = acc[i][j];
+    }
+  }
 }
 
 bool gemv_vector_ok(const Weight& w, const float* x) {
@@ -452,15 +498,14 @@ void launch_gemv(cudaStream_t st, const Weight& w, const float* x, float* y, int
   launch_gemv_multi(st, ws, ys, 1, x, n, num_sms);
 }
 
-void gemm_f32(cublasHandle_t h, cudaStream_t st, const float* w_f32, const float* x, float* y, int64_t ne0, int64_t ne1,
-              int64_t n) {
-  // Row-major y[n][ne1] = x[n][ne0] . W^T is column-major Y^T (ne1 x n) = W (as ne0 x ne1, transposed) . X^T.
-  const float one = 1.f, zero = 0.f;
-  if (cublasSetStream(h, st) != CUBLAS_STATUS_SUCCESS) fail(NBL_E_CUDA, "cublasSetStream failed");
-  const cublasStatus_t s =
-      cublasSgemm(h, CUBLAS_OP_T, CUBLAS_OP_N, static_cast<int>(ne1), static_cast<int>(n), static_cast<int>(ne0), &one,
-                  w_f32, static_cast<int>(ne0), x, static_cast<int>(ne0), &zero, y, static_cast<int>(ne1));
-  if (s != CUBLAS_STATUS_SUCCESS) fail(NBL_E_CUDA, "cublasSgemm failed (status " + std::to_string(int(s)) + ")");
+void launch_gemm_fallback(cudaStream_t st, const Weight& w, const float* x, float* y, int64_t n) {
+  const dim3 grid(static_cast<unsigned>((w.ne1 + kSgTile - 1) / kSgTile), static_cast<unsigned>((n + kSgTile - 1) / kSgTile));
+  if (grid.y > 65535u) fail(NBL_E_INVALID, "matmul: too many activation rows for the fallback GEMM");
+  if (w.dtype == NBL_F32)
+    sgemm_nt_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(w.dev), x, y, w.ne0, w.ne1, n);
+  else
+    sgemm_nt_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half*>(w.dev), x, y, w.ne0, w.ne1, n);
+  check_cuda(cudaGetLastError(), "fallback GEMM launch");
 }
 
 void launch_rmsnorm(cudaStream_t st, const float* x, const float* w, float* y, int64_t n, int64_t d, float eps) {

@@ -1,12 +1,11 @@
 // Device weights and the launches of the model's non-attention ops (model_ops.cu), shared with api.cu.
 #pragma once
-#include <cublas_v2.h>
 
 #include "nbl_internal.h"
 
 namespace nbl {
 
-// Activation rows up to which a matmul runs as the weight-streaming GEMV (decode); more rows use SGEMM.
+// Activation rows up to which a matmul runs as the weight-streaming GEMV (decode); more rows use a GEMM.
 constexpr int64_t kGemvMaxRows = 8;
 
 // A quantized weight's device arrays (quant_ops.cu): fp16 scale bits [rows][blocks], value bytes
@@ -27,21 +26,18 @@ struct QGemmOperand {
   float* scales_t = nullptr;
 };
 
-// One weight tensor on the device: ne1 rows of ne0 elements (F32, F16 or a quantized type), plus an fp32 copy of an
-// F16 matrix for the SGEMM path (equal to `dev` for F32; made on an F16 matrix's first multi-row matmul). For a
-// quantized type `dev` holds the arrays `q` points into.
+// One weight tensor on the device: ne1 rows of ne0 elements (F32, F16 or a quantized type). For a quantized type
+// `dev` holds the arrays `q` points into.
 struct Weight {
   int32_t dtype = NBL_F32;
   int64_t ne0 = 0, ne1 = 0;
   void* dev = nullptr;
-  float* f32 = nullptr;
   float *tf_hi = nullptr, *tf_lo = nullptr;  // an F32 matrix split into two tf32 terms for the tensor-core GEMM
   QWeightView q;
   QGemmOperand* qg = nullptr;
 };
 
 void launch_embed(cudaStream_t st, const Weight& table, const int32_t* ids, int64_t n, float* out, int num_sms);
-void launch_widen_f16(cudaStream_t st, const void* src, float* dst, int64_t count, int num_sms);
 // Up to kMaxMulti weights sharing one input, run as one GEMV launch (rows numbered consecutively).
 constexpr int kMaxMulti = 4;
 struct GemvBatch {
@@ -86,8 +82,9 @@ bool launch_gemv_qkv(cudaStream_t st, const Weight* const* ws, const float* x, i
 // All weights share ne0; n rows of x. Weights of mixed dtype, or unaligned ones, run one scalar launch each.
 void launch_gemv_multi(cudaStream_t st, const Weight* const* ws, float* const* ys, int count, const float* x,
                        int64_t n, int num_sms);
-void gemm_f32(cublasHandle_t h, cudaStream_t st, const float* w_f32, const float* x, float* y, int64_t ne0, int64_t ne1,
-              int64_t n);
+// y[n][ne1] = x . W^T for an F32 / F16 weight whose row width the tensor-core GEMM cannot tile (fgemm_supported
+// false): an fp32 CUDA-core GEMM of this library, any shape.
+void launch_gemm_fallback(cudaStream_t st, const Weight& w, const float* x, float* y, int64_t n);
 // f32_gemm.cu: the float matmul for more than kGemvMaxRows rows on the tensor cores at fp32 accuracy (activations
 // split into two 11-bit terms), for up to kMaxMulti weights of one type sharing x and ne0 in one launch. F16 weights:
 // w_hi[i] = the device fp16 matrix, w_lo[i] = NULL (kind::f16); F32 weights: w_hi[i] / w_lo[i] = the matrix's two

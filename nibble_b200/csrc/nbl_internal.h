@@ -62,12 +62,10 @@ struct nbl_ctx {
   size_t io_bytes = 0;
   cudaStream_t up_stream = nullptr, down_stream = nullptr, aux_stream = nullptr;
   std::vector<cudaEvent_t> events;
-  // the model's other ops (model_ops.cu): uploaded weights, the token-id staging buffer, the SGEMM handle
+  // the model's other ops (model_ops.cu): uploaded weights, the token-id staging buffer
   std::vector<nbl_weight*> weights;
   int32_t* ids = nullptr;
   int64_t ids_cap = 0;
-  void* cublas = nullptr;     // cublasHandle_t, created by nbl_reserve (max_rows > the GEMV limit) or first use
-  void* cublas_ws = nullptr;  // its fixed workspace
   void* qgemm_act = nullptr;  // activations quantized for the quantized tensor-core matmul
   size_t qgemm_act_bytes = 0;
   void* fgemm_act = nullptr;  // activations split into tf32 terms for the float tensor-core matmul
@@ -185,6 +183,12 @@ constexpr int kMaxPeers = 8;
 void launch_lse_exchange_peers(cudaStream_t st, const float* send, int64_t rows, int head_dim, int world, int rank,
                                float* const* recv, uint32_t* const* flags, uint32_t* sync, float* out, float* lse,
                                int* err, int num_sms);
+// The decode with that exchange fused in (nbl_attn_decode_peers): the decode kernel stores every finished
+// (row, head) straight into every rank's receive buffer and raises the flags; then the merge.
+void launch_decode_peers(cudaStream_t st, const nbl_kv* kv, const float* q, const int32_t* page_table,
+                         int32_t pt_stride, const int32_t* seq_lens, int n_rows, int n_heads, const DecodePlan& plan,
+                         void* scratch, unsigned* counts, int world, int rank, float* const* recv,
+                         uint32_t* const* flags, uint32_t* sync, float* out, float* lse, int* err, int num_sms);
 
 // prefill.cu
 void launch_prefill(cudaStream_t st, const nbl_kv* kv, const void* q, int64_t n_q_rows, const int32_t* q_start,

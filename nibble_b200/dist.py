@@ -95,6 +95,18 @@ class PeerExchange:
             self.ctx.handle, _ptr(send), self.rows, self.head_dim, self.world, self.rank, self._recv_ptrs,
             self._flag_ptrs, _ptr(self.sync), _ptr(out), _ptr(lse)))
 
+    def decode_exchange(self, kv, q, page_table, seq_lens, max_seq_len: int, out, lse=None):
+        """The decode of this rank's KV chunk with the exchange fused in (nbl_attn_decode_peers): q [rows, H, 64] fp32
+        with rows * H equal to this exchange's rows; out [rows, H, 64] (+ lse [rows, H]) receive the merged result of
+        all ranks' chunks. No send buffer: the decode kernel stores each finished row into every rank's buffer."""
+        from . import _abi, _ptr
+        if q.shape[0] * q.shape[1] != self.rows or self.head_dim != 64:
+            raise ValueError("q must hold this exchange's rows of head_dim 64")
+        _abi.check(_abi.lib.nbl_attn_decode_peers(
+            self.ctx.handle, kv.handle, _ptr(q), _ptr(page_table), page_table.shape[-1], _ptr(seq_lens), max_seq_len,
+            q.shape[0], q.shape[1], self.world, self.rank, self._recv_ptrs, self._flag_ptrs, _ptr(self.sync),
+            _ptr(out), _ptr(lse)))
+
     def close(self):
         self._handles = None
         self.recv = self.flags = self.sync = None

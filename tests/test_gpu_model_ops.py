@@ -39,8 +39,8 @@ def _summation_bound(w, x):
 @pytest.mark.parametrize("dt", ["f32", "f16"])
 @pytest.mark.parametrize("n", [1, 2, 3, 5, 8, 9, 33, 128, 130])
 def test_matmul_matches_oracle(nbl_ctx, dt, n):
-    """n <= 8 runs the weight-streaming GEMV (one instantiation per n), 9..127 SGEMM, n >= 128 the tensor-core GEMM
-    (kind::tf32 on operands split into tf32 terms); all within the bound of the reference's fp32 sum."""
+    """n <= 8 runs the weight-streaming GEMV (one instantiation per n), n > 8 the tensor-core GEMM (kind::f16 /
+    kind::tf32 on operands split into terms); all within the bound of the reference's fp32 sum."""
     import torch
     rng = np.random.default_rng(n * 7 + (dt == "f16"))
     for ne1, ne0 in [(37, 72), (1000, 256), (96, 2048)]:
@@ -76,7 +76,7 @@ def test_matmul_gemm_large_grid(nbl_ctx, dt):
 @pytest.mark.parametrize("dt", ["f32", "f16"])
 def test_matmul_unaligned_rows_and_pointers(nbl_ctx, dt):
     """Widths that are not whole 16-byte chunks, and an activation pointer off the 16-byte grid, take the scalar
-    GEMV; results are the same function."""
+    GEMV (and, for 12 rows of width 9, the CUDA-core GEMM); results are the same function."""
     import torch
     rng = np.random.default_rng(3)
     for ne1, ne0, n, off in [(45, 66, 3, 0), (33, 70, 1, 0), (40, 64, 2, 1), (17, 9, 12, 1)]:
@@ -89,6 +89,24 @@ def test_matmul_unaligned_rows_and_pointers(nbl_ctx, dt):
         nbl_ctx.matmul(wt, xd.data_ptr() + 4 * off, y, n)
         ref = oracle.matmul(w.view(np.uint16) if dt == "f16" else w, x, n)
         assert np.all(np.abs(host(y) - ref) <= _summation_bound(w, x) + 1e-30)
+        wt.close()
+
+
+@pytest.mark.parametrize("dt", ["f32", "f16"])
+def test_matmul_fallback_gemm_for_untileable_widths(nbl_ctx, dt):
+    """Row widths the tensor-core GEMM's TMA cannot tile (not a multiple of 8 for F16, 4 for F32) with n > 8 rows run
+    the library's fp32 CUDA-core GEMM: partial 64 x 64 tiles on both sides and a K tail, within the bound of the
+    reference's fp32 sum."""
+    import torch
+    rng = np.random.default_rng(77 + (dt == "f16"))
+    for ne1, ne0, n in [(130, 37, 70), (65, 1001, 9), (200, 9, 129), (1, 3, 300)]:
+        w = _weights(rng, ne1, ne0, dt)
+        x = rng.standard_normal((n, ne0)).astype(np.float32)
+        wt = nbl_ctx.weight(w)
+        y = torch.full((n, ne1), float("nan"), device="cuda")
+        nbl_ctx.matmul(wt, dev(x), y, n)
+        ref = oracle.matmul(w.view(np.uint16) if dt == "f16" else w, x, n)
+        assert np.all(np.abs(host(y) - ref) <= _summation_bound(w, x) + 1e-30), (ne1, ne0, n)
         wt.close()
 
 

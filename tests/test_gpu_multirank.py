@@ -2,7 +2,7 @@
 contiguous chunks, each attends its chunk with nbl_attn_decode (lse out), one NCCL all-gather moves the packed
 (O, lse) partials, and nbl_lse_merge gives both ranks the full-context result; the exchange over peer memory
 (nbl_lse_exchange_peers: stores into the other rank's symmetric-memory buffer, flags, merge) must give the same
-bits on five steps in a row. Checked against the CPU oracle on
+bits on five steps in a row, and so must the decode with that exchange fused into it (nbl_attn_decode_peers). Checked against the CPU oracle on
 the whole sequence (max relative error per head <= 1e-4), and the two ranks' merged outputs must be identical.
 
 Needs two GPUs (skipped otherwise). NVLS is off (NCCL_NVLS_ENABLE=0) and the process group has a short timeout,
@@ -86,6 +86,16 @@ def _worker(rank, world, port, outdir):
             px.exchange(send, merged_peer)
             ctx.check()
             assert torch.equal(merged, merged_peer), f"peer exchange differs at step {step}"
+        # the decode with the exchange fused in (nbl_attn_decode_peers): the decode kernel stores every finished row
+        # into both ranks' buffers and raises the flags itself; the same bits, call after call, interleaved with the
+        # unfused exchange (both advance the same step count)
+        for step in range(5):
+            merged_fused = torch.full((ROWS, H, D), float("nan"), device="cuda")
+            px.decode_exchange(kv, d(q), d(table), d(np.full(ROWS, my_len, np.int32)), max(1, my_len), merged_fused)
+            ctx.check()
+            assert torch.equal(merged.view(ROWS, H, D), merged_fused), f"fused decode + exchange differs at step {step}"
+            if step == 2:
+                px.exchange(send, merged_peer)
         px.close()
         np.save(os.path.join(outdir, f"merged{rank}.npy"), merged.cpu().numpy())
         dist.barrier()

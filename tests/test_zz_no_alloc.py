@@ -1,5 +1,5 @@
 """nbl_attn_decode_static -- the decode entry point that allocates no device memory -- against the ordinary
-nbl_attn_decode, through the C ABI.
+nbl_attn_decode and the CPU oracle, through the C ABI.
 
 Some callers cannot allocate device memory once they are running: an engine that hands all of a GPU's memory to
 its own pool at start-up, or a decode loop that cannot absorb cudaMalloc's device-wide synchronisation. For them
@@ -13,6 +13,7 @@ context so it also passes when run alone.
 import numpy as np
 import pytest
 
+import oracle
 from helpers import max_rel_err_per_head
 from nibble_b200.workloads import make_page_tables
 
@@ -40,7 +41,7 @@ def setup():
     pool = kv.tensor().view(torch.float16)
     pool.copy_(torch.randn(pool.shape, generator=g, device="cuda").half())
     d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()  # noqa: E731
-    yield ctx, kv, d(table), d(np.array(lens, np.int32)), max(lens), H
+    yield ctx, kv, d(table), d(np.array(lens, np.int32)), max(lens), H, table, lens
     kv.close()
     ctx.close()
 
@@ -48,7 +49,7 @@ def setup():
 @pytest.mark.parametrize("n_splits", [0, 5])
 def test_static_decode_matches_regular_on_two_calls_in_a_row(setup, n_splits):
     import torch
-    ctx, kv, table, lens, max_len, H = setup
+    ctx, kv, table, lens, max_len, H, np_table, np_lens = setup
     rows = lens.shape[0]
     qs = [torch.randn((rows, H, D), device="cuda", generator=torch.Generator(device="cuda").manual_seed(s))
           for s in (11, 12)]
@@ -67,12 +68,21 @@ def test_static_decode_matches_regular_on_two_calls_in_a_row(setup, n_splits):
         torch.cuda.synchronize()
         assert max_rel_err_per_head(out.cpu().numpy(), ref.cpu().numpy()) <= 1e-4
         np.testing.assert_allclose(lse.cpu().numpy(), ref_lse.cpu().numpy(), rtol=0, atol=2e-5)
+    # and against the CPU oracle (nibble's scalar attention restated) on the same fp16 pages
+    bits = kv.tensor().cpu().numpy().view(np.uint16)
+    KV = kv.n_kv_heads
+    for q, (out, _) in zip(qs, got):
+        qn, on = q.cpu().numpy(), out.cpu().numpy()
+        for r, L in enumerate(np_lens):
+            k, v = oracle.gather_pages(bits, np_table[r], L, KV, D, 16)
+            want = oracle.attention(qn[r][None], k, v, 1, L - 1, H, KV, D)[0]
+            assert max_rel_err_per_head(on[r], want) <= 1e-4, f"row {r} (length {L})"
 
 
 def test_static_decode_refuses_partials_larger_than_its_array(setup):
     import torch
     import nibble_b200 as nb
-    ctx, kv, table, lens, max_len, H = setup
+    ctx, kv, table, lens, max_len, H, _, _ = setup
     rows = 128  # 16 splits requested -> 10 splits of 2 pages: 10 x 128 rows x 32 heads x 65 floats = 10.6 MB > 8 MiB
     big_table = torch.zeros((rows, table.shape[-1]), dtype=torch.int32, device="cuda")
     big_lens = torch.full((rows,), 300, dtype=torch.int32, device="cuda")
