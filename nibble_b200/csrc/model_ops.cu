@@ -256,7 +256,7 @@ constexpr int kNormThreads = 256;
 // visible. A decode step is a chain of ~10 short dependent launches per layer, so hiding their launch latency
 // behind the GEMVs is worth 17-26 % of whole-model decode throughput. These kernels never signal their own
 // dependents early: whatever follows them starts only once they have finished (measured: letting the small
-// kernels release their successors at their start broke kernels that read their outputs).
+// kernels release their successors at their start made the batched-decoder and flat-route model checks fail).
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 template <typename... KArgs, typename... Args>
